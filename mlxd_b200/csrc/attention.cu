@@ -1,0 +1,499 @@
+// Attention for the decoder step (mlx_fast_scaled_dot_product_attention,
+// src/engine/forward.c:713-731, with the KV update of kvcache.c:98-180).
+//
+// * attention_decode: one new token. Split-KV flash-decode, grid (kv head,
+//   split). Each CTA also does the token's q/k RMSNorm + RoPE (fwd_attention
+//   :591-697) for its GQA group and the KV append (split 0 writes the slot;
+//   the split that covers the new position reads it from shared memory, so no
+//   CTA waits on another). Partial (max, sum, o) per split go to a scratch
+//   buffer; the last CTA of a kv head (atomic counter) merges them.
+// * attention_prefill: S queries over the cache, FA2-style mma.sync tiles,
+//   causal (bottom-right aligned) plus the sliding-window rule
+//   0 <= (pos_q - pos_k) < window (fwd_sliding_window_mask, forward.c:241-292).
+// * attention_small: head dims outside {64, 128} take mlx's composed
+//   fallback (q*scale in bf16, bf16 scores, precise softmax rounded to bf16,
+//   bf16 matmul with v), reproduced operation for operation.
+// Sliding-window caches are rings: position p lives in slot p % cap.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mlxd {
+
+// ------------------------------------------------------------------ decode
+
+constexpr int DEC_THREADS = 128;
+
+template <int D, int REP>
+__global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
+    constexpr int DL = D / 32;   // dims per lane
+    constexpr int NW = DEC_THREADS / 32;
+    __shared__ float s_vec[NW][D];
+    __shared__ float s_q[REP][D];
+    __shared__ __align__(16) uint16_t s_knew[D];
+    __shared__ __align__(16) uint16_t s_vnew[D];
+    __shared__ float s_m[NW][REP], s_l[NW][REP];
+    __shared__ float s_o[NW][REP][D];
+    __shared__ int s_last;
+
+    const int kh = blockIdx.x, split = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    const int pos = *a.d_pos;
+    const int T = pos + 1;
+    const int lo = a.window > 0 ? max(0, T - a.window) : 0;
+    const int span = T - lo;
+    const int s0 = lo + (int)(((long long)span * split) / a.nsplit);
+    const int s1 = lo + (int)(((long long)span * (split + 1)) / a.nsplit);
+    const int slot_new = pos % a.cap;
+    const uint16_t *qkv = a.qkv;
+    const int qstride = D * (a.gate ? 2 : 1);
+
+    // q heads of this GQA group and the new k: norm + rope, one warp each
+    for (int vi = warp; vi <= REP; vi += NW) {
+        float *v = s_vec[warp];
+        const uint16_t *src = vi < REP ? qkv + (size_t)(kh * REP + vi) * qstride
+                                       : qkv + a.qdim + (size_t)kh * D;
+        for (int d = lane; d < D; d += 32) v[d] = bf2f(src[d]);
+        __syncwarp();
+        head_norm_rope(v, D, vi < REP ? a.qn : a.kn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
+        if (vi < REP) {
+            for (int d = lane; d < D; d += 32) s_q[vi][d] = v[d];
+        } else {
+            for (int d = lane; d < D; d += 32) s_knew[d] = f2bf(v[d]);
+        }
+        __syncwarp();
+    }
+    for (int d = threadIdx.x; d < D; d += DEC_THREADS)
+        s_vnew[d] = qkv[a.qdim + (size_t)(a.hkv + kh) * D + d];
+    __syncthreads();
+    uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
+    uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
+    if (split == 0) {
+        for (int d = threadIdx.x; d < D; d += DEC_THREADS) {
+            kc[(size_t)slot_new * D + d] = s_knew[d];
+            vc[(size_t)slot_new * D + d] = s_vnew[d];
+        }
+    }
+
+    // q in registers, pre-scaled by 1/sqrt(D) * log2(e) for exp2
+    const float qscale = rsqrtf((float)D) * 1.4426950408889634f;
+    float q[REP][DL];
+#pragma unroll
+    for (int r = 0; r < REP; r++)
+#pragma unroll
+        for (int i = 0; i < DL; i++) q[r][i] = s_q[r][lane * DL + i] * qscale;
+
+    float m[REP], l[REP], o[REP][DL];
+#pragma unroll
+    for (int r = 0; r < REP; r++) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DL; i++) o[r][i] = 0.f;
+    }
+
+    auto load_row = [&](const uint16_t *base, const uint16_t *snew, int j, float (&dst)[DL]) {
+        const uint16_t *p = (j == pos) ? snew + lane * DL : base + (size_t)(j % a.cap) * D + lane * DL;
+        if constexpr (DL == 4) {
+            uint2 v = *reinterpret_cast<const uint2 *>(p);
+            dst[0] = lo_bf(v.x); dst[1] = hi_bf(v.x); dst[2] = lo_bf(v.y); dst[3] = hi_bf(v.y);
+        } else {
+            uint32_t v = *reinterpret_cast<const uint32_t *>(p);
+            dst[0] = lo_bf(v); dst[1] = hi_bf(v);
+        }
+    };
+
+    constexpr int U = 4;
+    for (int j0 = s0 + warp * U; j0 < s1; j0 += NW * U) {
+        float kr[U][DL], vr[U][DL];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            int j = j0 + u;
+            if (j < s1) {
+                load_row(kc, s_knew, j, kr[u]);
+                load_row(vc, s_vnew, j, vr[u]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            int j = j0 + u;
+            if (j >= s1) break;
+#pragma unroll
+            for (int r = 0; r < REP; r++) {
+                float s = 0.f;
+#pragma unroll
+                for (int i = 0; i < DL; i++) s = fmaf(q[r][i], kr[u][i], s);
+                s = warp_sum(s);
+                float mn = fmaxf(m[r], s);
+                float alpha = exp2f(m[r] - mn);
+                float p = exp2f(s - mn);
+                l[r] = l[r] * alpha + p;
+#pragma unroll
+                for (int i = 0; i < DL; i++) o[r][i] = fmaf(o[r][i], alpha, p * vr[u][i]);
+                m[r] = mn;
+            }
+        }
+    }
+    // merge the warps of this CTA
+#pragma unroll
+    for (int r = 0; r < REP; r++) {
+        if (lane == 0) {
+            s_m[warp][r] = m[r];
+            s_l[warp][r] = l[r];
+        }
+#pragma unroll
+        for (int i = 0; i < DL; i++) s_o[warp][r][lane * DL + i] = o[r][i];
+    }
+    __syncthreads();
+    float *part = a.part;
+    for (int idx = threadIdx.x; idx < REP * D; idx += DEC_THREADS) {
+        int r = idx / D, d = idx % D;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; w++) mx = fmaxf(mx, s_m[w][r]);
+        float ls = 0.f, os = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            float e = (s_m[w][r] == -INFINITY) ? 0.f : exp2f(s_m[w][r] - mx);
+            ls += s_l[w][r] * e;
+            os += s_o[w][r][d] * e;
+        }
+        int h = kh * REP + r;
+        float *rec = part + ((size_t)h * a.nsplit + split) * (D + 2);
+        rec[2 + d] = os;
+        if (d == 0) {
+            rec[0] = mx;
+            rec[1] = ls;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int old = atomicAdd(&a.count[kh], 1);
+        s_last = (old == a.nsplit - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // last split of this kv head: merge all splits
+    for (int idx = threadIdx.x; idx < REP * D; idx += DEC_THREADS) {
+        int r = idx / D, d = idx % D;
+        int h = kh * REP + r;
+        const float *base = part + (size_t)h * a.nsplit * (D + 2);
+        float mx = -INFINITY;
+        for (int sp = 0; sp < a.nsplit; sp++) mx = fmaxf(mx, __ldcg(base + (size_t)sp * (D + 2)));
+        float ls = 0.f, os = 0.f;
+        for (int sp = 0; sp < a.nsplit; sp++) {
+            const float *rec = base + (size_t)sp * (D + 2);
+            float ms = __ldcg(rec);
+            if (ms == -INFINITY) continue;
+            float e = exp2f(ms - mx);
+            ls += __ldcg(rec + 1) * e;
+            os += __ldcg(rec + 2 + d) * e;
+        }
+        float val = rbf(os / ls);
+        if (a.gate) {
+            float g = bf2f(qkv[(size_t)h * qstride + D + d]);
+            val = rbf(__fmul_rn(val, sigmoid_bf16(g)));
+        }
+        a.out[(size_t)h * D + d] = f2bf(val);
+    }
+    if (threadIdx.x == 0) a.count[kh] = 0;
+}
+
+template <int D>
+static int launch_decode(const AttnDecodeArgs &a, int rep, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.hkv, a.nsplit);
+    cfg.blockDim = dim3(DEC_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    switch (rep) {
+    case 1: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 1>, a)); return 0;
+    case 2: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 2>, a)); return 0;
+    case 4: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 4>, a)); return 0;
+    case 8: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 8>, a)); return 0;
+    default: set_error("attention_decode: GQA ratio %d not supported", rep); return -1;
+    }
+}
+
+int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+    int rep = a.hq / a.hkv;
+    int D = a.rope.D;
+    if (D == 128) return launch_decode<128>(a, rep, st, pdl);
+    if (D == 64) return launch_decode<64>(a, rep, st, pdl);
+    set_error("attention_decode: head_dim %d not supported", D);
+    return -1;
+}
+
+// ------------------------------------------------------------------ prefill
+
+constexpr int PF_BR = 64, PF_BC = 64, PF_THREADS = 128;
+
+template <int D>
+__global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(
+    const uint16_t *__restrict__ q, int S, int pos0, const uint16_t *__restrict__ kc,
+    const uint16_t *__restrict__ vc, int cap, int window, int hq, int hkv,
+    const uint16_t *__restrict__ gate_src, int qdim, int row_stride, uint16_t *__restrict__ out) {
+    constexpr int LD = D + 8;   // padded row (bank-conflict-free ldmatrix)
+    extern __shared__ __align__(16) uint16_t sm[];
+    uint16_t *sQ = sm;
+    uint16_t *sK = sQ + PF_BR * LD;
+    uint16_t *sV = sK + PF_BC * LD;
+    const int qt = blockIdx.x, h = blockIdx.y, kh = h / (hq / hkv);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int q0 = qt * PF_BR;
+    const int nq = min(PF_BR, S - q0);
+    const uint16_t *kbase = kc + (size_t)kh * cap * D;
+    const uint16_t *vbase = vc + (size_t)kh * cap * D;
+
+    // Q tile
+    for (int c = tid; c < PF_BR * (D / 8); c += PF_THREADS) {
+        int r = c / (D / 8), cc = c % (D / 8);
+        bool ok = r < nq;
+        const uint16_t *src = q + ((size_t)(q0 + (ok ? r : 0)) * hq + h) * D + cc * 8;
+        cp_async16_zfill(sQ + r * LD + cc * 8, src, ok);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    uint32_t qf[D / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; kk++) {
+        int r = warp * 16 + (lane & 15);
+        int c = kk * 16 + (lane >> 4) * 8;
+        ldmatrix_x4(qf[kk], sQ + r * LD + c);
+    }
+
+    const float sl2 = rsqrtf((float)D) * 1.4426950408889634f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    float oacc[D / 8][4];
+#pragma unroll
+    for (int n = 0; n < D / 8; n++) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
+
+    const int qp_lo = pos0 + q0, qp_hi = pos0 + q0 + nq - 1;   // absolute positions
+    int klo = 0;
+    if (window > 0) klo = max(0, qp_lo - window + 1);
+    const int khi = qp_hi + 1;
+    const int my_r0 = q0 + warp * 16 + g, my_r1 = my_r0 + 8;
+    const int my_p0 = pos0 + my_r0, my_p1 = pos0 + my_r1;
+
+    for (int kb = klo; kb < khi; kb += PF_BC) {
+        int nk = min(PF_BC, khi - kb);
+        __syncthreads();
+        for (int c = tid; c < PF_BC * (D / 8); c += PF_THREADS) {
+            int r = c / (D / 8), cc = c % (D / 8);
+            bool ok = r < nk;
+            size_t slot = (size_t)((kb + (ok ? r : 0)) % cap);
+            cp_async16_zfill(sK + r * LD + cc * 8, kbase + slot * D + cc * 8, ok);
+            cp_async16_zfill(sV + r * LD + cc * 8, vbase + slot * D + cc * 8, ok);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        // S = Q K^T (16 x 64 per warp)
+        float sacc[PF_BC / 8][4];
+#pragma unroll
+        for (int n = 0; n < PF_BC / 8; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; kk++) {
+#pragma unroll
+            for (int n = 0; n < PF_BC / 8; n += 2) {
+                uint32_t b[4];
+                int r = n * 8 + (lane & 7) + ((lane >> 4) << 3);
+                int c = kk * 16 + ((lane >> 3) & 1) * 8;
+                ldmatrix_x4(b, sK + r * LD + c);
+                mma_bf16_16816(sacc[n], qf[kk], b[0], b[1]);
+                mma_bf16_16816(sacc[n + 1], qf[kk], b[2], b[3]);
+            }
+        }
+        // mask + online softmax
+        float mnew[2] = {mrow[0], mrow[1]};
+#pragma unroll
+        for (int n = 0; n < PF_BC / 8; n++) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                int kp = kb + n * 8 + 2 * t + (e & 1);
+                int qp = (e < 2) ? my_p0 : my_p1;
+                int qr = (e < 2) ? my_r0 : my_r1;
+                bool ok = (kp - kb) < nk && kp <= qp && qr < S && (window <= 0 || qp - kp < window);
+                float v = ok ? sacc[n][e] * sl2 : -INFINITY;
+                sacc[n][e] = v;
+                mnew[e >> 1] = fmaxf(mnew[e >> 1], v);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            mnew[i] = fmaxf(mnew[i], __shfl_xor_sync(0xffffffffu, mnew[i], 1));
+            mnew[i] = fmaxf(mnew[i], __shfl_xor_sync(0xffffffffu, mnew[i], 2));
+        }
+        float alpha[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 2; i++) alpha[i] = (mnew[i] == -INFINITY) ? 1.f : exp2f(mrow[i] - mnew[i]);
+        uint32_t pf[PF_BC / 16][4];
+#pragma unroll
+        for (int n = 0; n < PF_BC / 8; n++) {
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float mm = mnew[e >> 1];
+                p[e] = (mm == -INFINITY) ? 0.f : exp2f(sacc[n][e] - mm);
+                rs[e >> 1] += p[e];
+            }
+            int kk = n >> 1;
+            if ((n & 1) == 0) {
+                pf[kk][0] = pack_bf2(p[0], p[1]);
+                pf[kk][1] = pack_bf2(p[2], p[3]);
+            } else {
+                pf[kk][2] = pack_bf2(p[0], p[1]);
+                pf[kk][3] = pack_bf2(p[2], p[3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 1);
+            rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 2);
+            lrow[i] = lrow[i] * alpha[i] + rs[i];
+            mrow[i] = mnew[i];
+        }
+#pragma unroll
+        for (int n = 0; n < D / 8; n++) {
+            oacc[n][0] *= alpha[0];
+            oacc[n][1] *= alpha[0];
+            oacc[n][2] *= alpha[1];
+            oacc[n][3] *= alpha[1];
+        }
+        // O += P V
+#pragma unroll
+        for (int kk = 0; kk < PF_BC / 16; kk++) {
+#pragma unroll
+            for (int n = 0; n < D / 8; n += 2) {
+                uint32_t b[4];
+                int r = kk * 16 + (lane & 15);
+                int c = n * 8 + (lane >> 4) * 8;
+                ldmatrix_x4_trans(b, sV + r * LD + c);
+                mma_bf16_16816(oacc[n], pf[kk], b[0], b[1]);
+                mma_bf16_16816(oacc[n + 1], pf[kk], b[2], b[3]);
+            }
+        }
+    }
+    // epilogue: O / l, optional qwen3_5 gate, bf16 out [S][hq][D]
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        int qr = (i == 0) ? my_r0 : my_r1;
+        if (qr >= S) continue;
+        float inv = lrow[i] > 0.f ? 1.f / lrow[i] : 0.f;
+        uint16_t *dst = out + ((size_t)qr * hq + h) * D;
+        const uint16_t *gp = gate_src ? gate_src + (size_t)qr * row_stride + (size_t)h * 2 * D + D : nullptr;
+#pragma unroll
+        for (int n = 0; n < D / 8; n++) {
+            int c = n * 8 + 2 * t;
+            float v0 = rbf(oacc[n][2 * i] * inv), v1 = rbf(oacc[n][2 * i + 1] * inv);
+            if (gp) {
+                v0 = rbf(__fmul_rn(v0, sigmoid_bf16(bf2f(gp[c]))));
+                v1 = rbf(__fmul_rn(v1, sigmoid_bf16(bf2f(gp[c + 1]))));
+            }
+            *reinterpret_cast<uint32_t *>(dst + c) = pack_bf2(v0, v1);
+        }
+    }
+}
+
+// ------------------------------------------------------------ small head dims
+// mlx composed fallback, exact order: one warp per (query, head).
+__global__ void attn_small_kernel(const uint16_t *__restrict__ q, int S, int pos0,
+                                  const uint16_t *__restrict__ kc, const uint16_t *__restrict__ vc,
+                                  int cap, int window, int hq, int hkv, int D,
+                                  const uint16_t *__restrict__ gate_src, int row_stride,
+                                  uint16_t *__restrict__ out, float *scratch, int tmax) {
+    int i = blockIdx.x, h = blockIdx.y, kh = h / (hq / hkv), lane = threadIdx.x;
+    float *sc = scratch + ((size_t)i * hq + h) * tmax;
+    int qp = pos0 + i;
+    int T = qp + 1;
+    int j0 = 0;
+    if (window > 0) {
+        if (S == 1) j0 = max(0, T - window);
+        else j0 = max(0, qp - window + 1);
+    }
+    const uint16_t *qv = q + ((size_t)i * hq + h) * D;
+    const uint16_t *K = kc + (size_t)kh * cap * D;
+    const uint16_t *V = vc + (size_t)kh * cap * D;
+    float sbf = rbf(rsqrtf((float)D));
+    for (int j = j0 + lane; j < T; j += 32) {
+        float a = 0.f;
+        for (int d = 0; d < D; d++) {
+            float qs = rbf(__fmul_rn(sbf, bf2f(qv[d])));
+            a = __fadd_rn(a, __fmul_rn(qs, bf2f(K[(size_t)(j % cap) * D + d])));
+        }
+        sc[j - j0] = rbf(a);
+    }
+    __syncwarp();
+    float mx = -INFINITY;
+    for (int j = lane; j < T - j0; j += 32) mx = fmaxf(mx, sc[j]);
+    mx = warp_max(mx);
+    for (int j = lane; j < T - j0; j += 32) sc[j] = own_expf(__fsub_rn(sc[j], mx));
+    __syncwarp();
+    float l = 0.f;
+    for (int j = 0; j < T - j0; j++) l = __fadd_rn(l, sc[j]);
+    for (int d = lane; d < D; d += 32) {
+        float o = 0.f;
+        for (int j = 0; j < T - j0; j++) {
+            float p = rbf(__fdiv_rn(sc[j], l));
+            o = __fadd_rn(o, __fmul_rn(p, bf2f(V[(size_t)((j0 + j) % cap) * D + d])));
+        }
+        float val = rbf(o);
+        if (gate_src) {
+            float g = bf2f(gate_src[(size_t)i * row_stride + (size_t)h * 2 * D + D + d]);
+            val = rbf(__fmul_rn(val, sigmoid_bf16(g)));
+        }
+        out[((size_t)i * hq + h) * D + d] = f2bf(val);
+    }
+}
+
+int attention_prefill(const uint16_t *q, int S, int pos0, const uint16_t *kc, const uint16_t *vc,
+                      int cap, int window, int hq, int hkv, int D, const uint16_t *gate_src,
+                      int qdim, uint16_t *out, cudaStream_t st) {
+    int row_stride = qdim + 2 * hkv * D;
+    if (D == 64 || D == 128) {
+        size_t smem = (size_t)(PF_BR + 2 * PF_BC) * (D + 8) * 2;
+        dim3 grid((S + PF_BR - 1) / PF_BR, hq);
+        if (D == 128) {
+            static bool set = false;
+            if (!set) {
+                MLXD_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<128>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                set = true;
+            }
+            attn_prefill_kernel<128><<<grid, PF_THREADS, smem, st>>>(
+                q, S, pos0, kc, vc, cap, window, hq, hkv, gate_src, qdim, row_stride, out);
+        } else {
+            attn_prefill_kernel<64><<<grid, PF_THREADS, smem, st>>>(
+                q, S, pos0, kc, vc, cap, window, hq, hkv, gate_src, qdim, row_stride, out);
+        }
+        MLXD_CHECK(cudaGetLastError());
+        return 0;
+    }
+    // composed path: scratch for the scores of every (query, head)
+    int tmax = pos0 + S;
+    if (window > 0 && tmax > window + S) tmax = window + S;
+    size_t need = (size_t)S * hq * tmax * sizeof(float);
+    static float *scr = nullptr;
+    static size_t scr_bytes = 0;
+    if (need > scr_bytes) {
+        if (scr) dev_free(scr);
+        scr = (float *)dev_alloc(need);
+        if (!scr) return -1;
+        scr_bytes = need;
+    }
+    dim3 grid(S, hq);
+    attn_small_kernel<<<grid, 32, 0, st>>>(q, S, pos0, kc, vc, cap, window, hq, hkv, D, gate_src,
+                                           row_stride, out, scr, tmax);
+    MLXD_CHECK(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace mlxd

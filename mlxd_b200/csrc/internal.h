@@ -1,0 +1,100 @@
+// Internal structures of libmlxd_cuda (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+#include <string>
+#include <vector>
+
+#include "../../include/mlxd_cuda.h"
+
+namespace mlxd {
+
+void set_error(const char *fmt, ...);
+bool cuda_ok(cudaError_t e, const char *what);
+#define MLXD_CHECK(call) do { if (!::mlxd::cuda_ok((call), #call)) return -1; } while (0)
+
+void *dev_alloc(size_t bytes);      // tracked cudaMalloc (nullptr + error on failure)
+void dev_free(void *p);
+
+// A projection in device memory. Quantized matrices live in the tile layout
+// written by repack: for row block rb (16 rows) and group g, 32 lanes of
+// group/4 bytes each (tiles), plus 8 scale/bias records per tile (sb).
+struct QMat {
+    int rows = 0, cols = 0;     // out, in (rows a multiple of 16)
+    int group = 64;
+    int sdtype = MLXD_BF16;     // scale/bias dtype
+    bool quant = true;
+    uint8_t *tiles = nullptr;
+    uint8_t *sb = nullptr;
+    uint16_t *dense = nullptr;  // [rows][cols] bf16 when !quant
+    size_t tile_bytes() const { return (size_t)rows / 16 * (cols / group) * 32 * (group / 4); }
+    size_t sb_bytes() const {
+        return (size_t)rows / 16 * (cols / group) * 8 * (sdtype == MLXD_F32 ? 16 : 8);
+    }
+};
+
+struct Layer {
+    QMat qkv, o, gateup, down;
+    uint16_t *ln1 = nullptr, *ln2 = nullptr, *qn = nullptr, *kn = nullptr;
+};
+
+// MLX-format embedding table kept for the row gather.
+struct Embed {
+    bool quant = true;
+    int sdtype = MLXD_BF16;
+    uint32_t *w = nullptr;   // [V][H/8]
+    void *s = nullptr, *b = nullptr;   // [V][H/G]
+    uint16_t *dense = nullptr;         // [V][H]
+};
+
+}  // namespace mlxd
+
+struct mlxd_model {
+    mlxd_model_config c;
+    int hq, hkv, qdim;          // local heads, q rows per token (x2 with gate)
+    int inter_local;            // local intermediate (tp shard)
+    int vocab_local, vocab_off; // lm_head shard
+    std::vector<mlxd::Layer> L;
+    mlxd::QMat lm;
+    mlxd::Embed embed;
+    uint16_t *norm = nullptr;
+    float *freqs = nullptr;     // llama3 freqs [D/2] (device) or null
+    // decode scratch
+    uint16_t *h = nullptr, *h1 = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr;
+    uint16_t *logits = nullptr;
+    float *part = nullptr;      // attention split partials
+    int *att_count = nullptr;   // per kv head split completion counters
+    unsigned long long *amax = nullptr;  // fused argmax key
+    int32_t *token = nullptr;   // device token slot
+    float *lp = nullptr;        // device logprob slot
+    float *part_h = nullptr;    // [hidden] f32 partial (tensor parallel)
+    float *rope_cs = nullptr;   // [positions][rope_dims/2][2] cos/sin
+    int rope_positions = 0;
+    int nsplit = 16;
+    // generate loop state
+    int32_t *ctx = nullptr;     // context ids (prompt + generated)
+    int32_t *n_ctx = nullptr;
+    int ctx_cap = 0;
+    void *graph_exec = nullptr; // cudaGraphExec_t of one greedy decode step
+    const void *graph_kv = nullptr;
+    bool graph_lp = false;
+    // prefill scratch (grown on demand)
+    int pre_cap = 0;
+    uint16_t *p_h = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_q = nullptr, *p_att = nullptr,
+             *p_act = nullptr, *p_tmp = nullptr;
+    int32_t *p_ids = nullptr;
+    float *p_part = nullptr;
+    cudaStream_t stream = nullptr;
+    // tensor parallel
+    void *nccl = nullptr;       // ncclComm_t when tp_size > 1
+    size_t weight_bytes = 0;
+};
+
+struct mlxd_kv {
+    int layers, hkv, d, cap;
+    int window;                 // ring buffer when > 0
+    int offset;                 // absolute positions written (host mirror)
+    uint16_t *k = nullptr, *v = nullptr;   // [L][hkv][cap][d]
+    int32_t *d_pos = nullptr;   // device copy of offset (position of the next token)
+};

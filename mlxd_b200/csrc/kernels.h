@@ -1,0 +1,82 @@
+// Host-side launchers of the device kernels (internal).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "internal.h"
+
+namespace mlxd {
+
+// ---- repack (qgemv.cu)
+// MLX-format triplet rows [r0, r0+nrows) x cols [c0, c0+ncols) of a source
+// with row strides ldw (u32 words) / lds (scale elements), written as
+// destination row blocks dst_rb0 + dst_rb_stride * i.
+int repack_quant(QMat &dst, const uint32_t *w, const void *s, const void *b, int sdtype,
+                 int ldw, int lds, int r0, int nrows, int c0, int dst_rb0, int dst_rb_stride,
+                 cudaStream_t st);
+
+// ---- decode GEMV (qgemv.cu)
+enum { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_PARTIAL_F32 = 4 };
+struct GemvArgs {
+    const uint8_t *tiles;
+    const uint8_t *sb;
+    int rows, cols;
+    const uint16_t *x;          // bf16 [cols]
+    const uint16_t *norm_w;     // PRO_RMSNORM
+    float eps;
+    uint16_t *y;                // bf16 [rows] (EPI_SWIGLU: [rows/2])
+    float *yf;                  // EPI_PARTIAL_F32: f32 [rows]
+    const uint16_t *residual;   // EPI_RESIDUAL
+    unsigned long long *amax;   // EPI_ARGMAX
+    int row_offset;             // EPI_ARGMAX: global index of row 0
+};
+int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl);
+
+// ---- prefill GEMM / dense (qgemm.cu)
+// y[S][rows] = x[S][cols] . W^T with epilogue (STORE/RESIDUAL/SWIGLU)
+int linear_multi(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi,
+                 const uint16_t *residual, float *yf, cudaStream_t st);
+
+// ---- small ops (ops.cu)
+int embed_rows(const Embed &e, int H, int group, const int32_t *ids, int S, uint16_t *h,
+               cudaStream_t st);
+int rmsnorm_rows(const uint16_t *x, int rows, int n, const uint16_t *w, float eps, uint16_t *y,
+                 cudaStream_t st);
+// prefill: q/k norm + rope + kv append for S tokens at positions pos0..pos0+S-1
+struct RopeArgs {
+    int D, rope_dims;
+    const float *cs;     // device cos/sin table [positions][rope_dims/2][2]
+};
+int qk_rope_append(const uint16_t *qkv, int S, int qdim, int hq, int hkv, int gate,
+                   const uint16_t *qn, const uint16_t *kn, float eps, RopeArgs r, int pos0,
+                   uint16_t *q_out, uint16_t *kc, uint16_t *vc, int cap, cudaStream_t st);
+int add_residual(uint16_t *h, const uint16_t *y, size_t n, cudaStream_t st);
+
+// ---- attention (attention.cu)
+struct AttnDecodeArgs {
+    const uint16_t *qkv;     // [qdim + 2*hkv*D]
+    int qdim, gate;
+    const uint16_t *qn, *kn;
+    float eps;
+    RopeArgs rope;
+    uint16_t *kc, *vc;       // layer cache [hkv][cap][D]
+    int cap, window;
+    const int32_t *d_pos;
+    int hq, hkv;
+    float *part;
+    int *count;
+    int nsplit;
+    uint16_t *out;           // [hq*D]
+};
+int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
+// prefill (S queries at positions pos0..): q [S][hq][D]; gate [S][qdim] or null
+int attention_prefill(const uint16_t *q, int S, int pos0, const uint16_t *kc,
+                      const uint16_t *vc, int cap, int window, int hq, int hkv, int D,
+                      const uint16_t *gate_src, int qdim, uint16_t *out, cudaStream_t st);
+
+// ---- sampler (sampler.cu)
+int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const int32_t *ctx,
+           int n_ctx, uint64_t step, int32_t *tok, float *lp, uint8_t *keep, cudaStream_t st);
+int argmax_decode(const unsigned long long *amax, int32_t *tok, cudaStream_t st);
+
+}  // namespace mlxd

@@ -1,0 +1,1121 @@
+// Model upload, KV cache, forward orchestration, generate loop: the C ABI of
+// libmlxd_cuda behind src/engine/{emodel,kvcache,sampler,engine}.c.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+#include <chrono>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <nccl.h>
+
+#include "internal.h"
+#include "kernels.h"
+
+using namespace mlxd;
+
+// ------------------------------------------------------------- small kernels
+
+namespace mlxd {
+
+__global__ void set_pos_kernel(int32_t *d_pos, int v) { *d_pos = v; }
+
+// end of one decode step: advance the position; with the fused argmax, turn
+// the winning key into the token id and clear the key for the next step;
+// append the token to the context list used by the repetition penalty.
+__global__ void step_finish_kernel(int32_t *d_pos, unsigned long long *amax, int32_t *token,
+                                   int32_t *ctx, int32_t *n_ctx) {
+    *d_pos += 1;
+    if (amax) {
+        *token = (int32_t)(0xFFFFFFFFu - (uint32_t)(*amax & 0xFFFFFFFFull));
+        *amax = 0ull;
+    }
+    if (ctx) {
+        ctx[*n_ctx] = *token;
+        *n_ctx += 1;
+    }
+}
+
+__global__ void append_token_kernel(int32_t *ctx, int idx, const int32_t *token) { ctx[idx] = *token; }
+
+__global__ void add_partial_kernel(uint16_t *h_out, const uint16_t *h_in, const float *part, int n) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h_out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(
+                   __fadd_rn(__uint_as_float((uint32_t)h_in[i] << 16),
+                             __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(part[i])) << 16))));
+}
+
+// raw logprob of the chosen token: x[tok] - logsumexp(x)
+__global__ void logprob_kernel(const uint16_t *logits, int V, const int32_t *tok, float *lp) {
+    __shared__ float sh[32];
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+        mx = fmaxf(mx, __uint_as_float((uint32_t)logits[i] << 16));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = -INFINITY;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) mx = fmaxf(mx, sh[i]);
+    __syncthreads();
+    float s = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+        s += expf(__uint_as_float((uint32_t)logits[i] << 16) - mx);
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += sh[i];
+        *lp = __uint_as_float((uint32_t)logits[*tok] << 16) - (mx + logf(t));
+    }
+}
+
+}  // namespace mlxd
+
+struct mlxd_linear {
+    QMat W;
+};
+
+// ---------------------------------------------------------------- helpers
+
+namespace {
+
+struct TensorSet {
+    std::unordered_map<std::string, const mlxd_tensor *> by_name;
+    std::vector<void *> temps;   // uploaded host tensors, freed after create
+    const mlxd_tensor *get(const std::string &n) const {
+        auto it = by_name.find(n);
+        return it == by_name.end() ? nullptr : it->second;
+    }
+    const void *dev(const mlxd_tensor *t, size_t bytes, cudaStream_t st) {
+        if (t->on_device) return t->data;
+        void *p = dev_alloc(bytes);
+        if (!p) return nullptr;
+        if (cudaMemcpyAsync(p, t->data, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            set_error("upload of %s failed", t->name);
+            dev_free(p);
+            return nullptr;
+        }
+        temps.push_back(p);
+        return p;
+    }
+    ~TensorSet() {
+        cudaDeviceSynchronize();
+        for (void *p : temps) dev_free(p);
+    }
+};
+
+size_t tensor_elems(const mlxd_tensor *t) {
+    size_t n = 1;
+    for (int i = 0; i < t->ndim; i++) n *= (size_t)t->shape[i];
+    return n;
+}
+size_t dt_size(int dt) { return dt == MLXD_BF16 ? 2 : 4; }
+
+// weights_get_triplet (weights.c:1053-1088): {base}.weight + optional
+// scales/biases; a partial triplet is an error.
+struct Triplet {
+    const mlxd_tensor *w = nullptr, *s = nullptr, *b = nullptr;
+    bool quant = false;
+    int rows = 0, cols = 0;
+};
+
+int get_triplet(const TensorSet &ts, const std::string &base, int group, Triplet &out) {
+    out = Triplet{};
+    out.w = ts.get(base + ".weight");
+    out.s = ts.get(base + ".scales");
+    out.b = ts.get(base + ".biases");
+    if (!out.w) {
+        set_error("missing tensor %s.weight", base.c_str());
+        return -1;
+    }
+    if ((out.s == nullptr) != (out.b == nullptr)) {
+        set_error("partial quantized triplet %s", base.c_str());
+        return -1;
+    }
+    if (out.w->ndim != 2) {
+        set_error("%s.weight must be 2-D", base.c_str());
+        return -1;
+    }
+    out.quant = out.s != nullptr;
+    out.rows = (int)out.w->shape[0];
+    if (out.quant) {
+        if (out.w->dtype != MLXD_U32) {
+            set_error("%s.weight: quantized weight must be U32", base.c_str());
+            return -1;
+        }
+        out.cols = (int)out.w->shape[1] * 8;
+        if (out.s->dtype != out.b->dtype || (out.s->dtype != MLXD_BF16 && out.s->dtype != MLXD_F32) ||
+            out.s->shape[0] != out.rows || out.s->shape[1] * group != out.cols ||
+            out.b->shape[0] != out.rows || out.b->shape[1] != out.s->shape[1]) {
+            set_error("%s: scales/biases shape or dtype mismatch", base.c_str());
+            return -1;
+        }
+    } else {
+        if (out.w->dtype != MLXD_BF16) {
+            set_error("%s.weight: dense weight must be BF16", base.c_str());
+            return -1;
+        }
+        out.cols = (int)out.w->shape[1];
+    }
+    return 0;
+}
+
+// one source block of rows [r0, r0+nr) x cols [c0, c0+nc) into a matrix
+struct Piece {
+    Triplet t;
+    int r0, nr, c0;
+    int dst_rb0, dst_rb_stride;   // quant: destination row blocks
+    int dst_row0;                 // dense: destination first row
+};
+
+int build_qmat(TensorSet &ts, QMat &M, int rows, int cols, int group, const std::vector<Piece> &pcs,
+               cudaStream_t st) {
+    M.rows = rows;
+    M.cols = cols;
+    M.group = group;
+    M.quant = pcs[0].t.quant;
+    for (auto &p : pcs) {
+        if (p.t.quant != M.quant) {
+            set_error("mixed quantized and dense projections in one fused matrix");
+            return -1;
+        }
+    }
+    if (M.quant) {
+        M.sdtype = pcs[0].t.s->dtype;
+        if (rows % 16 || cols % group) {
+            set_error("projection %dx%d does not tile (16 rows, group %d)", rows, cols, group);
+            return -1;
+        }
+        M.tiles = (uint8_t *)dev_alloc(M.tile_bytes());
+        M.sb = (uint8_t *)dev_alloc(M.sb_bytes());
+        if (!M.tiles || !M.sb) return -1;
+        for (auto &p : pcs) {
+            if (p.t.s->dtype != M.sdtype) {
+                set_error("mixed scale dtypes in one fused matrix");
+                return -1;
+            }
+            size_t wb = tensor_elems(p.t.w) * 4, sbb = tensor_elems(p.t.s) * dt_size(M.sdtype);
+            const uint32_t *w = (const uint32_t *)ts.dev(p.t.w, wb, st);
+            const void *s = ts.dev(p.t.s, sbb, st);
+            const void *b = ts.dev(p.t.b, sbb, st);
+            if (!w || !s || !b) return -1;
+            if (repack_quant(M, w, s, b, M.sdtype, p.t.cols / 8, p.t.cols / group, p.r0, p.nr, p.c0,
+                             p.dst_rb0, p.dst_rb_stride, st))
+                return -1;
+        }
+    } else {
+        M.dense = (uint16_t *)dev_alloc((size_t)rows * cols * 2);
+        if (!M.dense) return -1;
+        for (auto &p : pcs) {
+            const uint16_t *src = (const uint16_t *)p.t.w->data + (size_t)p.r0 * p.t.cols + p.c0;
+            cudaMemcpyKind kind = p.t.w->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+            MLXD_CHECK(cudaMemcpy2DAsync(M.dense + (size_t)p.dst_row0 * cols, (size_t)cols * 2, src,
+                                         (size_t)p.t.cols * 2, (size_t)cols * 2, p.nr, kind, st));
+        }
+    }
+    return 0;
+}
+
+void free_qmat(QMat &M) {
+    dev_free(M.tiles);
+    dev_free(M.sb);
+    dev_free(M.dense);
+    M = QMat{};
+}
+
+uint16_t *upload_vec(TensorSet &ts, const std::string &name, int n, cudaStream_t st) {
+    const mlxd_tensor *t = ts.get(name);
+    if (!t || t->dtype != MLXD_BF16 || (int)tensor_elems(t) != n) {
+        set_error("missing or bad tensor %s", name.c_str());
+        return nullptr;
+    }
+    uint16_t *p = (uint16_t *)dev_alloc((size_t)n * 2);
+    if (!p) return nullptr;
+    if (cudaMemcpyAsync(p, t->data, (size_t)n * 2,
+                        t->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        set_error("upload of %s failed", name.c_str());
+        return nullptr;
+    }
+    return p;
+}
+
+// fwd_rope_llama3_freqs (forward.c:323-358)
+int llama3_freqs(const mlxd_model_config &c, std::vector<float> &out) {
+    if (c.head_dim < 2 || (c.head_dim & 1) || c.rope_factor <= 0 || c.rope_orig_max <= 0 ||
+        c.rope_lo <= 0 || c.rope_hi <= c.rope_lo) {
+        set_error("invalid llama3 rope parameters");
+        return -1;
+    }
+    double base = c.rope_theta, f = c.rope_factor, lf = c.rope_lo, hf = c.rope_hi, old = c.rope_orig_max;
+    double low_wl = old / lf, high_wl = old / hf;
+    out.resize(c.head_dim / 2);
+    for (int i = 0; i < c.head_dim / 2; i++) {
+        double fr = pow(base, 2.0 * i / (double)c.head_dim);
+        double wl = 2.0 * M_PI * fr;
+        if (wl > low_wl) fr = fr * f;
+        else if (wl > high_wl) {
+            double sm = (old / wl - lf) / (hf - lf);
+            fr = fr / ((1.0 - sm) / f + sm);
+        }
+        out[i] = (float)fr;
+    }
+    return 0;
+}
+
+bool fast_decode_ok(const mlxd_model *m) {
+    int D = m->c.head_dim;
+    if (!(D == 64 || D == 128)) return false;
+    int rep = m->hq / m->hkv;
+    if (!(rep == 1 || rep == 2 || rep == 4 || rep == 8)) return false;
+    if (m->c.rope_dims != D) {
+        // partial rotary is handled by the shared norm+rope helper as well
+    }
+    for (auto &L : m->L)
+        if (!L.qkv.quant || !L.o.quant || !L.gateup.quant || !L.down.quant) return false;
+    return m->lm.quant;
+}
+
+ncclComm_t comm_of(mlxd_model *m) { return (ncclComm_t)m->nccl; }
+
+int allreduce_f32(mlxd_model *m, float *buf, size_t n, cudaStream_t st) {
+    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, comm_of(m), st);
+    if (r != ncclSuccess) {
+        set_error("ncclAllReduce: %s", ncclGetErrorString(r));
+        return -1;
+    }
+    return 0;
+}
+
+int ensure_prefill(mlxd_model *m, int S) {
+    if (S <= m->pre_cap) return 0;
+    dev_free(m->p_h); dev_free(m->p_x); dev_free(m->p_qkv); dev_free(m->p_q);
+    dev_free(m->p_att); dev_free(m->p_act); dev_free(m->p_tmp); dev_free(m->p_ids);
+    dev_free(m->p_part);
+    const mlxd_model_config &c = m->c;
+    int D = c.head_dim;
+    size_t qkvw = (size_t)m->qdim + 2 * (size_t)m->hkv * D;
+    m->p_h = (uint16_t *)dev_alloc((size_t)S * c.hidden * 2);
+    m->p_x = (uint16_t *)dev_alloc((size_t)S * c.hidden * 2);
+    m->p_qkv = (uint16_t *)dev_alloc((size_t)S * qkvw * 2);
+    m->p_q = (uint16_t *)dev_alloc((size_t)S * m->hq * D * 2);
+    m->p_att = (uint16_t *)dev_alloc((size_t)S * m->hq * D * 2);
+    m->p_act = (uint16_t *)dev_alloc((size_t)S * m->inter_local * 2);
+    m->p_tmp = (uint16_t *)dev_alloc((size_t)S * c.hidden * 2);
+    m->p_ids = (int32_t *)dev_alloc((size_t)S * 4);
+    m->p_part = c.tp_size > 1 ? (float *)dev_alloc((size_t)S * c.hidden * 4) : nullptr;
+    if (!m->p_h || !m->p_x || !m->p_qkv || !m->p_q || !m->p_att || !m->p_act || !m->p_tmp || !m->p_ids ||
+        (c.tp_size > 1 && !m->p_part))
+        return -1;
+    m->pre_cap = S;
+    return 0;
+}
+
+// y = W x for S tokens (S == 1 & quantized: decode GEMV semantics)
+int linear_any(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi, const uint16_t *res,
+               float *yf, cudaStream_t st) {
+    if (W.quant && S == 1) {
+        GemvArgs a = {};
+        a.x = x;
+        a.y = y;
+        a.yf = yf;
+        a.residual = res;
+        return qgemv(W, PRO_PLAIN, epi, a, st, false);
+    }
+    return linear_multi(W, x, S, y, epi, res, yf, st);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ forward
+
+namespace mlxd {
+
+// one token through every layer with the fused decode kernels
+static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool want_logits,
+                       uint16_t *logits_out, bool argmax, cudaStream_t st, bool pdl) {
+    const mlxd_model_config &c = m->c;
+    int H = c.hidden, D = c.head_dim;
+    bool tp = c.tp_size > 1;
+    if (embed_rows(m->embed, H, c.qgroup, ids_dev, 1, m->h, st)) return -1;
+    size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
+    for (int l = 0; l < c.layers; l++) {
+        Layer &L = m->L[l];
+        GemvArgs a = {};
+        a.x = m->h;
+        a.norm_w = L.ln1;
+        a.eps = c.eps;
+        a.y = m->qkv;
+        if (qgemv(L.qkv, PRO_RMSNORM, EPI_STORE, a, st, pdl)) return -1;
+        AttnDecodeArgs ad = {};
+        ad.qkv = m->qkv;
+        ad.qdim = m->qdim;
+        ad.gate = c.attn_gate;
+        ad.qn = c.qk_norm ? L.qn : nullptr;
+        ad.kn = c.qk_norm ? L.kn : nullptr;
+        ad.eps = c.eps;
+        ad.rope = RopeArgs{D, c.rope_dims, m->rope_cs};
+        ad.kc = kv->k + (size_t)l * layer_elems;
+        ad.vc = kv->v + (size_t)l * layer_elems;
+        ad.cap = kv->cap;
+        ad.window = kv->window;
+        ad.d_pos = kv->d_pos;
+        ad.hq = m->hq;
+        ad.hkv = m->hkv;
+        ad.part = m->part;
+        ad.count = m->att_count;
+        ad.nsplit = m->nsplit;
+        ad.out = m->att;
+        if (attention_decode(ad, st, pdl)) return -1;
+        GemvArgs o = {};
+        o.x = m->att;
+        if (tp) {
+            o.yf = m->part_h;
+            if (qgemv(L.o, PRO_PLAIN, EPI_PARTIAL_F32, o, st, pdl)) return -1;
+            if (allreduce_f32(m, m->part_h, H, st)) return -1;
+            add_partial_kernel<<<(H + 255) / 256, 256, 0, st>>>(m->h1, m->h, m->part_h, H);
+        } else {
+            o.y = m->h1;
+            o.residual = m->h;
+            if (qgemv(L.o, PRO_PLAIN, EPI_RESIDUAL, o, st, pdl)) return -1;
+        }
+        GemvArgs gu = {};
+        gu.x = m->h1;
+        gu.norm_w = L.ln2;
+        gu.eps = c.eps;
+        gu.y = m->act;
+        if (qgemv(L.gateup, PRO_RMSNORM, EPI_SWIGLU, gu, st, pdl)) return -1;
+        GemvArgs dn = {};
+        dn.x = m->act;
+        if (tp) {
+            dn.yf = m->part_h;
+            if (qgemv(L.down, PRO_PLAIN, EPI_PARTIAL_F32, dn, st, pdl)) return -1;
+            if (allreduce_f32(m, m->part_h, H, st)) return -1;
+            add_partial_kernel<<<(H + 255) / 256, 256, 0, st>>>(m->h, m->h1, m->part_h, H);
+        } else {
+            dn.y = m->h;
+            dn.residual = m->h1;
+            if (qgemv(L.down, PRO_PLAIN, EPI_RESIDUAL, dn, st, pdl)) return -1;
+        }
+    }
+    if (want_logits) {
+        GemvArgs lg = {};
+        lg.x = m->h;
+        lg.norm_w = m->norm;
+        lg.eps = c.eps;
+        lg.y = logits_out;
+        lg.amax = m->amax;
+        lg.row_offset = m->vocab_off;
+        if (qgemv(m->lm, PRO_RMSNORM, argmax ? EPI_ARGMAX : EPI_STORE, lg, st, pdl)) return -1;
+        if (argmax && tp) {
+            ncclResult_t r = ncclAllReduce(m->amax, m->amax, 1, ncclUint64, ncclMax, comm_of(m), st);
+            if (r != ncclSuccess) {
+                set_error("ncclAllReduce(max): %s", ncclGetErrorString(r));
+                return -1;
+            }
+        }
+    }
+    step_finish_kernel<<<1, 1, 0, st>>>(kv->d_pos, argmax ? m->amax : nullptr, m->token, nullptr,
+                                        nullptr);
+    MLXD_CHECK(cudaGetLastError());
+    return 0;
+}
+
+// S tokens through the generic kernels (prefill chunks; dense checkpoints)
+static int generic_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, int S, bool want_logits,
+                           uint16_t *logits_out, cudaStream_t st) {
+    const mlxd_model_config &c = m->c;
+    int H = c.hidden, D = c.head_dim;
+    bool tp = c.tp_size > 1;
+    if (ensure_prefill(m, S)) return -1;
+    int pos0 = kv->offset;
+    if (embed_rows(m->embed, H, c.qgroup, ids_dev, S, m->p_h, st)) return -1;
+    size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
+    for (int l = 0; l < c.layers; l++) {
+        Layer &L = m->L[l];
+        uint16_t *kc = kv->k + (size_t)l * layer_elems, *vc = kv->v + (size_t)l * layer_elems;
+        if (rmsnorm_rows(m->p_h, S, H, L.ln1, c.eps, m->p_x, st)) return -1;
+        if (linear_any(L.qkv, m->p_x, S, m->p_qkv, EPI_STORE, nullptr, nullptr, st)) return -1;
+        if (qk_rope_append(m->p_qkv, S, m->qdim, m->hq, m->hkv, c.attn_gate, c.qk_norm ? L.qn : nullptr,
+                           c.qk_norm ? L.kn : nullptr, c.eps, RopeArgs{D, c.rope_dims, m->rope_cs}, pos0,
+                           m->p_q, kc, vc, kv->cap, st))
+            return -1;
+        if (attention_prefill(m->p_q, S, pos0, kc, vc, kv->cap, kv->window, m->hq, m->hkv, D,
+                              c.attn_gate ? m->p_qkv : nullptr, m->qdim, m->p_att, st))
+            return -1;
+        if (tp) {
+            if (linear_any(L.o, m->p_att, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, st)) return -1;
+            if (allreduce_f32(m, m->p_part, (size_t)S * H, st)) return -1;
+            add_partial_kernel<<<(S * H + 255) / 256, 256, 0, st>>>(m->p_h, m->p_h, m->p_part, S * H);
+        } else if (linear_any(L.o, m->p_att, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, st)) {
+            return -1;
+        }
+        if (rmsnorm_rows(m->p_h, S, H, L.ln2, c.eps, m->p_x, st)) return -1;
+        if (linear_any(L.gateup, m->p_x, S, m->p_act, EPI_SWIGLU, nullptr, nullptr, st)) return -1;
+        if (tp) {
+            if (linear_any(L.down, m->p_act, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, st)) return -1;
+            if (allreduce_f32(m, m->p_part, (size_t)S * H, st)) return -1;
+            add_partial_kernel<<<(S * H + 255) / 256, 256, 0, st>>>(m->p_h, m->p_h, m->p_part, S * H);
+        } else if (linear_any(L.down, m->p_act, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, st)) {
+            return -1;
+        }
+    }
+    if (want_logits) {
+        const uint16_t *last = m->p_h + (size_t)(S - 1) * H;
+        if (rmsnorm_rows(last, 1, H, m->norm, c.eps, m->p_x, st)) return -1;
+        if (linear_any(m->lm, m->p_x, 1, logits_out, EPI_STORE, nullptr, nullptr, st)) return -1;
+    }
+    set_pos_kernel<<<1, 1, 0, st>>>(kv->d_pos, pos0 + S);
+    MLXD_CHECK(cudaGetLastError());
+    return 0;
+}
+
+static int check_room(const mlxd_model *m, const mlxd_kv *kv, int n) {
+    if (kv->offset + n > m->rope_positions) {
+        set_error("position %d beyond the %d positions of this model's RoPE table", kv->offset + n,
+                  m->rope_positions);
+        return -1;
+    }
+    if (kv->window <= 0 && kv->offset + n > kv->cap) {
+        set_error("KV cache full: %d + %d > capacity %d", kv->offset, n, kv->cap);
+        return -1;
+    }
+    if (kv->window > 0 && n > kv->cap - kv->window + 1) {
+        set_error("chunk of %d tokens does not fit the ring (capacity %d, window %d)", n, kv->cap,
+                  kv->window);
+        return -1;
+    }
+    return 0;
+}
+
+static int forward_dev(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, int n, bool want_logits,
+                       uint16_t *logits_out, cudaStream_t st) {
+    if (check_room(m, kv, n)) return -1;
+    int rc;
+    if (n == 1 && fast_decode_ok(m))
+        rc = decode_step(m, kv, ids_dev, want_logits, logits_out, false, st, false);
+    else
+        rc = generic_forward(m, kv, ids_dev, n, want_logits, logits_out, st);
+    if (rc) return -1;
+    kv->offset += n;
+    return 0;
+}
+
+}  // namespace mlxd
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" {
+
+int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const mlxd_tensor *tensors,
+                           int n_tensors) {
+    if (!out || !cfg || (!tensors && n_tensors)) {
+        set_error("model_create: null argument");
+        return -1;
+    }
+    const mlxd_model_config &c = *cfg;
+    int tp = c.tp_size > 0 ? c.tp_size : 1, rank = c.tp_size > 0 ? c.tp_rank : 0;
+    if (c.family < MLXD_QWEN3 || c.family > MLXD_QWEN3_5) {
+        set_error("unsupported model family %d", c.family);
+        return -1;
+    }
+    if (c.hidden <= 0 || c.layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
+        c.vocab <= 0 || c.inter <= 0 || c.n_heads % c.n_kv_heads) {
+        set_error("invalid model dimensions");
+        return -1;
+    }
+    if (c.qbits != 0 && c.qbits != 4) {
+        set_error("only 4-bit affine quantisation is supported (bits=%d)", c.qbits);
+        return -1;
+    }
+    if (c.qbits == 4 && c.qgroup != 32 && c.qgroup != 64) {
+        set_error("quantisation group %d not supported (32 or 64)", c.qgroup);
+        return -1;
+    }
+    if (c.n_heads % tp || c.n_kv_heads % tp || c.inter % tp || c.vocab % tp) {
+        set_error("tensor-parallel degree %d does not divide heads/intermediate/vocab", tp);
+        return -1;
+    }
+    if (c.rope_dims <= 0 || c.rope_dims > c.head_dim || (c.rope_dims & 1)) {
+        set_error("invalid rope dims %d", c.rope_dims);
+        return -1;
+    }
+    mlxd_model *m = new mlxd_model();
+    m->c = c;
+    m->c.tp_size = tp;
+    m->c.tp_rank = rank;
+    int G = c.qbits ? c.qgroup : 64;
+    int D = c.head_dim;
+    m->hq = c.n_heads / tp;
+    m->hkv = c.n_kv_heads / tp;
+    m->qdim = m->hq * D * (c.attn_gate ? 2 : 1);
+    m->inter_local = c.inter / tp;
+    m->vocab_local = c.vocab / tp;
+    m->vocab_off = rank * m->vocab_local;
+    cudaStream_t st = nullptr;
+    TensorSet ts;
+    for (int i = 0; i < n_tensors; i++) ts.by_name[tensors[i].name] = &tensors[i];
+    auto fail = [&]() {
+        mlxd_cuda_model_destroy(m);
+        return -1;
+    };
+    m->L.resize(c.layers);
+    int qrows_full = c.n_heads * D * (c.attn_gate ? 2 : 1);
+    int kvrows_full = c.n_kv_heads * D;
+    for (int l = 0; l < c.layers; l++) {
+        Layer &L = m->L[l];
+        std::string p = "model.layers." + std::to_string(l) + ".";
+        Triplet q, k, v, o, gt, up, dn;
+        if (get_triplet(ts, p + "self_attn.q_proj", G, q) || get_triplet(ts, p + "self_attn.k_proj", G, k) ||
+            get_triplet(ts, p + "self_attn.v_proj", G, v) || get_triplet(ts, p + "self_attn.o_proj", G, o) ||
+            get_triplet(ts, p + "mlp.gate_proj", G, gt) || get_triplet(ts, p + "mlp.up_proj", G, up) ||
+            get_triplet(ts, p + "mlp.down_proj", G, dn))
+            return fail();
+        if (q.rows != qrows_full || q.cols != c.hidden || k.rows != kvrows_full || v.rows != kvrows_full ||
+            k.cols != c.hidden || v.cols != c.hidden || o.rows != c.hidden || o.cols != c.n_heads * D ||
+            gt.rows != c.inter || up.rows != c.inter || gt.cols != c.hidden || up.cols != c.hidden ||
+            dn.rows != c.hidden || dn.cols != c.inter) {
+            set_error("layer %d: projection shapes do not match the config", l);
+            return fail();
+        }
+        int ql = m->qdim, kl = m->hkv * D;
+        // fused q|k|v rows (column-parallel slice by heads)
+        std::vector<Piece> qkv = {
+            {q, rank * ql, ql, 0, 0, 1, 0},
+            {k, rank * kl, kl, 0, ql / 16, 1, ql},
+            {v, rank * kl, kl, 0, (ql + kl) / 16, 1, ql + kl}};
+        if (build_qmat(ts, L.qkv, ql + 2 * kl, c.hidden, G, qkv, st)) return fail();
+        // o: row-parallel (input columns of this rank's heads)
+        int oc = m->hq * D;
+        if (build_qmat(ts, L.o, c.hidden, oc, G, {{o, 0, c.hidden, rank * oc, 0, 1, 0}}, st)) return fail();
+        // gate/up: quantized -> interleaved 16-row blocks; dense -> stacked
+        int il = m->inter_local;
+        std::vector<Piece> gu = {{gt, rank * il, il, 0, 0, 2, 0}, {up, rank * il, il, 0, 1, 2, il}};
+        if (build_qmat(ts, L.gateup, 2 * il, c.hidden, G, gu, st)) return fail();
+        if (build_qmat(ts, L.down, c.hidden, il, G, {{dn, 0, c.hidden, rank * il, 0, 1, 0}}, st)) return fail();
+        if (!(L.ln1 = upload_vec(ts, p + "input_layernorm.weight", c.hidden, st))) return fail();
+        if (!(L.ln2 = upload_vec(ts, p + "post_attention_layernorm.weight", c.hidden, st))) return fail();
+        if (c.qk_norm) {
+            if (!(L.qn = upload_vec(ts, p + "self_attn.q_norm.weight", D, st))) return fail();
+            if (!(L.kn = upload_vec(ts, p + "self_attn.k_norm.weight", D, st))) return fail();
+        }
+    }
+    // embedding (replicated, MLX format) and lm_head (vocab-parallel)
+    Triplet emb;
+    if (get_triplet(ts, "model.embed_tokens", G, emb)) return fail();
+    if (emb.rows != c.vocab || emb.cols != c.hidden) {
+        set_error("embed_tokens shape does not match the config");
+        return fail();
+    }
+    m->embed.quant = emb.quant;
+    if (emb.quant) {
+        m->embed.sdtype = emb.s->dtype;
+        size_t wb = tensor_elems(emb.w) * 4, sbb = tensor_elems(emb.s) * dt_size(emb.s->dtype);
+        m->embed.w = (uint32_t *)dev_alloc(wb);
+        m->embed.s = dev_alloc(sbb);
+        m->embed.b = dev_alloc(sbb);
+        if (!m->embed.w || !m->embed.s || !m->embed.b) return fail();
+        cudaMemcpyKind kind = emb.w->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+        if (!cuda_ok(cudaMemcpyAsync(m->embed.w, emb.w->data, wb, kind, st), "embed upload") ||
+            !cuda_ok(cudaMemcpyAsync(m->embed.s, emb.s->data, sbb, kind, st), "embed upload") ||
+            !cuda_ok(cudaMemcpyAsync(m->embed.b, emb.b->data, sbb, kind, st), "embed upload"))
+            return fail();
+    } else {
+        size_t b = tensor_elems(emb.w) * 2;
+        m->embed.dense = (uint16_t *)dev_alloc(b);
+        if (!m->embed.dense) return fail();
+        if (!cuda_ok(cudaMemcpyAsync(m->embed.dense, emb.w->data, b,
+                                     emb.w->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st),
+                     "embed upload"))
+            return fail();
+    }
+    Triplet lm;
+    if (c.tie) lm = emb;
+    else if (get_triplet(ts, "lm_head", G, lm)) return fail();
+    if (lm.rows != c.vocab || lm.cols != c.hidden) {
+        set_error("lm_head shape does not match the config");
+        return fail();
+    }
+    if (build_qmat(ts, m->lm, m->vocab_local, c.hidden, G, {{lm, m->vocab_off, m->vocab_local, 0, 0, 1, 0}}, st))
+        return fail();
+    if (!(m->norm = upload_vec(ts, "model.norm.weight", c.hidden, st))) return fail();
+
+    // RoPE cos/sin table, computed exactly as mlx_fast_rope's angle
+    // (inv_freq = 2^(-(i/half)*log2(theta)) or 1/freqs[i]; angle = pos*inv)
+    {
+        std::vector<float> fr;
+        if (c.rope_llama3 && llama3_freqs(c, fr)) return fail();
+        int half = c.rope_dims / 2;
+        int npos = c.max_pos > 0 ? c.max_pos : 4096;
+        if (npos > (1 << 20)) npos = 1 << 20;
+        std::vector<float> cs((size_t)npos * half * 2);
+        float lb = log2f(c.rope_theta);
+        std::vector<float> inv(half);
+        for (int i = 0; i < half; i++)
+            inv[i] = c.rope_llama3 ? 1.0f / fr[i] : exp2f(-((float)i / (float)half) * lb);
+        for (int p = 0; p < npos; p++) {
+            float L = (float)p;
+            for (int i = 0; i < half; i++) {
+                float th = L * inv[i];
+                cs[((size_t)p * half + i) * 2] = cosf(th);
+                cs[((size_t)p * half + i) * 2 + 1] = sinf(th);
+            }
+        }
+        m->rope_cs = (float *)dev_alloc(cs.size() * 4);
+        if (!m->rope_cs) return fail();
+        if (!cuda_ok(cudaMemcpy(m->rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload"))
+            return fail();
+        m->rope_positions = npos;
+    }
+
+    // decode scratch
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int ns = (2 * sms + m->hkv - 1) / m->hkv;
+    m->nsplit = ns < 1 ? 1 : (ns > 64 ? 64 : ns);
+    size_t qkvw = (size_t)m->qdim + 2 * (size_t)m->hkv * D;
+    m->h = (uint16_t *)dev_alloc((size_t)c.hidden * 2);
+    m->h1 = (uint16_t *)dev_alloc((size_t)c.hidden * 2);
+    m->qkv = (uint16_t *)dev_alloc(qkvw * 2);
+    m->att = (uint16_t *)dev_alloc((size_t)m->hq * D * 2);
+    m->act = (uint16_t *)dev_alloc((size_t)m->inter_local * 2);
+    m->logits = (uint16_t *)dev_alloc((size_t)m->vocab_local * 2);
+    m->part = (float *)dev_alloc((size_t)m->hq * m->nsplit * (D + 2) * 4);
+    m->att_count = (int *)dev_alloc((size_t)m->hkv * 4);
+    m->amax = (unsigned long long *)dev_alloc(8);
+    m->token = (int32_t *)dev_alloc(4);
+    m->part_h = (float *)dev_alloc((size_t)c.hidden * 4);
+    m->lp = (float *)dev_alloc(4);
+    if (!m->lp || !m->h || !m->h1 || !m->qkv || !m->att || !m->act || !m->logits || !m->part || !m->att_count ||
+        !m->amax || !m->token || !m->part_h)
+        return fail();
+    if (!cuda_ok(cudaMemset(m->att_count, 0, (size_t)m->hkv * 4), "memset") ||
+        !cuda_ok(cudaMemset(m->amax, 0, 8), "memset"))
+        return fail();
+    if (!cuda_ok(cudaDeviceSynchronize(), "model upload")) return fail();
+    for (auto &L : m->L)
+        m->weight_bytes += L.qkv.tile_bytes() + L.qkv.sb_bytes() + L.o.tile_bytes() + L.o.sb_bytes() +
+                           L.gateup.tile_bytes() + L.gateup.sb_bytes() + L.down.tile_bytes() + L.down.sb_bytes();
+    m->weight_bytes += m->lm.tile_bytes() + m->lm.sb_bytes();
+    *out = m;
+    return 0;
+}
+
+void mlxd_cuda_model_destroy(mlxd_model *m) {
+    if (!m) return;
+    cudaDeviceSynchronize();
+    if (m->graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
+    for (auto &L : m->L) {
+        free_qmat(L.qkv);
+        free_qmat(L.o);
+        free_qmat(L.gateup);
+        free_qmat(L.down);
+        dev_free(L.ln1);
+        dev_free(L.ln2);
+        dev_free(L.qn);
+        dev_free(L.kn);
+    }
+    free_qmat(m->lm);
+    dev_free(m->embed.w);
+    dev_free(m->embed.s);
+    dev_free(m->embed.b);
+    dev_free(m->embed.dense);
+    dev_free(m->norm);
+    dev_free(m->rope_cs);
+    for (void *p : {(void *)m->h, (void *)m->h1, (void *)m->qkv, (void *)m->att, (void *)m->act,
+                    (void *)m->logits, (void *)m->part, (void *)m->att_count, (void *)m->amax,
+                    (void *)m->token, (void *)m->part_h, (void *)m->p_h, (void *)m->p_x, (void *)m->p_qkv,
+                    (void *)m->p_q, (void *)m->p_att, (void *)m->p_act, (void *)m->p_tmp, (void *)m->p_ids,
+                    (void *)m->p_part, (void *)m->ctx, (void *)m->n_ctx, (void *)m->lp})
+        dev_free(p);
+    if (m->nccl) ncclCommDestroy((ncclComm_t)m->nccl);
+    delete m;
+}
+
+size_t mlxd_cuda_model_weight_bytes(const mlxd_model *m) { return m ? m->weight_bytes : 0; }
+
+int mlxd_cuda_nccl_unique_id(void *out128) {
+    ncclUniqueId id;
+    ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        set_error("ncclGetUniqueId: %s", ncclGetErrorString(r));
+        return -1;
+    }
+    memcpy(out128, &id, sizeof(id));
+    return 0;
+}
+
+int mlxd_cuda_model_tp_init(mlxd_model *m, const void *uid) {
+    if (!m || !uid) return -1;
+    if (m->c.tp_size <= 1) return 0;
+    ncclUniqueId id;
+    memcpy(&id, uid, sizeof(id));
+    ncclComm_t comm;
+    ncclResult_t r = ncclCommInitRank(&comm, m->c.tp_size, id, m->c.tp_rank);
+    if (r != ncclSuccess) {
+        set_error("ncclCommInitRank: %s", ncclGetErrorString(r));
+        return -1;
+    }
+    m->nccl = comm;
+    return 0;
+}
+
+int mlxd_cuda_kv_create(mlxd_kv **out, const mlxd_model *m, int capacity) {
+    if (!out || !m || capacity <= 0) {
+        set_error("kv_create: bad arguments");
+        return -1;
+    }
+    mlxd_kv *kv = new mlxd_kv();
+    kv->layers = m->c.layers;
+    kv->hkv = m->hkv;
+    kv->d = m->c.head_dim;
+    kv->cap = capacity;
+    kv->window = m->c.window;
+    kv->offset = 0;
+    if (kv->window > 0 && capacity < kv->window) {
+        set_error("ring capacity %d smaller than the window %d", capacity, kv->window);
+        delete kv;
+        return -1;
+    }
+    size_t n = (size_t)kv->layers * kv->hkv * kv->cap * kv->d;
+    kv->k = (uint16_t *)dev_alloc(n * 2);
+    kv->v = (uint16_t *)dev_alloc(n * 2);
+    kv->d_pos = (int32_t *)dev_alloc(4);
+    if (!kv->k || !kv->v || !kv->d_pos) {
+        mlxd_cuda_kv_destroy(kv);
+        return -1;
+    }
+    if (!cuda_ok(cudaMemset(kv->d_pos, 0, 4), "memset")) {
+        mlxd_cuda_kv_destroy(kv);
+        return -1;
+    }
+    *out = kv;
+    return 0;
+}
+
+void mlxd_cuda_kv_destroy(mlxd_kv *kv) {
+    if (!kv) return;
+    cudaDeviceSynchronize();
+    dev_free(kv->k);
+    dev_free(kv->v);
+    dev_free(kv->d_pos);
+    delete kv;
+}
+
+int mlxd_cuda_kv_offset(const mlxd_kv *kv, int layer) {
+    if (!kv || layer < 0 || layer >= kv->layers) return -1;
+    return kv->offset;
+}
+
+int mlxd_cuda_kv_capacity(const mlxd_kv *kv, int layer) {
+    if (!kv || layer < 0 || layer >= kv->layers) return -1;
+    return kv->cap;
+}
+
+int mlxd_cuda_kv_reset(mlxd_kv *kv) {
+    if (!kv) return -1;
+    kv->offset = 0;
+    MLXD_CHECK(cudaMemset(kv->d_pos, 0, 4));
+    MLXD_CHECK(cudaDeviceSynchronize());
+    return 0;
+}
+
+int mlxd_cuda_kv_read(mlxd_kv *kv, int layer, int is_value, uint16_t *host_out, int *n_out) {
+    if (!kv || layer < 0 || layer >= kv->layers || !host_out) return -1;
+    MLXD_CHECK(cudaDeviceSynchronize());
+    int live = kv->offset < kv->cap ? kv->offset : kv->cap;
+    int first = kv->offset - live;
+    size_t layer_elems = (size_t)kv->hkv * kv->cap * kv->d;
+    const uint16_t *base = (is_value ? kv->v : kv->k) + (size_t)layer * layer_elems;
+    for (int h = 0; h < kv->hkv; h++)
+        for (int i = 0; i < live; i++) {
+            int slot = (first + i) % kv->cap;
+            MLXD_CHECK(cudaMemcpy(host_out + ((size_t)h * live + i) * kv->d,
+                                  base + ((size_t)h * kv->cap + slot) * kv->d, (size_t)kv->d * 2,
+                                  cudaMemcpyDeviceToHost));
+        }
+    if (n_out) *n_out = live;
+    return 0;
+}
+
+int mlxd_cuda_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids, int n, int ids_on_device,
+                      int want_logits, void *logits_dev, void *stream) {
+    if (!m || !kv || !ids || n <= 0 || (want_logits && !logits_dev)) {
+        set_error("forward: bad arguments");
+        return -1;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    if (ensure_prefill(m, n)) return -1;
+    if (!ids_on_device) {
+        std::vector<int32_t> chk(ids, ids + n);
+        for (int i = 0; i < n; i++)
+            if (chk[i] < 0 || chk[i] >= m->c.vocab) {
+                set_error("token id %d out of range", chk[i]);
+                return -1;
+            }
+    }
+    MLXD_CHECK(cudaMemcpyAsync(m->p_ids, ids, (size_t)n * 4,
+                               ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+    return forward_dev(m, kv, m->p_ids, n, want_logits != 0, (uint16_t *)logits_dev, st);
+}
+
+// ---- single ops
+
+int mlxd_cuda_linear_create(mlxd_linear **out, const uint32_t *w, const void *scales, const void *biases,
+                            int sdtype, int rows, int cols, int group, int on_device) {
+    if (!out || !w || !scales || !biases) return -1;
+    mlxd_tensor tw = {"w", MLXD_U32, 2, {rows, cols / 8}, w, on_device};
+    mlxd_tensor tsc = {"w.scales", sdtype, 2, {rows, cols / group}, scales, on_device};
+    mlxd_tensor tb = {"w.biases", sdtype, 2, {rows, cols / group}, biases, on_device};
+    TensorSet ts;
+    Triplet t;
+    t.w = &tw;
+    t.s = &tsc;
+    t.b = &tb;
+    t.quant = true;
+    t.rows = rows;
+    t.cols = cols;
+    mlxd_linear *l = new mlxd_linear();
+    if (build_qmat(ts, l->W, rows, cols, group, {{t, 0, rows, 0, 0, 1, 0}}, nullptr)) {
+        free_qmat(l->W);
+        delete l;
+        return -1;
+    }
+    if (!cuda_ok(cudaDeviceSynchronize(), "linear upload")) {
+        free_qmat(l->W);
+        delete l;
+        return -1;
+    }
+    *out = l;
+    return 0;
+}
+
+void mlxd_cuda_linear_destroy(mlxd_linear *l) {
+    if (!l) return;
+    cudaDeviceSynchronize();
+    free_qmat(l->W);
+    delete l;
+}
+
+int mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *stream) {
+    if (!l || !x || !y || S <= 0) return -1;
+    return linear_any(l->W, (const uint16_t *)x, S, (uint16_t *)y, EPI_STORE, nullptr, nullptr,
+                      (cudaStream_t)stream);
+}
+
+int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y,
+                           float *ms_out) {
+    if (!ls || n <= 0 || iters <= 0 || !x || !y || !ms_out) return -1;
+    cudaStream_t st;
+    MLXD_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    int rc = 0;
+    for (int i = 0; i < n && !rc; i++)   // warm-up
+        rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr, st);
+    cudaEventRecord(a, st);
+    for (int it = 0; it < iters && !rc; it++)
+        for (int i = 0; i < n && !rc; i++)
+            rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr, st);
+    cudaEventRecord(b, st);
+    if (!rc && cuda_ok(cudaEventSynchronize(b), "linear_timed")) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, a, b);
+        *ms_out = ms / (float)(iters * n);
+    } else {
+        rc = -1;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+int mlxd_cuda_rmsnorm(const void *x, int rows, int n, const void *w, float eps, void *y, void *stream) {
+    return rmsnorm_rows((const uint16_t *)x, rows, n, (const uint16_t *)w, eps, (uint16_t *)y,
+                        (cudaStream_t)stream);
+}
+
+int mlxd_cuda_sample(const void *logits_dev, int dtype, int V, const mlxd_sampling *sp, const int32_t *ctx_dev,
+                     int n_ctx, uint64_t step, int32_t *tok_dev, float *logprob_dev, uint8_t *keep_dev,
+                     void *stream) {
+    if (!sp) return -1;
+    return sample(logits_dev, dtype, V, *sp, ctx_dev, n_ctx, step, tok_dev, logprob_dev, keep_dev,
+                  (cudaStream_t)stream);
+}
+
+// ---- generate (handle_generate_real, engine.c:360-602)
+
+int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n, int max_new,
+                       const mlxd_sampling *sp, int chunk, int32_t *out, float *logprobs, double *timing) {
+    if (!m || !kv || !prompt || !sp || !out) {
+        set_error("generate: null argument");
+        return -1;
+    }
+    if (n <= 0 || max_new <= 0) return 0;
+    if (n > m->c.max_pos && m->c.max_pos > 0) {
+        set_error("prompt token count %d exceeds max_position_embeddings %d", n, m->c.max_pos);
+        return -1;
+    }
+    if (chunk <= 0) chunk = 512;
+    for (int i = 0; i < n; i++)
+        if (prompt[i] < 0 || prompt[i] >= m->c.vocab) {
+            set_error("prompt token id %d out of range", prompt[i]);
+            return -1;
+        }
+    cudaStream_t st = m->stream;
+    if (!st) {
+        MLXD_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        m->stream = st;
+    }
+    if (mlxd_cuda_kv_reset(kv)) return -1;
+    // context list for the repetition penalty (prompt + generated)
+    int ctx_cap = n + max_new + 1;
+    if (ctx_cap > m->ctx_cap) {
+        dev_free(m->ctx);
+        m->ctx = (int32_t *)dev_alloc((size_t)ctx_cap * 4);
+        if (!m->ctx) return -1;
+        m->ctx_cap = ctx_cap;
+        if (!m->n_ctx) m->n_ctx = (int32_t *)dev_alloc(4);
+        if (!m->n_ctx) return -1;
+    }
+    int32_t *pin = nullptr;
+    MLXD_CHECK(cudaMallocHost(&pin, sizeof(int32_t) * (size_t)(n + 8) + sizeof(float) * 8));
+    float *pin_lp = (float *)(pin + n + 8);
+    struct PinGuard {
+        void *p;
+        ~PinGuard() { cudaFreeHost(p); }
+    } pg{pin};
+    memcpy(pin, prompt, sizeof(int32_t) * (size_t)n);
+    MLXD_CHECK(cudaMemcpyAsync(m->ctx, pin, sizeof(int32_t) * (size_t)n, cudaMemcpyHostToDevice, st));
+    int32_t nctx_h = n;
+    MLXD_CHECK(cudaMemcpyAsync(m->n_ctx, &nctx_h, 4, cudaMemcpyHostToDevice, st));
+
+    cudaEvent_t e0, e1, e2;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreate(&e2);
+    cudaEventRecord(e0, st);
+    // chunked prefill of prompt[:-1]
+    for (int pos = 0; pos < n - 1; pos += chunk) {
+        int len = (n - 1 - pos) < chunk ? (n - 1 - pos) : chunk;
+        if (ensure_prefill(m, len)) return -1;
+        MLXD_CHECK(cudaMemcpyAsync(m->p_ids, m->ctx + pos, (size_t)len * 4, cudaMemcpyDeviceToDevice, st));
+        if (forward_dev(m, kv, m->p_ids, len, false, nullptr, st)) return -1;
+    }
+    cudaEventRecord(e1, st);
+    bool greedy = sp->temperature < 0.01f;
+    bool fast = fast_decode_ok(m);
+    // device token slot starts as the last prompt token (the seed forward)
+    MLXD_CHECK(cudaMemcpyAsync(m->token, m->ctx + n - 1, 4, cudaMemcpyDeviceToDevice, st));
+    int emitted = 0;
+    int rc = 0;
+    // one decode step (forward of m->token, then the token choice), enqueued
+    auto enqueue_step = [&](int e) -> int {
+        if (check_room(m, kv, 1)) return -1;
+        if (fast && greedy) {
+            if (!m->graph_exec || m->graph_kv != kv || m->graph_lp != (logprobs != nullptr)) {
+                if (m->graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
+                m->graph_exec = nullptr;
+                cudaGraph_t g;
+                MLXD_CHECK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+                int r = decode_step(m, kv, m->token, true, m->logits, true, st, true);
+                if (!r && logprobs) logprob_kernel<<<1, 1024, 0, st>>>(m->logits, m->vocab_local, m->token, m->lp);
+                cudaError_t ce = cudaStreamEndCapture(st, &g);
+                if (r || ce != cudaSuccess) {
+                    if (!r) set_error("graph capture: %s", cudaGetErrorString(ce));
+                    return -1;
+                }
+                cudaGraphExec_t ge;
+                MLXD_CHECK(cudaGraphInstantiate(&ge, g, 0));
+                cudaGraphDestroy(g);
+                m->graph_exec = ge;
+                m->graph_kv = kv;
+                m->graph_lp = logprobs != nullptr;
+            }
+            MLXD_CHECK(cudaGraphLaunch((cudaGraphExec_t)m->graph_exec, st));
+        } else {
+            if (fast) {
+                if (decode_step(m, kv, m->token, true, m->logits, false, st, false)) return -1;
+            } else {
+                if (generic_forward(m, kv, m->token, 1, true, m->logits, st)) return -1;
+            }
+            if (m->c.tp_size > 1) {
+                set_error("sampled decoding with tensor parallelism is not supported");
+                return -1;
+            }
+            if (sample(m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, n + e, (uint64_t)e, m->token,
+                       logprobs ? m->lp : nullptr, nullptr, st))
+                return -1;
+            append_token_kernel<<<1, 1, 0, st>>>(m->ctx, n + e, m->token);
+        }
+        kv->offset += 1;
+        MLXD_CHECK(cudaMemcpyAsync(pin + n + (e & 1), m->token, 4, cudaMemcpyDeviceToHost, st));
+        if (logprobs) MLXD_CHECK(cudaMemcpyAsync(pin_lp + (e & 1), m->lp, 4, cudaMemcpyDeviceToHost, st));
+        return 0;
+    };
+    (void)nctx_h;
+    std::vector<cudaEvent_t> evs(2);
+    cudaEventCreateWithFlags(&evs[0], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&evs[1], cudaEventDisableTiming);
+    // per-step device timestamps (timing[4 + e]: end of step e, ms after prefill)
+    std::vector<cudaEvent_t> tev(timing ? max_new : 0);
+    for (auto &ev : tev) cudaEventCreate(&ev);
+    auto t0 = std::chrono::steady_clock::now();
+    if (enqueue_step(0)) { rc = -1; goto done; }
+    cudaEventRecord(evs[0], st);
+    if (timing) cudaEventRecord(tev[0], st);
+    for (int e = 0; e < max_new; e++) {
+        // lookahead: enqueue step e+1 before reading token e
+        bool more = e + 1 < max_new;
+        if (more) {
+            if (enqueue_step(e + 1)) { rc = -1; goto done; }
+            cudaEventRecord(evs[(e + 1) & 1], st);
+            if (timing) cudaEventRecord(tev[e + 1], st);
+        }
+        if (!cuda_ok(cudaEventSynchronize(evs[e & 1]), "decode step")) { rc = -1; goto done; }
+        int32_t tok = pin[n + (e & 1)];
+        if (tok < 0 || tok >= m->c.vocab) {
+            set_error("sampler produced an invalid token");
+            rc = -1;
+            goto done;
+        }
+        bool eos = false;
+        for (int i = 0; i < m->c.n_eos && i < 8; i++) eos |= (m->c.eos[i] == tok);
+        if (eos) break;
+        out[emitted] = tok;
+        if (logprobs) logprobs[emitted] = pin_lp[e & 1];
+        emitted++;
+    }
+    cudaEventRecord(e2, st);
+    if (!cuda_ok(cudaStreamSynchronize(st), "generate")) rc = -1;
+    if (timing) {
+        float pre = 0.f, dec = 0.f;
+        cudaEventElapsedTime(&pre, e0, e1);
+        cudaEventElapsedTime(&dec, e1, e2);
+        timing[0] = pre;
+        timing[1] = dec;
+        timing[2] = emitted;
+        timing[3] = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        for (int e = 0; e < emitted && e < (int)tev.size(); e++) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, e1, tev[e]);
+            timing[4 + e] = ms;
+        }
+    }
+done:
+    cudaStreamSynchronize(st);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    cudaEventDestroy(evs[0]);
+    cudaEventDestroy(evs[1]);
+    for (auto &ev : tev) cudaEventDestroy(ev);
+    return rc ? -1 : emitted;
+}
+
+}  // extern "C"

@@ -1,0 +1,30 @@
+"""Shared helpers for the parity tests (test-side only)."""
+import ctypes
+
+import numpy as np
+
+from oracle import pyoracle as po
+
+
+def orc_config(cfg):
+    """The oracle's config struct shares the C ABI config's leading fields."""
+    return po.OrcConfig.from_buffer_copy(bytes(cfg)[: ctypes.sizeof(po.OrcConfig)])
+
+
+def bf16_to_f32(a):
+    return (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(a):
+    return po.f32_to_bf16(a)
+
+
+def rand_bf16(shape, rng, scale=1.0):
+    return f32_to_bf16(rng.standard_normal(shape).astype(np.float32) * scale)
+
+
+def logits_close(g, o, max_abs=2e-2, mean_rel=1e-3):
+    """North-star logits tolerance: max-abs and mean-abs relative error."""
+    d = np.abs(g.astype(np.float64) - o.astype(np.float64))
+    mr = d.mean() / max(np.abs(o).mean(), 1e-12)
+    return float(d.max()) <= max_abs and mr <= mean_rel, float(d.max()), float(mr)
