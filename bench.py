@@ -38,6 +38,12 @@ MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 
 
+def metric_name(workload):
+    if workload == "qwen3-8b-4bit":
+        return "decode tokens/s at batch 1 (Qwen3-8B 4-bit)"
+    return "decode tokens/s at batch 1 (%s)" % workload
+
+
 def env_rank():
     r = int(os.environ.get("RANK", "0"))
     w = int(os.environ.get("WORLD_SIZE", "1"))
@@ -119,39 +125,17 @@ def dist_setup(world):
     return dist
 
 
-def gemv_roofline(cuda, kw, peak):
-    """Live qGEMV microbench at the workload's projection shapes. Weights are
-    rotated over copies totalling more than the 126 MB L2, so every launch
-    streams its weights from HBM."""
-    H, D = kw["hidden"], kw["head_dim"]
-    q, kv = kw["n_heads"] * D, kw["n_kv_heads"] * D
-    shapes = {"qkv": (q + 2 * kv, H), "o_proj": (H, q), "gate_up": (2 * kw["inter"], H),
-              "down": (H, kw["inter"])}
+def gemv_roofline(kw, peak):
+    """Live qGEMV microbench at the workload's projection shapes (weights
+    rotated over copies larger than L2, CUDA events in the library)."""
+    from mlxd_b200 import microbench
     out = {}
-    x = cuda.DeviceBuffer(max(c for _, c in shapes.values()) * 2)
-    cuda.check(cuda.lib().mlxd_cuda_synth_bf16(x.ptr, max(c for _, c in shapes.values()),
-                                               99, 1.0, 0.0, None), "synth")
-    y = cuda.DeviceBuffer(max(r for r, _ in shapes.values()) * 2)
-    for name, (rows, cols) in shapes.items():
-        wbytes = rows * cols // 2 + rows * (cols // 64) * 4
-        copies = max(2, int(400e6 // wbytes) + 1)
-        lins, bufs = [], []
-        for c in range(copies):
-            w = cuda.DeviceBuffer(rows * cols // 2)
-            s = cuda.DeviceBuffer(rows * cols // 64 * 2)
-            b = cuda.DeviceBuffer(rows * cols // 64 * 2)
-            cuda.check(cuda.lib().mlxd_cuda_synth_quantized(w.ptr, s.ptr, b.ptr, rows, cols, 64,
-                                                            1000 + c, 0.02, None), "synth")
-            lins.append(cuda.Linear(w, s, b, 64, rows=rows, cols=cols))
-            bufs.append((w, s, b))
-        del bufs
-        ms = cuda.linear_timed(lins, max(3, 200 // copies), x, y)
-        alg = wbytes + cols * 2 + rows * 2
-        gbs = alg / (ms * 1e-3) / 1e9
-        out[name] = {"rows": rows, "cols": cols, "us": round(ms * 1e3, 2),
-                     "bytes": alg, "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
-        for l in lins:
-            l.close()
+    for name, (rows, cols) in microbench.shapes_of(kw).items():
+        if name == "lm_head":
+            continue
+        r = microbench.measure(rows, cols)
+        r["frac"] = round(r["gbs"] / peak, 3)
+        out[name] = r
     return out
 
 
@@ -215,7 +199,7 @@ def run_reference(args, rank, world, lr):
     except Exception:
         host = cuda.synth_host_tensors(cfg, seed=0)
     cb = oracle_sample(kw, host, args.cpu_prompt, kw["vocab"], args.cpu_budget)
-    line = {"impl": "reference", "metric": "decode tokens/s at batch 1", "value": cb["value"],
+    line = {"impl": "reference", "metric": metric_name(args.workload), "value": cb["value"],
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "dtype": "u4 weights / bf16 activations (f32 accumulate)",
             "data": "synthetic", "vs_baseline": None,
@@ -299,8 +283,7 @@ def main():
     bpt, wbytes = bytes_per_token(kw, mean_ctx)
     step_gbs = bpt / world / (t_timed / K / 1e3) / 1e9
     line = {
-        "metric": "decode tokens/s at batch 1 (Qwen3-8B 4-bit)" if args.workload == "qwen3-8b-4bit"
-        else "decode tokens/s at batch 1 (%s)" % args.workload,
+        "metric": metric_name(args.workload),
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(t_timed / K, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
@@ -323,7 +306,7 @@ def main():
         "clocks": clk,
     }
     if args.roofline and rank == 0:
-        g = gemv_roofline(cuda, kw, peak)
+        g = gemv_roofline(kw, peak)
         dom = g["gate_up"]
         tr = load_traffic().get("gate_up")
         line["roofline"] = {"kernel": "qgemv (decode 4-bit GEMV), gate_up shape %dx%d" % (

@@ -22,6 +22,7 @@ namespace mlxd {
 // ------------------------------------------------------------------ decode
 
 constexpr int DEC_THREADS = 128;
+constexpr int DEC_MAX_SPLIT = 64;
 
 template <int D, int REP>
 __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
@@ -112,26 +113,47 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
             if (j < s1) {
                 load_row(kc, s_knew, j, kr[u]);
                 load_row(vc, s_vnew, j, vr[u]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < DL; i++) kr[u][i] = vr[u][i] = 0.f;
             }
         }
+        // U independent scores per head, then one online-softmax update
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            int j = j0 + u;
-            if (j >= s1) break;
+        for (int r = 0; r < REP; r++) {
+            float sc[U];
 #pragma unroll
-            for (int r = 0; r < REP; r++) {
-                float s = 0.f;
+            for (int u = 0; u < U; u++) {
+                float x = 0.f;
 #pragma unroll
-                for (int i = 0; i < DL; i++) s = fmaf(q[r][i], kr[u][i], s);
-                s = warp_sum(s);
-                float mn = fmaxf(m[r], s);
-                float alpha = exp2f(m[r] - mn);
-                float p = exp2f(s - mn);
-                l[r] = l[r] * alpha + p;
-#pragma unroll
-                for (int i = 0; i < DL; i++) o[r][i] = fmaf(o[r][i], alpha, p * vr[u][i]);
-                m[r] = mn;
+                for (int i = 0; i < DL; i++) x = fmaf(q[r][i], kr[u][i], x);
+                sc[u] = x;
             }
+#pragma unroll
+            for (int sh = 16; sh > 0; sh >>= 1)
+#pragma unroll
+                for (int u = 0; u < U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], sh);
+            float mn = m[r];
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (j0 + u < s1) mn = fmaxf(mn, sc[u]);
+            float alpha = exp2f(m[r] - mn);
+            float ps = 0.f;
+            float pu[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                pu[u] = (j0 + u < s1) ? exp2f(sc[u] - mn) : 0.f;
+                ps += pu[u];
+            }
+            l[r] = l[r] * alpha + ps;
+#pragma unroll
+            for (int i = 0; i < DL; i++) {
+                float acc = o[r][i] * alpha;
+#pragma unroll
+                for (int u = 0; u < U; u++) acc = fmaf(pu[u], vr[u][i], acc);
+                o[r][i] = acc;
+            }
+            m[r] = mn;
         }
     }
     // merge the warps of this CTA
@@ -175,26 +197,41 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // last split of this kv head: merge all splits
+    // last split of this kv head: merge all splits. Split weights
+    // 2^(m_s - m) / L per head first (in shared memory), then every output
+    // element is a dot product over the splits with independent loads.
+    __shared__ float s_w[REP][DEC_MAX_SPLIT];
+    for (int idx = threadIdx.x; idx < REP * a.nsplit; idx += DEC_THREADS) {
+        int r = idx / a.nsplit, sp = idx % a.nsplit;
+        s_w[r][sp] = __ldcg(part + ((size_t)(kh * REP + r) * a.nsplit + sp) * (D + 2));
+    }
+    __syncthreads();
+    if (threadIdx.x < REP) {
+        int r = threadIdx.x;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < a.nsplit; sp++) mx = fmaxf(mx, s_w[r][sp]);
+        float L = 0.f;
+        for (int sp = 0; sp < a.nsplit; sp++) {
+            float ms = s_w[r][sp];
+            float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
+            L += w * __ldcg(part + ((size_t)(kh * REP + r) * a.nsplit + sp) * (D + 2) + 1);
+            s_w[r][sp] = w;
+        }
+        float invL = 1.f / L;
+        for (int sp = 0; sp < a.nsplit; sp++) s_w[r][sp] *= invL;
+    }
+    __syncthreads();
     for (int idx = threadIdx.x; idx < REP * D; idx += DEC_THREADS) {
         int r = idx / D, d = idx % D;
         int h = kh * REP + r;
-        const float *base = part + (size_t)h * a.nsplit * (D + 2);
-        float mx = -INFINITY;
-        for (int sp = 0; sp < a.nsplit; sp++) mx = fmaxf(mx, __ldcg(base + (size_t)sp * (D + 2)));
-        float ls = 0.f, os = 0.f;
-        for (int sp = 0; sp < a.nsplit; sp++) {
-            const float *rec = base + (size_t)sp * (D + 2);
-            float ms = __ldcg(rec);
-            if (ms == -INFINITY) continue;
-            float e = exp2f(ms - mx);
-            ls += __ldcg(rec + 1) * e;
-            os += __ldcg(rec + 2 + d) * e;
-        }
-        float val = rbf(os / ls);
+        const float *base = part + (size_t)h * a.nsplit * (D + 2) + 2 + d;
+        float os = 0.f;
+#pragma unroll 8
+        for (int sp = 0; sp < a.nsplit; sp++) os = fmaf(s_w[r][sp], __ldcg(base + (size_t)sp * (D + 2)), os);
+        float val = rbf(os);
         if (a.gate) {
-            float g = bf2f(qkv[(size_t)h * qstride + D + d]);
-            val = rbf(__fmul_rn(val, sigmoid_bf16(g)));
+            float gv = bf2f(qkv[(size_t)h * qstride + D + d]);
+            val = rbf(__fmul_rn(val, sigmoid_bf16(gv)));
         }
         a.out[(size_t)h * D + d] = f2bf(val);
     }
@@ -335,24 +372,25 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(
         float alpha[2], rs[2] = {0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < 2; i++) alpha[i] = (mnew[i] == -INFINITY) ? 1.f : exp2f(mrow[i] - mnew[i]);
-        uint32_t pf[PF_BC / 16][4];
+        // P split as bf16 hi + bf16 lo so P.V keeps ~16 mantissa bits of the
+        // f32 probabilities (mlx keeps P in f32 for the product)
+        uint32_t pf[PF_BC / 16][4], pl[PF_BC / 16][4];
 #pragma unroll
         for (int n = 0; n < PF_BC / 8; n++) {
-            float p[4];
+            float p[4], lo[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 float mm = mnew[e >> 1];
                 p[e] = (mm == -INFINITY) ? 0.f : exp2f(sacc[n][e] - mm);
                 rs[e >> 1] += p[e];
+                lo[e] = p[e] - rbf(p[e]);
             }
             int kk = n >> 1;
-            if ((n & 1) == 0) {
-                pf[kk][0] = pack_bf2(p[0], p[1]);
-                pf[kk][1] = pack_bf2(p[2], p[3]);
-            } else {
-                pf[kk][2] = pack_bf2(p[0], p[1]);
-                pf[kk][3] = pack_bf2(p[2], p[3]);
-            }
+            int o = (n & 1) * 2;
+            pf[kk][o] = pack_bf2(p[0], p[1]);
+            pf[kk][o + 1] = pack_bf2(p[2], p[3]);
+            pl[kk][o] = pack_bf2(lo[0], lo[1]);
+            pl[kk][o + 1] = pack_bf2(lo[2], lo[3]);
         }
 #pragma unroll
         for (int i = 0; i < 2; i++) {
@@ -379,6 +417,8 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(
                 ldmatrix_x4_trans(b, sV + r * LD + c);
                 mma_bf16_16816(oacc[n], pf[kk], b[0], b[1]);
                 mma_bf16_16816(oacc[n + 1], pf[kk], b[2], b[3]);
+                mma_bf16_16816(oacc[n], pl[kk], b[0], b[1]);
+                mma_bf16_16816(oacc[n + 1], pl[kk], b[2], b[3]);
             }
         }
     }

@@ -27,11 +27,16 @@ struct QMat {
     bool quant = true;
     uint8_t *tiles = nullptr;
     uint8_t *sb = nullptr;
+    // decode fast path (group 64, bf16 scales, cols/64 a multiple of 8): the
+    // same scales/biases regrouped per row block and block of 8 groups, one
+    // 16-byte record per lane: (s,b) of rows g, g+8 x groups 2t, 2t+1
+    uint8_t *sb8 = nullptr;
     uint16_t *dense = nullptr;  // [rows][cols] bf16 when !quant
     size_t tile_bytes() const { return (size_t)rows / 16 * (cols / group) * 32 * (group / 4); }
     size_t sb_bytes() const {
         return (size_t)rows / 16 * (cols / group) * 8 * (sdtype == MLXD_F32 ? 16 : 8);
     }
+    bool fast8() const { return quant && group == 64 && sdtype == MLXD_BF16 && (cols / 64) % 8 == 0; }
 };
 
 struct Layer {
@@ -69,6 +74,8 @@ struct mlxd_model {
     int32_t *token = nullptr;   // device token slot
     float *lp = nullptr;        // device logprob slot
     float *part_h = nullptr;    // [hidden] f32 partial (tensor parallel)
+    float *gemv_ws = nullptr;   // decode GEMV split row-block partials
+    int *gemv_cnt = nullptr;    // decode GEMV per-unit counters
     float *rope_cs = nullptr;   // [positions][rope_dims/2][2] cos/sin
     int rope_positions = 0;
     int nsplit = 16;

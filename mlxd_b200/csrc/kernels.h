@@ -20,6 +20,7 @@ enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_PART
 struct GemvArgs {
     const uint8_t *tiles;
     const uint8_t *sb;
+    const uint8_t *sb8;         // fast-path scale/bias records (set by qgemv)
     int rows, cols;
     const uint16_t *x;          // bf16 [cols]
     const uint16_t *norm_w;     // PRO_RMSNORM
@@ -29,8 +30,14 @@ struct GemvArgs {
     const uint16_t *residual;   // EPI_RESIDUAL
     unsigned long long *amax;   // EPI_ARGMAX
     int row_offset;             // EPI_ARGMAX: global index of row 0
+    float *ws;                  // split row-block partials [units][slots][16 or 32]
+    int *cnt;                   // per-unit arrival counters (zero between launches)
+    int ws_slots;               // set by the launcher
 };
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl);
+// workspace floats one matrix needs (units -> counters)
+size_t gemv_workspace_floats(int rows, int cols, int group, int epi, int sms, int *units);
+int num_sms();
 
 // ---- prefill GEMM / dense (qgemm.cu)
 // y[S][rows] = x[S][cols] . W^T with epilogue (STORE/RESIDUAL/SWIGLU)
@@ -38,7 +45,7 @@ int linear_multi(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi,
                  const uint16_t *residual, float *yf, cudaStream_t st);
 
 // ---- small ops (ops.cu)
-int embed_rows(const Embed &e, int H, int group, const int32_t *ids, int S, uint16_t *h,
+int embed_rows(const Embed &e, int H, int group, int vocab, const int32_t *ids, int S, uint16_t *h,
                cudaStream_t st);
 int rmsnorm_rows(const uint16_t *x, int rows, int n, const uint16_t *w, float eps, uint16_t *y,
                  cudaStream_t st);

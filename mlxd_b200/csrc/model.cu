@@ -10,6 +10,7 @@
 #include <vector>
 
 #include <nccl.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "internal.h"
 #include "kernels.h"
@@ -76,6 +77,8 @@ __global__ void logprob_kernel(const uint16_t *logits, int V, const int32_t *tok
 
 struct mlxd_linear {
     QMat W;
+    float *ws = nullptr;
+    int *cnt = nullptr;
 };
 
 // ---------------------------------------------------------------- helpers
@@ -192,6 +195,10 @@ int build_qmat(TensorSet &ts, QMat &M, int rows, int cols, int group, const std:
         M.tiles = (uint8_t *)dev_alloc(M.tile_bytes());
         M.sb = (uint8_t *)dev_alloc(M.sb_bytes());
         if (!M.tiles || !M.sb) return -1;
+        if (M.fast8()) {
+            M.sb8 = (uint8_t *)dev_alloc(M.sb_bytes() * 2);   // 16 B per lane record
+            if (!M.sb8) return -1;
+        }
         for (auto &p : pcs) {
             if (p.t.s->dtype != M.sdtype) {
                 set_error("mixed scale dtypes in one fused matrix");
@@ -222,6 +229,7 @@ int build_qmat(TensorSet &ts, QMat &M, int rows, int cols, int group, const std:
 void free_qmat(QMat &M) {
     dev_free(M.tiles);
     dev_free(M.sb);
+    dev_free(M.sb8);
     dev_free(M.dense);
     M = QMat{};
 }
@@ -315,13 +323,15 @@ int ensure_prefill(mlxd_model *m, int S) {
 
 // y = W x for S tokens (S == 1 & quantized: decode GEMV semantics)
 int linear_any(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi, const uint16_t *res,
-               float *yf, cudaStream_t st) {
+               float *yf, float *ws, int *cnt, cudaStream_t st) {
     if (W.quant && S == 1) {
         GemvArgs a = {};
         a.x = x;
         a.y = y;
         a.yf = yf;
         a.residual = res;
+        a.ws = ws;
+        a.cnt = cnt;
         return qgemv(W, PRO_PLAIN, epi, a, st, false);
     }
     return linear_multi(W, x, S, y, epi, res, yf, st);
@@ -339,11 +349,13 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
     const mlxd_model_config &c = m->c;
     int H = c.hidden, D = c.head_dim;
     bool tp = c.tp_size > 1;
-    if (embed_rows(m->embed, H, c.qgroup, ids_dev, 1, m->h, st)) return -1;
+    if (embed_rows(m->embed, H, c.qgroup, c.vocab, ids_dev, 1, m->h, st)) return -1;
     size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
     for (int l = 0; l < c.layers; l++) {
         Layer &L = m->L[l];
         GemvArgs a = {};
+        a.ws = m->gemv_ws;
+        a.cnt = m->gemv_cnt;
         a.x = m->h;
         a.norm_w = L.ln1;
         a.eps = c.eps;
@@ -370,6 +382,8 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         ad.out = m->att;
         if (attention_decode(ad, st, pdl)) return -1;
         GemvArgs o = {};
+        o.ws = m->gemv_ws;
+        o.cnt = m->gemv_cnt;
         o.x = m->att;
         if (tp) {
             o.yf = m->part_h;
@@ -382,12 +396,16 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
             if (qgemv(L.o, PRO_PLAIN, EPI_RESIDUAL, o, st, pdl)) return -1;
         }
         GemvArgs gu = {};
+        gu.ws = m->gemv_ws;
+        gu.cnt = m->gemv_cnt;
         gu.x = m->h1;
         gu.norm_w = L.ln2;
         gu.eps = c.eps;
         gu.y = m->act;
         if (qgemv(L.gateup, PRO_RMSNORM, EPI_SWIGLU, gu, st, pdl)) return -1;
         GemvArgs dn = {};
+        dn.ws = m->gemv_ws;
+        dn.cnt = m->gemv_cnt;
         dn.x = m->act;
         if (tp) {
             dn.yf = m->part_h;
@@ -402,6 +420,8 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
     }
     if (want_logits) {
         GemvArgs lg = {};
+        lg.ws = m->gemv_ws;
+        lg.cnt = m->gemv_cnt;
         lg.x = m->h;
         lg.norm_w = m->norm;
         lg.eps = c.eps;
@@ -431,13 +451,13 @@ static int generic_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, i
     bool tp = c.tp_size > 1;
     if (ensure_prefill(m, S)) return -1;
     int pos0 = kv->offset;
-    if (embed_rows(m->embed, H, c.qgroup, ids_dev, S, m->p_h, st)) return -1;
+    if (embed_rows(m->embed, H, c.qgroup, c.vocab, ids_dev, S, m->p_h, st)) return -1;
     size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
     for (int l = 0; l < c.layers; l++) {
         Layer &L = m->L[l];
         uint16_t *kc = kv->k + (size_t)l * layer_elems, *vc = kv->v + (size_t)l * layer_elems;
         if (rmsnorm_rows(m->p_h, S, H, L.ln1, c.eps, m->p_x, st)) return -1;
-        if (linear_any(L.qkv, m->p_x, S, m->p_qkv, EPI_STORE, nullptr, nullptr, st)) return -1;
+        if (linear_any(L.qkv, m->p_x, S, m->p_qkv, EPI_STORE, nullptr, nullptr, m->gemv_ws, m->gemv_cnt, st)) return -1;
         if (qk_rope_append(m->p_qkv, S, m->qdim, m->hq, m->hkv, c.attn_gate, c.qk_norm ? L.qn : nullptr,
                            c.qk_norm ? L.kn : nullptr, c.eps, RopeArgs{D, c.rope_dims, m->rope_cs}, pos0,
                            m->p_q, kc, vc, kv->cap, st))
@@ -446,26 +466,26 @@ static int generic_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, i
                               c.attn_gate ? m->p_qkv : nullptr, m->qdim, m->p_att, st))
             return -1;
         if (tp) {
-            if (linear_any(L.o, m->p_att, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, st)) return -1;
+            if (linear_any(L.o, m->p_att, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, m->gemv_ws, m->gemv_cnt, st)) return -1;
             if (allreduce_f32(m, m->p_part, (size_t)S * H, st)) return -1;
             add_partial_kernel<<<(S * H + 255) / 256, 256, 0, st>>>(m->p_h, m->p_h, m->p_part, S * H);
-        } else if (linear_any(L.o, m->p_att, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, st)) {
+        } else if (linear_any(L.o, m->p_att, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, m->gemv_ws, m->gemv_cnt, st)) {
             return -1;
         }
         if (rmsnorm_rows(m->p_h, S, H, L.ln2, c.eps, m->p_x, st)) return -1;
-        if (linear_any(L.gateup, m->p_x, S, m->p_act, EPI_SWIGLU, nullptr, nullptr, st)) return -1;
+        if (linear_any(L.gateup, m->p_x, S, m->p_act, EPI_SWIGLU, nullptr, nullptr, m->gemv_ws, m->gemv_cnt, st)) return -1;
         if (tp) {
-            if (linear_any(L.down, m->p_act, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, st)) return -1;
+            if (linear_any(L.down, m->p_act, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, m->gemv_ws, m->gemv_cnt, st)) return -1;
             if (allreduce_f32(m, m->p_part, (size_t)S * H, st)) return -1;
             add_partial_kernel<<<(S * H + 255) / 256, 256, 0, st>>>(m->p_h, m->p_h, m->p_part, S * H);
-        } else if (linear_any(L.down, m->p_act, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, st)) {
+        } else if (linear_any(L.down, m->p_act, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, m->gemv_ws, m->gemv_cnt, st)) {
             return -1;
         }
     }
     if (want_logits) {
         const uint16_t *last = m->p_h + (size_t)(S - 1) * H;
         if (rmsnorm_rows(last, 1, H, m->norm, c.eps, m->p_x, st)) return -1;
-        if (linear_any(m->lm, m->p_x, 1, logits_out, EPI_STORE, nullptr, nullptr, st)) return -1;
+        if (linear_any(m->lm, m->p_x, 1, logits_out, EPI_STORE, nullptr, nullptr, m->gemv_ws, m->gemv_cnt, st)) return -1;
     }
     set_pos_kernel<<<1, 1, 0, st>>>(kv->d_pos, pos0 + S);
     MLXD_CHECK(cudaGetLastError());
@@ -670,6 +690,29 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         m->rope_positions = npos;
     }
 
+    // decode GEMV workspace: the largest need over this model's matrices
+    {
+        size_t ws = 0;
+        int units = 0;
+        auto need = [&](const QMat &M, int epi) {
+            if (!M.quant) return;
+            int u = 0;
+            size_t f = gemv_workspace_floats(M.rows, M.cols, M.group, epi, num_sms(), &u);
+            if (f > ws) ws = f;
+            if (u > units) units = u;
+        };
+        for (auto &L : m->L) {
+            need(L.qkv, EPI_STORE);
+            need(L.o, EPI_RESIDUAL);
+            need(L.gateup, EPI_SWIGLU);
+            need(L.down, EPI_RESIDUAL);
+        }
+        need(m->lm, EPI_ARGMAX);
+        m->gemv_ws = (float *)dev_alloc((ws ? ws : 16) * 4);
+        m->gemv_cnt = (int *)dev_alloc((size_t)(units ? units : 4) * 4);
+        if (!m->gemv_ws || !m->gemv_cnt) return fail();
+        if (!cuda_ok(cudaMemset(m->gemv_cnt, 0, (size_t)(units ? units : 4) * 4), "memset")) return fail();
+    }
     // decode scratch
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -729,7 +772,8 @@ void mlxd_cuda_model_destroy(mlxd_model *m) {
                     (void *)m->logits, (void *)m->part, (void *)m->att_count, (void *)m->amax,
                     (void *)m->token, (void *)m->part_h, (void *)m->p_h, (void *)m->p_x, (void *)m->p_qkv,
                     (void *)m->p_q, (void *)m->p_att, (void *)m->p_act, (void *)m->p_tmp, (void *)m->p_ids,
-                    (void *)m->p_part, (void *)m->ctx, (void *)m->n_ctx, (void *)m->lp})
+                    (void *)m->p_part, (void *)m->ctx, (void *)m->n_ctx, (void *)m->lp,
+                    (void *)m->gemv_ws, (void *)m->gemv_cnt})
         dev_free(p);
     if (m->nccl) ncclCommDestroy((ncclComm_t)m->nccl);
     delete m;
@@ -884,6 +928,14 @@ int mlxd_cuda_linear_create(mlxd_linear **out, const uint32_t *w, const void *sc
         delete l;
         return -1;
     }
+    int units = 0;
+    size_t wsf = gemv_workspace_floats(rows, cols, group, EPI_STORE, num_sms(), &units);
+    l->ws = (float *)dev_alloc((wsf ? wsf : 16) * 4);
+    l->cnt = (int *)dev_alloc((size_t)(units ? units : 4) * 4);
+    if (!l->ws || !l->cnt || !cuda_ok(cudaMemset(l->cnt, 0, (size_t)(units ? units : 4) * 4), "memset")) {
+        mlxd_cuda_linear_destroy(l);
+        return -1;
+    }
     if (!cuda_ok(cudaDeviceSynchronize(), "linear upload")) {
         free_qmat(l->W);
         delete l;
@@ -897,13 +949,15 @@ void mlxd_cuda_linear_destroy(mlxd_linear *l) {
     if (!l) return;
     cudaDeviceSynchronize();
     free_qmat(l->W);
+    dev_free(l->ws);
+    dev_free(l->cnt);
     delete l;
 }
 
 int mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *stream) {
     if (!l || !x || !y || S <= 0) return -1;
-    return linear_any(l->W, (const uint16_t *)x, S, (uint16_t *)y, EPI_STORE, nullptr, nullptr,
-                      (cudaStream_t)stream);
+    return linear_any(l->W, (const uint16_t *)x, S, (uint16_t *)y, EPI_STORE, nullptr, nullptr, l->ws,
+                      l->cnt, (cudaStream_t)stream);
 }
 
 int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y,
@@ -916,11 +970,13 @@ int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const
     cudaEventCreate(&b);
     int rc = 0;
     for (int i = 0; i < n && !rc; i++)   // warm-up
-        rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr, st);
+        rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr,
+                        ls[i]->ws, ls[i]->cnt, st);
     cudaEventRecord(a, st);
     for (int it = 0; it < iters && !rc; it++)
         for (int i = 0; i < n && !rc; i++)
-            rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr, st);
+            rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr,
+                            ls[i]->ws, ls[i]->cnt, st);
     cudaEventRecord(b, st);
     if (!rc && cuda_ok(cudaEventSynchronize(b), "linear_timed")) {
         float ms = 0.f;
@@ -1000,14 +1056,20 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     cudaEventCreate(&e1);
     cudaEventCreate(&e2);
     cudaEventRecord(e0, st);
+    nvtxRangePushA("prefill");
     // chunked prefill of prompt[:-1]
     for (int pos = 0; pos < n - 1; pos += chunk) {
         int len = (n - 1 - pos) < chunk ? (n - 1 - pos) : chunk;
-        if (ensure_prefill(m, len)) return -1;
-        MLXD_CHECK(cudaMemcpyAsync(m->p_ids, m->ctx + pos, (size_t)len * 4, cudaMemcpyDeviceToDevice, st));
-        if (forward_dev(m, kv, m->p_ids, len, false, nullptr, st)) return -1;
+        if (ensure_prefill(m, len) ||
+            !cuda_ok(cudaMemcpyAsync(m->p_ids, m->ctx + pos, (size_t)len * 4, cudaMemcpyDeviceToDevice, st),
+                     "prefill ids") ||
+            forward_dev(m, kv, m->p_ids, len, false, nullptr, st)) {
+            nvtxRangePop();
+            return -1;
+        }
     }
     cudaEventRecord(e1, st);
+    nvtxRangePop();
     bool greedy = sp->temperature < 0.01f;
     bool fast = fast_decode_ok(m);
     // device token slot starts as the last prompt token (the seed forward)
@@ -1059,13 +1121,22 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
         return 0;
     };
     (void)nctx_h;
+    std::chrono::steady_clock::time_point t0;
+    bool decode_range = false;
     std::vector<cudaEvent_t> evs(2);
     cudaEventCreateWithFlags(&evs[0], cudaEventDisableTiming);
     cudaEventCreateWithFlags(&evs[1], cudaEventDisableTiming);
     // per-step device timestamps (timing[4 + e]: end of step e, ms after prefill)
     std::vector<cudaEvent_t> tev(timing ? max_new : 0);
     for (auto &ev : tev) cudaEventCreate(&ev);
-    auto t0 = std::chrono::steady_clock::now();
+    // the host decode clock starts once the prefill has drained
+    if (timing && !cuda_ok(cudaStreamSynchronize(st), "prefill")) {
+        rc = -1;
+        goto done;
+    }
+    t0 = std::chrono::steady_clock::now();
+    nvtxRangePushA("decode");
+    decode_range = true;
     if (enqueue_step(0)) { rc = -1; goto done; }
     cudaEventRecord(evs[0], st);
     if (timing) cudaEventRecord(tev[0], st);
@@ -1108,6 +1179,7 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
         }
     }
 done:
+    if (decode_range) nvtxRangePop();
     cudaStreamSynchronize(st);
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);

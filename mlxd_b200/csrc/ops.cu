@@ -8,10 +8,13 @@ namespace mlxd {
 // fwd_embed (forward.c:65-147): gather rows of the MLX-format table,
 // dequantise scale*q + bias (one rounding), bf16 out.
 template <bool QUANT, bool SF32>
-__global__ void embed_kernel(Embed e, int H, int G, const int32_t *__restrict__ ids,
+__global__ void embed_kernel(Embed e, int H, int G, int V, const int32_t *__restrict__ ids,
                              uint16_t *__restrict__ h) {
     int s = blockIdx.x;
     int id = ids[s];
+    // an invalid id (a failed draw reports -1) reads row 0; the host rejects
+    // the step when it reads the token back
+    if (id < 0 || id >= V) id = 0;
     uint16_t *out = h + (size_t)s * H;
     if (QUANT) {
         const uint32_t *w = e.w + (size_t)id * (H / 8);
@@ -42,13 +45,13 @@ __global__ void embed_kernel(Embed e, int H, int G, const int32_t *__restrict__ 
     }
 }
 
-int embed_rows(const Embed &e, int H, int G, const int32_t *ids, int S, uint16_t *h,
+int embed_rows(const Embed &e, int H, int G, int V, const int32_t *ids, int S, uint16_t *h,
                cudaStream_t st) {
     if (e.quant) {
-        if (e.sdtype == MLXD_F32) embed_kernel<true, true><<<S, 128, 0, st>>>(e, H, G, ids, h);
-        else embed_kernel<true, false><<<S, 128, 0, st>>>(e, H, G, ids, h);
+        if (e.sdtype == MLXD_F32) embed_kernel<true, true><<<S, 128, 0, st>>>(e, H, G, V, ids, h);
+        else embed_kernel<true, false><<<S, 128, 0, st>>>(e, H, G, V, ids, h);
     } else {
-        embed_kernel<false, false><<<S, 128, 0, st>>>(e, H, G, ids, h);
+        embed_kernel<false, false><<<S, 128, 0, st>>>(e, H, G, V, ids, h);
     }
     MLXD_CHECK(cudaGetLastError());
     return 0;

@@ -94,6 +94,28 @@ __global__ void repack_sb_kernel(const void *__restrict__ s, const void *__restr
     }
 }
 
+// scales/biases of the decode fast path: record (rb, bk, lane) = bf16x2 (s, b)
+// for (row g, group 8bk+2t), (row g, 8bk+2t+1), (row g+8, 8bk+2t), (row g+8, 8bk+2t+1)
+__global__ void repack_sb8_kernel(const uint16_t *__restrict__ s, const uint16_t *__restrict__ b,
+                                  int lds, int r0, int g0, int nrb, int nbk,
+                                  uint8_t *__restrict__ sb8, int dst_rb0, int dst_rb_stride) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)nrb * nbk * 32) return;
+    int lane = (int)(idx & 31);
+    int bk = (int)((idx >> 5) % nbk);
+    int rb = (int)((idx >> 5) / nbk);
+    int gq = lane >> 2, t = lane & 3;
+    int rowA = r0 + rb * 16 + gq, rowB = rowA + 8;
+    int ga = g0 + bk * 8 + 2 * t, gb = ga + 1;
+    auto rec = [&](int row, int grp) -> uint32_t {
+        size_t i = (size_t)row * lds + grp;
+        return (uint32_t)s[i] | ((uint32_t)b[i] << 16);
+    };
+    uint4 o = make_uint4(rec(rowA, ga), rec(rowA, gb), rec(rowB, ga), rec(rowB, gb));
+    int drb = dst_rb0 + dst_rb_stride * rb;
+    *reinterpret_cast<uint4 *>(sb8 + (((size_t)drb * nbk + bk) * 32 + lane) * 16) = o;
+}
+
 int repack_quant(QMat &dst, const uint32_t *w, const void *s, const void *b, int sdtype, int ldw,
                  int lds, int r0, int nrows, int c0, int dst_rb0, int dst_rb_stride,
                  cudaStream_t st) {
@@ -123,6 +145,13 @@ int repack_quant(QMat &dst, const uint32_t *w, const void *s, const void *b, int
     else
         repack_sb_kernel<false><<<sblocks, 256, 0, st>>>(s, b, lds, r0, c0 / G, nrb, ng, dst.sb,
                                                          dst_rb0, dst_rb_stride, ng);
+    if (dst.sb8) {
+        int nbk = ng / 8;
+        size_t n8 = (size_t)nrb * nbk * 32;
+        repack_sb8_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, st>>>(
+            (const uint16_t *)s, (const uint16_t *)b, lds, r0, c0 / G, nrb, nbk, dst.sb8, dst_rb0,
+            dst_rb_stride);
+    }
     MLXD_CHECK(cudaGetLastError());
     return 0;
 }
@@ -152,14 +181,133 @@ MLXD_DEV unsigned long long argmax_key(float v, int idx) {
     return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
-constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_THREADS = 512;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+constexpr int GEMV_P = 8;            // tiles in flight per warp
 
-template <int G, bool SBF32, int PRO, int EPI, int RB>
-__global__ void __launch_bounds__(GEMV_THREADS, 2) qgemv_kernel(GemvArgs a) {
-    constexpr int XW = G / 8;           // x words per (group, t)
-    constexpr int P = (G == 64) ? 8 : 8; // prefetch depth (items)
-    constexpr int WB = G / 4;           // tile bytes per lane
-    constexpr int SBB = SBF32 ? 16 : 8; // sb bytes per record
+// Persistent stream-K GEMV. The T = (rows/16) * (cols/G) tiles, in memory
+// order, are cut into one contiguous range per warp (equal to within one
+// tile), so every warp streams its share of the weights with GEMV_P tile loads
+// in flight, issued before the prologue. An epilogue unit is one row block
+// (two, gate and up, for SwiGLU); a warp that covers a whole unit finishes it
+// from registers, otherwise each contributing warp writes its 16 (or 32)
+// partial sums to its own slot of the workspace and the last one to arrive
+// (atomic counter) adds the slots in order and runs the epilogue, so the
+// result does not depend on arrival order.
+
+// stream-K bookkeeping in "items": one tile (generic kernel) or one block
+// of 8 tiles (fast kernel); ipr = items per row block
+struct FlushCtx {
+    long long T, TW, gw, t_begin, t_end;
+    int ipr;
+};
+
+template <int EPI>
+MLXD_DEV void epilogue_row(const GemvArgs &a, int row, float acc) {
+    if constexpr (EPI == EPI_STORE) {
+        a.y[row] = f2bf(acc);
+    } else if constexpr (EPI == EPI_RESIDUAL) {
+        a.y[row] = f2bf(__fadd_rn(bf2f(a.residual[row]), rbf(acc)));
+    } else if constexpr (EPI == EPI_PARTIAL_F32) {
+        a.yf[row] = acc;
+    }
+}
+
+MLXD_DEV void argmax_rows(const GemvArgs &a, int lane, int row0, float v0, bool has0, int row1,
+                          float v1, bool has1) {
+    unsigned long long key = 0ull;
+    if (has0) {
+        a.y[row0] = f2bf(v0);
+        key = argmax_key(rbf(v0), a.row_offset + row0);
+    }
+    if (has1) {
+        a.y[row1] = f2bf(v1);
+        unsigned long long k1 = argmax_key(rbf(v1), a.row_offset + row1);
+        key = k1 > key ? k1 : key;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+    }
+    if (lane == 0) atomicMax(a.amax, key);
+}
+
+// out of line: runs once per row block a warp leaves
+template <int EPI>
+__device__ __noinline__ void gemv_flush(const GemvArgs &a, const FlushCtx &f, int rb, float y0,
+                                        float y1, int count) {
+    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    const int lane = threadIdx.x & 31, t = lane & 3, gq = lane >> 2;
+    const int ng = f.ipr;
+    const int unit = rb / UNIT_RB;
+    const int unit_tiles = ng * UNIT_RB;
+    if (UNIT_RB == 1 && count == ng) {
+        // whole row block in registers: lanes t == 0 hold rows gq, gq + 8
+        const int r0 = rb * 16 + gq, r1 = r0 + 8;
+        if constexpr (EPI == EPI_ARGMAX) {
+            argmax_rows(a, lane, r0, y0, t == 0, r1, y1, t == 0);
+        } else if (t == 0) {
+            epilogue_row<EPI>(a, r0, y0);
+            epilogue_row<EPI>(a, r1, y1);
+        }
+        return;
+    }
+    // contributor slot: order of this warp among the unit's warps
+    const long long first_tile = (long long)unit * unit_tiles;
+    const long long first_w = ((first_tile + 1) * f.TW + f.T - 1) / f.T - 1;
+    const int slot = (int)(f.gw - first_w);
+    float *rec = a.ws + ((size_t)unit * a.ws_slots + slot) * (16 * UNIT_RB);
+    const int half = (rb % UNIT_RB) * 16;
+    if (t == 0) {
+        rec[half + gq] = y0;
+        rec[half + gq + 8] = y1;
+        if (UNIT_RB == 2) {
+            // a half this warp does not cover is zero in its slot
+            if ((rb % 2) == 0 && (long long)(rb + 1) * ng >= f.t_end) {
+                rec[16 + gq] = 0.f;
+                rec[16 + gq + 8] = 0.f;
+            }
+            if ((rb % 2) == 1 && (long long)rb * ng <= f.t_begin) {
+                rec[gq] = 0.f;
+                rec[gq + 8] = 0.f;
+            }
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+        int old = atomicAdd(&a.cnt[unit], count);
+        last = (old + count == unit_tiles);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    const int nslots = (int)(((first_tile + unit_tiles) * f.TW + f.T - 1) / f.T - 1 - first_w) + 1;
+    float accs[UNIT_RB] = {};
+    if (lane < 16) {
+        for (int sl = 0; sl < nslots; sl++) {
+            const float *r = a.ws + ((size_t)unit * a.ws_slots + sl) * (16 * UNIT_RB);
+#pragma unroll
+            for (int u = 0; u < UNIT_RB; u++) accs[u] += __ldcg(r + u * 16 + lane);
+        }
+    }
+    if (lane == 0) a.cnt[unit] = 0;
+    if constexpr (EPI == EPI_SWIGLU) {
+        if (lane < 16) a.y[unit * 16 + lane] = f2bf(swiglu_bf16(rbf(accs[0]), rbf(accs[UNIT_RB - 1])));
+    } else if constexpr (EPI == EPI_ARGMAX) {
+        argmax_rows(a, lane, rb * 16 + lane, accs[0], lane < 16, 0, 0.f, false);
+    } else {
+        if (lane < 16) epilogue_row<EPI>(a, rb * 16 + lane, accs[0]);
+    }
+}
+
+template <int G, bool SBF32, int PRO, int EPI>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(GemvArgs a) {
+    constexpr int XW = G / 8;            // x words per (group, t)
+    constexpr int WB = G / 4;            // tile bytes per lane
+    constexpr int SBB = SBF32 ? 16 : 8;  // sb bytes per record
     using WT = typename Ld<G, false>::W;
     using ST = typename std::conditional<SBF32, uint4, uint2>::type;
 
@@ -167,24 +315,28 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) qgemv_kernel(GemvArgs a) {
     const int ng = a.cols / G;
     uint32_t *xp = reinterpret_cast<uint32_t *>(smem_raw);
     float *xs = reinterpret_cast<float *>(xp + (size_t)ng * 4 * XW);
-    float *red = xs + ng;                // [8][RB][16]
-    __shared__ float s_red[8];
+    __shared__ float s_red[GEMV_WARPS];
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3;
-    const int rb0 = blockIdx.x * RB;
-    const int g0 = (warp * ng) / 8, g1 = ((warp + 1) * ng) / 8;
-    const int nper = g1 - g0;
-    const int n_items = RB * nper;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
+    FlushCtx f;
+    f.ipr = ng;
+    f.T = (long long)(a.rows / 16) * ng;
+    // active warps: at most one per tile, so every active warp owns >= 1 tile
+    f.TW = min((long long)gridDim.x * GEMV_WARPS, f.T);
+    f.gw = (long long)blockIdx.x * GEMV_WARPS + warp;
+    f.t_begin = f.gw < f.TW ? f.T * f.gw / f.TW : f.T;
+    f.t_end = f.gw < f.TW ? f.T * (f.gw + 1) / f.TW : f.T;
+    const int n_items = (int)(f.t_end - f.t_begin);
+    const uint8_t *pw0 = a.tiles + ((size_t)f.t_begin * 32 + lane) * WB;
+    const uint8_t *ps0 = a.sb + ((size_t)f.t_begin * 8 + gq) * SBB;
 
-    WT wbuf[P];
-    ST sbuf[P];
+    WT wbuf[GEMV_P];
+    ST sbuf[GEMV_P];
 #pragma unroll
-    for (int p = 0; p < P; p++) {
+    for (int p = 0; p < GEMV_P; p++) {
         if (p < n_items) {
-            int rb = p / nper, g = g0 + p % nper;
-            size_t tile = (size_t)(rb0 + rb) * ng + g;
-            wbuf[p] = load_w<G>(a.tiles + (tile * 32 + lane) * WB);
-            sbuf[p] = load_sb<SBF32>(a.sb + (tile * 8 + (lane >> 2)) * SBB);
+            wbuf[p] = load_w<G>(pw0 + p * 32 * WB);
+            sbuf[p] = load_sb<SBF32>(ps0 + p * 8 * SBB);
         }
     }
 
@@ -194,20 +346,23 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) qgemv_kernel(GemvArgs a) {
     const int npairs = a.cols / 2;
     float inv = 1.0f;
     if (PRO == PRO_RMSNORM) {
+        // the oracle's association: Ta element-strided partials, butterfly
+        // within each warp, warp totals in order
+        const int n = a.cols;
+        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
         float acc = 0.f;
-        for (int p = tid; p < npairs; p += GEMV_THREADS) {
-            uint32_t v = x2[p];
-            float lo = lo_bf(v), hi = hi_bf(v);
-            acc = fmaf(lo, lo, acc);
-            acc = fmaf(hi, hi, acc);
-        }
+        if (tid < Ta)
+            for (int i = tid; i < n; i += Ta) {
+                float v = bf2f(a.x[i]);
+                acc = fmaf(v, v, acc);
+            }
         acc = warp_sum(acc);
         if (lane == 0) s_red[warp] = acc;
         __syncthreads();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) tot += s_red[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.cols), a.eps)));
+        for (int w = 0; w < GEMV_WARPS; w++) tot += s_red[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
     }
     const uint32_t *nw2 = reinterpret_cast<const uint32_t *>(a.norm_w);
     for (int p = tid; p < npairs; p += GEMV_THREADS) {
@@ -225,7 +380,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) qgemv_kernel(GemvArgs a) {
         xp[(gi * 4 + tt) * XW + j * 2 + hi] = v;
     }
     __syncthreads();
-    for (int gi = warp; gi < ng; gi += 8) {
+    for (int gi = warp; gi < ng; gi += GEMV_WARPS) {
         float s = 0.f;
         if (lane < 4 * XW) {
             uint32_t v = xp[gi * 4 * XW + lane];
@@ -236,124 +391,285 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) qgemv_kernel(GemvArgs a) {
     }
     __syncthreads();
     pdl_trigger();
+    if (n_items <= 0) return;
 
-    // ---- main loop over (row block, group) items of this warp
+    // ---- main loop: segments of one row block; one compare per tile
+    int rb = (int)(f.t_begin / ng);
+    int g = (int)(f.t_begin % ng);
+    int seg_first = 0;
+    int seg_last = min(ng - g, n_items) - 1;
+    const uint32_t *xptr = xp + (g * 4 + t) * XW;
+    const float *xsp = xs + g;
     float y0 = 0.f, y1 = 0.f;
-    for (int base = 0; base < n_items; base += P) {
+    for (int base = 0; base < n_items; base += GEMV_P) {
+        const uint8_t *pwn = pw0 + (size_t)(base + GEMV_P) * 32 * WB;
+        const uint8_t *psn = ps0 + (size_t)(base + GEMV_P) * 8 * SBB;
 #pragma unroll
-        for (int p = 0; p < P; p++) {
-            int i = base + p;
-            if (i < n_items) {
-                int rb = i / nper, g = g0 + i % nper;
-                WT wv = wbuf[p];
-                ST sv = sbuf[p];
-                int nx = i + P;
-                if (nx < n_items) {
-                    int nrb = nx / nper, ngg = g0 + nx % nper;
-                    size_t tile = (size_t)(rb0 + nrb) * ng + ngg;
-                    wbuf[p] = load_w<G>(a.tiles + (tile * 32 + lane) * WB);
-                    sbuf[p] = load_sb<SBF32>(a.sb + (tile * 8 + (lane >> 2)) * SBB);
-                }
-                float d[4] = {0.f, 0.f, 0.f, 0.f};
-                const uint4 *xq = reinterpret_cast<const uint4 *>(xp + (g * 4 + t) * XW);
-                if constexpr (G == 64) {
-                    uint4 xa = xq[0], xb = xq[1];
-                    uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        for (int p = 0; p < GEMV_P; p++) {
+            const int i = base + p;
+            if (i >= n_items) break;
+            WT wv = wbuf[p];
+            ST sv = sbuf[p];
+            if (i + GEMV_P < n_items) {
+                wbuf[p] = load_w<G>(pwn + p * 32 * WB);
+                sbuf[p] = load_sb<SBF32>(psn + p * 8 * SBB);
+            }
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint4 *xq = reinterpret_cast<const uint4 *>(xptr);
+            if constexpr (G == 64) {
+                uint4 xa = xq[0], xb = xq[1];
+                uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
-                                          nib_pair(wv.w, j)};
-                        mma_bf16_16816(d, af, xv[2 * j], xv[2 * j + 1]);
-                    }
-                } else {
-                    uint4 xa = xq[0];
-                    uint32_t xv[4] = {xa.x, xa.y, xa.z, xa.w};
+                for (int j = 0; j < 4; j++) {
+                    uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
+                                      nib_pair(wv.w, j)};
+                    mma_bf16_16816(d, af, xv[2 * j], xv[2 * j + 1]);
+                }
+            } else {
+                uint4 xa = xq[0];
+                uint32_t xv[4] = {xa.x, xa.y, xa.z, xa.w};
 #pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        uint32_t af[4] = {nib_pair(wv.x, 2 * j), nib_pair(wv.y, 2 * j),
-                                          nib_pair(wv.x, 2 * j + 1), nib_pair(wv.y, 2 * j + 1)};
-                        mma_bf16_16816(d, af, xv[2 * j], xv[2 * j + 1]);
-                    }
-                }
-                float sA, bA, sB, bB;
-                if constexpr (SBF32) {
-                    sA = __uint_as_float(sv.x); bA = __uint_as_float(sv.y);
-                    sB = __uint_as_float(sv.z); bB = __uint_as_float(sv.w);
-                } else {
-                    sA = lo_bf(sv.x); bA = hi_bf(sv.x);
-                    sB = lo_bf(sv.y); bB = hi_bf(sv.y);
-                }
-                float xsg = xs[g];
-                y0 = fmaf(sA, d[0], y0);
-                y0 = fmaf(fmaf(-128.f, sA, bA), xsg, y0);
-                y1 = fmaf(sB, d[2], y1);
-                y1 = fmaf(fmaf(-128.f, sB, bB), xsg, y1);
-                if (i % nper == nper - 1) {
-                    if (t == 0) {
-                        red[(warp * RB + rb) * 16 + (lane >> 2)] = y0;
-                        red[(warp * RB + rb) * 16 + (lane >> 2) + 8] = y1;
-                    }
-                    y0 = 0.f;
-                    y1 = 0.f;
+                for (int j = 0; j < 2; j++) {
+                    uint32_t af[4] = {nib_pair(wv.x, 2 * j), nib_pair(wv.y, 2 * j),
+                                      nib_pair(wv.x, 2 * j + 1), nib_pair(wv.y, 2 * j + 1)};
+                    mma_bf16_16816(d, af, xv[2 * j], xv[2 * j + 1]);
                 }
             }
-        }
-    }
-    if (nper == 0 && lane < 16)
-        for (int rb = 0; rb < RB; rb++) red[(warp * RB + rb) * 16 + lane] = 0.f;
-    __syncthreads();
-
-    // ---- cross-warp reduction (fixed order) and epilogue
-    if (tid < RB * 16) {
-        int rb = tid >> 4, r = tid & 15;
-        float acc = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; w++) acc += red[(w * RB + rb) * 16 + r];
-        int row = (rb0 + rb) * 16 + r;
-        if constexpr (EPI == EPI_STORE) {
-            a.y[row] = f2bf(acc);
-        } else if constexpr (EPI == EPI_RESIDUAL) {
-            a.y[row] = f2bf(__fadd_rn(bf2f(a.residual[row]), rbf(acc)));
-        } else if constexpr (EPI == EPI_SWIGLU) {
-            red[rb * 16 + r] = acc;  // warp 0 slots reused after the reduction
-        } else if constexpr (EPI == EPI_PARTIAL_F32) {
-            a.yf[row] = acc;
-        } else {
-            float v = rbf(acc);
-            a.y[row] = f2bf(acc);
-            unsigned long long key = argmax_key(v, a.row_offset + row);
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) {
-                unsigned long long other = __shfl_xor_sync(0xffffu, key, o, 16);
-                key = other > key ? other : key;
+            float sA, bA, sB, bB;
+            if constexpr (SBF32) {
+                sA = __uint_as_float(sv.x); bA = __uint_as_float(sv.y);
+                sB = __uint_as_float(sv.z); bB = __uint_as_float(sv.w);
+            } else {
+                sA = lo_bf(sv.x); bA = hi_bf(sv.x);
+                sB = lo_bf(sv.y); bB = hi_bf(sv.y);
             }
-            if (r == 0) atomicMax(a.amax, key);
-        }
-    }
-    if constexpr (EPI == EPI_SWIGLU) {
-        __syncthreads();
-        if (tid < RB * 8) {
-            int pair = tid >> 4, r = tid & 15;
-            float g = rbf(red[(2 * pair) * 16 + r]);
-            float u = rbf(red[(2 * pair + 1) * 16 + r]);
-            a.y[(blockIdx.x * (RB / 2) + pair) * 16 + r] = f2bf(swiglu_bf16(g, u));
+            const float xsg = *xsp;
+            y0 = fmaf(sA, d[0], y0);
+            y0 = fmaf(fmaf(-128.f, sA, bA), xsg, y0);
+            y1 = fmaf(sB, d[2], y1);
+            y1 = fmaf(fmaf(-128.f, sB, bB), xsg, y1);
+            xptr += 4 * XW;
+            xsp++;
+            if (i == seg_last) {
+                gemv_flush<EPI>(a, f, rb, y0, y1, i - seg_first + 1);
+                y0 = 0.f;
+                y1 = 0.f;
+                rb++;
+                seg_first = i + 1;
+                seg_last = min(i + ng, n_items - 1);
+                xptr = xp + t * XW;
+                xsp = xs;
+            }
         }
     }
 }
 
+// Decode fast path (group 64, bf16 scales, cols/64 a multiple of 8). The
+// unit of work is a block of 8 consecutive groups of one row block (8 tiles,
+// 4 KB contiguous). Its 8 tiles accumulate into ONE mma accumulator, tile p
+// feeding N-column p: the B operand is x for the lanes of column p and zero
+// for the rest, so after the block the accumulator holds the 8 group partial
+// sums of rows g and g+8 spread over the 4 lanes of a quad (columns 2t, 2t+1)
+// and the affine step (scale, bias) runs once per (row, group) instead of
+// once per lane. Scales/biases arrive as one 16-byte record per lane per
+// block (sb8 layout).
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
+    constexpr int G = 64, XW = 8;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int ng = a.cols / G, nbk = ng / 8;
+    uint32_t *xp = reinterpret_cast<uint32_t *>(smem_raw);
+    float *xs = reinterpret_cast<float *>(xp + (size_t)ng * 4 * XW);
+    __shared__ __align__(16) uint32_t s_zero[8];
+    __shared__ float s_red[GEMV_WARPS];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
+    FlushCtx f;
+    f.ipr = nbk;
+    f.T = (long long)(a.rows / 16) * nbk;
+    f.TW = min((long long)gridDim.x * GEMV_WARPS, f.T);
+    f.gw = (long long)blockIdx.x * GEMV_WARPS + warp;
+    f.t_begin = f.gw < f.TW ? f.T * f.gw / f.TW : f.T;
+    f.t_end = f.gw < f.TW ? f.T * (f.gw + 1) / f.TW : f.T;
+    const int n_items = (int)(f.t_end - f.t_begin);
+    const uint8_t *pw = a.tiles + ((size_t)f.t_begin * 8 * 32 + lane) * 16;
+    const uint8_t *ps = a.sb8 + ((size_t)f.t_begin * 32 + lane) * 16;
+
+    uint4 wbuf[8];
+    uint4 sbuf = make_uint4(0, 0, 0, 0);
+    if (n_items > 0) {
+#pragma unroll
+        for (int p = 0; p < 8; p++) wbuf[p] = ldg_nc_v4(pw + p * 512);
+        sbuf = ldg_nc_v4(ps);
+    }
+
+    // ---- prologue: x (optionally RMS-normalised) into the fragment order
+    pdl_wait();
+    if (tid < 8) s_zero[tid] = 0u;
+    const uint32_t *x2 = reinterpret_cast<const uint32_t *>(a.x);
+    const int npairs = a.cols / 2;
+    float inv = 1.0f;
+    if (PRO == PRO_RMSNORM) {
+        const int n = a.cols;
+        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
+        float acc = 0.f;
+        if (tid < Ta)
+            for (int i = tid; i < n; i += Ta) {
+                float v = bf2f(a.x[i]);
+                acc = fmaf(v, v, acc);
+            }
+        acc = warp_sum(acc);
+        if (lane == 0) s_red[warp] = acc;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < GEMV_WARPS; w++) tot += s_red[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
+    }
+    const uint32_t *nw2 = reinterpret_cast<const uint32_t *>(a.norm_w);
+    for (int p = tid; p < npairs; p += GEMV_THREADS) {
+        uint32_t v = x2[p];
+        if (PRO == PRO_RMSNORM) {
+            uint32_t wv = nw2[p];
+            float lo = rbf(__fmul_rn(lo_bf(wv), rbf(__fmul_rn(lo_bf(v), inv))));
+            float hi = rbf(__fmul_rn(hi_bf(wv), rbf(__fmul_rn(hi_bf(v), inv))));
+            v = pack_bf2(lo, hi);
+        }
+        int k = 2 * p;
+        int gi = k / G, kk = k % G;
+        int j = kk >> 4, w16 = kk & 15;
+        int hi = w16 >= 8, tt = (w16 & 7) >> 1;
+        xp[(gi * 4 + tt) * XW + j * 2 + hi] = v;
+    }
+    __syncthreads();
+    for (int gi = warp; gi < ng; gi += GEMV_WARPS) {
+        float sm = 0.f;
+        if (lane < 4 * XW) {
+            uint32_t v = xp[gi * 4 * XW + lane];
+            sm = lo_bf(v) + hi_bf(v);
+        }
+        sm = warp_sum(sm);
+        if (lane == 0) xs[gi] = sm;
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (n_items <= 0) return;
+
+    int rb = (int)(f.t_begin / nbk);
+    int bk = (int)(f.t_begin % nbk);
+    int seg_first = 0;
+    int seg_last = min(nbk - bk, n_items) - 1;
+    float y0 = 0.f, y1 = 0.f;
+    for (int i = 0; i < n_items; i++) {
+        const bool pre = i + 1 < n_items;
+        const uint8_t *pwn = pw + (size_t)(i + 1) * 4096;
+        const uint32_t *xb = xp + ((size_t)bk * 32 + t) * XW;   // group 8bk at +0, +p*32
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            const uint4 wv = wbuf[p];
+            if (pre) wbuf[p] = ldg_nc_v4(pwn + p * 512);
+            const uint4 *xq = reinterpret_cast<const uint4 *>(gq == p ? xb + p * 32 : s_zero);
+            const uint4 xa = xq[0], xc = xq[1];
+            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
+                                  nib_pair(wv.w, j)};
+                mma_bf16_16816(d, af, xv[2 * j], xv[2 * j + 1]);
+            }
+        }
+        const uint4 sv = sbuf;
+        if (pre) sbuf = ldg_nc_v4(ps + (size_t)(i + 1) * 512);
+        const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
+        const float s00 = lo_bf(sv.x), b00 = hi_bf(sv.x), s01 = lo_bf(sv.y), b01 = hi_bf(sv.y);
+        const float s10 = lo_bf(sv.z), b10 = hi_bf(sv.z), s11 = lo_bf(sv.w), b11 = hi_bf(sv.w);
+        y0 = fmaf(s00, d[0], y0);
+        y0 = fmaf(fmaf(-128.f, s00, b00), xsv.x, y0);
+        y0 = fmaf(s01, d[1], y0);
+        y0 = fmaf(fmaf(-128.f, s01, b01), xsv.y, y0);
+        y1 = fmaf(s10, d[2], y1);
+        y1 = fmaf(fmaf(-128.f, s10, b10), xsv.x, y1);
+        y1 = fmaf(s11, d[3], y1);
+        y1 = fmaf(fmaf(-128.f, s11, b11), xsv.y, y1);
+        if (i == seg_last) {
+            // the quad's four lanes hold disjoint groups of rows g, g+8
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+            y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+            y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+            gemv_flush<EPI>(a, f, rb, y0, y1, i - seg_first + 1);
+            y0 = 0.f;
+            y1 = 0.f;
+            rb++;
+            bk = 0;
+            seg_first = i + 1;
+            seg_last = min(i + nbk, n_items - 1);
+        } else {
+            bk++;
+        }
+    }
+}
+
+// grid and workspace slots of one launch
+static bool fast8_shape(int cols, int G) { return G == 64 && (cols / 64) % 8 == 0; }
+
+static void gemv_plan(int rows, int cols, int G, int epi, int sms, int *grid, int *slots,
+                      bool fast) {
+    const int ipr = fast ? cols / G / 8 : cols / G;   // items per row block
+    const long long T = (long long)(rows / 16) * ipr;
+    const long long min_items = fast ? 1 : 4;          // per warp
+    long long g = (T + GEMV_WARPS * min_items - 1) / (GEMV_WARPS * min_items);
+    if (g > sms) g = sms;
+    if (g < 1) g = 1;
+    *grid = (int)g;
+    long long TW = g * GEMV_WARPS < T ? g * GEMV_WARPS : T;
+    int unit_tiles = ipr * (epi == EPI_SWIGLU ? 2 : 1);
+    long long per_warp = T / TW;   // floor, >= 1 unless T < TW
+    long long s = per_warp > 0 ? (unit_tiles + per_warp - 1) / per_warp + 2 : unit_tiles + 1;
+    if (s > unit_tiles + 1) s = unit_tiles + 1;
+    *slots = (int)s;
+}
+
+size_t gemv_workspace_floats(int rows, int cols, int G, int epi, int sms, int *units_out) {
+    int grid, slots, g2, s2;
+    gemv_plan(rows, cols, G, epi, sms, &grid, &slots, false);
+    if (fast8_shape(cols, G)) {
+        gemv_plan(rows, cols, G, epi, sms, &g2, &s2, true);
+        if (s2 > slots) slots = s2;
+    }
+    int unit_rb = epi == EPI_SWIGLU ? 2 : 1;
+    int units = rows / 16 / unit_rb;
+    if (units_out) *units_out = units;
+    return (size_t)units * slots * 16 * unit_rb;
+}
+
+static int g_sms = 0;
+int num_sms() {
+    if (!g_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_sms <= 0) g_sms = 148;
+    }
+    return g_sms;
+}
+
 template <int G, bool SBF32, int PRO, int EPI>
-static int launch_gemv(const GemvArgs &a, cudaStream_t st, bool pdl) {
-    constexpr int RB = EPI == EPI_SWIGLU ? 2 : 1;
-    auto kern = qgemv_kernel<G, SBF32, PRO, EPI, RB>;
+static int launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
+    auto kern = qgemv_kernel<G, SBF32, PRO, EPI>;
     int ng = a.cols / G;
-    size_t smem = (size_t)ng * 4 * (G / 8) * 4 + (size_t)ng * 4 + 8 * RB * 16 * 4;
+    size_t smem = (size_t)ng * 4 * (G / 8) * 4 + (size_t)ng * 4;
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
         MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured = smem;
     }
+    int grid, slots;
+    gemv_plan(a.rows, a.cols, G, EPI, num_sms(), &grid, &slots, false);
+    a.ws_slots = slots;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.rows / 16 / RB);
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(GEMV_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -366,6 +682,51 @@ static int launch_gemv(const GemvArgs &a, cudaStream_t st, bool pdl) {
     return 0;
 }
 
+template <int PRO, int EPI>
+static int launch_gemv8(GemvArgs a, cudaStream_t st, bool pdl) {
+    auto kern = qgemv8_kernel<PRO, EPI>;
+    int ng = a.cols / 64;
+    size_t smem = (size_t)ng * 4 * 8 * 4 + (size_t)ng * 4;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = smem;
+    }
+    int grid, slots;
+    gemv_plan(a.rows, a.cols, 64, EPI, num_sms(), &grid, &slots, true);
+    a.ws_slots = slots;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
+    return 0;
+}
+
+static int dispatch_gemv8(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
+#define MLXD_GEMV8_CASE(P, E) \
+    if (pro == P && epi == E) return launch_gemv8<P, E>(a, st, pdl);
+    MLXD_GEMV8_CASE(PRO_PLAIN, EPI_STORE)
+    MLXD_GEMV8_CASE(PRO_PLAIN, EPI_RESIDUAL)
+    MLXD_GEMV8_CASE(PRO_PLAIN, EPI_SWIGLU)
+    MLXD_GEMV8_CASE(PRO_PLAIN, EPI_ARGMAX)
+    MLXD_GEMV8_CASE(PRO_PLAIN, EPI_PARTIAL_F32)
+    MLXD_GEMV8_CASE(PRO_RMSNORM, EPI_STORE)
+    MLXD_GEMV8_CASE(PRO_RMSNORM, EPI_RESIDUAL)
+    MLXD_GEMV8_CASE(PRO_RMSNORM, EPI_SWIGLU)
+    MLXD_GEMV8_CASE(PRO_RMSNORM, EPI_ARGMAX)
+    MLXD_GEMV8_CASE(PRO_RMSNORM, EPI_PARTIAL_F32)
+#undef MLXD_GEMV8_CASE
+    set_error("qgemv: bad prologue/epilogue");
+    return -1;
+}
+
 template <int G, bool SBF32>
 static int dispatch_gemv(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
 #define MLXD_GEMV_CASE(P, E) \
@@ -375,6 +736,7 @@ static int dispatch_gemv(int pro, int epi, const GemvArgs &a, cudaStream_t st, b
     MLXD_GEMV_CASE(PRO_PLAIN, EPI_SWIGLU)
     MLXD_GEMV_CASE(PRO_PLAIN, EPI_ARGMAX)
     MLXD_GEMV_CASE(PRO_PLAIN, EPI_PARTIAL_F32)
+    MLXD_GEMV_CASE(PRO_RMSNORM, EPI_PARTIAL_F32)
     MLXD_GEMV_CASE(PRO_RMSNORM, EPI_STORE)
     MLXD_GEMV_CASE(PRO_RMSNORM, EPI_RESIDUAL)
     MLXD_GEMV_CASE(PRO_RMSNORM, EPI_SWIGLU)
@@ -393,9 +755,17 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
     a.sb = W.sb;
     a.rows = W.rows;
     a.cols = W.cols;
+    if (!a.ws || !a.cnt) {
+        set_error("qgemv: no workspace");
+        return -1;
+    }
     if (W.rows % (epi == EPI_SWIGLU ? 32 : 16)) {
         set_error("qgemv: rows %d not a multiple of the row block", W.rows);
         return -1;
+    }
+    if (W.sb8 && W.fast8()) {
+        a.sb8 = W.sb8;
+        return dispatch_gemv8(pro, epi, a, st, pdl);
     }
     bool f32 = W.sdtype == MLXD_F32;
     if (W.group == 64) return f32 ? dispatch_gemv<64, true>(pro, epi, a, st, pdl)
