@@ -21,13 +21,15 @@ namespace mlxd {
 
 // ------------------------------------------------------------------ decode
 
-constexpr int DEC_THREADS = 128;
+constexpr int DEC_THREADS = 256;
 constexpr int DEC_MAX_SPLIT = 64;
 
 template <int D, int REP>
-__global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
+__global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeArgs a) {
     constexpr int DL = D / 32;   // dims per lane
     constexpr int NW = DEC_THREADS / 32;
+    constexpr int DEC_U = D == 128 ? 4 : 8;   // positions per warp per pass, loads in flight
+    using RowT = typename std::conditional<DL == 4, uint2, uint32_t>::type;
     __shared__ float s_vec[NW][D];
     __shared__ float s_q[REP][D];
     __shared__ __align__(16) uint16_t s_knew[D];
@@ -38,19 +40,45 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
 
     const int kh = blockIdx.x, split = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
+    // The position counter and the cache rows of earlier positions were
+    // written by earlier decode steps, so they are read before waiting on the
+    // q/k/v projection of this step: the cache stream overlaps its tail.
     const int pos = *a.d_pos;
     const int T = pos + 1;
     const int lo = a.window > 0 ? max(0, T - a.window) : 0;
     const int span = T - lo;
     const int s0 = lo + (int)(((long long)span * split) / a.nsplit);
     const int s1 = lo + (int)(((long long)span * (split + 1)) / a.nsplit);
+    const int per_warp = (s1 - s0 + NW - 1) / NW;
+    const int w0 = s0 + warp * per_warp;
+    const int w1 = min(s1, w0 + per_warp);
     const int slot_new = pos % a.cap;
+    uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
+    uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
+
+    RowT kraw[DEC_U], vraw[DEC_U];
+    auto fetch = [&](int j0) {
+#pragma unroll
+        for (int u = 0; u < DEC_U; u++) {
+            int j = j0 + u;
+            if (j < w1 && j != pos) {
+                const size_t off = (size_t)(j % a.cap) * D + lane * DL;
+                kraw[u] = *reinterpret_cast<const RowT *>(kc + off);
+                vraw[u] = *reinterpret_cast<const RowT *>(vc + off);
+            }
+        }
+    };
+    fetch(w0);
+
+    pdl_wait();
     const uint16_t *qkv = a.qkv;
     const int qstride = D * (a.gate ? 2 : 1);
-
-    // q heads of this GQA group and the new k: norm + rope, one warp each
-    for (int vi = warp; vi <= REP; vi += NW) {
+    // q heads of this GQA group, the new k (norm + rope) and the new v: one warp each
+    for (int vi = warp; vi <= REP + 1; vi += NW) {
+        if (vi == REP + 1) {
+            for (int d = lane; d < D; d += 32) s_vnew[d] = qkv[a.qdim + (size_t)(a.hkv + kh) * D + d];
+            continue;
+        }
         float *v = s_vec[warp];
         const uint16_t *src = vi < REP ? qkv + (size_t)(kh * REP + vi) * qstride
                                        : qkv + a.qdim + (size_t)kh * D;
@@ -64,11 +92,7 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
         }
         __syncwarp();
     }
-    for (int d = threadIdx.x; d < D; d += DEC_THREADS)
-        s_vnew[d] = qkv[a.qdim + (size_t)(a.hkv + kh) * D + d];
     __syncthreads();
-    uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
-    uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
     if (split == 0) {
         for (int d = threadIdx.x; d < D; d += DEC_THREADS) {
             kc[(size_t)slot_new * D + d] = s_knew[d];
@@ -93,26 +117,30 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
         for (int i = 0; i < DL; i++) o[r][i] = 0.f;
     }
 
-    auto load_row = [&](const uint16_t *base, const uint16_t *snew, int j, float (&dst)[DL]) {
-        const uint16_t *p = (j == pos) ? snew + lane * DL : base + (size_t)(j % a.cap) * D + lane * DL;
+    auto unpack = [&](const RowT &raw, float (&dst)[DL]) {
         if constexpr (DL == 4) {
-            uint2 v = *reinterpret_cast<const uint2 *>(p);
-            dst[0] = lo_bf(v.x); dst[1] = hi_bf(v.x); dst[2] = lo_bf(v.y); dst[3] = hi_bf(v.y);
+            dst[0] = lo_bf(raw.x); dst[1] = hi_bf(raw.x); dst[2] = lo_bf(raw.y); dst[3] = hi_bf(raw.y);
         } else {
-            uint32_t v = *reinterpret_cast<const uint32_t *>(p);
-            dst[0] = lo_bf(v); dst[1] = hi_bf(v);
+            dst[0] = lo_bf(raw); dst[1] = hi_bf(raw);
         }
     };
+    const RowT *knew_row = reinterpret_cast<const RowT *>(s_knew + lane * DL);
+    const RowT *vnew_row = reinterpret_cast<const RowT *>(s_vnew + lane * DL);
 
-    constexpr int U = 4;
-    for (int j0 = s0 + warp * U; j0 < s1; j0 += NW * U) {
-        float kr[U][DL], vr[U][DL];
+    for (int j0 = w0; j0 < w1; j0 += DEC_U) {
+        if (j0 != w0) fetch(j0);
+        float kr[DEC_U][DL], vr[DEC_U][DL];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
+        for (int u = 0; u < DEC_U; u++) {
             int j = j0 + u;
-            if (j < s1) {
-                load_row(kc, s_knew, j, kr[u]);
-                load_row(vc, s_vnew, j, vr[u]);
+            RowT kk = kraw[u], vv = vraw[u];
+            if (j == pos) {
+                kk = *knew_row;
+                vv = *vnew_row;
+            }
+            if (j < w1) {
+                unpack(kk, kr[u]);
+                unpack(vv, vr[u]);
             } else {
 #pragma unroll
                 for (int i = 0; i < DL; i++) kr[u][i] = vr[u][i] = 0.f;
@@ -121,9 +149,9 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
         // U independent scores per head, then one online-softmax update
 #pragma unroll
         for (int r = 0; r < REP; r++) {
-            float sc[U];
+            float sc[DEC_U];
 #pragma unroll
-            for (int u = 0; u < U; u++) {
+            for (int u = 0; u < DEC_U; u++) {
                 float x = 0.f;
 #pragma unroll
                 for (int i = 0; i < DL; i++) x = fmaf(q[r][i], kr[u][i], x);
@@ -132,17 +160,17 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
 #pragma unroll
             for (int sh = 16; sh > 0; sh >>= 1)
 #pragma unroll
-                for (int u = 0; u < U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], sh);
+                for (int u = 0; u < DEC_U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], sh);
             float mn = m[r];
 #pragma unroll
-            for (int u = 0; u < U; u++)
-                if (j0 + u < s1) mn = fmaxf(mn, sc[u]);
+            for (int u = 0; u < DEC_U; u++)
+                if (j0 + u < w1) mn = fmaxf(mn, sc[u]);
             float alpha = exp2f(m[r] - mn);
             float ps = 0.f;
-            float pu[U];
+            float pu[DEC_U];
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                pu[u] = (j0 + u < s1) ? exp2f(sc[u] - mn) : 0.f;
+            for (int u = 0; u < DEC_U; u++) {
+                pu[u] = (j0 + u < w1) ? exp2f(sc[u] - mn) : 0.f;
                 ps += pu[u];
             }
             l[r] = l[r] * alpha + ps;
@@ -150,7 +178,7 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(AttnDecodeArgs
             for (int i = 0; i < DL; i++) {
                 float acc = o[r][i] * alpha;
 #pragma unroll
-                for (int u = 0; u < U; u++) acc = fmaf(pu[u], vr[u][i], acc);
+                for (int u = 0; u < DEC_U; u++) acc = fmaf(pu[u], vr[u][i], acc);
                 o[r][i] = acc;
             }
             m[r] = mn;
