@@ -231,8 +231,10 @@ def test_fast_decode_path_logits_and_kv():
     for layer in range(cfg.layers):
         ok_ = bf16_to_f32(okv.read(layer))
         d = np.abs(bf16_to_f32(kv.read(layer)) - ok_)
-        # one-ulp cascade bound: mean error within one bf16 ulp of the mean value
-        assert d.max() < 5e-2 and d.mean() < 2.0 ** -8 * np.abs(ok_).mean()
+        # one-ulp flips cascade through the layers: the mean error stays
+        # within the mean bf16 ulp (2^(e-7)) of the oracle's values
+        ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ok_), 2.0 ** -60))) - 7)
+        assert d.max() < 5e-2 and d.mean() <= ulp.mean(), (d.mean(), ulp.mean())
 
 
 def synth_pair_std(cfg, seed, std):
