@@ -124,6 +124,19 @@ void mlxd_cuda_linear_destroy(mlxd_linear *l);
    (exact f32 dequantised product), S > 1 the prefill GEMM (bf16-rounded
    dequantised weights, the mlx qmm tile semantics). Device pointers. */
 int  mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *stream);
+/* One-token y[out] = x[in] . deq(W)^T that allocates nothing (no counterpart
+   in the reference): same decode GEMV and result as mlxd_cuda_linear with
+   S == 1, for callers that cannot allocate device memory when they call it:
+   code inside a caching allocator's callback (allocating would re-enter it)
+   and serving loops that hold all HBM under a fixed plan (a cudaMalloc there
+   can fail, and it synchronises the device). Its split partial sums live in
+   one static device array of 2 MiB + 64 KiB shared by every call on a
+   device; a matrix
+   needing more (over 262144 rows, or over 2^19 workspace floats) is rejected
+   with -1 and a message. The first call on each device looks the array up
+   and should come before any stream capture. Calls whose kernels can overlap
+   on the GPU (unordered streams) race on the array. Device pointers. */
+int  mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void *stream);
 /* qGEMV measurement (no reference counterpart; the survey's qmv microbench):
    launches the decode GEMV of n projections round-robin, iters rounds, on an
    internal stream bracketed by CUDA events; *ms_out = mean ms per launch.

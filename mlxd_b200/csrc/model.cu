@@ -960,6 +960,14 @@ int mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *
                       l->cnt, (cudaStream_t)stream);
 }
 
+int mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void *stream) {
+    if (!l || !x || !y) {
+        set_error("linear_noalloc: null argument");
+        return -1;
+    }
+    return qgemv_static_scratch(l->W, (const uint16_t *)x, (uint16_t *)y, (cudaStream_t)stream);
+}
+
 int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y,
                            float *ms_out) {
     if (!ls || n <= 0 || iters <= 0 || !x || !y || !ms_out) return -1;

@@ -16,6 +16,8 @@
 // applied per group in f32 as
 //     y += s * d + (b - 128 s) * sum(x over the group)
 // which is mlx's qmv factorisation (scale * sum(x*q) + bias * sum(x)).
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -774,6 +776,75 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
                                   : dispatch_gemv<32, false>(pro, epi, a, st, pdl);
     set_error("qgemv: group size %d not supported", W.group);
     return -1;
+}
+
+// ------------------------------------------ decode GEMV on static scratch
+//
+// The same decode GEMV for callers that cannot allocate device memory at the
+// time they call it: code running inside a caching allocator's callback or
+// out-of-memory handler (allocating there re-enters the allocator), and a
+// serving loop that owns all device memory up front under a fixed plan (a
+// cudaMalloc mid-loop can fail once the plan has taken the HBM, and its
+// implicit device synchronisation stalls every stream). Instead of the per-matrix workspace that mlxd_cuda_linear_create allocates,
+// the split row-block partial sums and their arrival counters live in one
+// fixed array of device memory below: STATIC_WS_FLOATS f32 partials (2 MiB)
+// followed by STATIC_WS_UNITS counters, which bounds a matrix at 262144 rows
+// and at 2^19 workspace floats (gemv_workspace_floats). Every call on a device
+// shares the array, and it keeps what the last call left there: the counters
+// are cleared on the caller's stream before each launch (the partial sums are
+// always written before they are read). Two calls whose kernels can overlap
+// on the GPU, i.e. on streams with no ordering between them, race on the
+// array and give wrong results.
+constexpr size_t STATIC_WS_FLOATS = (size_t)1 << 19;
+constexpr int STATIC_WS_UNITS = 1 << 14;
+constexpr int STATIC_MAX_DEVICES = 64;
+static __device__ __align__(256) float g_gemv_static_scratch[STATIC_WS_FLOATS + STATIC_WS_UNITS];
+
+// Address of the array on the current device. Looked up once per device, on
+// that device's first call (the lookup can load the module, so that first
+// call belongs before any stream capture); later calls read the table.
+static float *static_scratch_on_current_device() {
+    static std::mutex mu;
+    static float *addr[STATIC_MAX_DEVICES] = {};
+    int dev = 0;
+    if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return nullptr;
+    if (dev < 0 || dev >= STATIC_MAX_DEVICES) {
+        set_error("linear_noalloc: device %d beyond the %d supported", dev, STATIC_MAX_DEVICES);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        if (!cuda_ok(cudaGetSymbolAddress(&p, g_gemv_static_scratch), "cudaGetSymbolAddress"))
+            return nullptr;
+        addr[dev] = (float *)p;
+    }
+    return addr[dev];
+}
+
+int qgemv_static_scratch(const QMat &W, const uint16_t *x, uint16_t *y, cudaStream_t st) {
+    if (!W.quant) {
+        set_error("linear_noalloc: matrix is not quantized");
+        return -1;
+    }
+    int units = 0;
+    size_t wsf = gemv_workspace_floats(W.rows, W.cols, W.group, EPI_STORE, num_sms(), &units);
+    if (wsf > STATIC_WS_FLOATS || units > STATIC_WS_UNITS) {
+        set_error("linear_noalloc: a %d x %d matrix needs %zu workspace floats and %d counters; "
+                  "the static scratch holds %zu and %d",
+                  W.rows, W.cols, wsf, units, STATIC_WS_FLOATS, STATIC_WS_UNITS);
+        return -1;
+    }
+    float *base = static_scratch_on_current_device();
+    if (!base) return -1;
+    int *cnt = (int *)(base + STATIC_WS_FLOATS);
+    MLXD_CHECK(cudaMemsetAsync(cnt, 0, (size_t)units * sizeof(int), st));
+    GemvArgs a = {};
+    a.x = x;
+    a.y = y;
+    a.ws = base;
+    a.cnt = cnt;
+    return qgemv(W, PRO_PLAIN, EPI_STORE, a, st, false);
 }
 
 }  // namespace mlxd

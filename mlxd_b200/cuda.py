@@ -86,6 +86,7 @@ _SIGS = {
                                           C.c_int, C.c_int]),
     "mlxd_cuda_linear_destroy": (None, [P]),
     "mlxd_cuda_linear": (C.c_int, [P, P, C.c_int, P, P]),
+    "mlxd_cuda_linear_noalloc": (C.c_int, [P, P, P, P]),
     "mlxd_cuda_linear_timed": (C.c_int, [C.POINTER(P), C.c_int, C.c_int, P, P,
                                          C.POINTER(C.c_float)]),
     "mlxd_cuda_rmsnorm": (C.c_int, [P, C.c_int, C.c_int, P, C.c_float, P, P]),
