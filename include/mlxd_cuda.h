@@ -85,6 +85,11 @@ int  mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg,
                             const mlxd_tensor *tensors, int n_tensors);
 void mlxd_cuda_model_destroy(mlxd_model *m);
 size_t mlxd_cuda_model_weight_bytes(const mlxd_model *m);
+/* Decode path the model runs (no reference counterpart): 1 = the whole step
+   as one persistent kernel (opt-in: MLXD_MEGASTEP=1 in the environment when
+   the model is created; 4-bit group-64 bf16-scale checkpoints on one GPU),
+   0 = one kernel per projection / attention (default). */
+int  mlxd_cuda_model_decode_path(const mlxd_model *m);
 /* Tensor parallel: bind an NCCL communicator (unique id bytes from rank 0,
    128 bytes) before the first forward when tp_size > 1. */
 int  mlxd_cuda_model_tp_init(mlxd_model *m, const void *nccl_unique_id);

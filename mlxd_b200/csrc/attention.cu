@@ -21,11 +21,14 @@ namespace mlxd {
 
 // ------------------------------------------------------------------ decode
 
+MLXD_TRACE_BINDER(attention)
+
 constexpr int DEC_THREADS = 256;
 constexpr int DEC_MAX_SPLIT = 64;
 
 template <int D, int REP>
 __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeArgs a) {
+    MLXD_TRACE_START
     constexpr int DL = D / 32;   // dims per lane
     constexpr int NW = DEC_THREADS / 32;
     constexpr int DEC_U = D == 128 ? 4 : 8;   // positions per warp per pass, loads in flight
@@ -69,8 +72,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
         }
     };
     fetch(w0);
+    // the next kernel (the o projection) may start streaming its weights now
+    pdl_trigger();
 
     pdl_wait();
+    MLXD_TRACE_WAITED
     const uint16_t *qkv = a.qkv;
     const int qstride = D * (a.gate ? 2 : 1);
     // q heads of this GQA group, the new k (norm + rope) and the new v: one warp each
@@ -223,46 +229,60 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
         s_last = (old == a.nsplit - 1);
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        MLXD_TRACE_END(0x30)
+        return;
+    }
+
     __threadfence();
-    // last split of this kv head: merge all splits. Split weights
-    // 2^(m_s - m) / L per head first (in shared memory), then every output
-    // element is a dot product over the splits with independent loads.
+    // last split of this kv head: merge all splits. The (max, sum) pairs of
+    // every split are loaded in parallel, one warp per q head turns them
+    // into weights 2^(m_s - m) / L, then each output element is a dot
+    // product over the splits with 32 independent loads in flight.
     __shared__ float s_w[REP][DEC_MAX_SPLIT];
-    for (int idx = threadIdx.x; idx < REP * a.nsplit; idx += DEC_THREADS) {
-        int r = idx / a.nsplit, sp = idx % a.nsplit;
-        s_w[r][sp] = __ldcg(part + ((size_t)(kh * REP + r) * a.nsplit + sp) * (D + 2));
+    __shared__ float s_lw[REP][DEC_MAX_SPLIT];
+    const int ns = a.nsplit;
+    for (int idx = threadIdx.x; idx < REP * ns; idx += DEC_THREADS) {
+        int r = idx / ns, sp = idx % ns;
+        const float *rec = part + ((size_t)(kh * REP + r) * ns + sp) * (D + 2);
+        s_w[r][sp] = __ldcg(rec);
+        s_lw[r][sp] = __ldcg(rec + 1);
     }
     __syncthreads();
-    if (threadIdx.x < REP) {
-        int r = threadIdx.x;
-        float mx = -INFINITY;
-        for (int sp = 0; sp < a.nsplit; sp++) mx = fmaxf(mx, s_w[r][sp]);
-        float L = 0.f;
-        for (int sp = 0; sp < a.nsplit; sp++) {
-            float ms = s_w[r][sp];
-            float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
-            L += w * __ldcg(part + ((size_t)(kh * REP + r) * a.nsplit + sp) * (D + 2) + 1);
-            s_w[r][sp] = w;
-        }
-        float invL = 1.f / L;
-        for (int sp = 0; sp < a.nsplit; sp++) s_w[r][sp] *= invL;
+    for (int r = warp; r < REP; r += NW) {
+        const float m0 = lane < ns ? s_w[r][lane] : -INFINITY;
+        const float m1 = lane + 32 < ns ? s_w[r][lane + 32] : -INFINITY;
+        const float mx = warp_max(fmaxf(m0, m1));
+        const float w0 = m0 == -INFINITY ? 0.f : exp2f(m0 - mx);
+        const float w1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mx);
+        const float L = warp_sum(fmaf(w0, lane < ns ? s_lw[r][lane] : 0.f,
+                                      w1 * (lane + 32 < ns ? s_lw[r][lane + 32] : 0.f)));
+        const float invL = 1.f / L;
+        if (lane < ns) s_w[r][lane] = w0 * invL;
+        if (lane + 32 < ns) s_w[r][lane + 32] = w1 * invL;
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < REP * D; idx += DEC_THREADS) {
         int r = idx / D, d = idx % D;
         int h = kh * REP + r;
-        const float *base = part + (size_t)h * a.nsplit * (D + 2) + 2 + d;
-        float os = 0.f;
-#pragma unroll 8
-        for (int sp = 0; sp < a.nsplit; sp++) os = fmaf(s_w[r][sp], __ldcg(base + (size_t)sp * (D + 2)), os);
-        float val = rbf(os);
+        const float *base = part + (size_t)h * ns * (D + 2) + 2 + d;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int sp0 = 0; sp0 < ns; sp0 += 32) {
+            float v[32];
+#pragma unroll
+            for (int u = 0; u < 32; u++) v[u] = sp0 + u < ns ? __ldcg(base + (size_t)(sp0 + u) * (D + 2)) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 32; u++)
+                if (sp0 + u < ns) acc[u & 3] = fmaf(s_w[r][sp0 + u], v[u], acc[u & 3]);
+        }
+        float val = rbf((acc[0] + acc[1]) + (acc[2] + acc[3]));
         if (a.gate) {
             float gv = bf2f(qkv[(size_t)h * qstride + D + d]);
             val = rbf(__fmul_rn(val, sigmoid_bf16(gv)));
         }
         a.out[(size_t)h * D + d] = f2bf(val);
     }
+    MLXD_TRACE_END(0x31)
     if (threadIdx.x == 0) a.count[kh] = 0;
 }
 

@@ -74,6 +74,114 @@ MLXD_DEV uint2 ldg_nc_v2(const void *p) {
     return r;
 }
 
+// greedy key: order-preserving float bits over the first-index tie rule
+// (a larger key wins; equal values keep the smaller index)
+MLXD_DEV unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
+// x pair (k, k+1) of a decode-GEMV input into the fragment order of its
+// group: xp[(gi*4 + tt)*XW + j*2 + hi], XW = G/8 words per (group, t)
+MLXD_DEV void put_pair(uint32_t *xp, int G, int XW, int k, uint32_t v) {
+    const int gi = k / G, kk = k % G;
+    const int j = kk >> 4, w16 = kk & 15;
+    const int hi = w16 >= 8, tt = (w16 & 7) >> 1;
+    xp[(gi * 4 + tt) * XW + j * 2 + hi] = v;
+}
+
+// ---- bulk copies (cp.async.bulk, no multicast) and mbarriers
+MLXD_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+MLXD_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+MLXD_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// order this thread's generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy) writes to the same bytes
+MLXD_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+MLXD_DEV void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte
+// aligned) completing on `bar`
+MLXD_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+MLXD_DEV unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+MLXD_DEV bool mbar_try(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+    return ok != 0;
+}
+// wait for phase `parity` of `bar`; false after half a second
+MLXD_DEV bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try(addr, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (unsigned i = 1;; i++) {
+        if (mbar_try(addr, parity)) return true;
+        if ((i & 63u) == 0 && global_ns() - t0 > 500000000ull) return false;
+    }
+}
+
+// ---- optional timeline trace (compiled in with -DMLXD_TRACE only): thread 0
+// of every CTA of a traced kernel appends {tag<<32 | cta, start, waited, end}
+// (%globaltimer ns) to a device buffer whose word 0 counts the records.
+#ifdef MLXD_TRACE
+static __device__ unsigned long long *g_trace;
+MLXD_DEV unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define MLXD_TRACE_START unsigned long long tr_t0_ = gtime(), tr_t1_ = 0;
+#define MLXD_TRACE_WAITED tr_t1_ = gtime();
+#define MLXD_TRACE_RESTART tr_t0_ = gtime();
+#define MLXD_TRACE_END(tag)                                                                  \
+    if (g_trace && threadIdx.x == 0) {                                                       \
+        unsigned long long i_ = atomicAdd(g_trace, 1ull);                                    \
+        if (i_ < (1ull << 20)) {                                                             \
+            unsigned long long *r_ = g_trace + 4 + i_ * 4;                                   \
+            r_[0] = ((unsigned long long)(tag) << 32) | (blockIdx.x + blockIdx.y * gridDim.x); \
+            r_[1] = tr_t0_;                                                                  \
+            r_[2] = tr_t1_;                                                                  \
+            r_[3] = gtime();                                                                 \
+        }                                                                                    \
+    }
+#define MLXD_TRACE_REC(cond, tag, v1, v2, v3)                                            \
+    if (g_trace && (cond)) {                                                                 \
+        unsigned long long i_ = atomicAdd(g_trace, 1ull);                                    \
+        if (i_ < (1ull << 20)) {                                                             \
+            unsigned long long *r_ = g_trace + 4 + i_ * 4;                                   \
+            r_[0] = ((unsigned long long)(tag) << 32) | (blockIdx.x + blockIdx.y * gridDim.x); \
+            r_[1] = (v1);                                                                    \
+            r_[2] = (v2);                                                                    \
+            r_[3] = (v3);                                                                    \
+        }                                                                                    \
+    }
+#define MLXD_TRACE_BINDER(name) \
+    void trace_bind_##name(unsigned long long *p) { cudaMemcpyToSymbol(g_trace, &p, sizeof p); }
+#else
+#define MLXD_TRACE_START
+#define MLXD_TRACE_RESTART
+#define MLXD_TRACE_WAITED
+#define MLXD_TRACE_END(tag)
+#define MLXD_TRACE_REC(cond, tag, v1, v2, v3)
+#define MLXD_TRACE_BINDER(name)
+#endif
+
 // Programmatic dependent launch: wait for the producer grid / let the
 // consumer grid be scheduled. No-ops when the launch has no PDL attribute.
 MLXD_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

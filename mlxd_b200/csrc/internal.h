@@ -93,6 +93,8 @@ struct mlxd_model {
     int32_t *p_ids = nullptr;
     float *p_part = nullptr;
     cudaStream_t stream = nullptr;
+    // persistent single-kernel decode step (megastep.cu) when eligible
+    void *mega = nullptr;
     // tensor parallel
     void *nccl = nullptr;       // ncclComm_t when tp_size > 1
     size_t weight_bytes = 0;

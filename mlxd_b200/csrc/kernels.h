@@ -38,9 +38,19 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
 // workspace floats one matrix needs (units -> counters)
 size_t gemv_workspace_floats(int rows, int cols, int group, int epi, int sms, int *units);
 int num_sms();
+// nonzero once a decode GEMV gave up waiting on a bulk copy (read and cleared)
+int gemv_wait_timeouts();
 // decode GEMV (EPI_STORE) with its workspace in a static device array instead
 // of a caller-provided allocation; -1 when the matrix needs more than it holds
 int qgemv_static_scratch(const QMat &W, const uint16_t *x, uint16_t *y, cudaStream_t st);
+
+// ---- persistent decode step (megastep.cu)
+int megastep_setup(mlxd_model *m);          // 0 also when the model is not eligible
+void megastep_free(mlxd_model *m);
+bool megastep_ready(const mlxd_model *m, const mlxd_kv *kv);
+int megastep_launch(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, uint16_t *logits, bool argmax,
+                    cudaStream_t st);
+int megastep_timeouts(mlxd_model *m);
 
 // ---- prefill GEMM / dense (qgemm.cu)
 // y[S][rows] = x[S][cols] . W^T with epilogue (STORE/RESIDUAL/SWIGLU)

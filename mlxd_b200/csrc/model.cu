@@ -349,6 +349,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
     const mlxd_model_config &c = m->c;
     int H = c.hidden, D = c.head_dim;
     bool tp = c.tp_size > 1;
+    if (want_logits && megastep_ready(m, kv)) return megastep_launch(m, kv, ids_dev, logits_out, argmax, st);
     if (embed_rows(m->embed, H, c.qgroup, c.vocab, ids_dev, 1, m->h, st)) return -1;
     size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
     for (int l = 0; l < c.layers; l++) {
@@ -739,6 +740,7 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         !cuda_ok(cudaMemset(m->amax, 0, 8), "memset"))
         return fail();
     if (!cuda_ok(cudaDeviceSynchronize(), "model upload")) return fail();
+    if (megastep_setup(m)) return fail();
     for (auto &L : m->L)
         m->weight_bytes += L.qkv.tile_bytes() + L.qkv.sb_bytes() + L.o.tile_bytes() + L.o.sb_bytes() +
                            L.gateup.tile_bytes() + L.gateup.sb_bytes() + L.down.tile_bytes() + L.down.sb_bytes();
@@ -747,10 +749,13 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
     return 0;
 }
 
+int mlxd_cuda_model_decode_path(const mlxd_model *m) { return m && m->mega ? 1 : 0; }
+
 void mlxd_cuda_model_destroy(mlxd_model *m) {
     if (!m) return;
     cudaDeviceSynchronize();
     if (m->graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
+    megastep_free(m);
     for (auto &L : m->L) {
         free_qmat(L.qkv);
         free_qmat(L.o);
@@ -1172,6 +1177,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     }
     cudaEventRecord(e2, st);
     if (!cuda_ok(cudaStreamSynchronize(st), "generate")) rc = -1;
+    if (!rc && (gemv_wait_timeouts() || megastep_timeouts(m))) {
+        set_error("decode step gave up waiting (weight copy or grid barrier)");
+        rc = -1;
+    }
     if (timing) {
         float pre = 0.f, dec = 0.f;
         cudaEventElapsedTime(&pre, e0, e1);
@@ -1199,3 +1208,19 @@ done:
 }
 
 }  // extern "C"
+
+#ifdef MLXD_TRACE
+namespace mlxd {
+void trace_bind_qgemv(unsigned long long *p);
+void trace_bind_attention(unsigned long long *p);
+void trace_bind_megastep(unsigned long long *p);
+}
+// timeline trace of the decode kernels (trace builds only): buf is a device
+// buffer of 4 + 4 * 2^20 u64, word 0 zeroed by the caller
+extern "C" int mlxd_cuda_trace_bind(void *buf) {
+    mlxd::trace_bind_qgemv((unsigned long long *)buf);
+    mlxd::trace_bind_attention((unsigned long long *)buf);
+    mlxd::trace_bind_megastep((unsigned long long *)buf);
+    return 0;
+}
+#endif

@@ -17,6 +17,7 @@
 //     y += s * d + (b - 128 s) * sum(x over the group)
 // which is mlx's qmv factorisation (scale * sum(x*q) + bias * sum(x)).
 #include <mutex>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -177,11 +178,6 @@ MLXD_DEV typename std::conditional<F32, uint4, uint2>::type load_sb(const uint8_
     else return ldg_nc_v2(p);
 }
 
-MLXD_DEV unsigned long long argmax_key(float v, int idx) {
-    uint32_t u = __float_as_uint(v);
-    uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
-}
 
 constexpr int GEMV_THREADS = 512;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
@@ -305,6 +301,98 @@ __device__ __noinline__ void gemv_flush(const GemvArgs &a, const FlushCtx &f, in
     }
 }
 
+// Stage x (bf16 [cols]) for the decode GEMV into shared memory: optional
+// RMSNorm with the oracle's association (Ta element-strided partials,
+// butterfly within each warp, warp totals in order), then the fragment order
+// xp[(gi*4 + tt)*XW + j*2 + hi] and the per-group sums xs[gi]. Global reads
+// are 16-byte loads issued MAXV at a time per thread, so the prologue costs a
+// few memory latencies instead of one per element. xraw: cols bf16 of scratch
+// (used when NORM).
+// byte offset of the raw-x scratch after xp (ng*4*XW words) and xs (ng floats)
+static __host__ __device__ inline size_t xraw_offset(int ng, int XW) {
+    return (((size_t)ng * 4 * XW * 4 + (size_t)ng * 4 + 15) / 16) * 16;
+}
+template <int G, int NT, bool NORM>
+MLXD_DEV void stage_x(const GemvArgs &a, uint32_t *xp, float *xs, uint16_t *xraw, float *s_red) {
+    constexpr int XW = G / 8, MAXV = 4;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nv = a.cols / 8, ng = a.cols / G;
+    const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm_w);
+    for (int base = 0; base < nv; base += NT * MAXV) {
+        uint4 v[MAXV];
+#pragma unroll
+        for (int j = 0; j < MAXV; j++) {
+            const int i = base + tid + j * NT;
+            if (i < nv) v[j] = x4[i];
+        }
+#pragma unroll
+        for (int j = 0; j < MAXV; j++) {
+            const int i = base + tid + j * NT;
+            if (i >= nv) continue;
+            if (NORM) {
+                reinterpret_cast<uint4 *>(xraw)[i] = v[j];
+            } else {
+                put_pair(xp, G, XW, i * 8 + 0, v[j].x);
+                put_pair(xp, G, XW, i * 8 + 2, v[j].y);
+                put_pair(xp, G, XW, i * 8 + 4, v[j].z);
+                put_pair(xp, G, XW, i * 8 + 6, v[j].w);
+            }
+        }
+    }
+    if (NORM) {
+        __syncthreads();
+        const int n = a.cols;
+        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
+        float acc = 0.f;
+        if (tid < Ta)
+            for (int i = tid; i < n; i += Ta) {
+                const float f = bf2f(xraw[i]);
+                acc = fmaf(f, f, acc);
+            }
+        acc = warp_sum(acc);
+        if (lane == 0) s_red[warp] = acc;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < NT / 32; w++) tot += s_red[w];
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
+        for (int base = 0; base < nv; base += NT * MAXV) {
+            uint4 wv[MAXV];
+#pragma unroll
+            for (int j = 0; j < MAXV; j++) {
+                const int i = base + tid + j * NT;
+                if (i < nv) wv[j] = w4[i];
+            }
+#pragma unroll
+            for (int j = 0; j < MAXV; j++) {
+                const int i = base + tid + j * NT;
+                if (i >= nv) continue;
+                const uint4 xv = reinterpret_cast<const uint4 *>(xraw)[i];
+                const uint32_t xs4[4] = {xv.x, xv.y, xv.z, xv.w};
+                const uint32_t ws4[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float lo = rbf(__fmul_rn(lo_bf(ws4[q]), rbf(__fmul_rn(lo_bf(xs4[q]), inv))));
+                    const float hi = rbf(__fmul_rn(hi_bf(ws4[q]), rbf(__fmul_rn(hi_bf(xs4[q]), inv))));
+                    put_pair(xp, G, XW, i * 8 + 2 * q, pack_bf2(lo, hi));
+                }
+            }
+        }
+    }
+    __syncthreads();
+    for (int gi = warp; gi < ng; gi += NT / 32) {
+        float sm = 0.f;
+        if (lane < 4 * XW) {
+            const uint32_t v = xp[gi * 4 * XW + lane];
+            sm = lo_bf(v) + hi_bf(v);
+        }
+        sm = warp_sum(sm);
+        if (lane == 0) xs[gi] = sm;
+    }
+    __syncthreads();
+}
+
 template <int G, bool SBF32, int PRO, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(GemvArgs a) {
     constexpr int XW = G / 8;            // x words per (group, t)
@@ -317,6 +405,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(GemvArgs a) {
     const int ng = a.cols / G;
     uint32_t *xp = reinterpret_cast<uint32_t *>(smem_raw);
     float *xs = reinterpret_cast<float *>(xp + (size_t)ng * 4 * XW);
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw + xraw_offset(ng, XW));
     __shared__ float s_red[GEMV_WARPS];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
@@ -344,54 +433,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(GemvArgs a) {
 
     // ---- prologue: x (optionally RMS-normalised) into the fragment order
     pdl_wait();
-    const uint32_t *x2 = reinterpret_cast<const uint32_t *>(a.x);
-    const int npairs = a.cols / 2;
-    float inv = 1.0f;
-    if (PRO == PRO_RMSNORM) {
-        // the oracle's association: Ta element-strided partials, butterfly
-        // within each warp, warp totals in order
-        const int n = a.cols;
-        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
-        float acc = 0.f;
-        if (tid < Ta)
-            for (int i = tid; i < n; i += Ta) {
-                float v = bf2f(a.x[i]);
-                acc = fmaf(v, v, acc);
-            }
-        acc = warp_sum(acc);
-        if (lane == 0) s_red[warp] = acc;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < GEMV_WARPS; w++) tot += s_red[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
-    }
-    const uint32_t *nw2 = reinterpret_cast<const uint32_t *>(a.norm_w);
-    for (int p = tid; p < npairs; p += GEMV_THREADS) {
-        uint32_t v = x2[p];
-        if (PRO == PRO_RMSNORM) {
-            uint32_t wv = nw2[p];
-            float lo = rbf(__fmul_rn(lo_bf(wv), rbf(__fmul_rn(lo_bf(v), inv))));
-            float hi = rbf(__fmul_rn(hi_bf(wv), rbf(__fmul_rn(hi_bf(v), inv))));
-            v = pack_bf2(lo, hi);
-        }
-        int k = 2 * p;
-        int gi = k / G, kk = k % G;
-        int j = kk >> 4, w16 = kk & 15;
-        int hi = w16 >= 8, tt = (w16 & 7) >> 1;
-        xp[(gi * 4 + tt) * XW + j * 2 + hi] = v;
-    }
-    __syncthreads();
-    for (int gi = warp; gi < ng; gi += GEMV_WARPS) {
-        float s = 0.f;
-        if (lane < 4 * XW) {
-            uint32_t v = xp[gi * 4 * XW + lane];
-            s = lo_bf(v) + hi_bf(v);
-        }
-        s = warp_sum(s);
-        if (lane == 0) xs[gi] = s;
-    }
-    __syncthreads();
+    stage_x<G, GEMV_THREADS, PRO == PRO_RMSNORM>(a, xp, xs, xraw, s_red);
     pdl_trigger();
     if (n_items <= 0) return;
 
@@ -477,11 +519,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(GemvArgs a) {
 // block (sb8 layout).
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
+    MLXD_TRACE_START
     constexpr int G = 64, XW = 8;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int ng = a.cols / G, nbk = ng / 8;
     uint32_t *xp = reinterpret_cast<uint32_t *>(smem_raw);
     float *xs = reinterpret_cast<float *>(xp + (size_t)ng * 4 * XW);
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw + xraw_offset(ng, XW));
     __shared__ __align__(16) uint32_t s_zero[8];
     __shared__ float s_red[GEMV_WARPS];
 
@@ -508,52 +552,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
     // ---- prologue: x (optionally RMS-normalised) into the fragment order
     pdl_wait();
     if (tid < 8) s_zero[tid] = 0u;
-    const uint32_t *x2 = reinterpret_cast<const uint32_t *>(a.x);
-    const int npairs = a.cols / 2;
-    float inv = 1.0f;
-    if (PRO == PRO_RMSNORM) {
-        const int n = a.cols;
-        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
-        float acc = 0.f;
-        if (tid < Ta)
-            for (int i = tid; i < n; i += Ta) {
-                float v = bf2f(a.x[i]);
-                acc = fmaf(v, v, acc);
-            }
-        acc = warp_sum(acc);
-        if (lane == 0) s_red[warp] = acc;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < GEMV_WARPS; w++) tot += s_red[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
-    }
-    const uint32_t *nw2 = reinterpret_cast<const uint32_t *>(a.norm_w);
-    for (int p = tid; p < npairs; p += GEMV_THREADS) {
-        uint32_t v = x2[p];
-        if (PRO == PRO_RMSNORM) {
-            uint32_t wv = nw2[p];
-            float lo = rbf(__fmul_rn(lo_bf(wv), rbf(__fmul_rn(lo_bf(v), inv))));
-            float hi = rbf(__fmul_rn(hi_bf(wv), rbf(__fmul_rn(hi_bf(v), inv))));
-            v = pack_bf2(lo, hi);
-        }
-        int k = 2 * p;
-        int gi = k / G, kk = k % G;
-        int j = kk >> 4, w16 = kk & 15;
-        int hi = w16 >= 8, tt = (w16 & 7) >> 1;
-        xp[(gi * 4 + tt) * XW + j * 2 + hi] = v;
-    }
-    __syncthreads();
-    for (int gi = warp; gi < ng; gi += GEMV_WARPS) {
-        float sm = 0.f;
-        if (lane < 4 * XW) {
-            uint32_t v = xp[gi * 4 * XW + lane];
-            sm = lo_bf(v) + hi_bf(v);
-        }
-        sm = warp_sum(sm);
-        if (lane == 0) xs[gi] = sm;
-    }
-    __syncthreads();
+    MLXD_TRACE_WAITED
+    stage_x<G, GEMV_THREADS, PRO == PRO_RMSNORM>(a, xp, xs, xraw, s_red);
+    MLXD_TRACE_END(0x10 + EPI)
     pdl_trigger();
     if (n_items <= 0) return;
 
@@ -566,7 +567,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
         const bool pre = i + 1 < n_items;
         const uint8_t *pwn = pw + (size_t)(i + 1) * 4096;
         const uint32_t *xb = xp + ((size_t)bk * 32 + t) * XW;   // group 8bk at +0, +p*32
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        // four independent accumulators (one per 16-column chunk of a tile)
+        float dj[4][4] = {};
 #pragma unroll
         for (int p = 0; p < 8; p++) {
             const uint4 wv = wbuf[p];
@@ -578,9 +580,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
             for (int j = 0; j < 4; j++) {
                 uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
                                   nib_pair(wv.w, j)};
-                mma_bf16_16816(d, af, xv[2 * j], xv[2 * j + 1]);
+                mma_bf16_16816(dj[j], af, xv[2 * j], xv[2 * j + 1]);
             }
         }
+        float d[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) d[c] = (dj[0][c] + dj[1][c]) + (dj[2][c] + dj[3][c]);
         const uint4 sv = sbuf;
         if (pre) sbuf = ldg_nc_v4(ps + (size_t)(i + 1) * 512);
         const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
@@ -611,6 +616,202 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
             bk++;
         }
     }
+}
+
+// Decode fast path with bulk-copy prefetch (group 64, bf16 scales, cols/64 a
+// multiple of 8). One CTA of 8 warps per SM, two CTAs of consecutive launches
+// can share an SM. Each CTA owns a contiguous range of whole row blocks
+// (whole gate|up pairs for SwiGLU), so its packed weights and scale records
+// are two contiguous byte ranges. Warp w takes items w, w+8, w+16, ... of the
+// range (an item is one block of 8 groups of one row block: 4 KB of tiles +
+// 512 B of scale/bias records) and streams them through its own ring of
+// BW_NS shared-memory slots with cp.async.bulk, one mbarrier per slot. The
+// first BW_NS items of every warp are requested before griddepcontrol.wait:
+// weights do not depend on the previous kernel, so they stream while it
+// finishes. Per-warp partial sums of each row block go to shared memory and
+// are added in warp order at the end (no global workspace, deterministic).
+constexpr int BW_THREADS = 256, BW_WARPS = 8, BW_NS = 2;
+constexpr int BW_TILE_BYTES = 4096, BW_SB_BYTES = 512, BW_SLOT = BW_TILE_BYTES + BW_SB_BYTES;
+
+static __device__ int g_gemv_wait_timeout;
+MLXD_TRACE_BINDER(qgemv)
+
+struct BulkSmem {
+    size_t ring, bars, xp, xs, red, xraw, total;
+};
+static __host__ __device__ inline BulkSmem bulk_smem_layout(int cols, int nrb_max, bool norm) {
+    BulkSmem L;
+    const int ng = cols / 64;
+    L.ring = 0;
+    L.bars = L.ring + (size_t)BW_WARPS * BW_NS * BW_SLOT;
+    L.xp = L.bars + (size_t)BW_WARPS * BW_NS * 8;
+    L.xs = L.xp + (size_t)ng * 4 * 8 * 4;
+    L.red = L.xs + (((size_t)ng * 4 + 15) / 16) * 16;
+    L.xraw = L.red + (size_t)nrb_max * BW_WARPS * 16 * 4;
+    L.total = L.xraw + (norm ? (size_t)cols * 2 : 0);
+    return L;
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(BW_THREADS, 2) qgemv_bulk_kernel(GemvArgs a, int nrb_max) {
+    MLXD_TRACE_START
+    constexpr int G = 64, XW = 8;
+    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(16) uint32_t s_zero[8];
+    __shared__ float s_red[BW_WARPS];
+    __shared__ unsigned long long s_key[BW_WARPS];
+
+    const int ng = a.cols / G, nbk = ng / 8;
+    const BulkSmem L = bulk_smem_layout(a.cols, nrb_max, PRO == PRO_RMSNORM);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
+    const int n_units = a.rows / 16 / UNIT_RB;
+    const int u0 = (int)((long long)n_units * blockIdx.x / gridDim.x);
+    const int u1 = (int)((long long)n_units * (blockIdx.x + 1) / gridDim.x);
+    const int rb0 = u0 * UNIT_RB, nrb = (u1 - u0) * UNIT_RB;
+    const long long i0 = (long long)rb0 * nbk;
+    const int n_items = nrb * nbk;
+    const int my_n = n_items > warp ? (n_items - warp + BW_WARPS - 1) / BW_WARPS : 0;
+
+    unsigned char *ring = smem + L.ring + (size_t)warp * BW_NS * BW_SLOT;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * BW_NS;
+    uint32_t *xp = reinterpret_cast<uint32_t *>(smem + L.xp);
+    float *xs = reinterpret_cast<float *>(smem + L.xs);
+    float *red = reinterpret_cast<float *>(smem + L.red);
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem + L.xraw);
+
+    auto issue = [&](int k) {
+        const long long item = i0 + warp + (long long)k * BW_WARPS;
+        const int slot = k % BW_NS;
+        mbar_expect_tx(&bars[slot], BW_SLOT);
+        bulk_g2s(ring + slot * BW_SLOT, a.tiles + item * BW_TILE_BYTES, BW_TILE_BYTES, &bars[slot]);
+        bulk_g2s(ring + slot * BW_SLOT + BW_TILE_BYTES, a.sb8 + item * BW_SB_BYTES, BW_SB_BYTES,
+                 &bars[slot]);
+    };
+    if (lane == 0) {
+        for (int sl = 0; sl < BW_NS; sl++) mbar_init(&bars[sl], 1);
+        fence_mbar_init();
+        for (int k = 0; k < BW_NS && k < my_n; k++) issue(k);
+    }
+    for (int i = tid; i < nrb * BW_WARPS * 16; i += BW_THREADS) red[i] = 0.f;
+    if (tid < 8) s_zero[tid] = 0u;
+    pdl_trigger();
+
+    // ---- prologue: x (optionally RMS-normalised) into the fragment order
+    pdl_wait();
+    MLXD_TRACE_WAITED
+    stage_x<G, BW_THREADS, PRO == PRO_RMSNORM>(a, xp, xs, xraw, s_red);
+
+    // ---- main loop over this warp's items
+    bool timed_out = false;
+    int cur = -1;
+    float y0 = 0.f, y1 = 0.f;
+    auto flush = [&](int rbl) {
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        if (t == 0) {
+            red[(rbl * BW_WARPS + warp) * 16 + gq] = y0;
+            red[(rbl * BW_WARPS + warp) * 16 + gq + 8] = y1;
+        }
+    };
+    for (int k = 0; k < my_n; k++) {
+        const int slot = k % BW_NS;
+        if (!mbar_wait(&bars[slot], (uint32_t)(k / BW_NS) & 1u)) timed_out = true;
+        const int li = warp + k * BW_WARPS;
+        const int rbl = li / nbk, bk = li - rbl * nbk;
+        if (rbl != cur) {
+            if (cur >= 0) flush(cur);
+            cur = rbl;
+            y0 = 0.f;
+            y1 = 0.f;
+        }
+        const uint4 *wt = reinterpret_cast<const uint4 *>(ring + slot * BW_SLOT) + lane;
+        const uint4 sv = *(reinterpret_cast<const uint4 *>(ring + slot * BW_SLOT + BW_TILE_BYTES) + lane);
+        const uint32_t *xb = xp + ((size_t)bk * 32 + t) * XW;
+        // four independent accumulators (one per 16-column chunk of a tile)
+        float dj[4][4] = {};
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            const uint4 wv = wt[p * 32];
+            const uint4 *xq = reinterpret_cast<const uint4 *>(gq == p ? xb + p * 32 : s_zero);
+            const uint4 xa = xq[0], xc = xq[1];
+            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
+                                  nib_pair(wv.w, j)};
+                mma_bf16_16816(dj[j], af, xv[2 * j], xv[2 * j + 1]);
+            }
+        }
+        float d[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) d[c] = (dj[0][c] + dj[1][c]) + (dj[2][c] + dj[3][c]);
+        const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
+        const float s00 = lo_bf(sv.x), b00 = hi_bf(sv.x), s01 = lo_bf(sv.y), b01 = hi_bf(sv.y);
+        const float s10 = lo_bf(sv.z), b10 = hi_bf(sv.z), s11 = lo_bf(sv.w), b11 = hi_bf(sv.w);
+        y0 = fmaf(s00, d[0], y0);
+        y0 = fmaf(fmaf(-128.f, s00, b00), xsv.x, y0);
+        y0 = fmaf(s01, d[1], y0);
+        y0 = fmaf(fmaf(-128.f, s01, b01), xsv.y, y0);
+        y1 = fmaf(s10, d[2], y1);
+        y1 = fmaf(fmaf(-128.f, s10, b10), xsv.x, y1);
+        y1 = fmaf(s11, d[3], y1);
+        y1 = fmaf(fmaf(-128.f, s11, b11), xsv.y, y1);
+        // every lane's reads of the slot are done: refill it
+        __syncwarp();
+        if (lane == 0 && k + BW_NS < my_n) {
+            fence_proxy_async();
+            issue(k + BW_NS);
+        }
+    }
+    if (cur >= 0) flush(cur);
+    if (timed_out && lane == 0) atomicExch(&g_gemv_wait_timeout, 1);
+    __syncthreads();
+
+    // ---- epilogue: add the warps' partials in warp order
+    const int nu = nrb / UNIT_RB;
+    unsigned long long best = 0ull;
+    for (int idx = tid; idx < nu * 16; idx += BW_THREADS) {
+        const int ul = idx >> 4, q = idx & 15;
+        float acc[UNIT_RB];
+#pragma unroll
+        for (int u = 0; u < UNIT_RB; u++) {
+            const float *r = red + ((ul * UNIT_RB + u) * BW_WARPS) * 16 + q;
+            float sum = 0.f;
+#pragma unroll
+            for (int w = 0; w < BW_WARPS; w++) sum += r[w * 16];
+            acc[u] = sum;
+        }
+        if constexpr (EPI == EPI_SWIGLU) {
+            a.y[(size_t)(u0 + ul) * 16 + q] = f2bf(swiglu_bf16(rbf(acc[0]), rbf(acc[1])));
+        } else {
+            const int row = (rb0 + ul) * 16 + q;
+            if constexpr (EPI == EPI_ARGMAX) {
+                a.y[row] = f2bf(acc[0]);
+                unsigned long long key = argmax_key(rbf(acc[0]), a.row_offset + row);
+                best = key > best ? key : best;
+            } else {
+                epilogue_row<EPI>(a, row, acc[0]);
+            }
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0) s_key[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < BW_WARPS; w++) m = s_key[w] > m ? s_key[w] : m;
+            if (m) atomicMax(a.amax, m);
+        }
+    }
+    MLXD_TRACE_END(0x20 + EPI)
 }
 
 // grid and workspace slots of one launch
@@ -661,7 +862,7 @@ template <int G, bool SBF32, int PRO, int EPI>
 static int launch_gemv(GemvArgs a, cudaStream_t st, bool pdl) {
     auto kern = qgemv_kernel<G, SBF32, PRO, EPI>;
     int ng = a.cols / G;
-    size_t smem = (size_t)ng * 4 * (G / 8) * 4 + (size_t)ng * 4;
+    size_t smem = xraw_offset(ng, G / 8) + (size_t)a.cols * 2;
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
         MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -688,7 +889,7 @@ template <int PRO, int EPI>
 static int launch_gemv8(GemvArgs a, cudaStream_t st, bool pdl) {
     auto kern = qgemv8_kernel<PRO, EPI>;
     int ng = a.cols / 64;
-    size_t smem = (size_t)ng * 4 * 8 * 4 + (size_t)ng * 4;
+    size_t smem = xraw_offset(ng, 8) + (size_t)a.cols * 2;
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
         MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -709,6 +910,63 @@ static int launch_gemv8(GemvArgs a, cudaStream_t st, bool pdl) {
     cfg.numAttrs = pdl ? 1 : 0;
     MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
     return 0;
+}
+
+template <int PRO, int EPI>
+static int launch_gemv_bulk(GemvArgs a, cudaStream_t st, bool pdl) {
+    auto kern = qgemv_bulk_kernel<PRO, EPI>;
+    const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
+    const int n_units = a.rows / 16 / unit_rb;
+    int grid = num_sms();
+    if (grid > n_units) grid = n_units;
+    const int nrb_max = (n_units + grid - 1) / grid * unit_rb;
+    const size_t smem = bulk_smem_layout(a.cols, nrb_max, PRO == PRO_RMSNORM).total;
+    if (smem > 200 * 1024) {
+        set_error("qgemv: %d x %d needs %zu bytes of shared memory", a.rows, a.cols, smem);
+        return -1;
+    }
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(BW_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a, nrb_max));
+    return 0;
+}
+
+static int dispatch_gemv_bulk(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
+#define MLXD_GEMVB_CASE(P, E) \
+    if (pro == P && epi == E) return launch_gemv_bulk<P, E>(a, st, pdl);
+    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_STORE)
+    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_RESIDUAL)
+    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_SWIGLU)
+    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_ARGMAX)
+    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_PARTIAL_F32)
+    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_STORE)
+    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_RESIDUAL)
+    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_SWIGLU)
+    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_ARGMAX)
+    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_PARTIAL_F32)
+#undef MLXD_GEMVB_CASE
+    set_error("qgemv: bad prologue/epilogue");
+    return -1;
+}
+
+int gemv_wait_timeouts() {
+    int v = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemv_wait_timeout, sizeof v) != cudaSuccess) return -1;
+    if (v) cudaMemcpyToSymbol(g_gemv_wait_timeout, &z, sizeof z);
+    return v;
 }
 
 static int dispatch_gemv8(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
@@ -748,6 +1006,14 @@ static int dispatch_gemv(int pro, int epi, const GemvArgs &a, cudaStream_t st, b
     return -1;
 }
 
+// decode kernel for the group-64 fast layout: 0 = register-prefetch
+// stream-K (default, the faster one inside the decode graph), 1 = bulk-copy
+// prefetch into shared memory; MLXD_GEMV_KIND overrides
+static int g_gemv_kind = [] {
+    const char *e = getenv("MLXD_GEMV_KIND");
+    return e ? atoi(e) : 0;
+}();
+
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl) {
     if (!W.quant) {
         set_error("qgemv: matrix is not quantized");
@@ -761,12 +1027,17 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
         set_error("qgemv: no workspace");
         return -1;
     }
+    if (((uintptr_t)a.x | (uintptr_t)a.norm_w) & 15) {
+        set_error("qgemv: x and the norm weights must be 16-byte aligned");
+        return -1;
+    }
     if (W.rows % (epi == EPI_SWIGLU ? 32 : 16)) {
         set_error("qgemv: rows %d not a multiple of the row block", W.rows);
         return -1;
     }
     if (W.sb8 && W.fast8()) {
         a.sb8 = W.sb8;
+        if (g_gemv_kind == 1) return dispatch_gemv_bulk(pro, epi, a, st, pdl);
         return dispatch_gemv8(pro, epi, a, st, pdl);
     }
     bool f32 = W.sdtype == MLXD_F32;

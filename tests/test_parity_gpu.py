@@ -237,6 +237,30 @@ def test_fast_decode_path_logits_and_kv():
         assert d.max() < 5e-2 and d.mean() <= ulp.mean(), (d.mean(), ulp.mean())
 
 
+def test_persistent_step_matches_layer_kernels(monkeypatch):
+    """The single-kernel decode step and the per-op kernels compute the same
+    step in different summation orders: logits and KV rows within the
+    whole-forward bounds of each other."""
+    cfg = qwen3_small(layers=2)
+    host = cuda.synth_host_tensors(cfg, seed=2)
+    monkeypatch.setenv("MLXD_MEGASTEP", "1")
+    mp = cuda.Model(cfg, host)
+    monkeypatch.setenv("MLXD_MEGASTEP", "0")
+    ml = cuda.Model(cfg, host)
+    assert mp.decode_path() == 1 and ml.decode_path() == 0
+    rng = np.random.default_rng(9)
+    ids = rng.integers(0, cfg.vocab, 30).tolist()
+    kp, kl = mp.new_kv(64), ml.new_kv(64)
+    mp.forward(kp, ids[:20], want_logits=False)
+    ml.forward(kl, ids[:20], want_logits=False)
+    for t in ids[20:]:
+        ok, mx, mr = logits_close(bf16_to_f32(mp.forward(kp, [t])), bf16_to_f32(ml.forward(kl, [t])))
+        assert ok, (mx, mr)
+    for layer in range(cfg.layers):
+        d = np.abs(bf16_to_f32(kp.read(layer)) - bf16_to_f32(kl.read(layer)))
+        assert d.max() < 5e-2
+
+
 def synth_pair_std(cfg, seed, std):
     host = cuda.synth_host_tensors(cfg, seed=seed, std=std)
     return cuda.Model(cfg, host), po.Oracle(orc_config(cfg), host)
