@@ -313,7 +313,10 @@ def main():
         line["roofline"] = {"kernel": "qgemv (decode 4-bit GEMV), gate_up shape %dx%d" % (
             dom["rows"], dom["cols"]), "bound": "hbm", "achieved": dom["gbs"], "peak": peak,
             "unit": "GB/s", "frac": round(dom["gbs"] / peak, 4),
-            "traffic": tr, "peak_source": peak_src, "shapes": g}
+            "traffic": round(tr["bytes_per_launch"]) if tr else None,
+            "traffic_note": ("DRAM bytes read+written per launch, one ncu capture of this shape (%s); "
+                             "algorithmic bytes %d" % (tr["source"], dom["bytes"])) if tr else None,
+            "peak_source": peak_src, "shapes": g}
     if args.cpu_baseline and rank == 0 and world == 1:
         try:
             host = host_weights_from_gpu(cuda, cuda.synth_config(**kw, max_pos=P + total + 8))
