@@ -211,18 +211,19 @@ MLXD_DEV void ldmatrix_x4_trans(uint32_t (&r)[4], const void *smem) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
 }
-MLXD_DEV void cp_async16(void *smem, const void *gmem) {
-    uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(a), "l"(gmem));
-}
 MLXD_DEV void cp_async16_zfill(void *smem, const void *gmem, bool valid) {
     uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
     int src = valid ? 16 : 0;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(a), "l"(gmem), "r"(src));
 }
-MLXD_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+MLXD_DEV void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+MLXD_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
-MLXD_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N)); }
+MLXD_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
 // 4-bit nibble pair -> bf16x2 of (128 + q_lo, 128 + q_hi): nibbles i and i+4
 // of the word land in the low mantissa bits of 128.0 (0x4300), exact.

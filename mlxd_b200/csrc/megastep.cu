@@ -1,8 +1,8 @@
 // One greedy/logits decode step as a single persistent kernel.
 //
 // model_forward for one token (src/engine/emodel.c:221-337 with the layer of
-// forward.c:1288-1380) runs as one cooperative launch of one CTA per SM. The
-// step is a fixed sequence of phases: embed, then per layer
+// forward.c:1288-1380) runs as one cooperative launch of one CTA (16 warps)
+// per SM. The step is a fixed sequence of phases: embed, then per layer
 //   qkv  = W_qkv . rmsnorm(h)                        (fwd_attention :497-549)
 //   attn = SDPA(norm+rope(q), cache + norm+rope(k))  (:591-731)
 //   h1   = h + W_o . attn
@@ -12,20 +12,25 @@
 //
 // Every CTA owns a static share of every phase: whole row blocks (gate|up
 // pairs for SwiGLU) of each projection, one (kv head, split) of the
-// attention. One producer warp streams the CTA's packed weights and cached
-// K/V rows, phase after phase, into a ring of MS_NS shared-memory chunks
-// with cp.async.bulk (one mbarrier per chunk, no multicast); it waits only for
-// free slots, never for activations, so the HBM stream runs on across phase
-// boundaries while the consumer warps wait for the grid. Eight consumer warps
-// wait for the previous phase (a grid-wide arrival counter), stage the phase
-// input in shared memory, and consume the ring. Row-block partial sums are
-// added in warp order by the warp that completes the block (deterministic).
-// Attention partials of the splits of a kv head are merged by all CTAs of
-// that head after a per-head arrival counter.
+// attention. Warp w of a CTA takes items w, w+16, ... of its share (an item
+// is one block of 8 groups of one row block: 4 KB of packed weights + 512 B of
+// scale/bias records). A warp's items of all projection phases, in order, form
+// its weight stream, which it keeps two items ahead with cp.async into two
+// private shared-memory buffers: the copy of the item after next is issued as
+// soon as an item is consumed, across phase boundaries (and over the
+// attention phase, which reads the cache with its own register prefetch).
+// Weights and cached rows do not depend on the activations, so they stream
+// while the grid waits at the phase boundary. Phases are separated by a grid-wide arrival counter;
+// each CTA then stages the phase input (with RMSNorm) in shared memory.
+// Partial sums of each item are kept per item and added in item order by the
+// warp that completes a row block (deterministic). Attention partials of the
+// splits of a kv head are merged by all CTAs of that head after a per-head
+// arrival counter.
 //
-// All waits are bounded; on a timeout the kernel records an error flag,
-// keeps going to the end and the host reports the step as failed.
+// All waits are bounded; on a timeout the kernel records an error flag and
+// stops waiting, so the launch ends and the host reports the step as failed.
 #include <stdlib.h>
+#include <string.h>
 #include <algorithm>
 #include <vector>
 
@@ -36,14 +41,13 @@ namespace mlxd {
 
 MLXD_TRACE_BINDER(megastep)
 
-constexpr int MS_CONSUMERS = 16;
-constexpr int MS_CT = MS_CONSUMERS * 32;            // consumer threads
-constexpr int MS_THREADS = MS_CT + 32;              // + producer warp
-constexpr int MS_SLOT = 4608;                       // one item: 8 tiles + 512 B of scale/bias records
-constexpr int MS_IPC = 4;                           // items per ring chunk (one copy per chunk)
-constexpr int MS_CHUNK = MS_IPC * MS_SLOT;          // [4 x 4096 tiles | 4 x 512 records]
-constexpr int MS_NS = 7;                            // ring chunks
-constexpr int MS_POOL_ITEMS = 256;                  // item partial records (16 floats each)
+constexpr int MS_WARPS = 16;
+constexpr int MS_CT = MS_WARPS * 32;
+constexpr int MS_ITEM = 4608;                       // 8 tiles + 512 B of scale/bias records
+constexpr int MS_KB = 4;                            // cached positions per warp batch
+#ifndef MS_AHEAD
+#define MS_AHEAD 2                                  // stream items in flight per warp (1 or 2)
+#endif
 constexpr unsigned long long MS_WAIT_NS = 500000000ull;   // give up on a wait after 0.5 s
 
 struct MsMat {
@@ -55,7 +59,6 @@ struct MsLayer {
     const uint16_t *ln1, *ln2, *qn, *kn;
 };
 struct MsArgs {
-    const MsLayer *layers;
     int L;
     MsMat lm;
     const uint16_t *fnorm;
@@ -66,14 +69,7 @@ struct MsArgs {
     float eps;
     const float *rope_cs;
     int rope_dims;
-    uint16_t *kc, *vc;
-    size_t layer_elems;
-    int cap, window;
-    int32_t *d_pos;
-    const int32_t *ids;
-    unsigned long long *amax;   // null: no greedy key
     int32_t *token;
-    uint16_t *logits;           // null: logits not kept
     uint16_t *h, *h1, *qkv, *att, *act;
     float *part;                // [hq][nspl][D + 4]
     int *sync;                  // [0] grid arrivals, [1 + kh] attention arrivals
@@ -81,65 +77,84 @@ struct MsArgs {
     int *err;
 };
 
+// What changes from call to call (the cache, the position counter, the input
+// and output slots) is a kernel parameter passed on by value.
+struct MsCall {
+    uint16_t *kc, *vc;
+    size_t layer_elems;
+    int cap, window;
+    int32_t *d_pos;
+    const int32_t *ids;
+    unsigned long long *amax;   // null: no greedy key
+    uint16_t *logits;           // null: logits not kept
+};
+
+// The model's arguments and layer table live in constant memory (copied from
+// the model's fixed pinned block before each launch), so every warp reads
+// them through the constant cache and nothing goes to the phase functions by
+// address.
+constexpr int MS_MAX_LAYERS = 128;
+struct MsConst {
+    MsArgs a;
+    MsLayer layers[MS_MAX_LAYERS];
+};
+static __constant__ MsConst c_ms;
+#define MA (c_ms.a)
+
 struct MsSmem {
-    size_t ring, full, empty, cnt, red, scratch, actx, total;
+    size_t wbuf, scratch, pool, cnt, actx, total;
 };
 // scratch is shared by the phase input (xp, xs, raw x) and the attention
-// working set (q, new k/v, per-warp partials)
-static __host__ __device__ inline MsSmem ms_layout(int max_cols, int H, int D, int rep) {
+// working set (q, new k/v, per-warp partials); pool holds the partial sums
+// of every item of the CTA's largest phase share
+static __host__ __device__ inline MsSmem ms_layout(int max_cols, int H, int D, int rep, int pool_items,
+                                                   int pool_units) {
     MsSmem L;
-    L.ring = 0;
-    L.full = L.ring + (size_t)MS_NS * MS_CHUNK;
-    L.empty = L.full + MS_NS * 8;
-    L.cnt = L.empty + MS_NS * 8;
-    L.red = L.cnt + (size_t)MS_POOL_ITEMS * 4;
-    L.scratch = L.red + (size_t)MS_POOL_ITEMS * 16 * 4;
     const int ng = max_cols / 64;
     size_t gem = (size_t)ng * 128 + (((size_t)ng * 4 + 15) / 16) * 16 + (size_t)H * 2;
-    size_t att = (size_t)rep * D * 4 + (size_t)D * 4 + (size_t)MS_CONSUMERS * D * 4 +
-                 (size_t)8 * rep * 8 + (size_t)8 * rep * D * 4;
-    L.actx = L.scratch + (((gem > att ? gem : att) + 15) / 16) * 16;
+    size_t att = (size_t)rep * D * 4 + (size_t)D * 4 + (size_t)MS_WARPS * D * 4 + (size_t)8 * rep * 8 +
+                 (size_t)8 * rep * D * 4;
+    L.wbuf = 0;
+    L.scratch = (size_t)MS_WARPS * 2 * MS_ITEM;
+    L.pool = L.scratch + (((gem > att ? gem : att) + 15) / 16) * 16;
+    L.cnt = L.pool + (size_t)pool_items * 16 * 4;
+    L.actx = L.cnt + (((size_t)pool_units * 4 + 15) / 16) * 16;
     L.total = L.actx + (size_t)3 * D * 4;
     return L;
 }
 
-MLXD_DEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(MS_CT) : "memory"); }
 MLXD_DEV int ld_acquire(const int *p) {
     int v;
     asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-MLXD_DEV void mbar_arrive(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+MLXD_DEV int ld_relaxed(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
-// arrivals item k of a phase with n items owes its chunk's empty barrier:
-// the last item of a short final chunk also covers the missing items
-MLXD_DEV uint32_t ms_release_count(int k, int n) {
-    const int c0 = k & ~(MS_IPC - 1);
-    const int len = min(MS_IPC, n - c0);
-    return k == n - 1 ? (uint32_t)(MS_IPC - len + 1) : 1u;
-}
-// the ring chunk of chunk number g (a running count over the step)
-MLXD_DEV int ms_slot(long long g) { return (int)(g % MS_NS); }
-MLXD_DEV uint32_t ms_parity(long long g) { return (uint32_t)(g / MS_NS) & 1u; }
-// one thread: wait until *p >= target; false after MS_WAIT_NS
+// one thread: wait until *p >= target (false after MS_WAIT_NS). The polls are
+// relaxed; one acquiring load once the count is reached orders the reads
+// that follow (an acquire per poll would keep invalidating this SM's L1).
 MLXD_DEV bool ms_spin(const int *p, int target) {
-    if (ld_acquire(p) >= target) return true;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        __nanosleep(32);
-        if (ld_acquire(p) >= target) return true;
-        if (global_ns() - t0 > MS_WAIT_NS) return false;
+    if (ld_relaxed(p) < target) {
+        const unsigned long long t0 = global_ns();
+        for (;;) {
+            __nanosleep(32);
+            if (ld_relaxed(p) >= target) break;
+            if (global_ns() - t0 > MS_WAIT_NS) return false;
+        }
     }
+    return ld_acquire(p) >= target;
 }
 // A CTA that gave up on one wait (flag `dead` in shared memory, error word
-// set) stops waiting from then on: the producer stops issuing copies and the
-// consumers run through the remaining phases without waiting, so the launch
-// ends within about one wait limit per CTA.
+// set) stops waiting from then on and runs through the remaining phases, so
+// the launch ends within about one wait limit per CTA.
 MLXD_DEV void ms_fail(volatile int *dead, int *err) {
     *dead = 1;
     *err = 1;
 }
+MLXD_DEV void cbar() { __syncthreads(); }
 
 // the CTA's share of n units for phase ph (rotated so that no CTA takes the
 // larger share in every phase)
@@ -149,106 +164,103 @@ MLXD_DEV void ms_units(int n, int ph, int &u0, int &u1) {
     u0 = (int)((long long)n * c / G);
     u1 = (int)((long long)n * (c + 1) / G);
 }
+// items of the CTA's share of a projection phase; u0 = its first unit
+MLXD_DEV int ms_share(const MsMat &M, int unit_rb, int ph, int &u0) {
+    int u1;
+    ms_units(M.rows / 16 / unit_rb, ph, u0, u1);
+    return (u1 - u0) * unit_rb * (M.cols / 512);
+}
 
 struct MsAttnShare {
     int kh, sp;            // kh < 0: no attention work for this CTA
     int s0, s1, nc;        // positions [s0, s1) of the split; nc = cached rows in it
 };
-template <int D>
-MLXD_DEV MsAttnShare ms_attn_share(const MsArgs &a, int ph, int pos) {
+MLXD_DEV MsAttnShare ms_attn_share(int ph, int pos, int window) {
     MsAttnShare s;
     const int G = gridDim.x;
     const int c = (int)((blockIdx.x + (unsigned)ph * 37u) % (unsigned)G);
     s.kh = -1;
     s.sp = 0;
     s.s0 = s.s1 = s.nc = 0;
-    if (c >= a.hkv * a.nspl) return s;
-    s.kh = c / a.nspl;
-    s.sp = c % a.nspl;
+    if (c >= MA.hkv * MA.nspl) return s;
+    s.kh = c / MA.nspl;
+    s.sp = c % MA.nspl;
     const int T = pos + 1;
-    const int lo = a.window > 0 ? max(0, T - a.window) : 0;
+    const int lo = window > 0 ? max(0, T - window) : 0;
     const int span = T - lo;
-    s.s0 = lo + (int)((long long)span * s.sp / a.nspl);
-    s.s1 = lo + (int)((long long)span * (s.sp + 1) / a.nspl);
+    s.s0 = lo + (int)((long long)span * s.sp / MA.nspl);
+    s.s1 = lo + (int)((long long)span * (s.sp + 1) / MA.nspl);
     s.nc = max(0, min(s.s1, pos) - s.s0);
     return s;
 }
 
-// ---------------------------------------------------------------- producer
-template <int D>
-MLXD_DEV void ms_issue_gemv(const MsMat &M, int unit_rb, int ph, uint8_t *ring, uint64_t *full,
-                            uint64_t *empty, long long &seq, volatile int *dead, int *err) {
-    const int nbk = M.cols / 512;
-    int u0, u1;
-    ms_units(M.rows / 16 / unit_rb, ph, u0, u1);
-    const long long i0 = (long long)u0 * unit_rb * nbk;
-    const long long n = (long long)(u1 - u0) * unit_rb * nbk;
-#ifdef MLXD_TRACE
-    unsigned long long tw_ = 0, t0_ = gtime();
-#endif
-    for (long long k = 0; k < n; k += MS_IPC, seq++) {
-        const int slot = ms_slot(seq);
-        if (*dead) return;
-#ifdef MLXD_TRACE
-        unsigned long long ta_ = gtime();
-#endif
-        if (seq >= MS_NS && !mbar_wait(&empty[slot], ms_parity(seq) ^ 1u)) {
-            ms_fail(dead, err);
+// The warp's weight stream: its items of every projection phase in order
+// (projection phase g: 4 per layer, q|k|v, o, gate|up, down, then lm_head).
+struct MsStream {
+    int g;               // projection phase of the issue cursor; -1 when done
+    int j, m;            // next item of the warp's share in it, share size
+    long long i0;        // first item of the CTA's share in the matrix
+    const uint8_t *tiles, *sb8;
+    long long issued, consumed;
+};
+MLXD_DEV MsMat ms_proj(int g, int &unit_rb, int &ph) {
+    if (g >= 4 * MA.L) {
+        unit_rb = 1;
+        ph = 1 + 5 * MA.L;
+        return MA.lm;
+    }
+    const int l = g >> 2, r = g & 3;
+    ph = 1 + 5 * l + (r == 0 ? 0 : r + 1);   // q|k|v 1, o 3, gate|up 4, down 5
+    unit_rb = r == 2 ? 2 : 1;
+    return r == 0 ? c_ms.layers[l].qkv : r == 1 ? c_ms.layers[l].o : r == 2 ? c_ms.layers[l].gu
+                                                                           : c_ms.layers[l].down;
+}
+// move the cursor to the next phase in which the warp has items
+MLXD_DEV void ms_seek(MsStream &st, int warp) {
+    while (st.g >= 0) {
+        if (st.g > 4 * MA.L) {
+            st.g = -1;
             return;
         }
-#ifdef MLXD_TRACE
-        tw_ += gtime() - ta_;
-#endif
-        const uint32_t len = (uint32_t)min((long long)MS_IPC, n - k);
-        uint8_t *dst = ring + (size_t)slot * MS_CHUNK;
-        mbar_expect_tx(&full[slot], len * MS_SLOT);
-        bulk_g2s(dst, M.tiles + (i0 + k) * 4096, len * 4096, &full[slot]);
-        bulk_g2s(dst + MS_IPC * 4096, M.sb8 + (i0 + k) * 512, len * 512, &full[slot]);
-    }
-    MLXD_TRACE_REC((ph % 5) == 4 && ph < 12, 0x3100, tw_, gtime() - t0_, (unsigned long long)n)
-}
-
-template <int D>
-MLXD_DEV void ms_issue_attn(const MsArgs &a, int l, int ph, int pos, uint8_t *ring, uint64_t *full,
-                            uint64_t *empty, long long &seq, volatile int *dead) {
-    constexpr int RB = D * 2;                 // bytes of one cached row
-    constexpr int CP = MS_CHUNK / (2 * RB);   // positions per ring chunk
-    const MsAttnShare s = ms_attn_share<D>(a, ph, pos);
-    if (s.kh < 0) return;
-    const uint16_t *kc = a.kc + (size_t)l * a.layer_elems + (size_t)s.kh * a.cap * D;
-    const uint16_t *vc = a.vc + (size_t)l * a.layer_elems + (size_t)s.kh * a.cap * D;
-    for (int j0 = 0; j0 < s.nc; j0 += CP, seq++) {
-        const int slot = ms_slot(seq);
-        if (*dead) return;
-        if (seq >= MS_NS && !mbar_wait(&empty[slot], ms_parity(seq) ^ 1u)) {
-            ms_fail(dead, a.err);
-            return;
-        }
-        const int cnt = min(CP, s.nc - j0);
-        mbar_expect_tx(&full[slot], (uint32_t)(2 * cnt * RB));
-        const int p0 = s.s0 + j0;
-        const int r0 = p0 % a.cap;
-        const int n1 = min(cnt, a.cap - r0);   // rows before the ring wraps
-        uint8_t *dk = ring + (size_t)slot * MS_CHUNK;
-        uint8_t *dv = dk + CP * RB;
-        bulk_g2s(dk, kc + (size_t)r0 * D, n1 * RB, &full[slot]);
-        bulk_g2s(dv, vc + (size_t)r0 * D, n1 * RB, &full[slot]);
-        if (n1 < cnt) {
-            bulk_g2s(dk + n1 * RB, kc, (cnt - n1) * RB, &full[slot]);
-            bulk_g2s(dv + n1 * RB, vc, (cnt - n1) * RB, &full[slot]);
-        }
+        int urb, ph, u0;
+        const MsMat M = ms_proj(st.g, urb, ph);
+        const int n = ms_share(M, urb, ph, u0);
+        st.m = n > warp ? (n - warp + MS_WARPS - 1) / MS_WARPS : 0;
+        st.i0 = (long long)u0 * urb * (M.cols / 512);
+        st.tiles = M.tiles;
+        st.sb8 = M.sb8;
+        if (st.j < st.m) return;
+        st.g++;
+        st.j = 0;
     }
 }
+// request the stream's next item into the buffer the warp consumed last (one
+// commit group per stream position, empty past the end)
+MLXD_DEV void ms_issue(MsStream &st, unsigned char *wbuf, int warp, int lane) {
+    if (st.g >= 0) {
+        unsigned char *dst = wbuf + (st.issued & 1) * MS_ITEM + lane * 16;
+        const long long item = st.i0 + warp + (long long)st.j * MS_WARPS;
+        const uint8_t *t = st.tiles + item * 4096 + lane * 16;
+#pragma unroll
+        for (int p = 0; p < 8; p++) cp_async16(dst + p * 512, t + p * 512);
+        cp_async16(dst + 4096, st.sb8 + item * 512 + lane * 16);
+        st.j++;
+        ms_seek(st, warp);
+    }
+    cp_async_commit();
+    st.issued++;
+}
 
-// ---------------------------------------------------------------- consumers
 // phase input into the fragment order, consumer threads only: one 16-byte
 // load of x (and of the norm weights) per thread and pass, the RMSNorm with
 // the oracle's association (Ta element-strided partials, butterfly within
 // each warp, warp totals in order), and the per-group sums of x from eight
 // lanes' shuffles (a group of 64 is eight consecutive threads' vectors)
-template <bool NORM>
-MLXD_DEV void ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float eps, uint32_t *xp,
-                         float *xs, uint16_t *xraw, float *s_red) {
+// one copy of the code for every phase (instruction-cache friendly): the
+// norm is on when nw is given
+__device__ __noinline__ void ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float eps, uint32_t *xp,
+                                        float *xs, uint16_t *xraw, float *s_red) {
+    const bool NORM = nw != nullptr;
     constexpr int G = 64, XW = 8, MAXV = 4;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nv = cols / 8;
@@ -270,7 +282,7 @@ MLXD_DEV void ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float 
                 if (i < nv) reinterpret_cast<uint4 *>(xraw)[i] = v[j];
             }
         }
-        cbar();
+        __syncthreads();
         const int Ta = cols >= 1024 ? 256 : (cols >= 256 ? 128 : 32);
         float acc = 0.f;
         if (tid < Ta)
@@ -280,10 +292,10 @@ MLXD_DEV void ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float 
             }
         acc = warp_sum(acc);
         if (lane == 0) s_red[warp] = acc;
-        cbar();
+        __syncthreads();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < MS_CONSUMERS; w++) tot += s_red[w];
+        for (int w = 0; w < MS_WARPS; w++) tot += s_red[w];
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)cols), eps)));
     }
     for (int base = 0; base < nv; base += MS_CT * MAXV) {
@@ -321,7 +333,7 @@ MLXD_DEV void ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float 
             if (i < nv && (i & 7) == 0) xs[i >> 3] = gs;
         }
     }
-    cbar();
+    __syncthreads();
 }
 
 enum { MS_EPI_STORE = 0, MS_EPI_RESIDUAL = 1, MS_EPI_SWIGLU = 2, MS_EPI_LOGITS = 3 };
@@ -335,31 +347,29 @@ struct MsGemvOut {
 
 // one unit's rows once all its items are in: the items' partial sums added in
 // item order, then the epilogue (lanes 0..15, one row each)
-template <int EPI>
-MLXD_DEV void ms_unit_epilogue(const MsGemvOut &o, const float *ps, int nbk, int unit, int lane) {
-    constexpr int UNIT_RB = EPI == MS_EPI_SWIGLU ? 2 : 1;
+MLXD_DEV void ms_unit_epilogue(int EPI, const MsGemvOut &o, const float *ps, int nbk, int unit, int lane) {
+    const int UNIT_RB = EPI == MS_EPI_SWIGLU ? 2 : 1;
     unsigned long long key = 0ull;
     if (lane < 16) {
-        float acc[UNIT_RB];
-#pragma unroll
+        float acc[2] = {0.f, 0.f};
         for (int u = 0; u < UNIT_RB; u++) {
             float sum = 0.f;
             for (int i = u * nbk; i < (u + 1) * nbk; i++) sum += ps[i * 16 + lane];
             acc[u] = sum;
         }
         const int row = unit * 16 + lane;
-        if constexpr (EPI == MS_EPI_STORE) {
+        if (EPI == MS_EPI_STORE) {
             o.y[row] = f2bf(acc[0]);
-        } else if constexpr (EPI == MS_EPI_RESIDUAL) {
+        } else if (EPI == MS_EPI_RESIDUAL) {
             o.y[row] = f2bf(__fadd_rn(bf2f(o.residual[row]), rbf(acc[0])));
-        } else if constexpr (EPI == MS_EPI_SWIGLU) {
+        } else if (EPI == MS_EPI_SWIGLU) {
             o.y[row] = f2bf(swiglu_bf16(rbf(acc[0]), rbf(acc[1])));
         } else {
             if (o.y) o.y[row] = f2bf(acc[0]);
             key = argmax_key(rbf(acc[0]), o.row_offset + row);
         }
     }
-    if constexpr (EPI == MS_EPI_LOGITS) {
+    if (EPI == MS_EPI_LOGITS) {
 #pragma unroll
         for (int s = 16; s > 0; s >>= 1) {
             unsigned long long other = __shfl_xor_sync(0xffffffffu, key, s);
@@ -369,51 +379,33 @@ MLXD_DEV void ms_unit_epilogue(const MsGemvOut &o, const float *ps, int nbk, int
     }
 }
 
-// The consumer side of one projection phase. Warps take the phase's items in
-// order from a shared counter; each item's 16 (row) partial sums go to its own
-// place in the unit's record, and the warp whose item completes the unit adds
-// the record in item order and runs the epilogue. A ring slot is released only
-// after that, so a unit record is never reused while still being read:
-// MS_POOL_ITEMS >= MS_NS * MS_IPC + 2 * ipu.
-template <int EPI>
-__device__ __noinline__ void ms_gemv(const MsMat M, int u0, int n, long long base, const MsGemvOut o,
-                                     const uint8_t *ring, uint64_t *full, uint64_t *empty,
-                                     const uint32_t *xp, const float *xs, const uint32_t *s_zero,
-                                     int *s_cnt, float *pool, int *s_next, volatile int *dead,
-                                     int *err) {
-    constexpr int UNIT_RB = EPI == MS_EPI_SWIGLU ? 2 : 1;
-    const int lane = threadIdx.x & 31, t = lane & 3, gq = lane >> 2;
+// The warp's share of one projection phase, consumed from its weight stream
+// (the item now consumed has landed once at most one newer copy group is
+// pending); each consumed buffer is refilled with the stream's item after
+// next at once.
+MLXD_DEV void ms_gemv(int EPI, const MsMat M, int u0, int n, const MsGemvOut o, MsStream &st,
+                      unsigned char *wbuf, const uint32_t *xp, const float *xs, const uint32_t *s_zero,
+                      int *s_cnt, float *pool) {
+    const int UNIT_RB = EPI == MS_EPI_SWIGLU ? 2 : 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = lane & 3, gq = lane >> 2;
     const int nbk = M.cols / 512;
     const int ipu = nbk * UNIT_RB;
-    const int rp = MS_POOL_ITEMS / ipu;   // unit records in the pool
-#ifdef MLXD_TRACE
-    unsigned long long tw_ = 0, tc_ = 0, tl_ = gtime();
+    for (int k = warp; k < n; k += MS_WARPS) {
+#if MS_AHEAD == 1
+        ms_issue(st, wbuf, warp, lane);
 #endif
-    for (;;) {
-        int k = 0;
-        if (lane == 0) k = atomicAdd(s_next, 1);
-        k = __shfl_sync(0xffffffffu, k, 0);
-        if (k >= n) break;
-        const long long g = base + (k >> 2);
-        const int slot = ms_slot(g), sub = k & (MS_IPC - 1);
-        const bool live = __all_sync(0xffffffffu, !*dead);   // warp-uniform
-        if (live && !__all_sync(0xffffffffu, mbar_wait(&full[slot], ms_parity(g))) && lane == 0)
-            ms_fail(dead, err);
-#ifdef MLXD_TRACE
-        { unsigned long long t_ = gtime(); tw_ += t_ - tl_; tl_ = t_; }
-#endif
+        cp_async_wait<1>();
+
+        const unsigned char *buf = wbuf + (st.consumed & 1) * MS_ITEM + lane * 16;
         const int unit = k / ipu;
         const int iu = k - unit * ipu;
         const int bk = iu % nbk;
-        const uint8_t *sl = ring + (size_t)slot * MS_CHUNK;
-        const uint4 *wt = reinterpret_cast<const uint4 *>(sl + sub * 4096) + lane;
-        const uint4 sv = *(reinterpret_cast<const uint4 *>(sl + MS_IPC * 4096 + sub * 512) + lane);
         const uint32_t *xb = xp + ((size_t)bk * 32 + t) * 8;
         // four independent accumulators (one per 16-column chunk of a tile)
         float dj[4][4] = {};
 #pragma unroll
         for (int p = 0; p < 8; p++) {
-            const uint4 wv = wt[p * 32];
+            const uint4 wv = *reinterpret_cast<const uint4 *>(buf + p * 512);
             const uint4 *xq = reinterpret_cast<const uint4 *>(gq == p ? xb + p * 32 : s_zero);
             const uint4 xa = xq[0], xc = xq[1];
             const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
@@ -426,7 +418,8 @@ __device__ __noinline__ void ms_gemv(const MsMat M, int u0, int n, long long bas
         }
         float d[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) d[i] = (dj[0][i] + dj[1][i]) + (dj[2][i] + dj[3][i]);
+        for (int c = 0; c < 4; c++) d[c] = (dj[0][c] + dj[1][c]) + (dj[2][c] + dj[3][c]);
+        const uint4 sv = *reinterpret_cast<const uint4 *>(buf + 4096);
         const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
         const float s00 = lo_bf(sv.x), b00 = hi_bf(sv.x), s01 = lo_bf(sv.y), b01 = hi_bf(sv.y);
         const float s10 = lo_bf(sv.z), b10 = hi_bf(sv.z), s11 = lo_bf(sv.w), b11 = hi_bf(sv.w);
@@ -438,12 +431,17 @@ __device__ __noinline__ void ms_gemv(const MsMat M, int u0, int n, long long bas
         y1 = fmaf(fmaf(-128.f, s10, b10), xsv.x, y1);
         y1 = fmaf(s11, d[3], y1);
         y1 = fmaf(fmaf(-128.f, s11, b11), xsv.y, y1);
+        // this lane's reads of the buffer are done: refill it
+        st.consumed++;
+#if MS_AHEAD == 2
+        ms_issue(st, wbuf, warp, lane);
+#endif
         // the quad's four lanes hold disjoint groups of rows g, g+8
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
         y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
         y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
-        float *ps = pool + (size_t)(unit % rp) * ipu * 16;
+        float *ps = pool + (size_t)unit * ipu * 16;
         if (t == 0) {
             ps[iu * 16 + gq] = y0;
             ps[iu * 16 + gq + 8] = y1;
@@ -452,23 +450,17 @@ __device__ __noinline__ void ms_gemv(const MsMat M, int u0, int n, long long bas
         int done = 0;
         if (lane == 0) {
             __threadfence_block();
-            const int old = atomicAdd(&s_cnt[unit % rp], 1);
+            const int old = atomicAdd(&s_cnt[unit], 1);
             done = old + 1 == ipu;
-            if (done) s_cnt[unit % rp] = 0;
+            if (done) s_cnt[unit] = 0;
         }
         done = __shfl_sync(0xffffffffu, done, 0);
+
         if (done) {
             __threadfence_block();
-            ms_unit_epilogue<EPI>(o, ps, nbk, u0 + unit, lane);
+            ms_unit_epilogue(EPI, o, ps, nbk, u0 + unit, lane);
         }
-        __syncwarp();
-        if (lane == 0 && live) mbar_arrive(&empty[slot], ms_release_count(k, n));
-#ifdef MLXD_TRACE
-        { unsigned long long t_ = gtime(); tc_ += t_ - tl_; tl_ = t_; }
-#endif
     }
-    MLXD_TRACE_REC(lane == 0 && EPI == MS_EPI_SWIGLU && blockIdx.x < 16, 0x3000 + (threadIdx.x >> 5), tw_,
-                   tc_, (unsigned long long)n)
 }
 
 // online-softmax pair merge (log2 domain); m = -inf means empty
@@ -487,10 +479,10 @@ MLXD_DEV void sm_merge(float &m, float &l, float &o, float m2, float l2, float o
 // memory while the q|k|v phase still runs. actx: [D] qn, [D] kn, [rope_dims]
 // cos/sin pairs, as f32.
 template <int D>
-MLXD_DEV void ms_attn_preload(const MsArgs &a, const MsLayer &Ly, int pos, float *actx) {
+MLXD_DEV void ms_attn_preload(const MsLayer &Ly, int pos, float *actx) {
     const int tid = threadIdx.x;
-    const int half = a.rope_dims / 2;
-    const float *cs = a.rope_cs + (size_t)pos * half * 2;
+    const int half = MA.rope_dims / 2;
+    const float *cs = MA.rope_cs + (size_t)pos * half * 2;
     for (int i = tid; i < 2 * D + 2 * half; i += MS_CT) {
         float v;
         if (i < D) v = Ly.qn ? bf2f(Ly.qn[i]) : 1.f;
@@ -532,46 +524,61 @@ MLXD_DEV void ms_norm_rope(float *v, int D, const float *nwf, bool norm, float e
     __syncwarp();
 }
 
-// the consumer side of one attention phase
-template <int D, int REP>
-__device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int pos, const uint8_t *ring,
-                                          uint64_t *full, uint64_t *empty, long long base,
-                                          unsigned char *scratch, const float *actx, bool qk_norm,
-                                          volatile int *dead) {
+// cached rows of positions [j0, j0 + MS_KB) (clamped to j1) of one kv head
+template <int D>
+MLXD_DEV void ms_load_kv(typename std::conditional<D == 128, uint2, uint32_t>::type (&kb)[MS_KB],
+                         typename std::conditional<D == 128, uint2, uint32_t>::type (&vb)[MS_KB],
+                         const uint16_t *kc, const uint16_t *vc, int j0, int j1, int cap, int lane) {
+    using RowT = typename std::conditional<D == 128, uint2, uint32_t>::type;
     constexpr int DL = D / 32;
-    constexpr int RB = D * 2;
-    constexpr int CP = MS_SLOT / (2 * RB);     // positions per item (a quarter chunk)
-    constexpr int PB = 3;                      // positions scored together
+#pragma unroll
+    for (int u = 0; u < MS_KB; u++) {
+        const int j = min(j0 + u, j1 - 1);
+        if (j >= 0) {
+            const size_t off = (size_t)(j % cap) * D + lane * DL;
+            kb[u] = *reinterpret_cast<const RowT *>(kc + off);
+            vb[u] = *reinterpret_cast<const RowT *>(vc + off);
+        }
+    }
+}
+
+// the CTA's attention share; kb/vb hold the warp's first MS_KB cached rows on
+// entry; afterwards `it` gets the warp's first item of the o projection
+template <int D, int REP>
+__device__ __noinline__ void ms_attention(const MsCall kv, int l, int ph, int pos, const MsAttnShare s,
+                           typename std::conditional<D == 128, uint2, uint32_t>::type (&kb)[MS_KB],
+                           typename std::conditional<D == 128, uint2, uint32_t>::type (&vb)[MS_KB],
+                           unsigned char *scratch, const float *actx, bool qk_norm, volatile int *dead) {
+    constexpr int DL = D / 32;
+    constexpr int PB = MS_KB;                  // positions scored together
     using RowT = typename std::conditional<DL == 4, uint2, uint32_t>::type;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const MsAttnShare s = ms_attn_share<D>(a, ph, pos);
     if (s.kh < 0) return;
-    const int nck = (s.nc + CP - 1) / CP;
     const int kh = s.kh;
-#ifdef MLXD_TRACE
-    const unsigned long long ta0 = gtime();
-    unsigned long long ta1 = 0, ta2 = 0, ta3 = 0, ta4 = 0;
-#endif
+    const uint16_t *kc = kv.kc + (size_t)l * kv.layer_elems + (size_t)kh * kv.cap * D;
+    const uint16_t *vc = kv.vc + (size_t)l * kv.layer_elems + (size_t)kh * kv.cap * D;
+    const int per = (s.nc + MS_WARPS - 1) / MS_WARPS;
+    const int w0 = s.s0 + warp * per, w1 = min(s.s0 + s.nc, w0 + per);
 
     float *s_q = reinterpret_cast<float *>(scratch);                 // [REP][D]
     uint16_t *s_knew = reinterpret_cast<uint16_t *>(s_q + REP * D);  // [D]
     uint16_t *s_vnew = s_knew + D;                                   // [D]
     float *s_v = reinterpret_cast<float *>(s_vnew + D);              // [16][D] staging
-    float *s_ml = s_v + MS_CONSUMERS * D;                            // [8][REP][2]
+    float *s_ml = s_v + MS_WARPS * D;                                // [8][REP][2]
     float *s_o = s_ml + 8 * REP * 2;                                 // [8][REP][D]
 
     // q heads of the group, the new k (norm + rope) and the new v
-    const uint16_t *qkv = a.qkv;
-    for (int vi = warp; vi < REP + 2; vi += MS_CONSUMERS) {
+    const uint16_t *qkv = MA.qkv;
+    for (int vi = warp; vi < REP + 2; vi += MS_WARPS) {
         if (vi == REP + 1) {
-            for (int d = lane; d < D; d += 32) s_vnew[d] = qkv[a.qdim + (size_t)(a.hkv + kh) * D + d];
+            for (int d = lane; d < D; d += 32) s_vnew[d] = qkv[MA.qdim + (size_t)(MA.hkv + kh) * D + d];
             continue;
         }
         float *v = s_v + warp * D;
-        const uint16_t *src = vi < REP ? qkv + (size_t)(kh * REP + vi) * D : qkv + a.qdim + (size_t)kh * D;
+        const uint16_t *src = vi < REP ? qkv + (size_t)(kh * REP + vi) * D : qkv + MA.qdim + (size_t)kh * D;
         for (int d = lane; d < D; d += 32) v[d] = bf2f(src[d]);
         __syncwarp();
-        ms_norm_rope(v, D, vi < REP ? actx : actx + D, qk_norm, a.eps, actx + 2 * D, a.rope_dims);
+        ms_norm_rope(v, D, vi < REP ? actx : actx + D, qk_norm, MA.eps, actx + 2 * D, MA.rope_dims);
         if (vi < REP) {
             for (int d = lane; d < D; d += 32) s_q[vi * D + d] = v[d];
         } else {
@@ -579,18 +586,14 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         }
         __syncwarp();
     }
-    cbar();
+    __syncthreads();
     if (s.sp == 0) {
-        uint16_t *kc = a.kc + (size_t)l * a.layer_elems + ((size_t)kh * a.cap + pos % a.cap) * D;
-        uint16_t *vc = a.vc + (size_t)l * a.layer_elems + ((size_t)kh * a.cap + pos % a.cap) * D;
         for (int d = tid; d < D; d += MS_CT) {
-            kc[d] = s_knew[d];
-            vc[d] = s_vnew[d];
+            const size_t off = (size_t)(pos % kv.cap) * D + d;
+            const_cast<uint16_t *>(kc)[off] = s_knew[d];
+            const_cast<uint16_t *>(vc)[off] = s_vnew[d];
         }
     }
-#ifdef MLXD_TRACE
-    ta1 = gtime();
-#endif
     const float qscale = rsqrtf((float)D) * 1.4426950408889634f;
     float q[REP][DL], m[REP], lsum[REP], o[REP][DL];
 #pragma unroll
@@ -639,12 +642,11 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
             for (int u = 0; u < PB; u++)
                 if (u < nv) mn = fmaxf(mn, sc[r][u]);
             const float al = exp2f(m[r] - mn);
-            float pu[PB];
             float ps = 0.f;
 #pragma unroll
             for (int u = 0; u < PB; u++) {
-                pu[u] = u < nv ? exp2f(sc[r][u] - mn) : 0.f;
-                ps += pu[u];
+                sc[r][u] = u < nv ? exp2f(sc[r][u] - mn) : 0.f;
+                ps += sc[r][u];
             }
             lsum[r] = lsum[r] * al + ps;
 #pragma unroll
@@ -653,43 +655,26 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         }
 #pragma unroll
         for (int u = 0; u < PB; u++) {
-            if (u >= nv) break;
             float vf[DL];
             unpack(vr[u], vf);
-            // the weights were computed per head above; recompute is cheaper
-            // than keeping REP x PB of them live: p = 2^(score - m)
 #pragma unroll
-            for (int r = 0; r < REP; r++) {
-                const float p = exp2f(sc[r][u] - m[r]);
+            for (int r = 0; r < REP; r++)
 #pragma unroll
-                for (int i = 0; i < DL; i++) o[r][i] = fmaf(p, vf[i], o[r][i]);
-            }
+                for (int i = 0; i < DL; i++) o[r][i] = fmaf(sc[r][u], vf[i], o[r][i]);
         }
     };
-    for (int k = warp; k < nck; k += MS_CONSUMERS) {
-        const long long g = base + (k >> 2);
-        const int slot = ms_slot(g), sub = k & (MS_IPC - 1);
-        const bool live = __all_sync(0xffffffffu, !*dead);   // warp-uniform
-        if (live && !__all_sync(0xffffffffu, mbar_wait(&full[slot], ms_parity(g))) && lane == 0)
-            ms_fail(dead, a.err);
-        const uint8_t *sk = ring + (size_t)slot * MS_CHUNK + sub * CP * RB;
-        const uint8_t *sv = sk + MS_IPC * CP * RB;
-        const int cnt = min(CP, s.nc - k * CP);
-        for (int u0 = 0; u0 < cnt; u0 += PB) {
-            RowT kr[PB], vr[PB];
+    for (int j0 = w0; j0 < w1; j0 += PB) {
+        RowT kr[PB], vr[PB];
 #pragma unroll
-            for (int u = 0; u < PB; u++) {
-                const int uu = min(u0 + u, cnt - 1);
-                kr[u] = *reinterpret_cast<const RowT *>(sk + uu * RB + lane * DL * 2);
-                vr[u] = *reinterpret_cast<const RowT *>(sv + uu * RB + lane * DL * 2);
-            }
-            visit(kr, vr, min(PB, cnt - u0));
+        for (int u = 0; u < PB; u++) {
+            kr[u] = kb[u];
+            vr[u] = vb[u];
         }
-        __syncwarp();
-        if (lane == 0 && live) mbar_arrive(&empty[slot], ms_release_count(k, nck));
+        if (j0 + PB < w1) ms_load_kv<D>(kb, vb, kc, vc, j0 + PB, w1, kv.cap, lane);
+        visit(kr, vr, min(PB, w1 - j0));
     }
     // the new position (its row came from this step's projection)
-    if (warp == MS_CONSUMERS - 1 && pos >= s.s0 && pos < s.s1) {
+    if (warp == MS_WARPS - 1 && pos >= s.s0 && pos < s.s1) {
         RowT kr[PB], vr[PB];
 #pragma unroll
         for (int u = 0; u < PB; u++) {
@@ -698,12 +683,9 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         }
         visit(kr, vr, 1);
     }
-#ifdef MLXD_TRACE
-    ta2 = gtime();
-#endif
     // merge the warps of this CTA into the split's partial: warps 8..15 hand
     // their state to warps 0..7, which then write theirs for the final sum
-    static_assert(MS_CONSUMERS == 16, "two-round warp merge");
+    static_assert(MS_WARPS == 16, "two-round warp merge");
     auto put = [&](int slotw) {
 #pragma unroll
         for (int r = 0; r < REP; r++) {
@@ -719,7 +701,7 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         }
     };
     if (warp >= 8) put(warp - 8);
-    cbar();
+    __syncthreads();
     if (warp < 8) {
 #pragma unroll
         for (int r = 0; r < REP; r++) {
@@ -736,9 +718,9 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
             }
         }
     }
-    cbar();
+    __syncthreads();
     if (warp < 8) put(warp);
-    cbar();
+    __syncthreads();
     for (int idx = tid; idx < REP * D; idx += MS_CT) {
         const int r = idx / D, d = idx % D;
         float mm = -INFINITY, ll = 0.f, oo = 0.f;
@@ -746,7 +728,7 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         for (int w = 0; w < 8; w++)
             sm_merge(mm, ll, oo, s_ml[(w * REP + r) * 2], s_ml[(w * REP + r) * 2 + 1],
                      s_o[(w * REP + r) * D + d]);
-        float *rec = a.part + ((size_t)(kh * REP + r) * a.nspl + s.sp) * (D + 4);
+        float *rec = MA.part + ((size_t)(kh * REP + r) * MA.nspl + s.sp) * (D + 4);
         rec[d] = oo;
         if (d == 0) {
             rec[D] = mm;
@@ -754,37 +736,31 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         }
     }
     // wait for every split of this kv head, then merge a slice of its outputs
-    cbar();
-#ifdef MLXD_TRACE
-    ta3 = gtime();
-#endif
+    __syncthreads();
     if (tid == 0) {
         __threadfence();
-        atomicAdd(&a.sync[1 + kh], 1);
-        if (!*dead && !ms_spin(&a.sync[1 + kh], a.nspl * (l + 1))) ms_fail(dead, a.err);
+        atomicAdd(&MA.sync[1 + kh], 1);
+        if (!*dead && !ms_spin(&MA.sync[1 + kh], MA.nspl * (l + 1))) ms_fail(dead, MA.err);
     }
-    cbar();
-#ifdef MLXD_TRACE
-    ta4 = gtime();
-#endif
+    __syncthreads();
     const int n_out = REP * D;
-    const int o0 = (int)((long long)n_out * s.sp / a.nspl);
-    const int o1 = (int)((long long)n_out * (s.sp + 1) / a.nspl);
+    const int o0 = (int)((long long)n_out * s.sp / MA.nspl);
+    const int o1 = (int)((long long)n_out * (s.sp + 1) / MA.nspl);
     constexpr int MSPL = 4;   // splits per thread loaded together
     for (int base_o = o0; base_o < o1; base_o += MS_CT / 8) {
         const int oi = base_o + tid / 8, sub = tid % 8;
         float mm = -INFINITY, ll = 0.f, oo = 0.f;
         if (oi < o1) {
             const int r = oi / D, d = oi % D;
-            const float *rec = a.part + (size_t)(kh * REP + r) * a.nspl * (D + 4);
-            for (int sp0 = sub; sp0 < a.nspl; sp0 += 8 * MSPL) {
+            const float *rec = MA.part + (size_t)(kh * REP + r) * MA.nspl * (D + 4);
+            for (int sp0 = sub; sp0 < MA.nspl; sp0 += 8 * MSPL) {
                 float pm[MSPL], pl[MSPL], po[MSPL];
 #pragma unroll
                 for (int j = 0; j < MSPL; j++) {
                     const int sp = sp0 + 8 * j;
                     pm[j] = -INFINITY;
                     pl[j] = po[j] = 0.f;
-                    if (sp < a.nspl) {
+                    if (sp < MA.nspl) {
                         const float *rr = rec + (size_t)sp * (D + 4);
                         pm[j] = __ldcg(rr + D);
                         pl[j] = __ldcg(rr + D + 1);
@@ -804,214 +780,167 @@ __device__ __noinline__ void ms_attention(const MsArgs &a, int l, int ph, int po
         }
         if (oi < o1 && sub == 0) {
             const int r = oi / D, d = oi % D;
-            a.att[(size_t)(kh * REP + r) * D + d] = f2bf(oo / ll);
+            MA.att[(size_t)(kh * REP + r) * D + d] = f2bf(oo / ll);
         }
     }
-#ifdef MLXD_TRACE
-    MLXD_TRACE_REC(tid == 0 && l == 1, 0x5000, ta1 - ta0, ta2 - ta1, ta3 - ta2)
-    MLXD_TRACE_REC(tid == 0 && l == 1, 0x5001, ta4 - ta3, gtime() - ta4, (unsigned long long)nck)
-#endif
 }
 
 template <int D, int REP>
-__global__ void __launch_bounds__(MS_THREADS, 1) megastep_kernel(MsArgs a, int max_cols) {
+__global__ void __launch_bounds__(MS_CT, 1) megastep_kernel(const MsCall kv, int max_cols, int pool_items,
+                                                            int pool_units) {
+    using RowT = typename std::conditional<D == 128, uint2, uint32_t>::type;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(16) uint32_t s_zero[8];
-    __shared__ float s_red[MS_CONSUMERS];
+    __shared__ float s_red[MS_WARPS];
     __shared__ volatile int s_dead;
-    __shared__ int s_next;
-    const MsSmem Lo = ms_layout(max_cols, a.H, D, REP);
-    uint8_t *ring = smem + Lo.ring;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lo.full);
-    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + Lo.empty);
-    int *s_cnt = reinterpret_cast<int *>(smem + Lo.cnt);
-    float *pool = reinterpret_cast<float *>(smem + Lo.red);
-    unsigned char *scratch = smem + Lo.scratch;
-    float *actx = reinterpret_cast<float *>(smem + Lo.actx);
+    const MsSmem Lo = ms_layout(max_cols, MA.H, D, REP, pool_items, pool_units);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int pos = *a.d_pos;
+    unsigned char *wbuf = smem + Lo.wbuf + (size_t)warp * 2 * MS_ITEM;
+    unsigned char *scratch = smem + Lo.scratch;
+    float *pool = reinterpret_cast<float *>(smem + Lo.pool);
+    int *s_cnt = reinterpret_cast<int *>(smem + Lo.cnt);
+    float *actx = reinterpret_cast<float *>(smem + Lo.actx);
+    const int pos = *kv.d_pos;
     const int G = gridDim.x;
-
-    for (int i = tid; i < MS_POOL_ITEMS; i += MS_THREADS) s_cnt[i] = 0;
-    if (tid < 8) s_zero[tid] = 0u;
-    if (tid == 0) {
-        s_dead = 0;
-        s_next = 0;
-    }
-    if (tid == MS_CT) {
-        for (int i = 0; i < MS_NS; i++) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], MS_IPC);
-        }
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    if (warp == MS_CONSUMERS) {
-        // ---- producer: the CTA's weight and cache stream, in phase order
-        if (lane == 0) {
-            long long seq = 0;
-            for (int l = 0; l < a.L; l++) {
-                const MsLayer &Ly = a.layers[l];
-                const int ph = 1 + 5 * l;
-                ms_issue_gemv<D>(Ly.qkv, 1, ph, ring, full, empty, seq, &s_dead, a.err);
-                ms_issue_attn<D>(a, l, ph + 1, pos, ring, full, empty, seq, &s_dead);
-                ms_issue_gemv<D>(Ly.o, 1, ph + 2, ring, full, empty, seq, &s_dead, a.err);
-                ms_issue_gemv<D>(Ly.gu, 2, ph + 3, ring, full, empty, seq, &s_dead, a.err);
-                ms_issue_gemv<D>(Ly.down, 1, ph + 4, ring, full, empty, seq, &s_dead, a.err);
-            }
-            ms_issue_gemv<D>(a.lm, 1, 1 + 5 * a.L, ring, full, empty, seq, &s_dead, a.err);
-            // every issued copy has landed before the CTA (and its shared
-            // memory) goes away: the last fill of each slot
-            for (long long g = seq > MS_NS ? seq - MS_NS : 0; g < seq; g++)
-                if (!mbar_wait(&full[ms_slot(g)], ms_parity(g))) ms_fail(&s_dead, a.err);
-        }
-        return;
-    }
-
-    // ---- consumers
     uint32_t *xp = reinterpret_cast<uint32_t *>(scratch);
     const int ngmax = max_cols / 64;
     float *xs = reinterpret_cast<float *>(scratch + (size_t)ngmax * 128);
     uint16_t *xraw = reinterpret_cast<uint16_t *>(scratch + (size_t)ngmax * 128 +
                                                   (((size_t)ngmax * 4 + 15) / 16) * 16);
-    long long seq = 0;
+
+    for (int i = tid; i < pool_units; i += MS_CT) s_cnt[i] = 0;
+    if (tid < 8) s_zero[tid] = 0u;
+    if (tid == 0) s_dead = 0;
+
     int ph = 0;
     MLXD_TRACE_START
     auto phase_done = [&]() {
-        // every consumer's global writes of this phase (ordered before thread
-        // 0 by the CTA barrier, made visible by its fence), then one arrival
-        cbar();
+        // every thread's global writes of this phase (ordered before thread 0
+        // by the CTA barrier, made visible by its fence), then one arrival
+        __syncthreads();
         if (tid == 0) {
             __threadfence();
-            atomicAdd(&a.sync[0], 1);
+            atomicAdd(&MA.sync[0], 1);
         }
         MLXD_TRACE_END(0x1000 + ph)
         ph++;
     };
     auto phase_wait = [&]() {
         MLXD_TRACE_RESTART
-        if (tid == 0) {
-            s_next = 0;
-            if (!s_dead && !ms_spin(&a.sync[0], ph * G)) ms_fail(&s_dead, a.err);
-        }
-        cbar();
+        if (tid == 0 && !s_dead && !ms_spin(&MA.sync[0], ph * G)) ms_fail(&s_dead, MA.err);
+        __syncthreads();
         MLXD_TRACE_WAITED
     };
-    auto gemv_n = [&](const MsMat &M, int unit_rb, int &u0) {
-        int u1;
-        ms_units(M.rows / 16 / unit_rb, ph, u0, u1);
-        return (u1 - u0) * unit_rb * (M.cols / 512);
-    };
+
+    // the weight stream starts two items ahead, during the embedding phase
+    MsStream st;
+    st.g = 0;
+    st.j = 0;
+    st.issued = st.consumed = 0;
+    ms_seek(st, warp);
+    for (int i = 0; i < MS_AHEAD; i++) ms_issue(st, wbuf, warp, lane);
+    __syncthreads();
 
     // embed (fwd_embed, forward.c:65-147): this CTA's slice of the token's row
     {
-        int id = a.ids[0];
-        if (id < 0 || id >= a.vocab) id = 0;   // a failed draw; the host rejects the step
-        const int nv = a.H / 8;
+        int id = kv.ids[0];
+        if (id < 0 || id >= MA.vocab) id = 0;   // a failed draw; the host rejects the step
+        const int nv = MA.H / 8;
         const int v0 = (int)((long long)nv * blockIdx.x / G), v1 = (int)((long long)nv * (blockIdx.x + 1) / G);
-        const int ng = a.H / a.emb_g;
+        const int ng = MA.H / MA.emb_g;
         for (int i = v0 + tid; i < v1; i += MS_CT) {
-            const uint32_t w = a.emb_w[(size_t)id * nv + i];
-            const int g = (i * 8) / a.emb_g;
-            const float sc = bf2f(a.emb_s[(size_t)id * ng + g]), bi = bf2f(a.emb_b[(size_t)id * ng + g]);
+            const uint32_t w = MA.emb_w[(size_t)id * nv + i];
+            const int g = (i * 8) / MA.emb_g;
+            const float sc = bf2f(MA.emb_s[(size_t)id * ng + g]), bi = bf2f(MA.emb_b[(size_t)id * ng + g]);
             uint32_t o4[4];
 #pragma unroll
             for (int j = 0; j < 4; j++)
                 o4[j] = pack_bf2(__fmaf_rn(sc, (float)((w >> (8 * j)) & 0xF), bi),
                                  __fmaf_rn(sc, (float)((w >> (8 * j + 4)) & 0xF), bi));
-            *reinterpret_cast<uint4 *>(a.h + (size_t)i * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+            *reinterpret_cast<uint4 *>(MA.h + (size_t)i * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
         }
         phase_done();
     }
-    for (int l = 0; l < a.L; l++) {
-        const MsLayer &Ly = a.layers[l];
-        int u0, n;
-        // q|k|v
+    int u0, n;
+    for (int l = 0; l < MA.L; l++) {
+        const MsLayer &Ly = c_ms.layers[l];
+        // q|k|v; then the warp fetches its first cached rows of the attention
         phase_wait();
-        ms_stage_x<true>(a.h, Ly.ln1, Ly.qkv.cols, a.eps, xp, xs, xraw, s_red);
-        n = gemv_n(Ly.qkv, 1, u0);
-        ms_gemv<MS_EPI_STORE>(Ly.qkv, u0, n, seq, MsGemvOut{a.qkv, nullptr, nullptr, 0}, ring, full, empty,
-                              xp, xs, s_zero, s_cnt, pool, &s_next, &s_dead, a.err);
-        seq += (n + MS_IPC - 1) / MS_IPC;
-        ms_attn_preload<D>(a, Ly, pos, actx);
+        ms_stage_x(MA.h, Ly.ln1, Ly.qkv.cols, MA.eps, xp, xs, xraw, s_red);
+        n = ms_share(Ly.qkv, 1, ph, u0);
+        ms_gemv(MS_EPI_STORE, Ly.qkv, u0, n, MsGemvOut{MA.qkv, nullptr, nullptr, 0}, st, wbuf, xp, xs, s_zero,
+                              s_cnt, pool);
+
+        const MsAttnShare ash = ms_attn_share(ph + 1, pos, kv.window);
+        RowT kb[MS_KB], vb[MS_KB];
+        if (ash.kh >= 0) {
+            const int per = (ash.nc + MS_WARPS - 1) / MS_WARPS;
+            const int w0 = ash.s0 + warp * per, w1 = min(ash.s0 + ash.nc, w0 + per);
+            ms_load_kv<D>(kb, vb, kv.kc + (size_t)l * kv.layer_elems + (size_t)ash.kh * kv.cap * D,
+                          kv.vc + (size_t)l * kv.layer_elems + (size_t)ash.kh * kv.cap * D, w0, w1, kv.cap, lane);
+        }
+        ms_attn_preload<D>(Ly, pos, actx);
         phase_done();
         // attention
         phase_wait();
-        {
-            constexpr int CPC = MS_CHUNK / (4 * D);   // positions per ring chunk
-            const MsAttnShare sh = ms_attn_share<D>(a, ph, pos);
-            ms_attention<D, REP>(a, l, ph, pos, ring, full, empty, seq, scratch, actx, Ly.qn != nullptr,
-                                 &s_dead);
-            seq += sh.kh < 0 ? 0 : (sh.nc + CPC - 1) / CPC;
-        }
+        ms_attention<D, REP>(kv, l, ph, pos, ash, kb, vb, scratch, actx, Ly.qn != nullptr, &s_dead);
         phase_done();
         // o projection + residual
         phase_wait();
-        ms_stage_x<false>(a.att, nullptr, Ly.o.cols, a.eps, xp, xs, xraw, s_red);
-        n = gemv_n(Ly.o, 1, u0);
-        ms_gemv<MS_EPI_RESIDUAL>(Ly.o, u0, n, seq, MsGemvOut{a.h1, a.h, nullptr, 0}, ring, full, empty, xp,
-                                 xs, s_zero, s_cnt, pool, &s_next, &s_dead, a.err);
-        seq += (n + MS_IPC - 1) / MS_IPC;
+        ms_stage_x(MA.att, nullptr, Ly.o.cols, MA.eps, xp, xs, xraw, s_red);
+        n = ms_share(Ly.o, 1, ph, u0);
+        ms_gemv(MS_EPI_RESIDUAL, Ly.o, u0, n, MsGemvOut{MA.h1, MA.h, nullptr, 0}, st, wbuf, xp, xs, s_zero,
+                                 s_cnt, pool);
         phase_done();
         // gate|up + SwiGLU
         phase_wait();
-        ms_stage_x<true>(a.h1, Ly.ln2, Ly.gu.cols, a.eps, xp, xs, xraw, s_red);
-#ifdef MLXD_TRACE
-        const unsigned long long t_staged = gtime();
-#endif
-        n = gemv_n(Ly.gu, 2, u0);
-        ms_gemv<MS_EPI_SWIGLU>(Ly.gu, u0, n, seq, MsGemvOut{a.act, nullptr, nullptr, 0}, ring, full, empty,
-                               xp, xs, s_zero, s_cnt, pool, &s_next, &s_dead, a.err);
-        seq += (n + MS_IPC - 1) / MS_IPC;
-#ifdef MLXD_TRACE
-        const unsigned long long t_gemv = gtime();
-        cbar();
-        MLXD_TRACE_REC(tid == 0 && blockIdx.x < 32, 0x4000, t_staged - tr_t1_, t_gemv - t_staged, gtime() - t_gemv)
-#endif
+        ms_stage_x(MA.h1, Ly.ln2, Ly.gu.cols, MA.eps, xp, xs, xraw, s_red);
+        n = ms_share(Ly.gu, 2, ph, u0);
+        ms_gemv(MS_EPI_SWIGLU, Ly.gu, u0, n, MsGemvOut{MA.act, nullptr, nullptr, 0}, st, wbuf, xp, xs, s_zero,
+                               s_cnt, pool);
         phase_done();
         // down + residual
         phase_wait();
-        ms_stage_x<false>(a.act, nullptr, Ly.down.cols, a.eps, xp, xs, xraw, s_red);
-        n = gemv_n(Ly.down, 1, u0);
-        ms_gemv<MS_EPI_RESIDUAL>(Ly.down, u0, n, seq, MsGemvOut{a.h, a.h1, nullptr, 0}, ring, full, empty,
-                                 xp, xs, s_zero, s_cnt, pool, &s_next, &s_dead, a.err);
-        seq += (n + MS_IPC - 1) / MS_IPC;
+        ms_stage_x(MA.act, nullptr, Ly.down.cols, MA.eps, xp, xs, xraw, s_red);
+        n = ms_share(Ly.down, 1, ph, u0);
+        ms_gemv(MS_EPI_RESIDUAL, Ly.down, u0, n, MsGemvOut{MA.h, MA.h1, nullptr, 0}, st, wbuf, xp, xs, s_zero,
+                                 s_cnt, pool);
         phase_done();
     }
     // final norm + lm_head (+ greedy key)
     phase_wait();
-    ms_stage_x<true>(a.h, a.fnorm, a.lm.cols, a.eps, xp, xs, xraw, s_red);
-    {
-        int u0;
-        const int n = gemv_n(a.lm, 1, u0);
-        ms_gemv<MS_EPI_LOGITS>(a.lm, u0, n, seq, MsGemvOut{a.logits, nullptr, a.amax, 0}, ring, full, empty,
-                               xp, xs, s_zero, s_cnt, pool, &s_next, &s_dead, a.err);
-        seq += (n + MS_IPC - 1) / MS_IPC;
-    }
+    ms_stage_x(MA.h, MA.fnorm, MA.lm.cols, MA.eps, xp, xs, xraw, s_red);
+    n = ms_share(MA.lm, 1, ph, u0);
+    ms_gemv(MS_EPI_LOGITS, MA.lm, u0, n, MsGemvOut{kv.logits, nullptr, kv.amax, 0}, st, wbuf, xp, xs, s_zero,
+                           s_cnt, pool);
+    cp_async_wait<0>();
     phase_done();
     // step end (step_finish_kernel): token from the key, next position
     if (blockIdx.x == 0) {
         phase_wait();
         if (tid == 0) {
-            if (a.amax) {
-                const unsigned long long key = *a.amax;
-                *a.token = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
-                *a.amax = 0ull;
+            if (kv.amax) {
+                const unsigned long long key = *kv.amax;
+                *MA.token = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+                *kv.amax = 0ull;
             }
-            *a.d_pos = pos + 1;
+            *kv.d_pos = pos + 1;
         }
     }
 }
 
+}  // namespace mlxd
+
+namespace mlxd {
+
 // ------------------------------------------------------------------ host
 
 struct MegaState {
-    MsLayer *d_layers = nullptr;
+    MsConst *hc = nullptr;  // pinned host copy of the constant block
     int *sync = nullptr;   // [1 + hkv]
     int *err = nullptr;
     float *part = nullptr;
-    int nspl = 0, grid = 0, max_cols = 0, D = 0, rep = 0;
+    int nspl = 0, grid = 0, max_cols = 0, D = 0, rep = 0, pool_items = 0, pool_units = 0;
     size_t smem = 0;
 };
 
@@ -1019,14 +948,14 @@ template <int D, int REP>
 static int ms_prepare(size_t smem, int *blocks) {
     auto k = megastep_kernel<D, REP>;
     MLXD_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    MLXD_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, MS_THREADS, smem));
+    MLXD_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, MS_CT, smem));
     return 0;
 }
 template <int D, int REP>
-static int ms_launch(const MsArgs &a, const MegaState &S, cudaStream_t st) {
+static int ms_launch(const MsCall &kv, const MegaState &S, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S.grid);
-    cfg.blockDim = dim3(MS_THREADS);
+    cfg.blockDim = dim3(MS_CT);
     cfg.dynamicSmemBytes = S.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1034,7 +963,7 @@ static int ms_launch(const MsArgs &a, const MegaState &S, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MLXD_CHECK(cudaLaunchKernelEx(&cfg, megastep_kernel<D, REP>, a, S.max_cols));
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, megastep_kernel<D, REP>, kv, S.max_cols, S.pool_items, S.pool_units));
     return 0;
 }
 #define MLXD_MS_DISPATCH(FN, ...)                                        \
@@ -1053,8 +982,8 @@ static int ms_launch(const MsArgs &a, const MegaState &S, cudaStream_t st) {
 static int ms_prepare_any(int D, int rep, size_t smem, int *blocks) {
     MLXD_MS_DISPATCH(ms_prepare, smem, blocks)
 }
-static int ms_launch_any(int D, int rep, const MsArgs &a, const MegaState &S, cudaStream_t st) {
-    MLXD_MS_DISPATCH(ms_launch, a, S, st)
+static int ms_launch_any(int D, int rep, const MsCall &kv, const MegaState &S, cudaStream_t st) {
+    MLXD_MS_DISPATCH(ms_launch, kv, S, st)
 }
 
 static MsMat ms_mat(const QMat &q) { return MsMat{q.tiles, q.sb8, q.rows, q.cols}; }
@@ -1065,7 +994,7 @@ static bool ms_eligible(const mlxd_model *m) {
     const char *e = getenv("MLXD_MEGASTEP");
     if (!e || atoi(e) == 0) return false;
     const mlxd_model_config &c = m->c;
-    if (c.tp_size > 1 || c.attn_gate || c.qbits != 4) return false;
+    if (c.tp_size > 1 || c.attn_gate || c.qbits != 4 || c.layers > MS_MAX_LAYERS) return false;
     if (!m->embed.quant || m->embed.sdtype != MLXD_BF16 || c.hidden % c.qgroup) return false;
     const int rep = m->hq / m->hkv;
     if (!(c.head_dim == 128 || c.head_dim == 64) || !(rep == 1 || rep == 2 || rep == 4 || rep == 8))
@@ -1079,7 +1008,7 @@ static bool ms_eligible(const mlxd_model *m) {
 void megastep_free(mlxd_model *m) {
     MegaState *S = static_cast<MegaState *>(m->mega);
     if (!S) return;
-    dev_free(S->d_layers);
+    if (S->hc) cudaFreeHost(S->hc);
     dev_free(S->sync);
     dev_free(S->err);
     dev_free(S->part);
@@ -1096,44 +1025,47 @@ int megastep_setup(mlxd_model *m) {
     S->grid = num_sms();
     S->nspl = S->grid / m->hkv;
     S->max_cols = std::max(std::max(c.hidden, m->hq * c.head_dim), m->inter_local);
-    S->smem = ms_layout(S->max_cols, c.hidden, S->D, S->rep).total;
+    // the largest per-CTA share over the projection phases, in units and items
+    auto share = [&](const QMat &q, int unit_rb) {
+        const int units = q.rows / 16 / unit_rb;
+        const int per = (units + S->grid - 1) / S->grid;
+        S->pool_units = std::max(S->pool_units, per);
+        S->pool_items = std::max(S->pool_items, per * unit_rb * (q.cols / 512));
+    };
+    for (const Layer &L : m->L) {
+        share(L.qkv, 1);
+        share(L.o, 1);
+        share(L.gateup, 2);
+        share(L.down, 1);
+    }
+    share(m->lm, 1);
+    S->smem = ms_layout(S->max_cols, c.hidden, S->D, S->rep, S->pool_items, S->pool_units).total;
     int blocks = 0;
     if (S->nspl < 1 || S->smem > 227 * 1024 || ms_prepare_any(S->D, S->rep, S->smem, &blocks) || blocks < 1) {
         delete S;   // the layer-by-layer kernels serve this model
         return 0;
     }
-    std::vector<MsLayer> hl(c.layers);
+    MsConst *hc = nullptr;
+    if (!cuda_ok(cudaMallocHost(&hc, sizeof(MsConst)), "megastep constants")) {
+        delete S;
+        return -1;
+    }
+    memset(hc, 0, sizeof(MsConst));
+    S->hc = hc;
     for (int l = 0; l < c.layers; l++) {
         const Layer &L = m->L[l];
-        hl[l] = MsLayer{ms_mat(L.qkv), ms_mat(L.o), ms_mat(L.gateup), ms_mat(L.down),
-                        L.ln1, L.ln2, c.qk_norm ? L.qn : nullptr, c.qk_norm ? L.kn : nullptr};
+        hc->layers[l] = MsLayer{ms_mat(L.qkv), ms_mat(L.o), ms_mat(L.gateup), ms_mat(L.down),
+                                L.ln1, L.ln2, c.qk_norm ? L.qn : nullptr, c.qk_norm ? L.kn : nullptr};
     }
-    S->d_layers = (MsLayer *)dev_alloc(hl.size() * sizeof(MsLayer));
     S->sync = (int *)dev_alloc((size_t)(1 + m->hkv) * sizeof(int));
     S->err = (int *)dev_alloc(sizeof(int));
     S->part = (float *)dev_alloc((size_t)m->hq * S->nspl * (S->D + 4) * sizeof(float));
     m->mega = S;
-    if (!S->d_layers || !S->sync || !S->err || !S->part ||
-        !cuda_ok(cudaMemcpy(S->d_layers, hl.data(), hl.size() * sizeof(MsLayer), cudaMemcpyHostToDevice),
-                 "megastep layers") ||
-        !cuda_ok(cudaMemset(S->err, 0, sizeof(int)), "megastep err")) {
+    if (!S->sync || !S->err || !S->part || !cuda_ok(cudaMemset(S->err, 0, sizeof(int)), "megastep err")) {
         megastep_free(m);
         return -1;
     }
-    return 0;
-}
-
-bool megastep_ready(const mlxd_model *m, const mlxd_kv *kv) {
-    const MegaState *S = static_cast<const MegaState *>(m->mega);
-    return S && kv->d == S->D && kv->hkv == m->hkv;
-}
-
-int megastep_launch(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, uint16_t *logits, bool argmax,
-                    cudaStream_t st) {
-    const MegaState &S = *static_cast<const MegaState *>(m->mega);
-    const mlxd_model_config &c = m->c;
-    MsArgs a = {};
-    a.layers = S.d_layers;
+    MsArgs &a = hc->a;
     a.L = c.layers;
     a.lm = ms_mat(m->lm);
     a.fnorm = m->norm;
@@ -1149,27 +1081,43 @@ int megastep_launch(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, uint16_t
     a.eps = c.eps;
     a.rope_cs = m->rope_cs;
     a.rope_dims = c.rope_dims;
-    a.kc = kv->k;
-    a.vc = kv->v;
-    a.layer_elems = (size_t)kv->hkv * kv->cap * kv->d;
-    a.cap = kv->cap;
-    a.window = kv->window;
-    a.d_pos = kv->d_pos;
-    a.ids = ids_dev;
-    a.amax = argmax ? m->amax : nullptr;
     a.token = m->token;
-    a.logits = logits;
     a.h = m->h;
     a.h1 = m->h1;
     a.qkv = m->qkv;
     a.att = m->att;
     a.act = m->act;
-    a.part = S.part;
-    a.sync = S.sync;
-    a.nspl = S.nspl;
-    a.err = S.err;
+    a.part = S->part;
+    a.sync = S->sync;
+    a.nspl = S->nspl;
+    a.err = S->err;
+    return 0;
+}
+
+bool megastep_ready(const mlxd_model *m, const mlxd_kv *kv) {
+    const MegaState *S = static_cast<const MegaState *>(m->mega);
+    return S && kv->d == S->D && kv->hkv == m->hkv;
+}
+
+int megastep_launch(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, uint16_t *logits, bool argmax,
+                    cudaStream_t st) {
+    const MegaState &S = *static_cast<const MegaState *>(m->mega);
+    const mlxd_model_config &c = m->c;
+    MsCall kvc = {};
+    kvc.kc = kv->k;
+    kvc.vc = kv->v;
+    kvc.layer_elems = (size_t)kv->hkv * kv->cap * kv->d;
+    kvc.cap = kv->cap;
+    kvc.window = kv->window;
+    kvc.d_pos = kv->d_pos;
+    kvc.ids = ids_dev;
+    kvc.amax = argmax ? m->amax : nullptr;
+    kvc.logits = logits;
+    // the model's fixed block (never rewritten after set-up) into constant memory
+    MLXD_CHECK(cudaMemcpyToSymbolAsync(c_ms, S.hc, sizeof(MsArgs) + (size_t)c.layers * sizeof(MsLayer), 0,
+                                       cudaMemcpyHostToDevice, st));
     MLXD_CHECK(cudaMemsetAsync(S.sync, 0, (size_t)(1 + m->hkv) * sizeof(int), st));
-    return ms_launch_any(S.D, S.rep, a, S, st);
+    return ms_launch_any(S.D, S.rep, kvc, S, st);
 }
 
 // nonzero once a megastep launch gave up on a wait (read and cleared)
