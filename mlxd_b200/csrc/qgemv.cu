@@ -814,6 +814,156 @@ __global__ void __launch_bounds__(BW_THREADS, 2) qgemv_bulk_kernel(GemvArgs a, i
     MLXD_TRACE_END(0x20 + EPI)
 }
 
+// Decode fast path with whole row blocks per CTA (group 64, bf16 scales,
+// cols/64 a multiple of 8). CTA c owns units [c*U/G, (c+1)*U/G) (a unit is a
+// row block, or a gate|up pair for SwiGLU); warp w takes items w, w+16, ...
+// of that range (an item is one block of 8 groups of one row block) and
+// holds the next one in registers while computing the current one. Each
+// item's 16 partial sums go to their own place in shared memory and the warp
+// that completes a unit adds them in item order and runs the epilogue: no
+// global workspace, no grid-wide atomics, deterministic.
+constexpr int RB_THREADS = 512, RB_WARPS = 16;
+
+template <int EPI>
+MLXD_DEV void rb_epilogue(const GemvArgs &a, const float *ps, int nbk, int unit, int lane,
+                          unsigned long long &best) {
+    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    if (lane >= 16) return;
+    float acc[UNIT_RB];
+#pragma unroll
+    for (int u = 0; u < UNIT_RB; u++) {
+        float sum = 0.f;
+        for (int i = u * nbk; i < (u + 1) * nbk; i++) sum += ps[i * 16 + lane];
+        acc[u] = sum;
+    }
+    const int row = unit * 16 + lane;
+    if constexpr (EPI == EPI_SWIGLU) {
+        a.y[row] = f2bf(swiglu_bf16(rbf(acc[0]), rbf(acc[UNIT_RB - 1])));
+    } else if constexpr (EPI == EPI_ARGMAX) {
+        a.y[row] = f2bf(acc[0]);
+        const unsigned long long key = argmax_key(rbf(acc[0]), a.row_offset + row);
+        best = key > best ? key : best;
+    } else {
+        epilogue_row<EPI>(a, row, acc[0]);
+    }
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int pool_items) {
+    constexpr int G = 64, XW = 8;
+    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(16) uint32_t s_zero[8];
+    __shared__ float s_red[RB_WARPS];
+    __shared__ unsigned long long s_key[RB_WARPS];
+    const int ng = a.cols / G, nbk = ng / 8;
+    uint32_t *xp = reinterpret_cast<uint32_t *>(smem_raw);
+    float *xs = reinterpret_cast<float *>(xp + (size_t)ng * 4 * XW);
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw + xraw_offset(ng, XW));
+    float *pool = reinterpret_cast<float *>(smem_raw + ((xraw_offset(ng, XW) + (size_t)a.cols * 2 + 15) / 16) * 16);
+    int *s_cnt = reinterpret_cast<int *>(pool + (size_t)pool_items * 16);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
+    const int n_units = a.rows / 16 / UNIT_RB;
+    const int u0 = (int)((long long)n_units * blockIdx.x / gridDim.x);
+    const int u1 = (int)((long long)n_units * (blockIdx.x + 1) / gridDim.x);
+    const int ipu = nbk * UNIT_RB;
+    const int n = (u1 - u0) * ipu;
+    const long long i0 = (long long)u0 * ipu;
+    for (int i = tid; i < u1 - u0; i += RB_THREADS) s_cnt[i] = 0;
+
+    // the warp's first item streams while the previous kernel finishes
+    uint4 wbuf[8];
+    uint4 sbuf = make_uint4(0, 0, 0, 0);
+    if (warp < n) {
+        const uint8_t *pw = a.tiles + (i0 + warp) * 4096 + lane * 16;
+#pragma unroll
+        for (int p = 0; p < 8; p++) wbuf[p] = ldg_nc_v4(pw + p * 512);
+        sbuf = ldg_nc_v4(a.sb8 + (i0 + warp) * 512 + lane * 16);
+    }
+    pdl_wait();
+    if (tid < 8) s_zero[tid] = 0u;
+    stage_x<G, RB_THREADS, PRO == PRO_RMSNORM>(a, xp, xs, xraw, s_red);
+    pdl_trigger();
+
+    unsigned long long best = 0ull;
+    for (int k = warp; k < n; k += RB_WARPS) {
+        const bool pre = k + RB_WARPS < n;
+        const uint8_t *pwn = a.tiles + (i0 + k + RB_WARPS) * 4096 + lane * 16;
+        const int unit = k / ipu;
+        const int iu = k - unit * ipu;
+        const int bk = iu % nbk;
+        const uint32_t *xb = xp + ((size_t)bk * 32 + t) * XW;
+        // four independent accumulators (one per 16-column chunk of a tile)
+        float dj[4][4] = {};
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            const uint4 wv = wbuf[p];
+            if (pre) wbuf[p] = ldg_nc_v4(pwn + p * 512);
+            const uint4 *xq = reinterpret_cast<const uint4 *>(gq == p ? xb + p * 32 : s_zero);
+            const uint4 xa = xq[0], xc = xq[1];
+            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
+                                  nib_pair(wv.w, j)};
+                mma_bf16_16816(dj[j], af, xv[2 * j], xv[2 * j + 1]);
+            }
+        }
+        float d[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) d[c] = (dj[0][c] + dj[1][c]) + (dj[2][c] + dj[3][c]);
+        const uint4 sv = sbuf;
+        if (pre) sbuf = ldg_nc_v4(a.sb8 + (i0 + k + RB_WARPS) * 512 + lane * 16);
+        const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
+        const float s00 = lo_bf(sv.x), b00 = hi_bf(sv.x), s01 = lo_bf(sv.y), b01 = hi_bf(sv.y);
+        const float s10 = lo_bf(sv.z), b10 = hi_bf(sv.z), s11 = lo_bf(sv.w), b11 = hi_bf(sv.w);
+        float y0 = s00 * d[0];
+        y0 = fmaf(fmaf(-128.f, s00, b00), xsv.x, y0);
+        y0 = fmaf(s01, d[1], y0);
+        y0 = fmaf(fmaf(-128.f, s01, b01), xsv.y, y0);
+        float y1 = s10 * d[2];
+        y1 = fmaf(fmaf(-128.f, s10, b10), xsv.x, y1);
+        y1 = fmaf(s11, d[3], y1);
+        y1 = fmaf(fmaf(-128.f, s11, b11), xsv.y, y1);
+        // the quad's four lanes hold disjoint groups of rows g, g+8
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        float *ps = pool + (size_t)unit * ipu * 16;
+        if (t == 0) {
+            ps[iu * 16 + gq] = y0;
+            ps[iu * 16 + gq + 8] = y1;
+        }
+        __syncwarp();
+        int done = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            done = atomicAdd(&s_cnt[unit], 1) + 1 == ipu;
+        }
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done) {
+            __threadfence_block();
+            rb_epilogue<EPI>(a, ps, nbk, u0 + unit, lane, best);
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0) s_key[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < RB_WARPS; w++) m = s_key[w] > m ? s_key[w] : m;
+            if (m) atomicMax(a.amax, m);
+        }
+    }
+}
+
 // grid and workspace slots of one launch
 static bool fast8_shape(int cols, int G) { return G == 64 && (cols / 64) % 8 == 0; }
 
@@ -969,6 +1119,59 @@ int gemv_wait_timeouts() {
     return v;
 }
 
+template <int PRO, int EPI>
+static int launch_gemv8r(GemvArgs a, cudaStream_t st, bool pdl) {
+    auto kern = qgemv8r_kernel<PRO, EPI>;
+    const int ng = a.cols / 64;
+    const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
+    const int n_units = a.rows / 16 / unit_rb;
+    int grid = num_sms();
+    if (grid > n_units) grid = n_units;
+    const int per = (n_units + grid - 1) / grid;
+    const int pool_items = per * unit_rb * (a.cols / 512);
+    const size_t smem = ((xraw_offset(ng, 8) + (size_t)a.cols * 2 + 15) / 16) * 16 + (size_t)pool_items * 64 +
+                        (size_t)per * 4;
+    if (smem > 200 * 1024) {
+        set_error("qgemv: %d x %d needs %zu bytes of shared memory", a.rows, a.cols, smem);
+        return -1;
+    }
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(RB_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a, pool_items));
+    return 0;
+}
+
+static int dispatch_gemv8r(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
+#define MLXD_GEMVR_CASE(P, E) \
+    if (pro == P && epi == E) return launch_gemv8r<P, E>(a, st, pdl);
+    MLXD_GEMVR_CASE(PRO_PLAIN, EPI_STORE)
+    MLXD_GEMVR_CASE(PRO_PLAIN, EPI_RESIDUAL)
+    MLXD_GEMVR_CASE(PRO_PLAIN, EPI_SWIGLU)
+    MLXD_GEMVR_CASE(PRO_PLAIN, EPI_ARGMAX)
+    MLXD_GEMVR_CASE(PRO_PLAIN, EPI_PARTIAL_F32)
+    MLXD_GEMVR_CASE(PRO_RMSNORM, EPI_STORE)
+    MLXD_GEMVR_CASE(PRO_RMSNORM, EPI_RESIDUAL)
+    MLXD_GEMVR_CASE(PRO_RMSNORM, EPI_SWIGLU)
+    MLXD_GEMVR_CASE(PRO_RMSNORM, EPI_ARGMAX)
+    MLXD_GEMVR_CASE(PRO_RMSNORM, EPI_PARTIAL_F32)
+#undef MLXD_GEMVR_CASE
+    set_error("qgemv: bad prologue/epilogue");
+    return -1;
+}
+
 static int dispatch_gemv8(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
 #define MLXD_GEMV8_CASE(P, E) \
     if (pro == P && epi == E) return launch_gemv8<P, E>(a, st, pdl);
@@ -1006,12 +1209,13 @@ static int dispatch_gemv(int pro, int epi, const GemvArgs &a, cudaStream_t st, b
     return -1;
 }
 
-// decode kernel for the group-64 fast layout: 0 = register-prefetch
-// stream-K (default, the faster one inside the decode graph), 1 = bulk-copy
-// prefetch into shared memory; MLXD_GEMV_KIND overrides
+// decode kernel for the group-64 fast layout: 2 = whole row blocks per CTA
+// with register prefetch (default, the fastest inside the decode graph),
+// 0 = register-prefetch stream-K over warps, 1 = bulk-copy prefetch into
+// shared memory; MLXD_GEMV_KIND overrides
 static int g_gemv_kind = [] {
     const char *e = getenv("MLXD_GEMV_KIND");
-    return e ? atoi(e) : 0;
+    return e ? atoi(e) : 2;
 }();
 
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl) {
@@ -1038,6 +1242,7 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
     if (W.sb8 && W.fast8()) {
         a.sb8 = W.sb8;
         if (g_gemv_kind == 1) return dispatch_gemv_bulk(pro, epi, a, st, pdl);
+        if (g_gemv_kind == 2) return dispatch_gemv8r(pro, epi, a, st, pdl);
         return dispatch_gemv8(pro, epi, a, st, pdl);
     }
     bool f32 = W.sdtype == MLXD_F32;
