@@ -14,6 +14,10 @@
 //   fallback (q*scale in bf16, bf16 scores, precise softmax rounded to bf16,
 //   bf16 matmul with v), reproduced operation for operation.
 // Sliding-window caches are rings: position p lives in slot p % cap.
+#include <cooperative_groups.h>
+#include <stdlib.h>
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -306,9 +310,387 @@ static int launch_decode(const AttnDecodeArgs &a, int rep, cudaStream_t st, bool
     }
 }
 
+// ------------------------------------------------- decode, cluster merge
+//
+// The same step with the splits of one kv head forming one thread-block
+// cluster (CL CTAs of 16 warps): each CTA attends over its contiguous share
+// of the positions, merges its warps in shared memory, and after a cluster
+// barrier every CTA merges a slice of the head group's outputs from all CL
+// CTAs' shared memory (distributed shared memory), so no partial sums go
+// through global memory and no CTA waits for a last arriver.
+constexpr int CL_THREADS = 512, CL_WARPS = 16, CL_PB = 4;
+// opt-in (MLXD_ATTN_CLUSTER=1, read at each launch): on Qwen3-8B it runs as
+// fast as the split-merge kernel, which stays the default
+static bool attn_cluster_on() {
+    const char *e = getenv("MLXD_ATTN_CLUSTER");
+    return e && atoi(e) != 0;
+}
+
+template <int D, int REP>
+__global__ void __launch_bounds__(CL_THREADS, 1) attn_decode_cluster_kernel(AttnDecodeArgs a) {
+    MLXD_TRACE_START
+    namespace cg = cooperative_groups;
+    constexpr int DL = D / 32;
+    using RowT = typename std::conditional<DL == 4, uint2, uint32_t>::type;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CL = (int)cluster.num_blocks();
+    const int split = (int)cluster.block_rank();
+    const int kh = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float s_q[REP][D];
+    __shared__ __align__(16) uint16_t s_knew[D];
+    __shared__ __align__(16) uint16_t s_vnew[D];
+    __shared__ float s_wml[8][REP][2];
+    // the per-warp staging of the q/k vectors and, later, the warps' partial
+    // outputs share one buffer
+    constexpr int WO = 8 * REP * D > CL_WARPS * D ? 8 * REP * D : CL_WARPS * D;
+    __shared__ __align__(16) float s_buf[WO];
+    float (*s_vec)[D] = reinterpret_cast<float (*)[D]>(s_buf);
+    float (*s_wo)[REP][D] = reinterpret_cast<float (*)[REP][D]>(s_buf);
+    __shared__ float s_pm[REP], s_pl[REP];    // this CTA's merged partial
+    __shared__ __align__(16) float s_po[REP][D];
+
+    const int pos = *a.d_pos;
+    const int T = pos + 1;
+    const int lo = a.window > 0 ? max(0, T - a.window) : 0;
+    const int span = T - lo;
+    const int s0 = lo + (int)(((long long)span * split) / CL);
+    const int s1 = lo + (int)(((long long)span * (split + 1)) / CL);
+    const int nc = max(0, min(s1, pos) - s0);          // cached rows of this split
+    const int per = (nc + CL_WARPS - 1) / CL_WARPS;
+    const int w0 = s0 + warp * per, w1 = min(s0 + nc, w0 + per);
+    const uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
+    const uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
+
+    // two batches of cached rows stream before the projection is waited for
+    RowT kb[2][CL_PB], vb[2][CL_PB];
+    auto fetch = [&](const int b, int j0) {
+#pragma unroll
+        for (int u = 0; u < CL_PB; u++) {
+            const int j = min(j0 + u, w1 - 1);
+            if (j >= w0) {
+                const size_t off = (size_t)(j % a.cap) * D + lane * DL;
+                if (b == 0) {
+                    kb[0][u] = *reinterpret_cast<const RowT *>(kc + off);
+                    vb[0][u] = *reinterpret_cast<const RowT *>(vc + off);
+                } else {
+                    kb[1][u] = *reinterpret_cast<const RowT *>(kc + off);
+                    vb[1][u] = *reinterpret_cast<const RowT *>(vc + off);
+                }
+            }
+        }
+    };
+    fetch(0, w0);
+    fetch(1, w0 + CL_PB);
+    pdl_trigger();
+    pdl_wait();
+    MLXD_TRACE_WAITED
+
+    const uint16_t *qkv = a.qkv;
+    const int qstride = D * (a.gate ? 2 : 1);
+    for (int vi = warp; vi < REP + 2; vi += CL_WARPS) {
+        if (vi == REP + 1) {
+            for (int d = lane; d < D; d += 32) s_vnew[d] = qkv[a.qdim + (size_t)(a.hkv + kh) * D + d];
+            continue;
+        }
+        float *v = s_vec[warp];
+        const uint16_t *src = vi < REP ? qkv + (size_t)(kh * REP + vi) * qstride : qkv + a.qdim + (size_t)kh * D;
+        for (int d = lane; d < D; d += 32) v[d] = bf2f(src[d]);
+        __syncwarp();
+        head_norm_rope(v, D, vi < REP ? a.qn : a.kn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
+        if (vi < REP) {
+            for (int d = lane; d < D; d += 32) s_q[vi][d] = v[d];
+        } else {
+            for (int d = lane; d < D; d += 32) s_knew[d] = f2bf(v[d]);
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    if (split == 0) {
+        for (int d = tid; d < D; d += CL_THREADS) {
+            const size_t off = (size_t)(pos % a.cap) * D + d;
+            const_cast<uint16_t *>(kc)[off] = s_knew[d];
+            const_cast<uint16_t *>(vc)[off] = s_vnew[d];
+        }
+    }
+
+    const float qscale = rsqrtf((float)D) * 1.4426950408889634f;
+    float q[REP][DL], m[REP], lsum[REP], o[REP][DL];
+#pragma unroll
+    for (int r = 0; r < REP; r++) {
+        m[r] = -INFINITY;
+        lsum[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DL; i++) {
+            q[r][i] = s_q[r][lane * DL + i] * qscale;
+            o[r][i] = 0.f;
+        }
+    }
+    auto unpack = [&](const RowT &raw, float (&dst)[DL]) {
+        if constexpr (DL == 4) {
+            dst[0] = lo_bf(raw.x); dst[1] = hi_bf(raw.x); dst[2] = lo_bf(raw.y); dst[3] = hi_bf(raw.y);
+        } else {
+            dst[0] = lo_bf(raw); dst[1] = hi_bf(raw);
+        }
+    };
+    // nv (<= CL_PB) positions: independent scores, one reduction pass, one
+    // online-softmax update per head
+    auto visit = [&](const RowT (&kr)[CL_PB], const RowT (&vr)[CL_PB], int nv) {
+        float sc[REP][CL_PB];
+#pragma unroll
+        for (int u = 0; u < CL_PB; u++) {
+            float kf[DL];
+            unpack(kr[u], kf);
+#pragma unroll
+            for (int r = 0; r < REP; r++) {
+                float x = 0.f;
+#pragma unroll
+                for (int i = 0; i < DL; i++) x = fmaf(q[r][i], kf[i], x);
+                sc[r][u] = x;
+            }
+        }
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1)
+#pragma unroll
+            for (int r = 0; r < REP; r++)
+#pragma unroll
+                for (int u = 0; u < CL_PB; u++) sc[r][u] += __shfl_xor_sync(0xffffffffu, sc[r][u], sh);
+#pragma unroll
+        for (int r = 0; r < REP; r++) {
+            float mn = m[r];
+#pragma unroll
+            for (int u = 0; u < CL_PB; u++)
+                if (u < nv) mn = fmaxf(mn, sc[r][u]);
+            const float al = exp2f(m[r] - mn);
+            float ps = 0.f;
+#pragma unroll
+            for (int u = 0; u < CL_PB; u++) {
+                sc[r][u] = u < nv ? exp2f(sc[r][u] - mn) : 0.f;
+                ps += sc[r][u];
+            }
+            lsum[r] = lsum[r] * al + ps;
+#pragma unroll
+            for (int i = 0; i < DL; i++) o[r][i] *= al;
+            m[r] = mn;
+        }
+#pragma unroll
+        for (int u = 0; u < CL_PB; u++) {
+            float vf[DL];
+            unpack(vr[u], vf);
+#pragma unroll
+            for (int r = 0; r < REP; r++)
+#pragma unroll
+                for (int i = 0; i < DL; i++) o[r][i] = fmaf(sc[r][u], vf[i], o[r][i]);
+        }
+    };
+    // the batch index stays a compile-time constant (registers, not local memory)
+    auto step = [&](auto bc, int j0) {
+        constexpr int B = decltype(bc)::value;
+        RowT kr[CL_PB], vr[CL_PB];
+#pragma unroll
+        for (int u = 0; u < CL_PB; u++) {
+            kr[u] = kb[B][u];
+            vr[u] = vb[B][u];
+        }
+        if (j0 + 2 * CL_PB < w1) fetch(B, j0 + 2 * CL_PB);
+        visit(kr, vr, min(CL_PB, w1 - j0));
+    };
+    for (int j0 = w0; j0 < w1; j0 += 2 * CL_PB) {
+        step(std::integral_constant<int, 0>(), j0);
+        if (j0 + CL_PB < w1) step(std::integral_constant<int, 1>(), j0 + CL_PB);
+    }
+    // the new position (its row came from this step's projection)
+    if (warp == CL_WARPS - 1 && pos >= s0 && pos < s1) {
+        RowT kr[CL_PB], vr[CL_PB];
+#pragma unroll
+        for (int u = 0; u < CL_PB; u++) {
+            kr[u] = *reinterpret_cast<const RowT *>(s_knew + lane * DL);
+            vr[u] = *reinterpret_cast<const RowT *>(s_vnew + lane * DL);
+        }
+        visit(kr, vr, 1);
+    }
+    // warps 8..15 hand their state to warps 0..7, which write theirs
+    auto put = [&](int w) {
+#pragma unroll
+        for (int r = 0; r < REP; r++) {
+            if (lane == 0) {
+                s_wml[w][r][0] = m[r];
+                s_wml[w][r][1] = lsum[r];
+            }
+#pragma unroll
+            for (int i = 0; i < DL; i++) s_wo[w][r][lane * DL + i] = o[r][i];
+        }
+    };
+    if (warp >= 8) put(warp - 8);
+    __syncthreads();
+    if (warp < 8) {
+#pragma unroll
+        for (int r = 0; r < REP; r++) {
+            const float m2 = s_wml[warp][r][0], l2 = s_wml[warp][r][1];
+            const float mx = fmaxf(m[r], m2);
+            if (mx != -INFINITY) {
+                const float wa = m[r] == -INFINITY ? 0.f : exp2f(m[r] - mx);
+                const float wb = m2 == -INFINITY ? 0.f : exp2f(m2 - mx);
+#pragma unroll
+                for (int i = 0; i < DL; i++) o[r][i] = o[r][i] * wa + s_wo[warp][r][lane * DL + i] * wb;
+                lsum[r] = lsum[r] * wa + l2 * wb;
+                m[r] = mx;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp < 8) put(warp);
+    __syncthreads();
+    for (int idx = tid; idx < REP * D; idx += CL_THREADS) {
+        const int r = idx / D, d = idx % D;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; w++) mx = fmaxf(mx, s_wml[w][r][0]);
+        float ls = 0.f, os = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            const float e = s_wml[w][r][0] == -INFINITY ? 0.f : exp2f(s_wml[w][r][0] - mx);
+            ls += s_wml[w][r][1] * e;
+            os += s_wo[w][r][d] * e;
+        }
+        s_po[r][d] = os;
+        if (d == 0) {
+            s_pm[r] = mx;
+            s_pl[r] = ls;
+        }
+    }
+    cluster.sync();
+    // this CTA's slice of the head group's outputs, from every CTA's partial
+    const int n_out = REP * D;
+    const int o0 = (int)(((long long)n_out * split) / CL), o1 = (int)(((long long)n_out * (split + 1)) / CL);
+    const int lanes_per = 16;                       // splits handled per output, one per lane
+    for (int base_o = o0; base_o < o1; base_o += CL_THREADS / lanes_per) {
+        const int oi = base_o + tid / lanes_per, sub = tid % lanes_per;
+        float mm = -INFINITY, ll = 0.f, oo = 0.f;
+        if (oi < o1) {
+            const int r = oi / D, d = oi % D;
+            for (int sp = sub; sp < CL; sp += lanes_per) {
+                const float pm = *cluster.map_shared_rank(&s_pm[r], sp);
+                const float pl = *cluster.map_shared_rank(&s_pl[r], sp);
+                const float po = *cluster.map_shared_rank(&s_po[r][d], sp);
+                const float mx = fmaxf(mm, pm);
+                if (mx != -INFINITY) {
+                    const float wa = mm == -INFINITY ? 0.f : exp2f(mm - mx);
+                    const float wb = pm == -INFINITY ? 0.f : exp2f(pm - mx);
+                    ll = ll * wa + pl * wb;
+                    oo = oo * wa + po * wb;
+                    mm = mx;
+                }
+            }
+        }
+#pragma unroll
+        for (int sh = 1; sh < lanes_per; sh <<= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, mm, sh);
+            const float l2 = __shfl_xor_sync(0xffffffffu, ll, sh);
+            const float o2 = __shfl_xor_sync(0xffffffffu, oo, sh);
+            const float mx = fmaxf(mm, m2);
+            if (mx != -INFINITY) {
+                const float wa = mm == -INFINITY ? 0.f : exp2f(mm - mx);
+                const float wb = m2 == -INFINITY ? 0.f : exp2f(m2 - mx);
+                ll = ll * wa + l2 * wb;
+                oo = oo * wa + o2 * wb;
+                mm = mx;
+            }
+        }
+        if (oi < o1 && sub == 0) {
+            const int r = oi / D, d = oi % D;
+            const int h = kh * REP + r;
+            float val = rbf(oo / ll);
+            if (a.gate) {
+                const float gv = bf2f(qkv[(size_t)h * qstride + D + d]);
+                val = rbf(__fmul_rn(val, sigmoid_bf16(gv)));
+            }
+            a.out[(size_t)h * D + d] = f2bf(val);
+        }
+    }
+    // every CTA's shared memory stays until all slices are read
+    cluster.sync();
+    MLXD_TRACE_END(0x32)
+}
+
+template <int D, int REP>
+static int launch_decode_cluster(const AttnDecodeArgs &a, int cl, cudaStream_t st, bool pdl) {
+    auto kern = attn_decode_cluster_kernel<D, REP>;
+    static bool configured = false;
+    if (!configured) {
+        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl, a.hkv);
+    cfg.blockDim = dim3(CL_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
+    return 0;
+}
+
+// cluster size for a head group: 16 CTAs when the device schedules eight of
+// those clusters at once, else 8; 0 when no cluster fits (split-merge runs)
+template <int D, int REP>
+static int cluster_size(int hkv) {
+    static int cached = -1;
+    if (cached < 0) {
+        cached = 0;
+        auto kern = attn_decode_cluster_kernel<D, REP>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        for (int cl : {16, 8}) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(cl, 8);
+            cfg.blockDim = dim3(CL_THREADS);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = cl;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 8) {
+                cached = cl;
+                break;
+            }
+        }
+        cudaGetLastError();
+    }
+    (void)hkv;
+    return cached;
+}
+
+template <int D>
+static int decode_cluster_any(const AttnDecodeArgs &a, int rep, cudaStream_t st, bool pdl) {
+    int cl = 0;
+    switch (rep) {
+    case 1: cl = cluster_size<D, 1>(a.hkv); return cl ? launch_decode_cluster<D, 1>(a, cl, st, pdl) : 1;
+    case 2: cl = cluster_size<D, 2>(a.hkv); return cl ? launch_decode_cluster<D, 2>(a, cl, st, pdl) : 1;
+    case 4: cl = cluster_size<D, 4>(a.hkv); return cl ? launch_decode_cluster<D, 4>(a, cl, st, pdl) : 1;
+    case 8: cl = cluster_size<D, 8>(a.hkv); return cl ? launch_decode_cluster<D, 8>(a, cl, st, pdl) : 1;
+    default: return 1;
+    }
+}
+
 int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
     int rep = a.hq / a.hkv;
     int D = a.rope.D;
+    if (attn_cluster_on()) {
+        // 1: no cluster configuration fits; the split-merge kernel runs
+        int rc = D == 128 ? decode_cluster_any<128>(a, rep, st, pdl)
+                          : D == 64 ? decode_cluster_any<64>(a, rep, st, pdl) : 1;
+        if (rc <= 0) return rc;
+    }
     if (D == 128) return launch_decode<128>(a, rep, st, pdl);
     if (D == 64) return launch_decode<64>(a, rep, st, pdl);
     set_error("attention_decode: head_dim %d not supported", D);

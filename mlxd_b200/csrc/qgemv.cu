@@ -850,6 +850,7 @@ MLXD_DEV void rb_epilogue(const GemvArgs &a, const float *ps, int nbk, int unit,
 
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int pool_items) {
+    MLXD_TRACE_START
     constexpr int G = 64, XW = 8;
     constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -882,6 +883,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
         sbuf = ldg_nc_v4(a.sb8 + (i0 + warp) * 512 + lane * 16);
     }
     pdl_wait();
+    MLXD_TRACE_WAITED
     if (tid < 8) s_zero[tid] = 0u;
     stage_x<G, RB_THREADS, PRO == PRO_RMSNORM>(a, xp, xs, xraw, s_red);
     pdl_trigger();
@@ -962,6 +964,10 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
             if (m) atomicMax(a.amax, m);
         }
     }
+#ifdef MLXD_TRACE
+    __syncthreads();
+    MLXD_TRACE_END(0x40 + EPI)
+#endif
 }
 
 // grid and workspace slots of one launch

@@ -261,6 +261,27 @@ def test_persistent_step_matches_layer_kernels(monkeypatch):
         assert d.max() < 5e-2
 
 
+@pytest.mark.parametrize("family,kw", [(cuda.QWEN3, {}), (cuda.MISTRAL, dict(window=24)),
+                                       (cuda.QWEN3, dict(n_kv_heads=8))])
+def test_cluster_attention_matches_oracle(monkeypatch, family, kw):
+    """Decode attention with the splits of a kv head merged through
+    distributed shared memory (MLXD_ATTN_CLUSTER=1) against the oracle, on a
+    plain cache, a wrapping sliding-window ring and one query head per kv head."""
+    monkeypatch.setenv("MLXD_ATTN_CLUSTER", "1")
+    cfg = qwen3_small(family=family, layers=2, **kw)
+    m, o = synth_pair(cfg, seed=6)
+    rng = np.random.default_rng(6)
+    ids = rng.integers(0, cfg.vocab, 60).tolist()
+    kv = m.new_kv(40 if kw.get("window") else 96)
+    okv = o.new_kv(96)
+    for a0 in range(0, 48, 16):
+        m.forward(kv, ids[a0:a0 + 16], want_logits=False)
+        o.forward(okv, ids[a0:a0 + 16], want_logits=False)
+    for t in ids[48:]:
+        ok, mx, mr = logits_close(bf16_to_f32(m.forward(kv, [t])), o.forward(okv, [t]))
+        assert ok, (mx, mr)
+
+
 def synth_pair_std(cfg, seed, std):
     host = cuda.synth_host_tensors(cfg, seed=seed, std=std)
     return cuda.Model(cfg, host), po.Oracle(orc_config(cfg), host)
