@@ -29,60 +29,87 @@ MLXD_TRACE_BINDER(attention)
 
 constexpr int DEC_THREADS = 256;
 constexpr int DEC_MAX_SPLIT = 64;
+constexpr int DEC_CH = 32;     // cached positions per shared-memory chunk
+constexpr int DEC_PB = 4;      // positions scored together by one warp
 
+template <int D>
+static constexpr size_t dec_smem_bytes() { return (size_t)2 * 2 * DEC_CH * D * 2; }
+
+// One new token, split-KV over (kv head, split) CTAs of 8 warps. Before
+// griddepcontrol.wait, i.e. while the q|k|v projection still runs, each CTA
+// requests its first two chunks of cached K/V rows into shared memory
+// (cp.async; the rows of earlier positions do not depend on this step) and
+// loads the q/k norm weights and the position's cos/sin row. After the wait
+// it normalises and rotates q and k (fwd_attention :591-697), split 0 appends
+// the new K/V row, and the warps score the chunk rows from shared memory (4
+// positions per warp per pass, one online-softmax update per pass). The CTA's
+// warps are merged in shared memory, the split's (max, sum, o) goes to a
+// scratch buffer and the last CTA of a kv head (atomic counter) merges all
+// splits with every load of a pass in flight at once.
 template <int D, int REP>
 __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeArgs a) {
     MLXD_TRACE_START
     constexpr int DL = D / 32;   // dims per lane
     constexpr int NW = DEC_THREADS / 32;
-    constexpr int DEC_U = D == 128 ? 4 : 8;   // positions per warp per pass, loads in flight
     using RowT = typename std::conditional<DL == 4, uint2, uint32_t>::type;
+    extern __shared__ __align__(16) unsigned char dec_smem[];   // [2 chunks][K|V][DEC_CH][D] bf16
     __shared__ float s_vec[NW][D];
     __shared__ float s_q[REP][D];
+    __shared__ float s_nw[2][D];          // q and k norm weights
+    __shared__ float s_cs[D];             // cos/sin of the position (rope_dims/2 pairs)
     __shared__ __align__(16) uint16_t s_knew[D];
     __shared__ __align__(16) uint16_t s_vnew[D];
     __shared__ float s_m[NW][REP], s_l[NW][REP];
     __shared__ float s_o[NW][REP][D];
+    __shared__ float s_w[REP][DEC_MAX_SPLIT];
+    __shared__ float s_lw[REP][DEC_MAX_SPLIT];
     __shared__ int s_last;
 
     const int kh = blockIdx.x, split = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // The position counter and the cache rows of earlier positions were
-    // written by earlier decode steps, so they are read before waiting on the
-    // q/k/v projection of this step: the cache stream overlaps its tail.
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int pos = *a.d_pos;
     const int T = pos + 1;
     const int lo = a.window > 0 ? max(0, T - a.window) : 0;
     const int span = T - lo;
     const int s0 = lo + (int)(((long long)span * split) / a.nsplit);
     const int s1 = lo + (int)(((long long)span * (split + 1)) / a.nsplit);
-    const int per_warp = (s1 - s0 + NW - 1) / NW;
-    const int w0 = s0 + warp * per_warp;
-    const int w1 = min(s1, w0 + per_warp);
+    const int nc = max(0, min(s1, pos) - s0);    // cached rows of this split
+    const int nchunks = (nc + DEC_CH - 1) / DEC_CH;
     const int slot_new = pos % a.cap;
     uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
     uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
 
-    RowT kraw[DEC_U], vraw[DEC_U];
-    auto fetch = [&](int j0) {
-#pragma unroll
-        for (int u = 0; u < DEC_U; u++) {
-            int j = j0 + u;
-            if (j < w1 && j != pos) {
-                const size_t off = (size_t)(j % a.cap) * D + lane * DL;
-                kraw[u] = *reinterpret_cast<const RowT *>(kc + off);
-                vraw[u] = *reinterpret_cast<const RowT *>(vc + off);
-            }
+    // chunk c of the split's cached rows into buffer c & 1 (16 bytes per copy)
+    constexpr int RV = D / 8;                  // 16-byte vectors per row
+    auto issue = [&](int c) {
+        uint16_t *buf = reinterpret_cast<uint16_t *>(dec_smem) + (size_t)(c & 1) * 2 * DEC_CH * D;
+        const int j0 = s0 + c * DEC_CH;
+        const int n = min(DEC_CH, nc - c * DEC_CH);
+        for (int i = tid; i < 2 * n * RV; i += DEC_THREADS) {
+            const int kv = i / (n * RV), rem = i - kv * n * RV, r = rem / RV, v = rem - r * RV;
+            const uint16_t *src = (kv ? vc : kc) + (size_t)((j0 + r) % a.cap) * D + v * 8;
+            cp_async16(buf + ((size_t)kv * DEC_CH + r) * D + v * 8, src);
         }
+        cp_async_commit();
     };
-    fetch(w0);
-    // the next kernel (the o projection) may start streaming its weights now
+    issue(0);
+    issue(1);
+    // norm weights and the rotation row are fixed for this step
+    {
+        const int half = a.rope.rope_dims / 2;
+        const float *cs = a.rope.cs + (size_t)pos * half * 2;
+        for (int i = tid; i < D; i += DEC_THREADS) {
+            s_nw[0][i] = a.qn ? bf2f(a.qn[i]) : 1.f;
+            s_nw[1][i] = a.kn ? bf2f(a.kn[i]) : 1.f;
+            if (i < 2 * half) s_cs[i] = cs[i];
+        }
+    }
     pdl_trigger();
-
     pdl_wait();
     MLXD_TRACE_WAITED
     const uint16_t *qkv = a.qkv;
     const int qstride = D * (a.gate ? 2 : 1);
+    const bool norm = a.qn != nullptr;
     // q heads of this GQA group, the new k (norm + rope) and the new v: one warp each
     for (int vi = warp; vi <= REP + 1; vi += NW) {
         if (vi == REP + 1) {
@@ -94,7 +121,35 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
                                        : qkv + a.qdim + (size_t)kh * D;
         for (int d = lane; d < D; d += 32) v[d] = bf2f(src[d]);
         __syncwarp();
-        head_norm_rope(v, D, vi < REP ? a.qn : a.kn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
+        // head_norm_rope with the staged weights and row: same arithmetic
+        if (norm) {
+            float acc = 0.f;
+            for (int d = lane; d < D; d += 32) acc = fmaf(v[d], v[d], acc);
+            acc = warp_sum(acc);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)D), a.eps)));
+            __syncwarp();
+            const float *nw = s_nw[vi < REP ? 0 : 1];
+            for (int d = lane; d < D; d += 32) v[d] = rbf(__fmul_rn(nw[d], rbf(__fmul_rn(v[d], inv))));
+            __syncwarp();
+        }
+        {
+            const int half = a.rope.rope_dims / 2;
+            float ra[4], rb[4];
+            int cnt = 0;
+            for (int i = lane; i < half; i += 32, cnt++) {
+                const float x1 = v[i], x2 = v[i + half];
+                const float co = s_cs[2 * i], si = s_cs[2 * i + 1];
+                ra[cnt] = rbf(__fsub_rn(__fmul_rn(x1, co), __fmul_rn(x2, si)));
+                rb[cnt] = rbf(__fadd_rn(__fmul_rn(x1, si), __fmul_rn(x2, co)));
+            }
+            __syncwarp();
+            cnt = 0;
+            for (int i = lane; i < half; i += 32, cnt++) {
+                v[i] = ra[cnt];
+                v[i + half] = rb[cnt];
+            }
+            __syncwarp();
+        }
         if (vi < REP) {
             for (int d = lane; d < D; d += 32) s_q[vi][d] = v[d];
         } else {
@@ -104,7 +159,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
     }
     __syncthreads();
     if (split == 0) {
-        for (int d = threadIdx.x; d < D; d += DEC_THREADS) {
+        for (int d = tid; d < D; d += DEC_THREADS) {
             kc[(size_t)slot_new * D + d] = s_knew[d];
             vc[(size_t)slot_new * D + d] = s_vnew[d];
         }
@@ -112,21 +167,17 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
 
     // q in registers, pre-scaled by 1/sqrt(D) * log2(e) for exp2
     const float qscale = rsqrtf((float)D) * 1.4426950408889634f;
-    float q[REP][DL];
-#pragma unroll
-    for (int r = 0; r < REP; r++)
-#pragma unroll
-        for (int i = 0; i < DL; i++) q[r][i] = s_q[r][lane * DL + i] * qscale;
-
-    float m[REP], l[REP], o[REP][DL];
+    float q[REP][DL], m[REP], l[REP], o[REP][DL];
 #pragma unroll
     for (int r = 0; r < REP; r++) {
         m[r] = -INFINITY;
         l[r] = 0.f;
 #pragma unroll
-        for (int i = 0; i < DL; i++) o[r][i] = 0.f;
+        for (int i = 0; i < DL; i++) {
+            q[r][i] = s_q[r][lane * DL + i] * qscale;
+            o[r][i] = 0.f;
+        }
     }
-
     auto unpack = [&](const RowT &raw, float (&dst)[DL]) {
         if constexpr (DL == 4) {
             dst[0] = lo_bf(raw.x); dst[1] = hi_bf(raw.x); dst[2] = lo_bf(raw.y); dst[3] = hi_bf(raw.y);
@@ -134,65 +185,85 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
             dst[0] = lo_bf(raw); dst[1] = hi_bf(raw);
         }
     };
-    const RowT *knew_row = reinterpret_cast<const RowT *>(s_knew + lane * DL);
-    const RowT *vnew_row = reinterpret_cast<const RowT *>(s_vnew + lane * DL);
-
-    for (int j0 = w0; j0 < w1; j0 += DEC_U) {
-        if (j0 != w0) fetch(j0);
-        float kr[DEC_U][DL], vr[DEC_U][DL];
+    // nv (<= DEC_PB) rows: independent scores, one reduction pass, one
+    // online-softmax update per head
+    auto visit = [&](const RowT (&kr)[DEC_PB], const RowT (&vr)[DEC_PB], int nv) {
+        float sc[REP][DEC_PB];
 #pragma unroll
-        for (int u = 0; u < DEC_U; u++) {
-            int j = j0 + u;
-            RowT kk = kraw[u], vv = vraw[u];
-            if (j == pos) {
-                kk = *knew_row;
-                vv = *vnew_row;
-            }
-            if (j < w1) {
-                unpack(kk, kr[u]);
-                unpack(vv, vr[u]);
-            } else {
+        for (int u = 0; u < DEC_PB; u++) {
+            float kf[DL];
+            unpack(kr[u], kf);
 #pragma unroll
-                for (int i = 0; i < DL; i++) kr[u][i] = vr[u][i] = 0.f;
-            }
-        }
-        // U independent scores per head, then one online-softmax update
-#pragma unroll
-        for (int r = 0; r < REP; r++) {
-            float sc[DEC_U];
-#pragma unroll
-            for (int u = 0; u < DEC_U; u++) {
+            for (int r = 0; r < REP; r++) {
                 float x = 0.f;
 #pragma unroll
-                for (int i = 0; i < DL; i++) x = fmaf(q[r][i], kr[u][i], x);
-                sc[u] = x;
+                for (int i = 0; i < DL; i++) x = fmaf(q[r][i], kf[i], x);
+                sc[r][u] = x;
             }
+        }
 #pragma unroll
-            for (int sh = 16; sh > 0; sh >>= 1)
+        for (int sh = 16; sh > 0; sh >>= 1)
 #pragma unroll
-                for (int u = 0; u < DEC_U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], sh);
+            for (int r = 0; r < REP; r++)
+#pragma unroll
+                for (int u = 0; u < DEC_PB; u++) sc[r][u] += __shfl_xor_sync(0xffffffffu, sc[r][u], sh);
+#pragma unroll
+        for (int r = 0; r < REP; r++) {
             float mn = m[r];
 #pragma unroll
-            for (int u = 0; u < DEC_U; u++)
-                if (j0 + u < w1) mn = fmaxf(mn, sc[u]);
-            float alpha = exp2f(m[r] - mn);
+            for (int u = 0; u < DEC_PB; u++)
+                if (u < nv) mn = fmaxf(mn, sc[r][u]);
+            const float al = exp2f(m[r] - mn);
             float ps = 0.f;
-            float pu[DEC_U];
 #pragma unroll
-            for (int u = 0; u < DEC_U; u++) {
-                pu[u] = (j0 + u < w1) ? exp2f(sc[u] - mn) : 0.f;
-                ps += pu[u];
+            for (int u = 0; u < DEC_PB; u++) {
+                sc[r][u] = u < nv ? exp2f(sc[r][u] - mn) : 0.f;
+                ps += sc[r][u];
             }
-            l[r] = l[r] * alpha + ps;
+            l[r] = l[r] * al + ps;
 #pragma unroll
-            for (int i = 0; i < DL; i++) {
-                float acc = o[r][i] * alpha;
-#pragma unroll
-                for (int u = 0; u < DEC_U; u++) acc = fmaf(pu[u], vr[u][i], acc);
-                o[r][i] = acc;
-            }
+            for (int i = 0; i < DL; i++) o[r][i] *= al;
             m[r] = mn;
         }
+#pragma unroll
+        for (int u = 0; u < DEC_PB; u++) {
+            float vf[DL];
+            unpack(vr[u], vf);
+#pragma unroll
+            for (int r = 0; r < REP; r++)
+#pragma unroll
+                for (int i = 0; i < DL; i++) o[r][i] = fmaf(sc[r][u], vf[i], o[r][i]);
+        }
+    };
+    for (int c = 0; c < nchunks; c++) {
+        cp_async_wait<1>();
+        __syncthreads();
+        const uint16_t *buf = reinterpret_cast<const uint16_t *>(dec_smem) + (size_t)(c & 1) * 2 * DEC_CH * D;
+        const int n = min(DEC_CH, nc - c * DEC_CH);
+        const int r0 = warp * DEC_PB;
+        if (r0 < n) {
+            RowT kr[DEC_PB], vr[DEC_PB];
+#pragma unroll
+            for (int u = 0; u < DEC_PB; u++) {
+                const int r = min(r0 + u, n - 1);
+                kr[u] = *reinterpret_cast<const RowT *>(buf + (size_t)r * D + lane * DL);
+                vr[u] = *reinterpret_cast<const RowT *>(buf + (size_t)(DEC_CH + r) * D + lane * DL);
+            }
+            visit(kr, vr, min(DEC_PB, n - r0));
+        }
+        __syncthreads();
+        if (c + 2 < nchunks) issue(c + 2);
+        else cp_async_commit();
+    }
+    // the new position (its row came from this step's projection)
+    if (warp == 0 && pos >= s0 && pos < s1) {
+        RowT kr[DEC_PB], vr[DEC_PB];
+#pragma unroll
+        for (int u = 0; u < DEC_PB; u++) {
+            kr[u] = *reinterpret_cast<const RowT *>(s_knew + lane * DL);
+            vr[u] = *reinterpret_cast<const RowT *>(s_vnew + lane * DL);
+        }
+        visit(kr, vr, 1);
     }
     // merge the warps of this CTA
 #pragma unroll
@@ -206,19 +277,19 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
     }
     __syncthreads();
     float *part = a.part;
-    for (int idx = threadIdx.x; idx < REP * D; idx += DEC_THREADS) {
-        int r = idx / D, d = idx % D;
+    for (int idx = tid; idx < REP * D; idx += DEC_THREADS) {
+        const int r = idx / D, d = idx % D;
         float mx = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NW; w++) mx = fmaxf(mx, s_m[w][r]);
         float ls = 0.f, os = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; w++) {
-            float e = (s_m[w][r] == -INFINITY) ? 0.f : exp2f(s_m[w][r] - mx);
+            const float e = (s_m[w][r] == -INFINITY) ? 0.f : exp2f(s_m[w][r] - mx);
             ls += s_l[w][r] * e;
             os += s_o[w][r][d] * e;
         }
-        int h = kh * REP + r;
+        const int h = kh * REP + r;
         float *rec = part + ((size_t)h * a.nsplit + split) * (D + 2);
         rec[2 + d] = os;
         if (d == 0) {
@@ -226,10 +297,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
             rec[1] = ls;
         }
     }
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int old = atomicAdd(&a.count[kh], 1);
+    if (tid == 0) {
+        __threadfence();
+        const int old = atomicAdd(&a.count[kh], 1);
         s_last = (old == a.nsplit - 1);
     }
     __syncthreads();
@@ -237,57 +308,84 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
         MLXD_TRACE_END(0x30)
         return;
     }
-
     __threadfence();
     // last split of this kv head: merge all splits. The (max, sum) pairs of
     // every split are loaded in parallel, one warp per q head turns them
     // into weights 2^(m_s - m) / L, then each output element is a dot
-    // product over the splits with 32 independent loads in flight.
-    __shared__ float s_w[REP][DEC_MAX_SPLIT];
-    __shared__ float s_lw[REP][DEC_MAX_SPLIT];
+    // product over the splits with all of its loads in flight at once.
     const int ns = a.nsplit;
-    for (int idx = threadIdx.x; idx < REP * ns; idx += DEC_THREADS) {
-        int r = idx / ns, sp = idx % ns;
+    for (int idx = tid; idx < REP * ns; idx += DEC_THREADS) {
+        const int r = idx / ns, sp = idx % ns;
         const float *rec = part + ((size_t)(kh * REP + r) * ns + sp) * (D + 2);
         s_w[r][sp] = __ldcg(rec);
         s_lw[r][sp] = __ldcg(rec + 1);
     }
     __syncthreads();
     for (int r = warp; r < REP; r += NW) {
+        const float *sl = s_lw[r];
         const float m0 = lane < ns ? s_w[r][lane] : -INFINITY;
         const float m1 = lane + 32 < ns ? s_w[r][lane + 32] : -INFINITY;
         const float mx = warp_max(fmaxf(m0, m1));
         const float w0 = m0 == -INFINITY ? 0.f : exp2f(m0 - mx);
         const float w1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mx);
-        const float L = warp_sum(fmaf(w0, lane < ns ? s_lw[r][lane] : 0.f,
-                                      w1 * (lane + 32 < ns ? s_lw[r][lane + 32] : 0.f)));
+        const float L = warp_sum(fmaf(w0, lane < ns ? sl[lane] : 0.f, w1 * (lane + 32 < ns ? sl[lane + 32] : 0.f)));
         const float invL = 1.f / L;
+        __syncwarp();
         if (lane < ns) s_w[r][lane] = w0 * invL;
         if (lane + 32 < ns) s_w[r][lane + 32] = w1 * invL;
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < REP * D; idx += DEC_THREADS) {
-        int r = idx / D, d = idx % D;
-        int h = kh * REP + r;
-        const float *base = part + (size_t)h * ns * (D + 2) + 2 + d;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int sp0 = 0; sp0 < ns; sp0 += 32) {
-            float v[32];
+    // REP*D outputs x ns splits: each thread takes its outputs in pairs and
+    // the splits 16 at a time, with all 32 loads of a round in flight
+    for (int ob = tid; ob < REP * D; ob += 2 * DEC_THREADS) {
+        const int oi[2] = {ob, ob + DEC_THREADS};
+        float acc[2] = {0.f, 0.f};
+        for (int sp0 = 0; sp0 < ns; sp0 += 16) {
+            float v[2][16];
 #pragma unroll
-            for (int u = 0; u < 32; u++) v[u] = sp0 + u < ns ? __ldcg(base + (size_t)(sp0 + u) * (D + 2)) : 0.f;
+            for (int e = 0; e < 2; e++) {
+                const int r = oi[e] / D, d = oi[e] % D;
+                const float *base = part + (size_t)(kh * REP + r) * ns * (D + 2) + 2 + d;
 #pragma unroll
-            for (int u = 0; u < 32; u++)
-                if (sp0 + u < ns) acc[u & 3] = fmaf(s_w[r][sp0 + u], v[u], acc[u & 3]);
+                for (int j = 0; j < 16; j++)
+                    v[e][j] = oi[e] < REP * D && sp0 + j < ns ? __ldcg(base + (size_t)(sp0 + j) * (D + 2)) : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int r = min(oi[e], REP * D - 1) / D;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (sp0 + j < ns) acc[e] = fmaf(s_w[r][sp0 + j], v[e][j], acc[e]);
+            }
         }
-        float val = rbf((acc[0] + acc[1]) + (acc[2] + acc[3]));
-        if (a.gate) {
-            float gv = bf2f(qkv[(size_t)h * qstride + D + d]);
-            val = rbf(__fmul_rn(val, sigmoid_bf16(gv)));
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            if (oi[e] >= REP * D) continue;
+            const int r = oi[e] / D, d = oi[e] % D;
+            const int h = kh * REP + r;
+            float val = rbf(acc[e]);
+            if (a.gate) {
+                const float gv = bf2f(qkv[(size_t)h * qstride + D + d]);
+                val = rbf(__fmul_rn(val, sigmoid_bf16(gv)));
+            }
+            a.out[(size_t)h * D + d] = f2bf(val);
         }
-        a.out[(size_t)h * D + d] = f2bf(val);
     }
+    if (tid == 0) a.count[kh] = 0;
     MLXD_TRACE_END(0x31)
-    if (threadIdx.x == 0) a.count[kh] = 0;
+}
+
+template <int D, int REP>
+static int launch_decode_rep(cudaLaunchConfig_t &cfg, const AttnDecodeArgs &a) {
+    auto kern = attn_decode_kernel<D, REP>;
+    static bool configured = false;
+    if (!configured) {
+        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)dec_smem_bytes<D>()));
+        configured = true;
+    }
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
+    return 0;
 }
 
 template <int D>
@@ -295,6 +393,7 @@ static int launch_decode(const AttnDecodeArgs &a, int rep, cudaStream_t st, bool
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.hkv, a.nsplit);
     cfg.blockDim = dim3(DEC_THREADS);
+    cfg.dynamicSmemBytes = dec_smem_bytes<D>();
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -302,10 +401,10 @@ static int launch_decode(const AttnDecodeArgs &a, int rep, cudaStream_t st, bool
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     switch (rep) {
-    case 1: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 1>, a)); return 0;
-    case 2: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 2>, a)); return 0;
-    case 4: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 4>, a)); return 0;
-    case 8: MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, 8>, a)); return 0;
+    case 1: return launch_decode_rep<D, 1>(cfg, a);
+    case 2: return launch_decode_rep<D, 2>(cfg, a);
+    case 4: return launch_decode_rep<D, 4>(cfg, a);
+    case 8: return launch_decode_rep<D, 8>(cfg, a);
     default: set_error("attention_decode: GQA ratio %d not supported", rep); return -1;
     }
 }
