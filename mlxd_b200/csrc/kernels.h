@@ -38,8 +38,6 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
 // workspace floats one matrix needs (units -> counters)
 size_t gemv_workspace_floats(int rows, int cols, int group, int epi, int sms, int *units);
 int num_sms();
-// nonzero once a decode GEMV gave up waiting on a bulk copy (read and cleared)
-int gemv_wait_timeouts();
 // decode GEMV (EPI_STORE) with its workspace in a static device array instead
 // of a caller-provided allocation; -1 when the matrix needs more than it holds
 int qgemv_static_scratch(const QMat &W, const uint16_t *x, uint16_t *y, cudaStream_t st);

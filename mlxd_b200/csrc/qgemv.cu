@@ -618,202 +618,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv8_kernel(GemvArgs a) {
     }
 }
 
-// Decode fast path with bulk-copy prefetch (group 64, bf16 scales, cols/64 a
-// multiple of 8). One CTA of 8 warps per SM, two CTAs of consecutive launches
-// can share an SM. Each CTA owns a contiguous range of whole row blocks
-// (whole gate|up pairs for SwiGLU), so its packed weights and scale records
-// are two contiguous byte ranges. Warp w takes items w, w+8, w+16, ... of the
-// range (an item is one block of 8 groups of one row block: 4 KB of tiles +
-// 512 B of scale/bias records) and streams them through its own ring of
-// BW_NS shared-memory slots with cp.async.bulk, one mbarrier per slot. The
-// first BW_NS items of every warp are requested before griddepcontrol.wait:
-// weights do not depend on the previous kernel, so they stream while it
-// finishes. Per-warp partial sums of each row block go to shared memory and
-// are added in warp order at the end (no global workspace, deterministic).
-constexpr int BW_THREADS = 256, BW_WARPS = 8, BW_NS = 2;
-constexpr int BW_TILE_BYTES = 4096, BW_SB_BYTES = 512, BW_SLOT = BW_TILE_BYTES + BW_SB_BYTES;
-
-static __device__ int g_gemv_wait_timeout;
-MLXD_TRACE_BINDER(qgemv)
-
-struct BulkSmem {
-    size_t ring, bars, xp, xs, red, xraw, total;
-};
-static __host__ __device__ inline BulkSmem bulk_smem_layout(int cols, int nrb_max, bool norm) {
-    BulkSmem L;
-    const int ng = cols / 64;
-    L.ring = 0;
-    L.bars = L.ring + (size_t)BW_WARPS * BW_NS * BW_SLOT;
-    L.xp = L.bars + (size_t)BW_WARPS * BW_NS * 8;
-    L.xs = L.xp + (size_t)ng * 4 * 8 * 4;
-    L.red = L.xs + (((size_t)ng * 4 + 15) / 16) * 16;
-    L.xraw = L.red + (size_t)nrb_max * BW_WARPS * 16 * 4;
-    L.total = L.xraw + (norm ? (size_t)cols * 2 : 0);
-    return L;
-}
-
-template <int PRO, int EPI>
-__global__ void __launch_bounds__(BW_THREADS, 2) qgemv_bulk_kernel(GemvArgs a, int nrb_max) {
-    MLXD_TRACE_START
-    constexpr int G = 64, XW = 8;
-    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
-    extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(16) uint32_t s_zero[8];
-    __shared__ float s_red[BW_WARPS];
-    __shared__ unsigned long long s_key[BW_WARPS];
-
-    const int ng = a.cols / G, nbk = ng / 8;
-    const BulkSmem L = bulk_smem_layout(a.cols, nrb_max, PRO == PRO_RMSNORM);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
-    const int n_units = a.rows / 16 / UNIT_RB;
-    const int u0 = (int)((long long)n_units * blockIdx.x / gridDim.x);
-    const int u1 = (int)((long long)n_units * (blockIdx.x + 1) / gridDim.x);
-    const int rb0 = u0 * UNIT_RB, nrb = (u1 - u0) * UNIT_RB;
-    const long long i0 = (long long)rb0 * nbk;
-    const int n_items = nrb * nbk;
-    const int my_n = n_items > warp ? (n_items - warp + BW_WARPS - 1) / BW_WARPS : 0;
-
-    unsigned char *ring = smem + L.ring + (size_t)warp * BW_NS * BW_SLOT;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * BW_NS;
-    uint32_t *xp = reinterpret_cast<uint32_t *>(smem + L.xp);
-    float *xs = reinterpret_cast<float *>(smem + L.xs);
-    float *red = reinterpret_cast<float *>(smem + L.red);
-    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem + L.xraw);
-
-    auto issue = [&](int k) {
-        const long long item = i0 + warp + (long long)k * BW_WARPS;
-        const int slot = k % BW_NS;
-        mbar_expect_tx(&bars[slot], BW_SLOT);
-        bulk_g2s(ring + slot * BW_SLOT, a.tiles + item * BW_TILE_BYTES, BW_TILE_BYTES, &bars[slot]);
-        bulk_g2s(ring + slot * BW_SLOT + BW_TILE_BYTES, a.sb8 + item * BW_SB_BYTES, BW_SB_BYTES,
-                 &bars[slot]);
-    };
-    if (lane == 0) {
-        for (int sl = 0; sl < BW_NS; sl++) mbar_init(&bars[sl], 1);
-        fence_mbar_init();
-        for (int k = 0; k < BW_NS && k < my_n; k++) issue(k);
-    }
-    for (int i = tid; i < nrb * BW_WARPS * 16; i += BW_THREADS) red[i] = 0.f;
-    if (tid < 8) s_zero[tid] = 0u;
-    pdl_trigger();
-
-    // ---- prologue: x (optionally RMS-normalised) into the fragment order
-    pdl_wait();
-    MLXD_TRACE_WAITED
-    stage_x<G, BW_THREADS, PRO == PRO_RMSNORM>(a, xp, xs, xraw, s_red);
-
-    // ---- main loop over this warp's items
-    bool timed_out = false;
-    int cur = -1;
-    float y0 = 0.f, y1 = 0.f;
-    auto flush = [&](int rbl) {
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
-        if (t == 0) {
-            red[(rbl * BW_WARPS + warp) * 16 + gq] = y0;
-            red[(rbl * BW_WARPS + warp) * 16 + gq + 8] = y1;
-        }
-    };
-    for (int k = 0; k < my_n; k++) {
-        const int slot = k % BW_NS;
-        if (!mbar_wait(&bars[slot], (uint32_t)(k / BW_NS) & 1u)) timed_out = true;
-        const int li = warp + k * BW_WARPS;
-        const int rbl = li / nbk, bk = li - rbl * nbk;
-        if (rbl != cur) {
-            if (cur >= 0) flush(cur);
-            cur = rbl;
-            y0 = 0.f;
-            y1 = 0.f;
-        }
-        const uint4 *wt = reinterpret_cast<const uint4 *>(ring + slot * BW_SLOT) + lane;
-        const uint4 sv = *(reinterpret_cast<const uint4 *>(ring + slot * BW_SLOT + BW_TILE_BYTES) + lane);
-        const uint32_t *xb = xp + ((size_t)bk * 32 + t) * XW;
-        // four independent accumulators (one per 16-column chunk of a tile)
-        float dj[4][4] = {};
-#pragma unroll
-        for (int p = 0; p < 8; p++) {
-            const uint4 wv = wt[p * 32];
-            const uint4 *xq = reinterpret_cast<const uint4 *>(gq == p ? xb + p * 32 : s_zero);
-            const uint4 xa = xq[0], xc = xq[1];
-            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
-                                  nib_pair(wv.w, j)};
-                mma_bf16_16816(dj[j], af, xv[2 * j], xv[2 * j + 1]);
-            }
-        }
-        float d[4];
-#pragma unroll
-        for (int c = 0; c < 4; c++) d[c] = (dj[0][c] + dj[1][c]) + (dj[2][c] + dj[3][c]);
-        const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
-        const float s00 = lo_bf(sv.x), b00 = hi_bf(sv.x), s01 = lo_bf(sv.y), b01 = hi_bf(sv.y);
-        const float s10 = lo_bf(sv.z), b10 = hi_bf(sv.z), s11 = lo_bf(sv.w), b11 = hi_bf(sv.w);
-        y0 = fmaf(s00, d[0], y0);
-        y0 = fmaf(fmaf(-128.f, s00, b00), xsv.x, y0);
-        y0 = fmaf(s01, d[1], y0);
-        y0 = fmaf(fmaf(-128.f, s01, b01), xsv.y, y0);
-        y1 = fmaf(s10, d[2], y1);
-        y1 = fmaf(fmaf(-128.f, s10, b10), xsv.x, y1);
-        y1 = fmaf(s11, d[3], y1);
-        y1 = fmaf(fmaf(-128.f, s11, b11), xsv.y, y1);
-        // every lane's reads of the slot are done: refill it
-        __syncwarp();
-        if (lane == 0 && k + BW_NS < my_n) {
-            fence_proxy_async();
-            issue(k + BW_NS);
-        }
-    }
-    if (cur >= 0) flush(cur);
-    if (timed_out && lane == 0) atomicExch(&g_gemv_wait_timeout, 1);
-    __syncthreads();
-
-    // ---- epilogue: add the warps' partials in warp order
-    const int nu = nrb / UNIT_RB;
-    unsigned long long best = 0ull;
-    for (int idx = tid; idx < nu * 16; idx += BW_THREADS) {
-        const int ul = idx >> 4, q = idx & 15;
-        float acc[UNIT_RB];
-#pragma unroll
-        for (int u = 0; u < UNIT_RB; u++) {
-            const float *r = red + ((ul * UNIT_RB + u) * BW_WARPS) * 16 + q;
-            float sum = 0.f;
-#pragma unroll
-            for (int w = 0; w < BW_WARPS; w++) sum += r[w * 16];
-            acc[u] = sum;
-        }
-        if constexpr (EPI == EPI_SWIGLU) {
-            a.y[(size_t)(u0 + ul) * 16 + q] = f2bf(swiglu_bf16(rbf(acc[0]), rbf(acc[1])));
-        } else {
-            const int row = (rb0 + ul) * 16 + q;
-            if constexpr (EPI == EPI_ARGMAX) {
-                a.y[row] = f2bf(acc[0]);
-                unsigned long long key = argmax_key(rbf(acc[0]), a.row_offset + row);
-                best = key > best ? key : best;
-            } else {
-                epilogue_row<EPI>(a, row, acc[0]);
-            }
-        }
-    }
-    if constexpr (EPI == EPI_ARGMAX) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-            best = other > best ? other : best;
-        }
-        if (lane == 0) s_key[warp] = best;
-        __syncthreads();
-        if (tid == 0) {
-            unsigned long long m = 0ull;
-            for (int w = 0; w < BW_WARPS; w++) m = s_key[w] > m ? s_key[w] : m;
-            if (m) atomicMax(a.amax, m);
-        }
-    }
-    MLXD_TRACE_END(0x20 + EPI)
-}
-
 // Decode fast path with whole row blocks per CTA (group 64, bf16 scales,
 // cols/64 a multiple of 8). CTA c owns units [c*U/G, (c+1)*U/G) (a unit is a
 // row block, or a gate|up pair for SwiGLU); warp w takes items w, w+16, ...
@@ -822,6 +626,8 @@ __global__ void __launch_bounds__(BW_THREADS, 2) qgemv_bulk_kernel(GemvArgs a, i
 // item's 16 partial sums go to their own place in shared memory and the warp
 // that completes a unit adds them in item order and runs the epilogue: no
 // global workspace, no grid-wide atomics, deterministic.
+MLXD_TRACE_BINDER(qgemv)
+
 constexpr int RB_THREADS = 512, RB_WARPS = 16;
 
 template <int EPI>
@@ -1068,62 +874,6 @@ static int launch_gemv8(GemvArgs a, cudaStream_t st, bool pdl) {
     return 0;
 }
 
-template <int PRO, int EPI>
-static int launch_gemv_bulk(GemvArgs a, cudaStream_t st, bool pdl) {
-    auto kern = qgemv_bulk_kernel<PRO, EPI>;
-    const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
-    const int n_units = a.rows / 16 / unit_rb;
-    int grid = num_sms();
-    if (grid > n_units) grid = n_units;
-    const int nrb_max = (n_units + grid - 1) / grid * unit_rb;
-    const size_t smem = bulk_smem_layout(a.cols, nrb_max, PRO == PRO_RMSNORM).total;
-    if (smem > 200 * 1024) {
-        set_error("qgemv: %d x %d needs %zu bytes of shared memory", a.rows, a.cols, smem);
-        return -1;
-    }
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured = smem;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(BW_THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a, nrb_max));
-    return 0;
-}
-
-static int dispatch_gemv_bulk(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
-#define MLXD_GEMVB_CASE(P, E) \
-    if (pro == P && epi == E) return launch_gemv_bulk<P, E>(a, st, pdl);
-    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_STORE)
-    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_RESIDUAL)
-    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_SWIGLU)
-    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_ARGMAX)
-    MLXD_GEMVB_CASE(PRO_PLAIN, EPI_PARTIAL_F32)
-    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_STORE)
-    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_RESIDUAL)
-    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_SWIGLU)
-    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_ARGMAX)
-    MLXD_GEMVB_CASE(PRO_RMSNORM, EPI_PARTIAL_F32)
-#undef MLXD_GEMVB_CASE
-    set_error("qgemv: bad prologue/epilogue");
-    return -1;
-}
-
-int gemv_wait_timeouts() {
-    int v = 0, z = 0;
-    if (cudaMemcpyFromSymbol(&v, g_gemv_wait_timeout, sizeof v) != cudaSuccess) return -1;
-    if (v) cudaMemcpyToSymbol(g_gemv_wait_timeout, &z, sizeof z);
-    return v;
-}
 
 template <int PRO, int EPI>
 static int launch_gemv8r(GemvArgs a, cudaStream_t st, bool pdl) {
@@ -1215,10 +965,9 @@ static int dispatch_gemv(int pro, int epi, const GemvArgs &a, cudaStream_t st, b
     return -1;
 }
 
-// decode kernel for the group-64 fast layout: 2 = whole row blocks per CTA
-// with register prefetch (default, the fastest inside the decode graph),
-// 0 = register-prefetch stream-K over warps, 1 = bulk-copy prefetch into
-// shared memory; MLXD_GEMV_KIND overrides
+// decode kernel for the group-64 fast layout: whole row blocks per CTA with
+// register prefetch (default, the fastest inside the decode graph), or
+// MLXD_GEMV_KIND=0 for the register-prefetch stream-K split over warps
 static int g_gemv_kind = [] {
     const char *e = getenv("MLXD_GEMV_KIND");
     return e ? atoi(e) : 2;
@@ -1247,8 +996,7 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
     }
     if (W.sb8 && W.fast8()) {
         a.sb8 = W.sb8;
-        if (g_gemv_kind == 1) return dispatch_gemv_bulk(pro, epi, a, st, pdl);
-        if (g_gemv_kind == 2) return dispatch_gemv8r(pro, epi, a, st, pdl);
+        if (g_gemv_kind != 0) return dispatch_gemv8r(pro, epi, a, st, pdl);
         return dispatch_gemv8(pro, epi, a, st, pdl);
     }
     bool f32 = W.sdtype == MLXD_F32;
