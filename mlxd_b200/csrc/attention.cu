@@ -94,6 +94,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
     };
     issue(0);
     issue(1);
+    l2_prefetch_share(a.pf);
     // norm weights and the rotation row are fixed for this step
     {
         const int half = a.rope.rope_dims / 2;
@@ -158,6 +159,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
         __syncwarp();
     }
     __syncthreads();
+#ifdef MLXD_TRACE
+    const unsigned long long tr_prep_ = gtime();
+#endif
     if (split == 0) {
         for (int d = tid; d < D; d += DEC_THREADS) {
             kc[(size_t)slot_new * D + d] = s_knew[d];
@@ -265,6 +269,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
         }
         visit(kr, vr, 1);
     }
+#ifdef MLXD_TRACE
+    const unsigned long long tr_loop_ = gtime();
+#endif
     // merge the warps of this CTA
 #pragma unroll
     for (int r = 0; r < REP; r++) {
@@ -304,6 +311,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) attn_decode_kernel(AttnDecodeA
         s_last = (old == a.nsplit - 1);
     }
     __syncthreads();
+    MLXD_TRACE_REC(tid == 0, 0x38 + s_last, tr_prep_, tr_loop_, gtime())
     if (!s_last) {
         MLXD_TRACE_END(0x30)
         return;

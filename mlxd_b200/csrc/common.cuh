@@ -4,6 +4,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "internal.h"
+
 #ifndef __CUDACC__
 #error "common.cuh is CUDA-only"
 #endif
@@ -71,6 +73,20 @@ MLXD_DEV uint2 ldg_nc_v2(const void *p) {
     uint2 r;
     asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
                  : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
+// weight loads marked first for eviction from L2 once read (each byte of the
+// weight stream is read once per step)
+MLXD_DEV uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+MLXD_DEV uint4 ldg_nc_v4_ef(const void *p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(pol));
     return r;
 }
 
@@ -181,6 +197,31 @@ MLXD_DEV unsigned long long gtime() {
 #define MLXD_TRACE_REC(cond, tag, v1, v2, v3)
 #define MLXD_TRACE_BINDER(name)
 #endif
+
+// ---- L2 prefetch of upcoming weights. A decode kernel is handed byte ranges
+// of the weight stream that later kernels of the step will read; each CTA
+// requests its share into L2 with cp.async.bulk.prefetch.L2 before waiting on
+// its producer, so HBM keeps streaming across kernel boundaries. Ranges and
+// sizes are multiples of 16 bytes (cudaMalloc'd arrays of 16-byte records).
+// (PfList: internal.h)
+MLXD_DEV void l2_prefetch_bulk(const void *p, unsigned int bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// this CTA's share of every range, 64 KB per request, spread over its warps
+MLXD_DEV void l2_prefetch_share(const mlxd::PfList &pf) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane != 0) return;
+    const unsigned G = gridDim.x * gridDim.y, c = blockIdx.x + blockIdx.y * gridDim.x;
+    constexpr unsigned CH = 64u * 1024u;
+    for (int r = 0; r < pf.n; r++) {
+        const unsigned long long n16 = pf.bytes[r] >> 4;
+        const unsigned long long b0 = (n16 * c / G) << 4, b1 = (n16 * (c + 1) / G) << 4;
+        for (unsigned long long o = b0 + (unsigned long long)warp * CH; o < b1; o += (unsigned long long)nw * CH) {
+            const unsigned long long len = b1 - o < CH ? b1 - o : CH;
+            l2_prefetch_bulk(pf.p[r] + o, (unsigned int)len);
+        }
+    }
+}
 
 // Programmatic dependent launch: wait for the producer grid / let the
 // consumer grid be scheduled. No-ops when the launch has no PDL attribute.

@@ -14,6 +14,15 @@ void set_error(const char *fmt, ...);
 bool cuda_ok(cudaError_t e, const char *what);
 #define MLXD_CHECK(call) do { if (!::mlxd::cuda_ok((call), #call)) return -1; } while (0)
 
+// Byte ranges of the weight stream that one decode launch requests into L2
+// (multiples of 16 bytes, 16-byte aligned); n = 0: none.
+constexpr int PF_MAX = 8;
+struct PfList {
+    const unsigned char *p[PF_MAX];
+    unsigned int bytes[PF_MAX];
+    int n;
+};
+
 void *dev_alloc(size_t bytes);      // tracked cudaMalloc (nullptr + error on failure)
 void dev_free(void *p);
 
@@ -31,6 +40,13 @@ struct QMat {
     // same scales/biases regrouped per row block and block of 8 groups, one
     // 16-byte record per lane: (s,b) of rows g, g+8 x groups 2t, 2t+1
     uint8_t *sb8 = nullptr;
+    // integer-MMA decode layout (same eligibility as sb8): tiles whose lane
+    // words carry the u8 A fragments of two m16n8k32 MMAs (low nibbles: group
+    // columns 0-31, high nibbles: 32-63), and per (row block, block of 8
+    // groups) 16 records of 32 B: (s, b) of rows g, g+8 for the four groups
+    // 2j + h (j = 0..3) that lanes (g, 2h) and (g, 2h+1) scale
+    uint8_t *ti8 = nullptr;
+    uint8_t *sbi = nullptr;
     uint16_t *dense = nullptr;  // [rows][cols] bf16 when !quant
     size_t tile_bytes() const { return (size_t)rows / 16 * (cols / group) * 32 * (group / 4); }
     size_t sb_bytes() const {

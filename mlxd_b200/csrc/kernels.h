@@ -21,6 +21,7 @@ struct GemvArgs {
     const uint8_t *tiles;
     const uint8_t *sb;
     const uint8_t *sb8;         // fast-path scale/bias records (set by qgemv)
+    const uint8_t *ti8, *sbi;   // integer-MMA layout (set by qgemv)
     int rows, cols;
     const uint16_t *x;          // bf16 [cols]
     const uint16_t *norm_w;     // PRO_RMSNORM
@@ -33,8 +34,11 @@ struct GemvArgs {
     float *ws;                  // split row-block partials [units][slots][16 or 32]
     int *cnt;                   // per-unit arrival counters (zero between launches)
     int ws_slots;               // set by the launcher
+    PfList pf;                  // weight-stream ranges this launch requests into L2
 };
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl);
+// the arrays (pointer, bytes) that the decode GEMV of W reads, in order
+void qgemv_stream(const QMat &W, std::vector<std::pair<const unsigned char *, size_t>> &out);
 // workspace floats one matrix needs (units -> counters)
 size_t gemv_workspace_floats(int rows, int cols, int group, int epi, int sms, int *units);
 int num_sms();
@@ -85,6 +89,7 @@ struct AttnDecodeArgs {
     int *count;
     int nsplit;
     uint16_t *out;           // [hq*D]
+    PfList pf;               // weight-stream ranges this launch requests into L2
 };
 int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
 // prefill (S queries at positions pos0..): q [S][hq][D]; gate [S][qdim] or null

@@ -197,7 +197,9 @@ int build_qmat(TensorSet &ts, QMat &M, int rows, int cols, int group, const std:
         if (!M.tiles || !M.sb) return -1;
         if (M.fast8()) {
             M.sb8 = (uint8_t *)dev_alloc(M.sb_bytes() * 2);   // 16 B per lane record
-            if (!M.sb8) return -1;
+            M.ti8 = (uint8_t *)dev_alloc(M.tile_bytes());
+            M.sbi = (uint8_t *)dev_alloc(M.sb_bytes());
+            if (!M.sb8 || !M.ti8 || !M.sbi) return -1;
         }
         for (auto &p : pcs) {
             if (p.t.s->dtype != M.sdtype) {
@@ -230,6 +232,8 @@ void free_qmat(QMat &M) {
     dev_free(M.tiles);
     dev_free(M.sb);
     dev_free(M.sb8);
+    dev_free(M.ti8);
+    dev_free(M.sbi);
     dev_free(M.dense);
     M = QMat{};
 }
@@ -343,6 +347,75 @@ int linear_any(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi, co
 
 namespace mlxd {
 
+// The decode step's weight stream: the arrays each decode GEMV reads, in
+// launch order (per layer q|k|v, o, gate|up, down; then lm_head). Launch k
+// requests stream bytes [C_k + LA, C_(k+1) + LA) into L2 (C_k: offset of its
+// own first byte), so the next LA bytes are in flight while it runs; the
+// lm_head launch requests the first LA bytes of the next step. LA is set in MB
+// by MLXD_PF_MB; it is off by default: on Qwen3-8B the step measured 532
+// tokens/s without it, 515 at 32 MB and 499 at 64 MB (the kernels' time is
+// in their prologues and waits, not in their weight loads).
+struct StreamSeg {
+    const unsigned char *p;
+    size_t n, off;
+};
+static size_t pf_lookahead() {
+    static const size_t v = [] {
+        const char *e = getenv("MLXD_PF_MB");
+        return (size_t)(e ? atoi(e) : 0) << 20;
+    }();
+    return v;
+}
+static void pf_window(const std::vector<StreamSeg> &segs, size_t lo, size_t hi, PfList &pf) {
+    pf.n = 0;
+    for (const StreamSeg &g : segs) {
+        const size_t a = std::max(lo, g.off), b = std::min(hi, g.off + g.n);
+        if (a >= b) continue;
+        if (pf.n == PF_MAX) return;
+        const size_t a16 = (a - g.off) & ~(size_t)15, b16 = std::min(g.n, ((b - g.off) + 15) & ~(size_t)15);
+        pf.p[pf.n] = g.p + a16;
+        pf.bytes[pf.n] = (unsigned)(b16 - a16);
+        pf.n++;
+    }
+}
+struct StreamPlan {
+    std::vector<StreamSeg> segs;
+    std::vector<size_t> start;   // per matrix in launch order, then the total
+    size_t la = 0;
+    void build(const mlxd_model *m) {
+        std::vector<std::pair<const unsigned char *, size_t>> arr;
+        auto add = [&](const QMat &q) {
+            start.push_back(segs.empty() ? 0 : segs.back().off + segs.back().n);
+            arr.clear();
+            qgemv_stream(q, arr);
+            for (auto &x : arr) {
+                const size_t off = segs.empty() ? 0 : segs.back().off + segs.back().n;
+                segs.push_back(StreamSeg{x.first, x.second, off});
+            }
+        };
+        for (const Layer &L : m->L) {
+            add(L.qkv);
+            add(L.o);
+            add(L.gateup);
+            add(L.down);
+        }
+        add(m->lm);
+        start.push_back(segs.empty() ? 0 : segs.back().off + segs.back().n);
+        la = pf_lookahead();
+    }
+    // the window of the GEMV of matrix k (launch order)
+    void gemv(size_t k, PfList &pf) const {
+        pf.n = 0;
+        if (!la) return;
+        const size_t K = start.size() - 1;
+        if (k + 1 == K) {   // lm_head: the head of the next step's stream
+            pf_window(segs, 0, std::min(la, start[K]), pf);
+            return;
+        }
+        pf_window(segs, start[k] + la, std::min(start[k + 1] + la, start[K]), pf);
+    }
+};
+
 // one token through every layer with the fused decode kernels
 static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool want_logits,
                        uint16_t *logits_out, bool argmax, cudaStream_t st, bool pdl) {
@@ -352,9 +425,12 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
     if (want_logits && megastep_ready(m, kv)) return megastep_launch(m, kv, ids_dev, logits_out, argmax, st);
     if (embed_rows(m->embed, H, c.qgroup, c.vocab, ids_dev, 1, m->h, st)) return -1;
     size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
+    StreamPlan plan;
+    plan.build(m);
     for (int l = 0; l < c.layers; l++) {
         Layer &L = m->L[l];
         GemvArgs a = {};
+        plan.gemv(4 * l, a.pf);
         a.ws = m->gemv_ws;
         a.cnt = m->gemv_cnt;
         a.x = m->h;
@@ -383,6 +459,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         ad.out = m->att;
         if (attention_decode(ad, st, pdl)) return -1;
         GemvArgs o = {};
+        plan.gemv(4 * l + 1, o.pf);
         o.ws = m->gemv_ws;
         o.cnt = m->gemv_cnt;
         o.x = m->att;
@@ -397,6 +474,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
             if (qgemv(L.o, PRO_PLAIN, EPI_RESIDUAL, o, st, pdl)) return -1;
         }
         GemvArgs gu = {};
+        plan.gemv(4 * l + 2, gu.pf);
         gu.ws = m->gemv_ws;
         gu.cnt = m->gemv_cnt;
         gu.x = m->h1;
@@ -405,6 +483,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         gu.y = m->act;
         if (qgemv(L.gateup, PRO_RMSNORM, EPI_SWIGLU, gu, st, pdl)) return -1;
         GemvArgs dn = {};
+        plan.gemv(4 * l + 3, dn.pf);
         dn.ws = m->gemv_ws;
         dn.cnt = m->gemv_cnt;
         dn.x = m->act;
@@ -421,6 +500,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
     }
     if (want_logits) {
         GemvArgs lg = {};
+        plan.gemv(4 * (size_t)c.layers, lg.pf);
         lg.ws = m->gemv_ws;
         lg.cnt = m->gemv_cnt;
         lg.x = m->h;

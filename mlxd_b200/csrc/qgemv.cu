@@ -119,6 +119,64 @@ __global__ void repack_sb8_kernel(const uint16_t *__restrict__ s, const uint16_t
     *reinterpret_cast<uint4 *>(sb8 + (((size_t)drb * nbk + bk) * 32 + lane) * 16) = o;
 }
 
+// Integer-MMA tile layout (group 64): lane L = 4g + t of tile (rb, grp) holds
+// four words; word i covers row g + 8(i&1) and group columns
+// k = 16(i>>1) + 4t + j (j = 0..3, byte j): its low nibble is q(row, k), its
+// high nibble q(row, k + 32). Masking the low nibbles gives the u8 A fragment
+// of mma.m16n8k32 for columns 0-31 of the group, shifting and masking the
+// high nibbles the one for columns 32-63.
+__global__ void repack_i8_kernel(const uint32_t *__restrict__ w, int ldw, int r0, int c0, int nrb,
+                                 int ng, uint8_t *__restrict__ tiles, int dst_rb0, int dst_rb_stride,
+                                 int dst_ng) {
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)nrb * ng * 32) return;
+    const int lane = (int)(idx & 31);
+    const int g = (int)((idx >> 5) % ng);
+    const int rb = (int)((idx >> 5) / ng);
+    const int gq = lane >> 2, t = lane & 3;
+    auto q = [&](int row, int k) -> uint32_t {
+        const int col = c0 + g * 64 + k;
+        return (w[(size_t)row * ldw + (col >> 3)] >> (4 * (col & 7))) & 0xFu;
+    };
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int row = r0 + rb * 16 + gq + 8 * (i & 1);
+        const int kb = 16 * (i >> 1) + 4 * t;
+        uint32_t v = 0;
+        for (int j = 0; j < 4; j++) v |= (q(row, kb + j) | (q(row, kb + j + 32) << 4)) << (8 * j);
+        o[i] = v;
+    }
+    const size_t tile = (size_t)(dst_rb0 + dst_rb_stride * rb) * dst_ng + g;
+    *reinterpret_cast<uint4 *>(tiles + (tile * 32 + lane) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// scale/bias records of the integer-MMA layout: record (rb, bk, g, h), 32 B:
+// for j = 0..3, (s, b) of row g then of row g + 8 for group 8bk + 2j + h
+__global__ void repack_sbi_kernel(const uint16_t *__restrict__ s, const uint16_t *__restrict__ b,
+                                  int lds, int r0, int g0, int nrb, int nbk,
+                                  uint8_t *__restrict__ sbi, int dst_rb0, int dst_rb_stride) {
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)nrb * nbk * 16) return;
+    const int h = (int)(idx & 1);
+    const int gq = (int)((idx >> 1) & 7);
+    const int bk = (int)((idx >> 4) % nbk);
+    const int rb = (int)((idx >> 4) / nbk);
+    const int rowA = r0 + rb * 16 + gq, rowB = rowA + 8;
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const size_t grp = (size_t)g0 + bk * 8 + 2 * j + h;
+        const size_t ia = (size_t)rowA * lds + grp, ib = (size_t)rowB * lds + grp;
+        o[2 * j] = (uint32_t)s[ia] | ((uint32_t)b[ia] << 16);
+        o[2 * j + 1] = (uint32_t)s[ib] | ((uint32_t)b[ib] << 16);
+    }
+    const size_t rec = ((size_t)(dst_rb0 + dst_rb_stride * rb) * nbk + bk) * 16 + gq * 2 + h;
+    uint4 *dst = reinterpret_cast<uint4 *>(sbi + rec * 32);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
 int repack_quant(QMat &dst, const uint32_t *w, const void *s, const void *b, int sdtype, int ldw,
                  int lds, int r0, int nrows, int c0, int dst_rb0, int dst_rb_stride,
                  cudaStream_t st) {
@@ -153,6 +211,15 @@ int repack_quant(QMat &dst, const uint32_t *w, const void *s, const void *b, int
         size_t n8 = (size_t)nrb * nbk * 32;
         repack_sb8_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, st>>>(
             (const uint16_t *)s, (const uint16_t *)b, lds, r0, c0 / G, nrb, nbk, dst.sb8, dst_rb0,
+            dst_rb_stride);
+    }
+    if (dst.ti8 && dst.sbi) {
+        repack_i8_kernel<<<blocks, 256, 0, st>>>(w, ldw, r0, c0, nrb, ng, dst.ti8, dst_rb0,
+                                                 dst_rb_stride, ng);
+        const int nbk = ng / 8;
+        const size_t ni = (size_t)nrb * nbk * 16;
+        repack_sbi_kernel<<<(unsigned)((ni + 255) / 256), 256, 0, st>>>(
+            (const uint16_t *)s, (const uint16_t *)b, lds, r0, c0 / G, nrb, nbk, dst.sbi, dst_rb0,
             dst_rb_stride);
     }
     MLXD_CHECK(cudaGetLastError());
@@ -688,6 +755,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
         for (int p = 0; p < 8; p++) wbuf[p] = ldg_nc_v4(pw + p * 512);
         sbuf = ldg_nc_v4(a.sb8 + (i0 + warp) * 512 + lane * 16);
     }
+    l2_prefetch_share(a.pf);
     pdl_wait();
     MLXD_TRACE_WAITED
     if (tid < 8) s_zero[tid] = 0u;
@@ -773,6 +841,316 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
 #ifdef MLXD_TRACE
     __syncthreads();
     MLXD_TRACE_END(0x40 + EPI)
+#endif
+}
+
+// ---------------------------------------------- integer-MMA decode GEMV
+//
+// mlx's qmv computes, per output row, sum over groups of
+//     scale * sum_k(x_k * q_k) + bias * sum_k(x_k)
+// in f32 (src/engine/forward.c:17-32). Here sum_k(x_k * q_k) runs on the
+// integer tensor pipe: x is written once per launch as a fixed-point vector
+// X_k = round(x_k * 2^(20-E)) with E the exponent of max|x|, so |X_k| < 2^21,
+// and X_k is split into three int8 digits X = d0 + 128 d1 + 16384 d2
+// (d0, d1 in [0, 127], d2 signed). A bf16 x_k within 13 binades of the
+// largest is exact in X; smaller ones round at 2^(E-21), below the rounding
+// of an f32 sum of the products. mma.m16n8k32 (u8 weights x s8 digits, s32
+// accumulate, exact) then takes 32 columns of 16 rows per instruction with
+// its 8 N columns holding (group parity, digit): the two groups of a pair
+// share one accumulator, each confined to its own columns. Per pair, a
+// lane holds two digit columns of one group for rows g and g+8; it
+// recombines them in f32 and applies that group's scale, and lanes with
+// even t also add bias * sum(x over the group). The exponent factor is
+// applied once per item, and the quad sum gives the item's 16 partials.
+// Two MMAs and about twenty instructions per 512-byte tile, against four
+// bf16 MMAs and ~67 instructions for the bf16 fragment kernel above.
+constexpr int I8_DIGITS = 3;
+constexpr int I8_ENT = 4 * I8_DIGITS;   // B-fragment entries per group: (digit, t)
+
+// smem: raw x (bf16 [cols]), then B fragments xb[group][digit][t] (16 B:
+// b0, b1 of the low-nibble MMA, b0, b1 of the high-nibble MMA), then per
+// block of 8 groups the bias multipliers xsum4[t][j] (the group sum for even
+// t, 0 for odd t), a 16-byte zero entry, the item partials and the counters
+struct I8Smem {
+    size_t xb, xsum, zero, pool, cnt, total;
+};
+static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int pool_units) {
+    I8Smem L;
+    const int ng = cols / 64;
+    L.xb = (((size_t)cols * 2 + 15) / 16) * 16;
+    L.xsum = L.xb + (size_t)ng * I8_ENT * 16;
+    L.zero = L.xsum + (size_t)(ng / 8) * 64;
+    L.pool = L.zero + 16;
+    L.cnt = L.pool + (size_t)pool_items * 64;
+    L.total = L.cnt + (size_t)pool_units * 4;
+    return L;
+}
+
+// x (optionally RMS-normalised with the oracle's association) into the
+// fixed-point B fragments; returns the factor 2^(E-20) (NaN when x holds a
+// non-finite value, so that the outputs are NaN as in the f32 sum)
+template <int NT, bool NORM>
+MLXD_DEV float stage_x_i8(const GemvArgs &a, unsigned char *smem, float *s_red, unsigned *s_max) {
+    constexpr int MAXV = 4;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = a.cols, nv = n / 8, ng = n / 64;
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem);
+    const I8Smem L = i8_layout(n, 0, 0);
+    uint32_t *xbw = reinterpret_cast<uint32_t *>(smem + L.xb);
+    float *xsum4 = reinterpret_cast<float *>(smem + L.xsum);
+    const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm_w);
+    if (tid < 4) reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;
+    for (int base = 0; base < nv; base += NT * MAXV) {
+        uint4 v[MAXV];
+#pragma unroll
+        for (int j = 0; j < MAXV; j++) {
+            const int i = base + tid + j * NT;
+            if (i < nv) v[j] = x4[i];
+        }
+#pragma unroll
+        for (int j = 0; j < MAXV; j++) {
+            const int i = base + tid + j * NT;
+            if (i < nv) reinterpret_cast<uint4 *>(xraw)[i] = v[j];
+        }
+    }
+    if (NORM) {
+        __syncthreads();
+        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
+        float acc = 0.f;
+        if (tid < Ta)
+            for (int i = tid; i < n; i += Ta) {
+                const float f = bf2f(xraw[i]);
+                acc = fmaf(f, f, acc);
+            }
+        acc = warp_sum(acc);
+        if (lane == 0) s_red[warp] = acc;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < NT / 32; w++) tot += s_red[w];
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
+        for (int base = 0; base < nv; base += NT * MAXV) {
+            uint4 wv[MAXV];
+#pragma unroll
+            for (int j = 0; j < MAXV; j++) {
+                const int i = base + tid + j * NT;
+                if (i < nv) wv[j] = w4[i];
+            }
+#pragma unroll
+            for (int j = 0; j < MAXV; j++) {
+                const int i = base + tid + j * NT;
+                if (i >= nv) continue;
+                uint4 xv = reinterpret_cast<const uint4 *>(xraw)[i];
+                uint32_t *xs4 = &xv.x;
+                const uint32_t ws4[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float lo = rbf(__fmul_rn(lo_bf(ws4[q]), rbf(__fmul_rn(lo_bf(xs4[q]), inv))));
+                    const float hi = rbf(__fmul_rn(hi_bf(ws4[q]), rbf(__fmul_rn(hi_bf(xs4[q]), inv))));
+                    xs4[q] = pack_bf2(lo, hi);
+                }
+                reinterpret_cast<uint4 *>(xraw)[i] = xv;
+            }
+        }
+    }
+    __syncthreads();
+    // group sums (bias multipliers) and the largest magnitude
+    unsigned mx = 0u;
+    for (int g = warp; g < ng; g += NT / 32) {
+        const uint32_t v = reinterpret_cast<const uint32_t *>(xraw)[g * 32 + lane];
+        mx = max(mx, max(v & 0x7fffu, (v >> 16) & 0x7fffu));
+        const float sm = warp_sum(lo_bf(v) + hi_bf(v));
+        if (lane == 0) {
+            const int bk = g >> 3, j = (g & 7) >> 1, h = g & 1;
+            xsum4[bk * 16 + (2 * h) * 4 + j] = sm;
+            xsum4[bk * 16 + (2 * h + 1) * 4 + j] = 0.f;
+        }
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if (lane == 0) s_max[warp] = mx;
+    __syncthreads();
+    mx = 0u;
+#pragma unroll
+    for (int w = 0; w < NT / 32; w++) mx = max(mx, s_max[w]);
+    int E = (int)(mx >> 7) - 127;            // exponent of the largest |x|
+    if (E < -100) E = -100;                  // zero / subnormal: digits round to 0
+    const float sc = __int_as_float((127 + 20 - E) << 23);
+    const float lscale = mx >= 0x7f80u ? __int_as_float(0x7fc00000) : __int_as_float((127 + E - 20) << 23);
+    // digit planes: item (g, m, b, t) covers group columns 32m + 16b + 4t + j
+    for (int it = tid; it < ng * 16; it += NT) {
+        const int t = it & 3, b = (it >> 2) & 1, m = (it >> 3) & 1, g = it >> 4;
+        const int k0 = g * 64 + 32 * m + 16 * b + 4 * t;
+        const uint2 raw = *reinterpret_cast<const uint2 *>(xraw + k0);
+        const float xf[4] = {lo_bf(raw.x), hi_bf(raw.x), lo_bf(raw.y), hi_bf(raw.y)};
+        uint32_t R[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int X = __float2int_rn(__fmul_rn(xf[j], sc));
+            R[j] = ((uint32_t)X & 0x7fu) | (((uint32_t)X << 1) & 0x7f00u) | (((uint32_t)X << 2) & 0xff0000u);
+        }
+        const uint32_t lo01 = __byte_perm(R[0], R[1], 0x5140), lo23 = __byte_perm(R[2], R[3], 0x5140);
+        const uint32_t p0 = __byte_perm(lo01, lo23, 0x5410);
+        const uint32_t p1 = __byte_perm(lo01, lo23, 0x7632);
+        const uint32_t p2 = __byte_perm(__byte_perm(R[0], R[1], 0x0062), __byte_perm(R[2], R[3], 0x0062), 0x5410);
+        uint32_t *e = xbw + ((size_t)g * I8_ENT + t) * 4 + 2 * m + b;
+        e[0] = p0;
+        e[16] = p1;
+        e[32] = p2;
+    }
+    __syncthreads();
+    return lscale;
+}
+
+MLXD_DEV void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// whole row blocks per CTA, as qgemv8r_kernel: warp w takes items w, w+16,
+// ... of the CTA's units and holds the next one (4 KB of tiles + its two
+// 16-byte scale/bias words) in registers while computing the current one
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int pool_items) {
+    MLXD_TRACE_START
+    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ float s_red[RB_WARPS];
+    __shared__ unsigned s_max[RB_WARPS];
+    __shared__ unsigned long long s_key[RB_WARPS];
+    const int nbk = a.cols / 512;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
+    const int n_units = a.rows / 16 / UNIT_RB;
+    const int u0 = (int)((long long)n_units * blockIdx.x / gridDim.x);
+    const int u1 = (int)((long long)n_units * (blockIdx.x + 1) / gridDim.x);
+    const int ipu = nbk * UNIT_RB;
+    const int n = (u1 - u0) * ipu;
+    const long long i0 = (long long)u0 * ipu;
+    const I8Smem L = i8_layout(a.cols, pool_items, (u1 - u0));
+    float *pool = reinterpret_cast<float *>(smem_raw + L.pool);
+    int *s_cnt = reinterpret_cast<int *>(smem_raw + L.cnt);
+    for (int i = tid; i < u1 - u0; i += RB_THREADS) s_cnt[i] = 0;
+
+    // the warp's first item streams while the previous kernel finishes, and
+    // later kernels' weights are requested into L2
+    const uint64_t pol = l2_policy_evict_first();
+    const uint8_t *sbl = a.sbi + (gq * 2 + (t >> 1)) * 32;
+    uint4 wbuf[8];
+    uint4 sb0 = make_uint4(0, 0, 0, 0), sb1 = sb0;
+    if (warp < n) {
+        const uint8_t *pw = a.ti8 + (i0 + warp) * 4096 + lane * 16;
+#pragma unroll
+        for (int p = 0; p < 8; p++) wbuf[p] = ldg_nc_v4_ef(pw + p * 512, pol);
+        sb0 = ldg_nc_v4_ef(sbl + (i0 + warp) * 512, pol);
+        sb1 = ldg_nc_v4_ef(sbl + (i0 + warp) * 512 + 16, pol);
+    }
+    l2_prefetch_share(a.pf);
+    pdl_wait();
+    MLXD_TRACE_WAITED
+    const float lscale = stage_x_i8<RB_THREADS, PRO == PRO_RMSNORM>(a, smem_raw, s_red, s_max);
+    pdl_trigger();
+#ifdef MLXD_TRACE
+    const unsigned long long tr_staged_ = gtime();
+#endif
+
+    // this lane's B-fragment entries: group parity h = gq >> 2, digit gq & 3
+    // (digit 3 and the other parity read the zero entry)
+    const int dg = gq & 3, hh = gq >> 2;
+    const uint4 *xb = reinterpret_cast<const uint4 *>(smem_raw + L.xb);
+    const uint4 *zero = reinterpret_cast<const uint4 *>(smem_raw + L.zero);
+    const bool act0 = dg < I8_DIGITS && hh == 0, act1 = dg < I8_DIGITS && hh == 1;
+    const uint4 *xb0 = act0 ? xb + dg * 4 + t : zero;
+    const uint4 *xb1 = act1 ? xb + I8_ENT + dg * 4 + t : zero;
+    const int st0 = act0 ? 2 * I8_ENT : 0, st1 = act1 ? 2 * I8_ENT : 0;   // per group pair
+    const float lt = (t & 1) ? lscale * 16384.f : lscale;
+    const float *xsum4 = reinterpret_cast<const float *>(smem_raw + L.xsum) + t * 4;
+    constexpr uint32_t M4 = 0x0f0f0f0fu;
+
+    unsigned long long best = 0ull;
+    for (int k = warp; k < n; k += RB_WARPS) {
+        const bool pre = k + RB_WARPS < n;
+        const uint8_t *pwn = a.ti8 + (i0 + k + RB_WARPS) * 4096 + lane * 16;
+        const int unit = k / ipu;
+        const int iu = k - unit * ipu;
+        const int bk = iu % nbk;
+        const uint4 sA = sb0, sB = sb1;
+        if (pre) {
+            sb0 = ldg_nc_v4_ef(sbl + (i0 + k + RB_WARPS) * 512, pol);
+            sb1 = ldg_nc_v4_ef(sbl + (i0 + k + RB_WARPS) * 512 + 16, pol);
+        }
+        const float4 xs = *reinterpret_cast<const float4 *>(xsum4 + bk * 16);
+        const float xsj[4] = {xs.x, xs.y, xs.z, xs.w};
+        const uint32_t sbw[8] = {sA.x, sA.y, sA.z, sA.w, sB.x, sB.y, sB.z, sB.w};
+        float y0 = 0.f, y1 = 0.f, yb0 = 0.f, yb1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int p = 2 * j + u;
+                const uint4 wv = wbuf[p];
+                if (pre) wbuf[p] = ldg_nc_v4_ef(pwn + p * 512, pol);
+                const int pair = bk * 4 + j;
+                const uint4 bq = u == 0 ? xb0[pair * st0] : xb1[pair * st1];
+                const uint32_t alo[4] = {wv.x & M4, wv.y & M4, wv.z & M4, wv.w & M4};
+                const uint32_t ahi[4] = {(wv.x >> 4) & M4, (wv.y >> 4) & M4, (wv.z >> 4) & M4,
+                                         (wv.w >> 4) & M4};
+                mma_u8s8_16832(acc, alo, bq.x, bq.y);
+                mma_u8s8_16832(acc, ahi, bq.z, bq.w);
+            }
+            const float a0 = fmaf((float)acc[1], 128.f, (float)acc[0]);
+            const float a1 = fmaf((float)acc[3], 128.f, (float)acc[2]);
+            const uint32_t r0 = sbw[2 * j], r1 = sbw[2 * j + 1];
+            y0 = fmaf(lo_bf(r0), a0, y0);
+            y1 = fmaf(lo_bf(r1), a1, y1);
+            yb0 = fmaf(hi_bf(r0), xsj[j], yb0);
+            yb1 = fmaf(hi_bf(r1), xsj[j], yb1);
+        }
+        y0 = fmaf(y0, lt, yb0);
+        y1 = fmaf(y1, lt, yb1);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        float *ps = pool + (size_t)unit * ipu * 16;
+        if (t == 0) {
+            ps[iu * 16 + gq] = y0;
+            ps[iu * 16 + gq + 8] = y1;
+        }
+        __syncwarp();
+        int done = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            done = atomicAdd(&s_cnt[unit], 1) + 1 == ipu;
+        }
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done) {
+            __threadfence_block();
+            rb_epilogue<EPI>(a, ps, nbk, u0 + unit, lane, best);
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0) s_key[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < RB_WARPS; w++) m = s_key[w] > m ? s_key[w] : m;
+            if (m) atomicMax(a.amax, m);
+        }
+    }
+#ifdef MLXD_TRACE
+    const unsigned long long tr_loop_ = gtime();
+    __syncthreads();
+    MLXD_TRACE_REC(tid == 0, 0x60 + EPI, tr_staged_, tr_loop_, gtime())
+    MLXD_TRACE_END(0x50 + EPI)
 #endif
 }
 
@@ -910,6 +1288,57 @@ static int launch_gemv8r(GemvArgs a, cudaStream_t st, bool pdl) {
     return 0;
 }
 
+template <int PRO, int EPI>
+static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
+    auto kern = qgemv_i8_kernel<PRO, EPI>;
+    const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
+    const int n_units = a.rows / 16 / unit_rb;
+    int grid = num_sms();
+    if (grid > n_units) grid = n_units;
+    const int per = (n_units + grid - 1) / grid;
+    const int pool_items = per * unit_rb * (a.cols / 512);
+    const size_t smem = i8_layout(a.cols, pool_items, per).total;
+    if (smem > 200 * 1024) {
+        set_error("qgemv: %d x %d needs %zu bytes of shared memory", a.rows, a.cols, smem);
+        return -1;
+    }
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(RB_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a, pool_items));
+    return 0;
+}
+
+static int dispatch_gemv_i8(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
+#define MLXD_GEMVI_CASE(P, E) \
+    if (pro == P && epi == E) return launch_gemv_i8<P, E>(a, st, pdl);
+    MLXD_GEMVI_CASE(PRO_PLAIN, EPI_STORE)
+    MLXD_GEMVI_CASE(PRO_PLAIN, EPI_RESIDUAL)
+    MLXD_GEMVI_CASE(PRO_PLAIN, EPI_SWIGLU)
+    MLXD_GEMVI_CASE(PRO_PLAIN, EPI_ARGMAX)
+    MLXD_GEMVI_CASE(PRO_PLAIN, EPI_PARTIAL_F32)
+    MLXD_GEMVI_CASE(PRO_RMSNORM, EPI_STORE)
+    MLXD_GEMVI_CASE(PRO_RMSNORM, EPI_RESIDUAL)
+    MLXD_GEMVI_CASE(PRO_RMSNORM, EPI_SWIGLU)
+    MLXD_GEMVI_CASE(PRO_RMSNORM, EPI_ARGMAX)
+    MLXD_GEMVI_CASE(PRO_RMSNORM, EPI_PARTIAL_F32)
+#undef MLXD_GEMVI_CASE
+    set_error("qgemv: bad prologue/epilogue");
+    return -1;
+}
+
 static int dispatch_gemv8r(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
 #define MLXD_GEMVR_CASE(P, E) \
     if (pro == P && epi == E) return launch_gemv8r<P, E>(a, st, pdl);
@@ -965,12 +1394,12 @@ static int dispatch_gemv(int pro, int epi, const GemvArgs &a, cudaStream_t st, b
     return -1;
 }
 
-// decode kernel for the group-64 fast layout: whole row blocks per CTA with
-// register prefetch (default, the fastest inside the decode graph), or
-// MLXD_GEMV_KIND=0 for the register-prefetch stream-K split over warps
+// decode kernel for the group-64 fast layout: the integer-MMA kernel over the
+// ti8/sbi layout (default, 3), the bf16-fragment kernel with whole row blocks
+// per CTA (MLXD_GEMV_KIND=2) or its stream-K split over warps (0)
 static int g_gemv_kind = [] {
     const char *e = getenv("MLXD_GEMV_KIND");
-    return e ? atoi(e) : 2;
+    return e ? atoi(e) : 3;
 }();
 
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl) {
@@ -994,6 +1423,11 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
         set_error("qgemv: rows %d not a multiple of the row block", W.rows);
         return -1;
     }
+    if (W.ti8 && W.sbi && W.fast8() && g_gemv_kind == 3) {
+        a.ti8 = W.ti8;
+        a.sbi = W.sbi;
+        return dispatch_gemv_i8(pro, epi, a, st, pdl);
+    }
     if (W.sb8 && W.fast8()) {
         a.sb8 = W.sb8;
         if (g_gemv_kind != 0) return dispatch_gemv8r(pro, epi, a, st, pdl);
@@ -1006,6 +1440,20 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
                                   : dispatch_gemv<32, false>(pro, epi, a, st, pdl);
     set_error("qgemv: group size %d not supported", W.group);
     return -1;
+}
+
+void qgemv_stream(const QMat &W, std::vector<std::pair<const unsigned char *, size_t>> &out) {
+    if (!W.quant) return;
+    if (W.ti8 && W.sbi && W.fast8() && g_gemv_kind == 3) {
+        out.emplace_back(W.ti8, W.tile_bytes());
+        out.emplace_back(W.sbi, W.sb_bytes());
+    } else if (W.sb8 && W.fast8()) {
+        out.emplace_back(W.tiles, W.tile_bytes());
+        out.emplace_back(W.sb8, W.sb_bytes() * 2);
+    } else {
+        out.emplace_back(W.tiles, W.tile_bytes());
+        out.emplace_back(W.sb, W.sb_bytes());
+    }
 }
 
 // ------------------------------------------ decode GEMV on static scratch
