@@ -792,6 +792,12 @@ static int decode_cluster_any(const AttnDecodeArgs &a, int rep, cudaStream_t st,
 int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
     int rep = a.hq / a.hkv;
     int D = a.rope.D;
+    {
+        // tensor-core kernel with a cluster per kv head (attention_tc.cu);
+        // 1: it does not serve this shape
+        const int rc = attention_decode_tc(a, st, pdl);
+        if (rc <= 0) return rc;
+    }
     if (attn_cluster_on()) {
         // 1: no cluster configuration fits; the split-merge kernel runs
         int rc = D == 128 ? decode_cluster_any<128>(a, rep, st, pdl)

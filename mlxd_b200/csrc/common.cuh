@@ -165,12 +165,18 @@ MLXD_DEV unsigned long long gtime() {
 #define MLXD_TRACE_START unsigned long long tr_t0_ = gtime(), tr_t1_ = 0;
 #define MLXD_TRACE_WAITED tr_t1_ = gtime();
 #define MLXD_TRACE_RESTART tr_t0_ = gtime();
+MLXD_DEV unsigned smid_() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
 #define MLXD_TRACE_END(tag)                                                                  \
     if (g_trace && threadIdx.x == 0) {                                                       \
         unsigned long long i_ = atomicAdd(g_trace, 1ull);                                    \
         if (i_ < (1ull << 20)) {                                                             \
             unsigned long long *r_ = g_trace + 4 + i_ * 4;                                   \
-            r_[0] = ((unsigned long long)(tag) << 32) | (blockIdx.x + blockIdx.y * gridDim.x); \
+            r_[0] = ((unsigned long long)(tag) << 32) | ((unsigned long long)smid_() << 20) |  \
+                    (blockIdx.x + blockIdx.y * gridDim.x);                                   \
             r_[1] = tr_t0_;                                                                  \
             r_[2] = tr_t1_;                                                                  \
             r_[3] = gtime();                                                                 \
@@ -187,6 +193,7 @@ MLXD_DEV unsigned long long gtime() {
             r_[3] = (v3);                                                                    \
         }                                                                                    \
     }
+#define MLXD_TRACE_T(var) const unsigned long long var = gtime();
 #define MLXD_TRACE_BINDER(name) \
     void trace_bind_##name(unsigned long long *p) { cudaMemcpyToSymbol(g_trace, &p, sizeof p); }
 #else
@@ -196,6 +203,7 @@ MLXD_DEV unsigned long long gtime() {
 #define MLXD_TRACE_END(tag)
 #define MLXD_TRACE_REC(cond, tag, v1, v2, v3)
 #define MLXD_TRACE_BINDER(name)
+#define MLXD_TRACE_T(var)
 #endif
 
 // ---- L2 prefetch of upcoming weights. A decode kernel is handed byte ranges

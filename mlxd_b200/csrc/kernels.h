@@ -92,6 +92,9 @@ struct AttnDecodeArgs {
     PfList pf;               // weight-stream ranges this launch requests into L2
 };
 int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
+// the tensor-core decode kernel (one cluster per kv head): 0 launched, 1 not
+// applicable to the shape or device, -1 error
+int attention_decode_tc(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
 // prefill (S queries at positions pos0..): q [S][hq][D]; gate [S][qdim] or null
 int attention_prefill(const uint16_t *q, int S, int pos0, const uint16_t *kc,
                       const uint16_t *vc, int cap, int window, int hq, int hkv, int D,

@@ -13,8 +13,8 @@
 // Every CTA owns a static share of every phase: whole row blocks (gate|up
 // pairs for SwiGLU) of each projection, one (kv head, split) of the
 // attention. Warp w of a CTA takes items w, w+16, ... of its share (an item
-// is one block of 8 groups of one row block: 4 KB of packed weights + 512 B of
-// scale/bias records). A warp's items of all projection phases, in order, form
+// is one block of 8 groups of one row block: 4 KB of packed weights in the
+// integer-MMA layout + 512 B of scale/bias records, as qgemv_i8_kernel). A warp's items of all projection phases, in order, form
 // its weight stream, which it keeps two items ahead with cp.async into two
 // private shared-memory buffers: the copy of the item after next is issued as
 // soon as an item is consumed, across phase boundaries (and over the
@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemv_i8.cuh"
 #include "kernels.h"
 
 namespace mlxd {
@@ -51,7 +52,7 @@ constexpr int MS_KB = 4;                            // cached positions per warp
 constexpr unsigned long long MS_WAIT_NS = 500000000ull;   // give up on a wait after 0.5 s
 
 struct MsMat {
-    const uint8_t *tiles, *sb8;
+    const uint8_t *tiles, *sbr;   // integer-MMA tiles and scale/bias records
     int rows, cols;
 };
 struct MsLayer {
@@ -102,22 +103,28 @@ static __constant__ MsConst c_ms;
 #define MA (c_ms.a)
 
 struct MsSmem {
-    size_t wbuf, scratch, pool, cnt, actx, total;
+    size_t wbuf, xb, xsum, zero, u, cnt, actx, total;
 };
-// scratch is shared by the phase input (xp, xs, raw x) and the attention
-// working set (q, new k/v, per-warp partials); pool holds the partial sums
-// of every item of the CTA's largest phase share
+// The phase input staged as integer-MMA B fragments (xb, xsum, zero, as
+// gemv_i8.cuh); u holds the raw x while it is staged and the item partials
+// of the CTA's share afterwards; the attention working set (q, new k/v,
+// per-warp partials) reuses the space from xb on.
 static __host__ __device__ inline MsSmem ms_layout(int max_cols, int H, int D, int rep, int pool_items,
                                                    int pool_units) {
     MsSmem L;
     const int ng = max_cols / 64;
-    size_t gem = (size_t)ng * 128 + (((size_t)ng * 4 + 15) / 16) * 16 + (size_t)H * 2;
-    size_t att = (size_t)rep * D * 4 + (size_t)D * 4 + (size_t)MS_WARPS * D * 4 + (size_t)8 * rep * 8 +
-                 (size_t)8 * rep * D * 4;
+    const size_t att = (size_t)rep * D * 4 + (size_t)D * 4 + (size_t)MS_WARPS * D * 4 + (size_t)8 * rep * 8 +
+                       (size_t)8 * rep * D * 4;
+    const size_t xraw = (((size_t)(max_cols > H ? max_cols : H) * 2 + 15) / 16) * 16;
+    const size_t pool = (size_t)pool_items * 64;
     L.wbuf = 0;
-    L.scratch = (size_t)MS_WARPS * 2 * MS_ITEM;
-    L.pool = L.scratch + (((gem > att ? gem : att) + 15) / 16) * 16;
-    L.cnt = L.pool + (size_t)pool_items * 16 * 4;
+    L.xb = (size_t)MS_WARPS * 2 * MS_ITEM;
+    L.xsum = L.xb + (size_t)ng * I8_ENT * 16;
+    L.zero = L.xsum + (size_t)(ng / 8) * 64 + 64;
+    L.u = L.zero + 16;
+    size_t end = L.u + (xraw > pool ? xraw : pool);
+    if (L.xb + att > end) end = L.xb + att;
+    L.cnt = ((end + 15) / 16) * 16;
     L.actx = L.cnt + (((size_t)pool_units * 4 + 15) / 16) * 16;
     L.total = L.actx + (size_t)3 * D * 4;
     return L;
@@ -200,7 +207,7 @@ struct MsStream {
     int g;               // projection phase of the issue cursor; -1 when done
     int j, m;            // next item of the warp's share in it, share size
     long long i0;        // first item of the CTA's share in the matrix
-    const uint8_t *tiles, *sb8;
+    const uint8_t *tiles, *sbr;
     long long issued, consumed;
 };
 MLXD_DEV MsMat ms_proj(int g, int &unit_rb, int &ph) {
@@ -228,7 +235,7 @@ MLXD_DEV void ms_seek(MsStream &st, int warp) {
         st.m = n > warp ? (n - warp + MS_WARPS - 1) / MS_WARPS : 0;
         st.i0 = (long long)u0 * urb * (M.cols / 512);
         st.tiles = M.tiles;
-        st.sb8 = M.sb8;
+        st.sbr = M.sbr;
         if (st.j < st.m) return;
         st.g++;
         st.j = 0;
@@ -243,7 +250,7 @@ MLXD_DEV void ms_issue(MsStream &st, unsigned char *wbuf, int warp, int lane) {
         const uint8_t *t = st.tiles + item * 4096 + lane * 16;
 #pragma unroll
         for (int p = 0; p < 8; p++) cp_async16(dst + p * 512, t + p * 512);
-        cp_async16(dst + 4096, st.sb8 + item * 512 + lane * 16);
+        cp_async16(dst + 4096, st.sbr + item * 512 + lane * 16);
         st.j++;
         ms_seek(st, warp);
     }
@@ -251,89 +258,13 @@ MLXD_DEV void ms_issue(MsStream &st, unsigned char *wbuf, int warp, int lane) {
     st.issued++;
 }
 
-// phase input into the fragment order, consumer threads only: one 16-byte
-// load of x (and of the norm weights) per thread and pass, the RMSNorm with
-// the oracle's association (Ta element-strided partials, butterfly within
-// each warp, warp totals in order), and the per-group sums of x from eight
-// lanes' shuffles (a group of 64 is eight consecutive threads' vectors)
-// one copy of the code for every phase (instruction-cache friendly): the
-// norm is on when nw is given
-__device__ __noinline__ void ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float eps, uint32_t *xp,
-                                        float *xs, uint16_t *xraw, float *s_red) {
-    const bool NORM = nw != nullptr;
-    constexpr int G = 64, XW = 8, MAXV = 4;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nv = cols / 8;
-    const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(nw);
-    float inv = 1.f;
-    if (NORM) {
-        // raw x for the strided sum of squares
-        for (int base = 0; base < nv; base += MS_CT * MAXV) {
-            uint4 v[MAXV];
-#pragma unroll
-            for (int j = 0; j < MAXV; j++) {
-                const int i = base + tid + j * MS_CT;
-                if (i < nv) v[j] = x4[i];
-            }
-#pragma unroll
-            for (int j = 0; j < MAXV; j++) {
-                const int i = base + tid + j * MS_CT;
-                if (i < nv) reinterpret_cast<uint4 *>(xraw)[i] = v[j];
-            }
-        }
-        __syncthreads();
-        const int Ta = cols >= 1024 ? 256 : (cols >= 256 ? 128 : 32);
-        float acc = 0.f;
-        if (tid < Ta)
-            for (int i = tid; i < cols; i += Ta) {
-                const float f = bf2f(xraw[i]);
-                acc = fmaf(f, f, acc);
-            }
-        acc = warp_sum(acc);
-        if (lane == 0) s_red[warp] = acc;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < MS_WARPS; w++) tot += s_red[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)cols), eps)));
-    }
-    for (int base = 0; base < nv; base += MS_CT * MAXV) {
-        uint4 v[MAXV], wv[MAXV];
-#pragma unroll
-        for (int j = 0; j < MAXV; j++) {
-            const int i = base + tid + j * MS_CT;
-            if (i < nv) {
-                v[j] = NORM ? reinterpret_cast<const uint4 *>(xraw)[i] : x4[i];
-                if (NORM) wv[j] = w4[i];
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < MAXV; j++) {
-            const int i = base + tid + j * MS_CT;
-            uint32_t e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-            float gs = 0.f;
-            if (i < nv) {
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    if (NORM) {
-                        const uint32_t wq = q == 0 ? wv[j].x : q == 1 ? wv[j].y : q == 2 ? wv[j].z : wv[j].w;
-                        const float lo = rbf(__fmul_rn(lo_bf(wq), rbf(__fmul_rn(lo_bf(e[q]), inv))));
-                        const float hi = rbf(__fmul_rn(hi_bf(wq), rbf(__fmul_rn(hi_bf(e[q]), inv))));
-                        e[q] = pack_bf2(lo, hi);
-                    }
-                    put_pair(xp, G, XW, i * 8 + 2 * q, e[q]);
-                    gs += lo_bf(e[q]) + hi_bf(e[q]);
-                }
-            }
-            // eight consecutive threads hold one group of 64
-            gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-            gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-            gs += __shfl_xor_sync(0xffffffffu, gs, 4);
-            if (i < nv && (i & 7) == 0) xs[i >> 3] = gs;
-        }
-    }
-    __syncthreads();
+// phase input as integer-MMA B fragments (one copy of the code for every
+// phase, instruction-cache friendly; the norm is on when nw is given)
+__device__ __noinline__ float ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float eps,
+                                         unsigned char *smem, const MsSmem &Lo, float *s_red, unsigned *s_max) {
+    return i8_stage<MS_CT>(x, nw, cols, eps, reinterpret_cast<uint16_t *>(smem + Lo.u),
+                           reinterpret_cast<uint32_t *>(smem + Lo.xb), reinterpret_cast<float *>(smem + Lo.xsum),
+                           reinterpret_cast<uint32_t *>(smem + Lo.zero), s_red, s_max);
 }
 
 enum { MS_EPI_STORE = 0, MS_EPI_RESIDUAL = 1, MS_EPI_SWIGLU = 2, MS_EPI_LOGITS = 3 };
@@ -384,8 +315,7 @@ MLXD_DEV void ms_unit_epilogue(int EPI, const MsGemvOut &o, const float *ps, int
 // pending); each consumed buffer is refilled with the stream's item after
 // next at once.
 MLXD_DEV void ms_gemv(int EPI, const MsMat M, int u0, int n, const MsGemvOut o, MsStream &st,
-                      unsigned char *wbuf, const uint32_t *xp, const float *xs, const uint32_t *s_zero,
-                      int *s_cnt, float *pool) {
+                      unsigned char *wbuf, const I8Lane &IL, int *s_cnt, float *pool) {
     const int UNIT_RB = EPI == MS_EPI_SWIGLU ? 2 : 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = lane & 3, gq = lane >> 2;
     const int nbk = M.cols / 512;
@@ -395,52 +325,26 @@ MLXD_DEV void ms_gemv(int EPI, const MsMat M, int u0, int n, const MsGemvOut o, 
         ms_issue(st, wbuf, warp, lane);
 #endif
         cp_async_wait<1>();
+        __syncwarp();   // the lanes' copies of the item, seen by every lane
 
-        const unsigned char *buf = wbuf + (st.consumed & 1) * MS_ITEM + lane * 16;
+        const unsigned char *buf = wbuf + (st.consumed & 1) * MS_ITEM;
         const int unit = k / ipu;
         const int iu = k - unit * ipu;
         const int bk = iu % nbk;
-        const uint32_t *xb = xp + ((size_t)bk * 32 + t) * 8;
-        // four independent accumulators (one per 16-column chunk of a tile)
-        float dj[4][4] = {};
+        uint4 w[8];
 #pragma unroll
-        for (int p = 0; p < 8; p++) {
-            const uint4 wv = *reinterpret_cast<const uint4 *>(buf + p * 512);
-            const uint4 *xq = reinterpret_cast<const uint4 *>(gq == p ? xb + p * 32 : s_zero);
-            const uint4 xa = xq[0], xc = xq[1];
-            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                uint32_t af[4] = {nib_pair(wv.x, j), nib_pair(wv.z, j), nib_pair(wv.y, j),
-                                  nib_pair(wv.w, j)};
-                mma_bf16_16816(dj[j], af, xv[2 * j], xv[2 * j + 1]);
-            }
-        }
-        float d[4];
-#pragma unroll
-        for (int c = 0; c < 4; c++) d[c] = (dj[0][c] + dj[1][c]) + (dj[2][c] + dj[3][c]);
-        const uint4 sv = *reinterpret_cast<const uint4 *>(buf + 4096);
-        const float2 xsv = *reinterpret_cast<const float2 *>(xs + bk * 8 + 2 * t);
-        const float s00 = lo_bf(sv.x), b00 = hi_bf(sv.x), s01 = lo_bf(sv.y), b01 = hi_bf(sv.y);
-        const float s10 = lo_bf(sv.z), b10 = hi_bf(sv.z), s11 = lo_bf(sv.w), b11 = hi_bf(sv.w);
-        float y0 = s00 * d[0];
-        y0 = fmaf(fmaf(-128.f, s00, b00), xsv.x, y0);
-        y0 = fmaf(s01, d[1], y0);
-        y0 = fmaf(fmaf(-128.f, s01, b01), xsv.y, y0);
-        float y1 = s10 * d[2];
-        y1 = fmaf(fmaf(-128.f, s10, b10), xsv.x, y1);
-        y1 = fmaf(s11, d[3], y1);
-        y1 = fmaf(fmaf(-128.f, s11, b11), xsv.y, y1);
-        // this lane's reads of the buffer are done: refill it
+        for (int p = 0; p < 8; p++) w[p] = *reinterpret_cast<const uint4 *>(buf + p * 512 + lane * 16);
+        const unsigned char *rec = buf + 4096 + (gq * 2 + (t >> 1)) * 32;
+        const uint4 sA = *reinterpret_cast<const uint4 *>(rec);
+        const uint4 sB = *reinterpret_cast<const uint4 *>(rec + 16);
+        // every lane's reads of the buffer are done: refill it
+        __syncwarp();
         st.consumed++;
 #if MS_AHEAD == 2
         ms_issue(st, wbuf, warp, lane);
 #endif
-        // the quad's four lanes hold disjoint groups of rows g, g+8
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        float y0, y1;
+        i8_item(w, sA, sB, IL, bk, y0, y1, I8NoRefill{});
         float *ps = pool + (size_t)unit * ipu * 16;
         if (t == 0) {
             ps[iu * 16 + gq] = y0;
@@ -790,26 +694,24 @@ __global__ void __launch_bounds__(MS_CT, 1) megastep_kernel(const MsCall kv, int
                                                             int pool_units) {
     using RowT = typename std::conditional<D == 128, uint2, uint32_t>::type;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(16) uint32_t s_zero[8];
     __shared__ float s_red[MS_WARPS];
+    __shared__ unsigned s_max[MS_WARPS];
     __shared__ volatile int s_dead;
     const MsSmem Lo = ms_layout(max_cols, MA.H, D, REP, pool_items, pool_units);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned char *wbuf = smem + Lo.wbuf + (size_t)warp * 2 * MS_ITEM;
-    unsigned char *scratch = smem + Lo.scratch;
-    float *pool = reinterpret_cast<float *>(smem + Lo.pool);
+    unsigned char *scratch = smem + Lo.xb;
+    float *pool = reinterpret_cast<float *>(smem + Lo.u);
     int *s_cnt = reinterpret_cast<int *>(smem + Lo.cnt);
     float *actx = reinterpret_cast<float *>(smem + Lo.actx);
     const int pos = *kv.d_pos;
     const int G = gridDim.x;
-    uint32_t *xp = reinterpret_cast<uint32_t *>(scratch);
-    const int ngmax = max_cols / 64;
-    float *xs = reinterpret_cast<float *>(scratch + (size_t)ngmax * 128);
-    uint16_t *xraw = reinterpret_cast<uint16_t *>(scratch + (size_t)ngmax * 128 +
-                                                  (((size_t)ngmax * 4 + 15) / 16) * 16);
+    const uint32_t *xbw = reinterpret_cast<const uint32_t *>(smem + Lo.xb);
+    const float *xsum4 = reinterpret_cast<const float *>(smem + Lo.xsum);
+    const uint32_t *zero16 = reinterpret_cast<const uint32_t *>(smem + Lo.zero);
+    float lsc;
 
     for (int i = tid; i < pool_units; i += MS_CT) s_cnt[i] = 0;
-    if (tid < 8) s_zero[tid] = 0u;
     if (tid == 0) s_dead = 0;
 
     int ph = 0;
@@ -866,10 +768,12 @@ __global__ void __launch_bounds__(MS_CT, 1) megastep_kernel(const MsCall kv, int
         const MsLayer &Ly = c_ms.layers[l];
         // q|k|v; then the warp fetches its first cached rows of the attention
         phase_wait();
-        ms_stage_x(MA.h, Ly.ln1, Ly.qkv.cols, MA.eps, xp, xs, xraw, s_red);
+        lsc = ms_stage_x(MA.h, Ly.ln1, Ly.qkv.cols, MA.eps, smem, Lo, s_red, s_max);
+        MLXD_TRACE_T(tr_st0_)
         n = ms_share(Ly.qkv, 1, ph, u0);
-        ms_gemv(MS_EPI_STORE, Ly.qkv, u0, n, MsGemvOut{MA.qkv, nullptr, nullptr, 0}, st, wbuf, xp, xs, s_zero,
-                              s_cnt, pool);
+        ms_gemv(MS_EPI_STORE, Ly.qkv, u0, n, MsGemvOut{MA.qkv, nullptr, nullptr, 0}, st, wbuf,
+                i8_lane(xbw, xsum4, zero16, lsc), s_cnt, pool);
+                MLXD_TRACE_REC(tid == 0, 0x2000 + ph, tr_t1_, tr_st0_, gtime())
 
         const MsAttnShare ash = ms_attn_share(ph + 1, pos, kv.window);
         RowT kb[MS_KB], vb[MS_KB];
@@ -887,32 +791,40 @@ __global__ void __launch_bounds__(MS_CT, 1) megastep_kernel(const MsCall kv, int
         phase_done();
         // o projection + residual
         phase_wait();
-        ms_stage_x(MA.att, nullptr, Ly.o.cols, MA.eps, xp, xs, xraw, s_red);
+        lsc = ms_stage_x(MA.att, nullptr, Ly.o.cols, MA.eps, smem, Lo, s_red, s_max);
+        MLXD_TRACE_T(tr_st1_)
         n = ms_share(Ly.o, 1, ph, u0);
-        ms_gemv(MS_EPI_RESIDUAL, Ly.o, u0, n, MsGemvOut{MA.h1, MA.h, nullptr, 0}, st, wbuf, xp, xs, s_zero,
-                                 s_cnt, pool);
+        ms_gemv(MS_EPI_RESIDUAL, Ly.o, u0, n, MsGemvOut{MA.h1, MA.h, nullptr, 0}, st, wbuf,
+                i8_lane(xbw, xsum4, zero16, lsc), s_cnt, pool);
+                MLXD_TRACE_REC(tid == 0, 0x2000 + ph, tr_t1_, tr_st1_, gtime())
         phase_done();
         // gate|up + SwiGLU
         phase_wait();
-        ms_stage_x(MA.h1, Ly.ln2, Ly.gu.cols, MA.eps, xp, xs, xraw, s_red);
+        lsc = ms_stage_x(MA.h1, Ly.ln2, Ly.gu.cols, MA.eps, smem, Lo, s_red, s_max);
+        MLXD_TRACE_T(tr_st2_)
         n = ms_share(Ly.gu, 2, ph, u0);
-        ms_gemv(MS_EPI_SWIGLU, Ly.gu, u0, n, MsGemvOut{MA.act, nullptr, nullptr, 0}, st, wbuf, xp, xs, s_zero,
-                               s_cnt, pool);
+        ms_gemv(MS_EPI_SWIGLU, Ly.gu, u0, n, MsGemvOut{MA.act, nullptr, nullptr, 0}, st, wbuf,
+                i8_lane(xbw, xsum4, zero16, lsc), s_cnt, pool);
+                MLXD_TRACE_REC(tid == 0, 0x2000 + ph, tr_t1_, tr_st2_, gtime())
         phase_done();
         // down + residual
         phase_wait();
-        ms_stage_x(MA.act, nullptr, Ly.down.cols, MA.eps, xp, xs, xraw, s_red);
+        lsc = ms_stage_x(MA.act, nullptr, Ly.down.cols, MA.eps, smem, Lo, s_red, s_max);
+        MLXD_TRACE_T(tr_st3_)
         n = ms_share(Ly.down, 1, ph, u0);
-        ms_gemv(MS_EPI_RESIDUAL, Ly.down, u0, n, MsGemvOut{MA.h, MA.h1, nullptr, 0}, st, wbuf, xp, xs, s_zero,
-                                 s_cnt, pool);
+        ms_gemv(MS_EPI_RESIDUAL, Ly.down, u0, n, MsGemvOut{MA.h, MA.h1, nullptr, 0}, st, wbuf,
+                i8_lane(xbw, xsum4, zero16, lsc), s_cnt, pool);
+                MLXD_TRACE_REC(tid == 0, 0x2000 + ph, tr_t1_, tr_st3_, gtime())
         phase_done();
     }
     // final norm + lm_head (+ greedy key)
     phase_wait();
-    ms_stage_x(MA.h, MA.fnorm, MA.lm.cols, MA.eps, xp, xs, xraw, s_red);
+    lsc = ms_stage_x(MA.h, MA.fnorm, MA.lm.cols, MA.eps, smem, Lo, s_red, s_max);
+    MLXD_TRACE_T(tr_st4_)
     n = ms_share(MA.lm, 1, ph, u0);
-    ms_gemv(MS_EPI_LOGITS, MA.lm, u0, n, MsGemvOut{kv.logits, nullptr, kv.amax, 0}, st, wbuf, xp, xs, s_zero,
-                           s_cnt, pool);
+    ms_gemv(MS_EPI_LOGITS, MA.lm, u0, n, MsGemvOut{kv.logits, nullptr, kv.amax, 0}, st, wbuf,
+            i8_lane(xbw, xsum4, zero16, lsc), s_cnt, pool);
+            MLXD_TRACE_REC(tid == 0, 0x2000 + ph, tr_t1_, tr_st4_, gtime())
     cp_async_wait<0>();
     phase_done();
     // step end (step_finish_kernel): token from the key, next position
@@ -986,7 +898,7 @@ static int ms_launch_any(int D, int rep, const MsCall &kv, const MegaState &S, c
     MLXD_MS_DISPATCH(ms_launch, kv, S, st)
 }
 
-static MsMat ms_mat(const QMat &q) { return MsMat{q.tiles, q.sb8, q.rows, q.cols}; }
+static MsMat ms_mat(const QMat &q) { return MsMat{q.ti8, q.sbi, q.rows, q.cols}; }
 
 static bool ms_eligible(const mlxd_model *m) {
     // opt-in (MLXD_MEGASTEP=1 when the model is created): on Qwen3-8B the
@@ -999,7 +911,7 @@ static bool ms_eligible(const mlxd_model *m) {
     const int rep = m->hq / m->hkv;
     if (!(c.head_dim == 128 || c.head_dim == 64) || !(rep == 1 || rep == 2 || rep == 4 || rep == 8))
         return false;
-    auto ok = [](const QMat &q) { return q.quant && q.fast8() && q.sb8 && q.rows % 16 == 0; };
+    auto ok = [](const QMat &q) { return q.quant && q.fast8() && q.ti8 && q.sbi && q.rows % 16 == 0; };
     for (const Layer &L : m->L)
         if (!ok(L.qkv) || !ok(L.o) || !ok(L.gateup) || !ok(L.down) || L.gateup.rows % 32) return false;
     return ok(m->lm);

@@ -1294,6 +1294,7 @@ namespace mlxd {
 void trace_bind_qgemv(unsigned long long *p);
 void trace_bind_attention(unsigned long long *p);
 void trace_bind_megastep(unsigned long long *p);
+void trace_bind_attention_tc(unsigned long long *p);
 }
 // timeline trace of the decode kernels (trace builds only): buf is a device
 // buffer of 4 + 4 * 2^20 u64, word 0 zeroed by the caller
@@ -1301,6 +1302,7 @@ extern "C" int mlxd_cuda_trace_bind(void *buf) {
     mlxd::trace_bind_qgemv((unsigned long long *)buf);
     mlxd::trace_bind_attention((unsigned long long *)buf);
     mlxd::trace_bind_megastep((unsigned long long *)buf);
+    mlxd::trace_bind_attention_tc((unsigned long long *)buf);
     return 0;
 }
 #endif

@@ -20,6 +20,7 @@
 #include <stdlib.h>
 
 #include "common.cuh"
+#include "gemv_i8.cuh"
 #include "kernels.h"
 
 namespace mlxd {
@@ -864,9 +865,6 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
 // applied once per item, and the quad sum gives the item's 16 partials.
 // Two MMAs and about twenty instructions per 512-byte tile, against four
 // bf16 MMAs and ~67 instructions for the bf16 fragment kernel above.
-constexpr int I8_DIGITS = 3;
-constexpr int I8_ENT = 4 * I8_DIGITS;   // B-fragment entries per group: (digit, t)
-
 // smem: raw x (bf16 [cols]), then B fragments xb[group][digit][t] (16 B:
 // b0, b1 of the low-nibble MMA, b0, b1 of the high-nibble MMA), then per
 // block of 8 groups the bias multipliers xsum4[t][j] (the group sum for even
@@ -884,130 +882,6 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
     L.cnt = L.pool + (size_t)pool_items * 64;
     L.total = L.cnt + (size_t)pool_units * 4;
     return L;
-}
-
-// x (optionally RMS-normalised with the oracle's association) into the
-// fixed-point B fragments; returns the factor 2^(E-20) (NaN when x holds a
-// non-finite value, so that the outputs are NaN as in the f32 sum)
-template <int NT, bool NORM>
-MLXD_DEV float stage_x_i8(const GemvArgs &a, unsigned char *smem, float *s_red, unsigned *s_max) {
-    constexpr int MAXV = 4;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = a.cols, nv = n / 8, ng = n / 64;
-    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem);
-    const I8Smem L = i8_layout(n, 0, 0);
-    uint32_t *xbw = reinterpret_cast<uint32_t *>(smem + L.xb);
-    float *xsum4 = reinterpret_cast<float *>(smem + L.xsum);
-    const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm_w);
-    if (tid < 4) reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;
-    for (int base = 0; base < nv; base += NT * MAXV) {
-        uint4 v[MAXV];
-#pragma unroll
-        for (int j = 0; j < MAXV; j++) {
-            const int i = base + tid + j * NT;
-            if (i < nv) v[j] = x4[i];
-        }
-#pragma unroll
-        for (int j = 0; j < MAXV; j++) {
-            const int i = base + tid + j * NT;
-            if (i < nv) reinterpret_cast<uint4 *>(xraw)[i] = v[j];
-        }
-    }
-    if (NORM) {
-        __syncthreads();
-        const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
-        float acc = 0.f;
-        if (tid < Ta)
-            for (int i = tid; i < n; i += Ta) {
-                const float f = bf2f(xraw[i]);
-                acc = fmaf(f, f, acc);
-            }
-        acc = warp_sum(acc);
-        if (lane == 0) s_red[warp] = acc;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < NT / 32; w++) tot += s_red[w];
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), a.eps)));
-        for (int base = 0; base < nv; base += NT * MAXV) {
-            uint4 wv[MAXV];
-#pragma unroll
-            for (int j = 0; j < MAXV; j++) {
-                const int i = base + tid + j * NT;
-                if (i < nv) wv[j] = w4[i];
-            }
-#pragma unroll
-            for (int j = 0; j < MAXV; j++) {
-                const int i = base + tid + j * NT;
-                if (i >= nv) continue;
-                uint4 xv = reinterpret_cast<const uint4 *>(xraw)[i];
-                uint32_t *xs4 = &xv.x;
-                const uint32_t ws4[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const float lo = rbf(__fmul_rn(lo_bf(ws4[q]), rbf(__fmul_rn(lo_bf(xs4[q]), inv))));
-                    const float hi = rbf(__fmul_rn(hi_bf(ws4[q]), rbf(__fmul_rn(hi_bf(xs4[q]), inv))));
-                    xs4[q] = pack_bf2(lo, hi);
-                }
-                reinterpret_cast<uint4 *>(xraw)[i] = xv;
-            }
-        }
-    }
-    __syncthreads();
-    // group sums (bias multipliers) and the largest magnitude
-    unsigned mx = 0u;
-    for (int g = warp; g < ng; g += NT / 32) {
-        const uint32_t v = reinterpret_cast<const uint32_t *>(xraw)[g * 32 + lane];
-        mx = max(mx, max(v & 0x7fffu, (v >> 16) & 0x7fffu));
-        const float sm = warp_sum(lo_bf(v) + hi_bf(v));
-        if (lane == 0) {
-            const int bk = g >> 3, j = (g & 7) >> 1, h = g & 1;
-            xsum4[bk * 16 + (2 * h) * 4 + j] = sm;
-            xsum4[bk * 16 + (2 * h + 1) * 4 + j] = 0.f;
-        }
-    }
-    mx = __reduce_max_sync(0xffffffffu, mx);
-    if (lane == 0) s_max[warp] = mx;
-    __syncthreads();
-    mx = 0u;
-#pragma unroll
-    for (int w = 0; w < NT / 32; w++) mx = max(mx, s_max[w]);
-    int E = (int)(mx >> 7) - 127;            // exponent of the largest |x|
-    if (E < -100) E = -100;                  // zero / subnormal: digits round to 0
-    const float sc = __int_as_float((127 + 20 - E) << 23);
-    const float lscale = mx >= 0x7f80u ? __int_as_float(0x7fc00000) : __int_as_float((127 + E - 20) << 23);
-    // digit planes: item (g, m, b, t) covers group columns 32m + 16b + 4t + j
-    for (int it = tid; it < ng * 16; it += NT) {
-        const int t = it & 3, b = (it >> 2) & 1, m = (it >> 3) & 1, g = it >> 4;
-        const int k0 = g * 64 + 32 * m + 16 * b + 4 * t;
-        const uint2 raw = *reinterpret_cast<const uint2 *>(xraw + k0);
-        const float xf[4] = {lo_bf(raw.x), hi_bf(raw.x), lo_bf(raw.y), hi_bf(raw.y)};
-        uint32_t R[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int X = __float2int_rn(__fmul_rn(xf[j], sc));
-            R[j] = ((uint32_t)X & 0x7fu) | (((uint32_t)X << 1) & 0x7f00u) | (((uint32_t)X << 2) & 0xff0000u);
-        }
-        const uint32_t lo01 = __byte_perm(R[0], R[1], 0x5140), lo23 = __byte_perm(R[2], R[3], 0x5140);
-        const uint32_t p0 = __byte_perm(lo01, lo23, 0x5410);
-        const uint32_t p1 = __byte_perm(lo01, lo23, 0x7632);
-        const uint32_t p2 = __byte_perm(__byte_perm(R[0], R[1], 0x0062), __byte_perm(R[2], R[3], 0x0062), 0x5410);
-        uint32_t *e = xbw + ((size_t)g * I8_ENT + t) * 4 + 2 * m + b;
-        e[0] = p0;
-        e[16] = p1;
-        e[32] = p2;
-    }
-    __syncthreads();
-    return lscale;
-}
-
-MLXD_DEV void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // whole row blocks per CTA, as qgemv8r_kernel: warp w takes items w, w+16,
@@ -1050,24 +924,17 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
     l2_prefetch_share(a.pf);
     pdl_wait();
     MLXD_TRACE_WAITED
-    const float lscale = stage_x_i8<RB_THREADS, PRO == PRO_RMSNORM>(a, smem_raw, s_red, s_max);
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw);
+    uint32_t *xbw = reinterpret_cast<uint32_t *>(smem_raw + L.xb);
+    float *xsum4 = reinterpret_cast<float *>(smem_raw + L.xsum);
+    uint32_t *zero16 = reinterpret_cast<uint32_t *>(smem_raw + L.zero);
+    const float lscale = i8_stage<RB_THREADS>(a.x, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols, a.eps, xraw,
+                                              xbw, xsum4, zero16, s_red, s_max);
     pdl_trigger();
 #ifdef MLXD_TRACE
     const unsigned long long tr_staged_ = gtime();
 #endif
-
-    // this lane's B-fragment entries: group parity h = gq >> 2, digit gq & 3
-    // (digit 3 and the other parity read the zero entry)
-    const int dg = gq & 3, hh = gq >> 2;
-    const uint4 *xb = reinterpret_cast<const uint4 *>(smem_raw + L.xb);
-    const uint4 *zero = reinterpret_cast<const uint4 *>(smem_raw + L.zero);
-    const bool act0 = dg < I8_DIGITS && hh == 0, act1 = dg < I8_DIGITS && hh == 1;
-    const uint4 *xb0 = act0 ? xb + dg * 4 + t : zero;
-    const uint4 *xb1 = act1 ? xb + I8_ENT + dg * 4 + t : zero;
-    const int st0 = act0 ? 2 * I8_ENT : 0, st1 = act1 ? 2 * I8_ENT : 0;   // per group pair
-    const float lt = (t & 1) ? lscale * 16384.f : lscale;
-    const float *xsum4 = reinterpret_cast<const float *>(smem_raw + L.xsum) + t * 4;
-    constexpr uint32_t M4 = 0x0f0f0f0fu;
+    const I8Lane IL = i8_lane(xbw, xsum4, zero16, lscale);
 
     unsigned long long best = 0ull;
     for (int k = warp; k < n; k += RB_WARPS) {
@@ -1081,40 +948,10 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
             sb0 = ldg_nc_v4_ef(sbl + (i0 + k + RB_WARPS) * 512, pol);
             sb1 = ldg_nc_v4_ef(sbl + (i0 + k + RB_WARPS) * 512 + 16, pol);
         }
-        const float4 xs = *reinterpret_cast<const float4 *>(xsum4 + bk * 16);
-        const float xsj[4] = {xs.x, xs.y, xs.z, xs.w};
-        const uint32_t sbw[8] = {sA.x, sA.y, sA.z, sA.w, sB.x, sB.y, sB.z, sB.w};
-        float y0 = 0.f, y1 = 0.f, yb0 = 0.f, yb1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int p = 2 * j + u;
-                const uint4 wv = wbuf[p];
-                if (pre) wbuf[p] = ldg_nc_v4_ef(pwn + p * 512, pol);
-                const int pair = bk * 4 + j;
-                const uint4 bq = u == 0 ? xb0[pair * st0] : xb1[pair * st1];
-                const uint32_t alo[4] = {wv.x & M4, wv.y & M4, wv.z & M4, wv.w & M4};
-                const uint32_t ahi[4] = {(wv.x >> 4) & M4, (wv.y >> 4) & M4, (wv.z >> 4) & M4,
-                                         (wv.w >> 4) & M4};
-                mma_u8s8_16832(acc, alo, bq.x, bq.y);
-                mma_u8s8_16832(acc, ahi, bq.z, bq.w);
-            }
-            const float a0 = fmaf((float)acc[1], 128.f, (float)acc[0]);
-            const float a1 = fmaf((float)acc[3], 128.f, (float)acc[2]);
-            const uint32_t r0 = sbw[2 * j], r1 = sbw[2 * j + 1];
-            y0 = fmaf(lo_bf(r0), a0, y0);
-            y1 = fmaf(lo_bf(r1), a1, y1);
-            yb0 = fmaf(hi_bf(r0), xsj[j], yb0);
-            yb1 = fmaf(hi_bf(r1), xsj[j], yb1);
-        }
-        y0 = fmaf(y0, lt, yb0);
-        y1 = fmaf(y1, lt, yb1);
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        float y0, y1;
+        i8_item(wbuf, sA, sB, IL, bk, y0, y1, [&](int p) {
+            if (pre) wbuf[p] = ldg_nc_v4_ef(pwn + p * 512, pol);
+        });
         float *ps = pool + (size_t)unit * ipu * 16;
         if (t == 0) {
             ps[iu * 16 + gq] = y0;
