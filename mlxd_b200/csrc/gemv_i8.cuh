@@ -28,37 +28,64 @@ MLXD_DEV void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, u
 // even t, 0 for odd t). xraw: cols bf16 of scratch; zero16: a 16-byte entry
 // set to zero. Returns 2^(E-20) (NaN when x holds a non-finite value, so that
 // the outputs are NaN as in the f32 sum). Ends with a CTA barrier.
+//
+// Work unit: item it = 16 g + 8 m + 4 b + t covers the 4 features
+// 64 g + 32 m + 16 b + 4 t .. +3, i.e. one byte of each digit plane; the 16
+// items of a group sit in 16 consecutive threads. x is read once from global
+// memory in this layout (and, for the norm, also in the strided layout of the
+// sum of squares, both loads in flight together); the norm weights are read
+// before the caller waits on the producer (i8_stage_pre).
 template <int NT>
-MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float eps, uint16_t *xraw,
-                        uint32_t *xbw, float *xsum4, uint32_t *zero16, float *s_red, unsigned *s_max) {
-    constexpr int MAXV = 4;
-    const bool NORM = norm_w != nullptr;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nv = n / 8, ng = n / 64;
-    const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(norm_w);
-    if (tid < 4) zero16[tid] = 0u;
-    for (int base = 0; base < nv; base += NT * MAXV) {
-        uint4 v[MAXV];
+struct I8Pre {
+    static constexpr int MAXI = 4;       // items per thread kept in registers
+    uint2 w[MAXI];                       // norm weights of the thread's items
+};
+template <int NT>
+MLXD_DEV void i8_stage_pre(I8Pre<NT> &pre, const uint16_t *norm_w, int n) {
+    if (!norm_w) return;
+    const int ni = n / 4;
 #pragma unroll
-        for (int j = 0; j < MAXV; j++) {
-            const int i = base + tid + j * NT;
-            if (i < nv) v[j] = x4[i];
-        }
-#pragma unroll
-        for (int j = 0; j < MAXV; j++) {
-            const int i = base + tid + j * NT;
-            if (i < nv) reinterpret_cast<uint4 *>(xraw)[i] = v[j];
+    for (int k = 0; k < I8Pre<NT>::MAXI; k++) {
+        const int it = threadIdx.x + k * NT;
+        if (it < ni) {
+            const int g = it >> 4, r = it & 15;
+            pre.w[k] = *reinterpret_cast<const uint2 *>(norm_w + g * 64 + (r >> 3) * 32 + ((r >> 2) & 1) * 16 + (r & 3) * 4);
         }
     }
+}
+MLXD_DEV int i8_feature(int it) {
+    const int g = it >> 4, r = it & 15;
+    return g * 64 + (r >> 3) * 32 + ((r >> 2) & 1) * 16 + (r & 3) * 4;
+}
+template <int NT>
+MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float eps, uint16_t *xraw,
+                        uint32_t *xbw, float *xsum4, uint32_t *zero16, float *s_red, unsigned *s_max,
+                        const I8Pre<NT> &pre) {
+    constexpr int MAXI = I8Pre<NT>::MAXI;
+    const bool NORM = norm_w != nullptr;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ni = n / 4, ng = n / 64;
+    if (tid < 4) zero16[tid] = 0u;
+    // x in the item layout (the first MAXI items of the thread in registers)
+    uint2 xv[MAXI];
+#pragma unroll
+    for (int k = 0; k < MAXI; k++) {
+        const int it = tid + k * NT;
+        if (it < ni) xv[k] = *reinterpret_cast<const uint2 *>(x + i8_feature(it));
+    }
+    float inv = 1.f;
     if (NORM) {
-        __syncthreads();
         const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
         float acc = 0.f;
         if (tid < Ta)
-            for (int i = tid; i < n; i += Ta) {
-                const float f = bf2f(xraw[i]);
-                acc = fmaf(f, f, acc);
+            for (int base = tid; base < n; base += 16 * Ta) {
+                // 16 strided loads in flight, then the partial in element order
+                float f[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) f[j] = base + j * Ta < n ? bf2f(x[base + j * Ta]) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (base + j * Ta < n) acc = fmaf(f[j], f[j], acc);
             }
         acc = warp_sum(acc);
         if (lane == 0) s_red[warp] = acc;
@@ -66,42 +93,50 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
         float tot = 0.f;
 #pragma unroll
         for (int w = 0; w < NT / 32; w++) tot += s_red[w];
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
-        for (int base = 0; base < nv; base += NT * MAXV) {
-            uint4 wv[MAXV];
-#pragma unroll
-            for (int j = 0; j < MAXV; j++) {
-                const int i = base + tid + j * NT;
-                if (i < nv) wv[j] = w4[i];
-            }
-#pragma unroll
-            for (int j = 0; j < MAXV; j++) {
-                const int i = base + tid + j * NT;
-                if (i >= nv) continue;
-                uint4 xv = reinterpret_cast<const uint4 *>(xraw)[i];
-                uint32_t *xs4 = &xv.x;
-                const uint32_t ws4[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const float lo = rbf(__fmul_rn(lo_bf(ws4[q]), rbf(__fmul_rn(lo_bf(xs4[q]), inv))));
-                    const float hi = rbf(__fmul_rn(hi_bf(ws4[q]), rbf(__fmul_rn(hi_bf(xs4[q]), inv))));
-                    xs4[q] = pack_bf2(lo, hi);
-                }
-                reinterpret_cast<uint4 *>(xraw)[i] = xv;
-            }
-        }
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
     }
-    __syncthreads();
-    // group sums (bias multipliers) and the largest magnitude
+    // normalised values (bf16) of the thread's items, group sums, max |x|
     unsigned mx = 0u;
-    for (int g = warp; g < ng; g += NT / 32) {
-        const uint32_t v = reinterpret_cast<const uint32_t *>(xraw)[g * 32 + lane];
-        mx = max(mx, max(v & 0x7fffu, (v >> 16) & 0x7fffu));
-        const float sm = warp_sum(lo_bf(v) + hi_bf(v));
-        if (lane == 0) {
-            const int bk = g >> 3, j = (g & 7) >> 1, h = g & 1;
-            xsum4[bk * 16 + (2 * h) * 4 + j] = sm;
-            xsum4[bk * 16 + (2 * h + 1) * 4 + j] = 0.f;
+    for (int k0 = 0; k0 * NT < ni; k0 += MAXI) {
+#pragma unroll
+        for (int k = 0; k < MAXI; k++) {
+            const int it = tid + (k0 + k) * NT;
+            const bool in = it < ni;
+            uint2 v = make_uint2(0u, 0u);
+            if (in) {
+                if (k0 == 0) {
+                    v = xv[k];
+                } else {
+                    v = *reinterpret_cast<const uint2 *>(x + i8_feature(it));
+                }
+                if (NORM) {
+                    const uint2 wv = k0 == 0 ? pre.w[k]
+                                             : *reinterpret_cast<const uint2 *>(norm_w + i8_feature(it));
+                    uint32_t *e = &v.x;
+                    const uint32_t w2[2] = {wv.x, wv.y};
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        const float lo = rbf(__fmul_rn(lo_bf(w2[q]), rbf(__fmul_rn(lo_bf(e[q]), inv))));
+                        const float hi = rbf(__fmul_rn(hi_bf(w2[q]), rbf(__fmul_rn(hi_bf(e[q]), inv))));
+                        e[q] = pack_bf2(lo, hi);
+                    }
+                }
+                *reinterpret_cast<uint2 *>(xraw + 4 * it) = v;   // item order
+                mx = max(mx, max(max(v.x & 0x7fffu, (v.x >> 16) & 0x7fffu),
+                                 max(v.y & 0x7fffu, (v.y >> 16) & 0x7fffu)));
+            }
+            // group sum: the 16 items of a group are 16 consecutive threads
+            float sm = (lo_bf(v.x) + hi_bf(v.x)) + (lo_bf(v.y) + hi_bf(v.y));
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 8);
+            if (in && (it & 15) == 0) {
+                const int g = it >> 4;
+                const int bk = g >> 3, j = (g & 7) >> 1, h = g & 1;
+                xsum4[bk * 16 + (2 * h) * 4 + j] = sm;
+                xsum4[bk * 16 + (2 * h + 1) * 4 + j] = 0.f;
+            }
         }
     }
     mx = __reduce_max_sync(0xffffffffu, mx);
@@ -113,18 +148,21 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
     int E = (int)(mx >> 7) - 127;            // exponent of the largest |x|
     if (E < -100) E = -100;                  // zero / subnormal: digits round to 0
     const float sc = __int_as_float((127 + 20 - E) << 23);
+    // round(x * sc) + 1.5 * 2^23 as an f32 (|x * sc| < 2^21, one rounding):
+    // its low 22 bits are those of X = round(x * sc), so the digits come
+    // straight from the bits (d0 = bits 0-6, d1 = 7-13, d2 = 14-21 signed)
+    constexpr float MAGIC = 12582912.0f;
     const float lscale = mx >= 0x7f80u ? __int_as_float(0x7fc00000) : __int_as_float((127 + E - 20) << 23);
-    // digit planes: item (g, m, b, t) covers group columns 32m + 16b + 4t + j
-    for (int it = tid; it < ng * 16; it += NT) {
+    // digit planes of each item: one byte per digit
+    for (int it = tid; it < ni; it += NT) {
         const int t = it & 3, b = (it >> 2) & 1, m = (it >> 3) & 1, g = it >> 4;
-        const int k0 = g * 64 + 32 * m + 16 * b + 4 * t;
-        const uint2 raw = *reinterpret_cast<const uint2 *>(xraw + k0);
+        const uint2 raw = *reinterpret_cast<const uint2 *>(xraw + 4 * it);
         const float xf[4] = {lo_bf(raw.x), hi_bf(raw.x), lo_bf(raw.y), hi_bf(raw.y)};
         uint32_t R[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const int X = __float2int_rn(__fmul_rn(xf[j], sc));
-            R[j] = ((uint32_t)X & 0x7fu) | (((uint32_t)X << 1) & 0x7f00u) | (((uint32_t)X << 2) & 0xff0000u);
+            const uint32_t X = __float_as_uint(__fmaf_rn(xf[j], sc, MAGIC));
+            R[j] = (X & 0x7fu) | ((X << 1) & 0x7f00u) | ((X << 2) & 0xff0000u);
         }
         const uint32_t lo01 = __byte_perm(R[0], R[1], 0x5140), lo23 = __byte_perm(R[2], R[3], 0x5140);
         const uint32_t p0 = __byte_perm(lo01, lo23, 0x5410);

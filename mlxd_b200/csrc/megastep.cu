@@ -262,9 +262,11 @@ MLXD_DEV void ms_issue(MsStream &st, unsigned char *wbuf, int warp, int lane) {
 // phase, instruction-cache friendly; the norm is on when nw is given)
 __device__ __noinline__ float ms_stage_x(const uint16_t *x, const uint16_t *nw, int cols, float eps,
                                          unsigned char *smem, const MsSmem &Lo, float *s_red, unsigned *s_max) {
+    I8Pre<MS_CT> pre;
+    i8_stage_pre<MS_CT>(pre, nw, cols);
     return i8_stage<MS_CT>(x, nw, cols, eps, reinterpret_cast<uint16_t *>(smem + Lo.u),
                            reinterpret_cast<uint32_t *>(smem + Lo.xb), reinterpret_cast<float *>(smem + Lo.xsum),
-                           reinterpret_cast<uint32_t *>(smem + Lo.zero), s_red, s_max);
+                           reinterpret_cast<uint32_t *>(smem + Lo.zero), s_red, s_max, pre);
 }
 
 enum { MS_EPI_STORE = 0, MS_EPI_RESIDUAL = 1, MS_EPI_SWIGLU = 2, MS_EPI_LOGITS = 3 };

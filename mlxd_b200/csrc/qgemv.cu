@@ -922,6 +922,8 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
         sb1 = ldg_nc_v4_ef(sbl + (i0 + warp) * 512 + 16, pol);
     }
     l2_prefetch_share(a.pf);
+    I8Pre<RB_THREADS> pre;
+    i8_stage_pre<RB_THREADS>(pre, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols);
     pdl_wait();
     MLXD_TRACE_WAITED
     uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw);
@@ -929,7 +931,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
     float *xsum4 = reinterpret_cast<float *>(smem_raw + L.xsum);
     uint32_t *zero16 = reinterpret_cast<uint32_t *>(smem_raw + L.zero);
     const float lscale = i8_stage<RB_THREADS>(a.x, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols, a.eps, xraw,
-                                              xbw, xsum4, zero16, s_red, s_max);
+                                              xbw, xsum4, zero16, s_red, s_max, pre);
     pdl_trigger();
 #ifdef MLXD_TRACE
     const unsigned long long tr_staged_ = gtime();
