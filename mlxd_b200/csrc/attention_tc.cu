@@ -3,10 +3,10 @@
 // src/engine/forward.c:713-731, with the q/k RMSNorm + RoPE of :591-697 and
 // the KV append of kvcache.c:98-180).
 //
-// Cluster (CL CTAs of 4 warps) per kv head; CTA r of the cluster takes the
+// Cluster (CL CTAs of 8 warps) per kv head; CTA r of the cluster takes the
 // r-th of CL equal slices of the attended positions (lo, pos], each warp an
 // equal part of that slice, in chunks of 16 positions. Before waiting on the
-// q|k|v projection a warp requests its first three chunks of cached K and V
+// q|k|v projection a warp requests its first two chunks of cached K and V
 // rows into a private shared-memory ring (cp.async, rows XOR-swizzled in
 // 16-byte pieces so that ldmatrix reads are conflict-free); the cached rows
 // do not depend on this step. After the wait every warp normalises and
@@ -34,7 +34,7 @@ namespace mlxd {
 
 MLXD_TRACE_BINDER(attention_tc)
 
-constexpr int TC_WARPS = 4, TC_THREADS = 128, TC_ROWS = 16, TC_NBUF = 3;
+constexpr int TC_WARPS = 8, TC_THREADS = 256, TC_ROWS = 16, TC_NBUF = 2;
 
 template <int D, int REP>
 struct TcSmem {
@@ -45,7 +45,10 @@ struct TcSmem {
     static constexpr size_t wml = wo + (size_t)TC_WARPS * REP * D * 4;   // [warps][REP][2]
     static constexpr size_t cml = wml + (size_t)TC_WARPS * REP * 2 * 4;  // [REP][2] CTA partial
     static constexpr size_t co = cml + (size_t)REP * 2 * 4;             // [REP][D] CTA partial
-    static constexpr size_t total = co + (size_t)REP * D * 4;
+    // inbox of the cluster merge: per source CTA (at most 16), (m, l) of the
+    // slice's head and the slice's REP*D/CL partial outputs
+    static constexpr size_t inbox = co + (size_t)REP * D * 4;
+    static constexpr size_t total = inbox + (size_t)16 * (2 + REP * D / 8) * 4;
 };
 
 // byte offset of 16-byte piece c of row r in a chunk's K or V rows
@@ -67,6 +70,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
     const int rank = (int)cluster.block_rank();
     const int kh = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
+    // first cluster barrier phase: every CTA of the cluster has started before
+    // any of them writes into another's shared memory (waited before the push)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     extern __shared__ __align__(128) unsigned char sm[];
     unsigned char *ring = sm + (size_t)warp * TC_NBUF * 2 * L::CB;
     uint16_t *sq = reinterpret_cast<uint16_t *>(sm + L::q) + (size_t)warp * REP * D;
@@ -123,45 +129,61 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
     pdl_wait();
     MLXD_TRACE_WAITED
 
-    // head_norm_rope in registers: the oracle's association (lane-strided
-    // fmaf partials, butterfly), the same rounding points
+    // head_norm_rope in registers for the group's q heads and the new k
+    // (vector REP), their reductions interleaved: the oracle's association
+    // (lane-strided fmaf partials, butterfly o = 16..1), its rounding points
     const bool norm = a.qn != nullptr;
-    auto norm_rope = [&](float (&v)[DS], const float (&nw)[DS]) {
-        if (norm) {
-            float acc = 0.f;
-#pragma unroll
-            for (int i = 0; i < DS; i++) acc = fmaf(v[i], v[i], acc);
-            acc = warp_sum(acc);
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)D), a.eps)));
-#pragma unroll
-            for (int i = 0; i < DS; i++) v[i] = rbf(__fmul_rn(nw[i], rbf(__fmul_rn(v[i], inv))));
-        }
-#pragma unroll
-        for (int i = 0; i < HL; i++) {
-            const float x1 = v[i], x2 = v[i + HL];
-            v[i] = rbf(__fsub_rn(__fmul_rn(x1, rc[i]), __fmul_rn(x2, rs[i])));
-            v[i + HL] = rbf(__fadd_rn(__fmul_rn(x1, rs[i]), __fmul_rn(x2, rc[i])));
-        }
-    };
     const uint16_t *qkv = a.qkv;
     const int qstride = D * (a.gate ? 2 : 1);
-    float kn[DS];
-    uint16_t vn[DS];
+    // every load of the new q/k/v rows in flight before any arithmetic
+    uint16_t raw[REP + 1][DS], vn[DS];
 #pragma unroll
     for (int i = 0; i < DS; i++) {
-        kn[i] = bf2f(qkv[a.qdim + (size_t)kh * D + lane + 32 * i]);
+        raw[REP][i] = qkv[a.qdim + (size_t)kh * D + lane + 32 * i];
         vn[i] = qkv[a.qdim + (size_t)(a.hkv + kh) * D + lane + 32 * i];
+#pragma unroll
+        for (int h = 0; h < REP; h++) raw[h][i] = qkv[(size_t)(kh * REP + h) * qstride + lane + 32 * i];
+    }
+    float vv[REP + 1][DS];
+#pragma unroll
+    for (int h = 0; h <= REP; h++)
+#pragma unroll
+        for (int i = 0; i < DS; i++) vv[h][i] = bf2f(raw[h][i]);
+    if (norm) {
+        float acc[REP + 1];
+#pragma unroll
+        for (int h = 0; h <= REP; h++) {
+            acc[h] = 0.f;
+#pragma unroll
+            for (int i = 0; i < DS; i++) acc[h] = fmaf(vv[h][i], vv[h][i], acc[h]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int h = 0; h <= REP; h++) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
+#pragma unroll
+        for (int h = 0; h <= REP; h++) {
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc[h], (float)D), a.eps)));
+#pragma unroll
+            for (int i = 0; i < DS; i++)
+                vv[h][i] = rbf(__fmul_rn(h < REP ? qnw[i] : knw[i], rbf(__fmul_rn(vv[h][i], inv))));
+        }
     }
 #pragma unroll
-    for (int h = 0; h < REP; h++) {
-        float qv[DS];
+    for (int h = 0; h <= REP; h++)
 #pragma unroll
-        for (int i = 0; i < DS; i++) qv[i] = bf2f(qkv[(size_t)(kh * REP + h) * qstride + lane + 32 * i]);
-        norm_rope(qv, qnw);
+        for (int i = 0; i < HL; i++) {
+            const float x1 = vv[h][i], x2 = vv[h][i + HL];
+            vv[h][i] = rbf(__fsub_rn(__fmul_rn(x1, rc[i]), __fmul_rn(x2, rs[i])));
+            vv[h][i + HL] = rbf(__fadd_rn(__fmul_rn(x1, rs[i]), __fmul_rn(x2, rc[i])));
+        }
 #pragma unroll
-        for (int i = 0; i < DS; i++) sq[h * D + lane + 32 * i] = f2bf(qv[i]);
-    }
-    norm_rope(kn, knw);
+    for (int h = 0; h < REP; h++)
+#pragma unroll
+        for (int i = 0; i < DS; i++) sq[h * D + lane + 32 * i] = f2bf(vv[h][i]);
+    float kn[DS];
+#pragma unroll
+    for (int i = 0; i < DS; i++) kn[i] = vv[REP][i];
     if (rank == 0 && warp == 0) {
         const size_t slot = (size_t)(pos % a.cap) * D;
 #pragma unroll
@@ -179,6 +201,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
         qa[kk][1] = gq < REP ? *reinterpret_cast<const uint32_t *>(sq + gq * D + 16 * kk + 8 + 2 * t) : 0u;
     }
 
+    MLXD_TRACE_T(tr_prep_)
     const float qscale = rsqrtf((float)D) * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
     float o[NTO][4];
@@ -262,6 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
         issue(c + TC_NBUF);
     }
     cp_async_wait<0>();
+    MLXD_TRACE_T(tr_loop_)
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
     // the warps' partials, then the CTA's
@@ -295,29 +319,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
             cml[2 * h + 1] = ls;
         }
     }
-    cluster.sync();
-    // this CTA's slice of the group's outputs, merged over the cluster
-    const int nout = REP * D;
-    const int o0 = (int)((long long)nout * rank / CL), o1 = (int)((long long)nout * (rank + 1) / CL);
-    for (int oi = o0 + tid; oi < o1; oi += TC_THREADS) {
+    __syncthreads();
+    MLXD_TRACE_T(tr_cmerge_)
+    // push: CTA s owns outputs [s*SL, (s+1)*SL) of the group (SL = REP*D/CL,
+    // within one head); every CTA writes its partial of that slice, with the
+    // head's (m, l), into the owner's inbox row `rank`
+    constexpr int SL = REP * D / CL;
+    constexpr int ROW = 2 + SL;
+    float *inbox = reinterpret_cast<float *>(sm + L::inbox);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    for (int e = tid; e < CL * ROW; e += TC_THREADS) {
+        const int sidx = e / ROW, k = e % ROW;
+        const int oi = sidx * SL + (k >= 2 ? k - 2 : 0);
+        const float v = k == 0 ? cml[2 * (oi / D)] : k == 1 ? cml[2 * (oi / D) + 1] : co[oi];
+        float *dst = cluster.map_shared_rank(inbox, sidx);
+        dst[rank * ROW + k] = v;
+    }
+    cluster.sync();   // every partial has landed in its owner's inbox
+    MLXD_TRACE_T(tr_csync_)
+    MLXD_TRACE_REC(tid == 0, 0x71, tr_prep_, tr_loop_, tr_cmerge_)
+    if (tid < SL) {
+        const int oi = rank * SL + tid;
         const int h = oi / D, d = oi % D;
-        float mr[CL], lr[CL], orr[CL];
         float mm = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < CL; r++) {
-            const float *pcml = cluster.map_shared_rank(cml, r);
-            const float *pco = cluster.map_shared_rank(co, r);
-            mr[r] = pcml[2 * h];
-            lr[r] = pcml[2 * h + 1];
-            orr[r] = pco[h * D + d];
-            mm = fmaxf(mm, mr[r]);
-        }
+        for (int r = 0; r < CL; r++) mm = fmaxf(mm, inbox[r * ROW]);
         float ls = 0.f, os = 0.f;
 #pragma unroll
         for (int r = 0; r < CL; r++) {
-            const float e = mr[r] == -INFINITY ? 0.f : exp2f(mr[r] - mm);
-            ls = fmaf(lr[r], e, ls);
-            os = fmaf(orr[r], e, os);
+            const float mr = inbox[r * ROW];
+            const float e = mr == -INFINITY ? 0.f : exp2f(mr - mm);
+            ls = fmaf(inbox[r * ROW + 1], e, ls);
+            os = fmaf(inbox[r * ROW + 2 + tid], e, os);
         }
         const int hg = kh * REP + h;
         float val = rbf(os / ls);
@@ -327,7 +360,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
         }
         a.out[(size_t)hg * D + d] = f2bf(val);
     }
-    cluster.sync();   // peers' shared memory stays valid until every CTA merged
+    MLXD_TRACE_REC(tid == 0, 0x72, tr_csync_, gtime(), gtime())
     MLXD_TRACE_END(0x70)
 }
 

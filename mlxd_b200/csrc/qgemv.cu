@@ -884,17 +884,21 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
     return L;
 }
 
-// whole row blocks per CTA, as qgemv8r_kernel: warp w takes items w, w+16,
-// ... of the CTA's units and holds the next one (4 KB of tiles + its two
-// 16-byte scale/bias words) in registers while computing the current one
-template <int PRO, int EPI>
-__global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int pool_items) {
+// Whole row blocks per CTA, as qgemv8r_kernel: warp w of the NW warps takes
+// items w, w+NW, ... of the CTA's units and keeps the next DEPTH items
+// (4 KB of tiles + two 16-byte scale/bias words each) in registers while
+// computing the current one, the first DEPTH of them requested before the
+// PDL wait.
+template <int PRO, int EPI, int NW, int DEPTH>
+__global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int pool_items) {
     MLXD_TRACE_START
+    constexpr int NT = NW * 32;
     constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    static_assert(DEPTH == 1 || DEPTH == 2, "register item buffers");
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ float s_red[RB_WARPS];
-    __shared__ unsigned s_max[RB_WARPS];
-    __shared__ unsigned long long s_key[RB_WARPS];
+    __shared__ float s_red[NW];
+    __shared__ unsigned s_max[NW];
+    __shared__ unsigned long long s_key[NW];
     const int nbk = a.cols / 512;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
     const int n_units = a.rows / 16 / UNIT_RB;
@@ -906,32 +910,35 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
     const I8Smem L = i8_layout(a.cols, pool_items, (u1 - u0));
     float *pool = reinterpret_cast<float *>(smem_raw + L.pool);
     int *s_cnt = reinterpret_cast<int *>(smem_raw + L.cnt);
-    for (int i = tid; i < u1 - u0; i += RB_THREADS) s_cnt[i] = 0;
+    for (int i = tid; i < u1 - u0; i += NT) s_cnt[i] = 0;
 
-    // the warp's first item streams while the previous kernel finishes, and
-    // later kernels' weights are requested into L2
+    // the warp's first items stream while the previous kernel finishes
     const uint64_t pol = l2_policy_evict_first();
     const uint8_t *sbl = a.sbi + (gq * 2 + (t >> 1)) * 32;
-    uint4 wbuf[8];
-    uint4 sb0 = make_uint4(0, 0, 0, 0), sb1 = sb0;
-    if (warp < n) {
-        const uint8_t *pw = a.ti8 + (i0 + warp) * 4096 + lane * 16;
+    uint4 wb[DEPTH][8];
+    uint4 sb[DEPTH][2];
+    auto load = [&](int d, int k) {
+        if (k < n) {
+            const uint8_t *pw = a.ti8 + (i0 + k) * 4096 + lane * 16;
 #pragma unroll
-        for (int p = 0; p < 8; p++) wbuf[p] = ldg_nc_v4_ef(pw + p * 512, pol);
-        sb0 = ldg_nc_v4_ef(sbl + (i0 + warp) * 512, pol);
-        sb1 = ldg_nc_v4_ef(sbl + (i0 + warp) * 512 + 16, pol);
-    }
+            for (int p = 0; p < 8; p++) wb[d][p] = ldg_nc_v4_ef(pw + p * 512, pol);
+            sb[d][0] = ldg_nc_v4_ef(sbl + (i0 + k) * 512, pol);
+            sb[d][1] = ldg_nc_v4_ef(sbl + (i0 + k) * 512 + 16, pol);
+        }
+    };
+#pragma unroll
+    for (int d = 0; d < DEPTH; d++) load(d, warp + d * NW);
     l2_prefetch_share(a.pf);
-    I8Pre<RB_THREADS> pre;
-    i8_stage_pre<RB_THREADS>(pre, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols);
+    I8Pre<NT> pre;
+    i8_stage_pre<NT>(pre, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols);
     pdl_wait();
     MLXD_TRACE_WAITED
     uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw);
     uint32_t *xbw = reinterpret_cast<uint32_t *>(smem_raw + L.xb);
     float *xsum4 = reinterpret_cast<float *>(smem_raw + L.xsum);
     uint32_t *zero16 = reinterpret_cast<uint32_t *>(smem_raw + L.zero);
-    const float lscale = i8_stage<RB_THREADS>(a.x, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols, a.eps, xraw,
-                                              xbw, xsum4, zero16, s_red, s_max, pre);
+    const float lscale = i8_stage<NT>(a.x, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols, a.eps, xraw, xbw,
+                                      xsum4, zero16, s_red, s_max, pre);
     pdl_trigger();
 #ifdef MLXD_TRACE
     const unsigned long long tr_staged_ = gtime();
@@ -939,20 +946,22 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
     const I8Lane IL = i8_lane(xbw, xsum4, zero16, lscale);
 
     unsigned long long best = 0ull;
-    for (int k = warp; k < n; k += RB_WARPS) {
-        const bool pre = k + RB_WARPS < n;
-        const uint8_t *pwn = a.ti8 + (i0 + k + RB_WARPS) * 4096 + lane * 16;
+    // item k from buffer d; the buffer is refilled with item k + DEPTH*NW
+    auto process = [&](int d, int k) {
+        const int kn = k + DEPTH * NW;
+        const bool more = kn < n;
+        const uint8_t *pwn = a.ti8 + (i0 + kn) * 4096 + lane * 16;
         const int unit = k / ipu;
         const int iu = k - unit * ipu;
         const int bk = iu % nbk;
-        const uint4 sA = sb0, sB = sb1;
-        if (pre) {
-            sb0 = ldg_nc_v4_ef(sbl + (i0 + k + RB_WARPS) * 512, pol);
-            sb1 = ldg_nc_v4_ef(sbl + (i0 + k + RB_WARPS) * 512 + 16, pol);
+        const uint4 sA = sb[d][0], sB = sb[d][1];
+        if (more) {
+            sb[d][0] = ldg_nc_v4_ef(sbl + (i0 + kn) * 512, pol);
+            sb[d][1] = ldg_nc_v4_ef(sbl + (i0 + kn) * 512 + 16, pol);
         }
         float y0, y1;
-        i8_item(wbuf, sA, sB, IL, bk, y0, y1, [&](int p) {
-            if (pre) wbuf[p] = ldg_nc_v4_ef(pwn + p * 512, pol);
+        i8_item(wb[d], sA, sB, IL, bk, y0, y1, [&](int p) {
+            if (more) wb[d][p] = ldg_nc_v4_ef(pwn + p * 512, pol);
         });
         float *ps = pool + (size_t)unit * ipu * 16;
         if (t == 0) {
@@ -970,6 +979,10 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
             __threadfence_block();
             rb_epilogue<EPI>(a, ps, nbk, u0 + unit, lane, best);
         }
+    };
+    for (int k = warp; k < n; k += DEPTH * NW) {
+        process(0, k);
+        if (DEPTH == 2 && k + NW < n) process(DEPTH - 1, k + NW);
     }
     if constexpr (EPI == EPI_ARGMAX) {
 #pragma unroll
@@ -981,7 +994,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv_i8_kernel(GemvArgs a, int
         __syncthreads();
         if (tid == 0) {
             unsigned long long m = 0ull;
-            for (int w = 0; w < RB_WARPS; w++) m = s_key[w] > m ? s_key[w] : m;
+            for (int w = 0; w < NW; w++) m = s_key[w] > m ? s_key[w] : m;
             if (m) atomicMax(a.amax, m);
         }
     }
@@ -1127,9 +1140,9 @@ static int launch_gemv8r(GemvArgs a, cudaStream_t st, bool pdl) {
     return 0;
 }
 
-template <int PRO, int EPI>
-static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
-    auto kern = qgemv_i8_kernel<PRO, EPI>;
+template <int PRO, int EPI, int NW, int DEPTH>
+static int launch_gemv_i8_cfg(GemvArgs a, cudaStream_t st, bool pdl) {
+    auto kern = qgemv_i8_kernel<PRO, EPI, NW, DEPTH>;
     const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
     const int n_units = a.rows / 16 / unit_rb;
     int grid = num_sms();
@@ -1148,7 +1161,7 @@ static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(RB_THREADS);
+    cfg.blockDim = dim3(NW * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1158,6 +1171,13 @@ static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
     cfg.numAttrs = pdl ? 1 : 0;
     MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a, pool_items));
     return 0;
+}
+
+// 16 warps with one item in registers ahead: on Qwen3-8B 608 tokens/s,
+// against 582 for 12 warps x 2 items and 479 for 16 x 2 (register spills)
+template <int PRO, int EPI>
+static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
+    return launch_gemv_i8_cfg<PRO, EPI, 16, 1>(a, st, pdl);
 }
 
 static int dispatch_gemv_i8(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
