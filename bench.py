@@ -125,6 +125,15 @@ def dist_setup(world):
     return dist
 
 
+def max_over_ranks(dist, values):
+    """Element-wise max of per-rank device times (the job is as slow as its
+    slowest rank)."""
+    import torch
+    v = torch.tensor([float(x) for x in values], dtype=torch.float64)
+    dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return [float(x) for x in v]
+
+
 def gemv_roofline(kw, peak):
     """Live qGEMV microbench at the workload's projection shapes (weights
     rotated over copies larger than L2, CUDA events in the library)."""
@@ -272,10 +281,7 @@ def main():
     wall_ms = float(tm["decode_wall_ms"])
     prefill_ms = float(tm["prefill_ms"])
     if dist:
-        import torch
-        v = torch.tensor([t_timed, wall_ms, prefill_ms], dtype=torch.float64)
-        dist.all_reduce(v, op=dist.ReduceOp.MAX)
-        t_timed, wall_ms, prefill_ms = (float(x) for x in v)
+        t_timed, wall_ms, prefill_ms = max_over_ranks(dist, [t_timed, wall_ms, prefill_ms])
     value = K / (t_timed / 1e3)
     e2e_value = total / (wall_ms / 1e3)
     peak, peak_src = hbm_peak()

@@ -94,6 +94,15 @@ int  mlxd_cuda_model_decode_path(const mlxd_model *m);
    128 bytes) before the first forward when tp_size > 1. */
 int  mlxd_cuda_model_tp_init(mlxd_model *m, const void *nccl_unique_id);
 int  mlxd_cuda_nccl_unique_id(void *out128);
+/* Tensor-parallel shard plan, host only (no device call). The reference has
+   no multi-GPU path (one mlx stream, src/engine/engine.c:360-602); this is
+   the partition mlxd_cuda_model_create applies when tp_size > 1: q, k, v,
+   gate, up and lm_head are split by rows (heads, intermediate, vocab), o and
+   down by columns (row-parallel, on quantisation-group boundaries). Writes
+   ranges[8][4] = {row0, rows, col0, cols} for q, k, v, o, gate, up, down,
+   lm_head of the full matrices; -1 (last_error set) when `size` does not
+   divide the heads, intermediate or vocab. */
+int  mlxd_cuda_tp_plan(const mlxd_model_config *cfg, int rank, int size, int *ranges);
 
 /* ---- KV cache (kvcache.h:11-51) ----------------------------------------
    Preallocated per-layer [Hkv][capacity][D] bf16 storage. With a sliding

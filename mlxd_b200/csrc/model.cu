@@ -610,6 +610,27 @@ static int forward_dev(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, int n
 
 extern "C" {
 
+int mlxd_cuda_tp_plan(const mlxd_model_config *cfg, int rank, int size, int *r) {
+    if (!cfg || !r || size < 1 || rank < 0 || rank >= size) {
+        set_error("tp_plan: bad arguments");
+        return -1;
+    }
+    const mlxd_model_config &c = *cfg;
+    if (c.n_heads % size || c.n_kv_heads % size || c.inter % size || c.vocab % size) {
+        set_error("tensor-parallel degree %d does not divide heads/intermediate/vocab", size);
+        return -1;
+    }
+    const int D = c.head_dim, H = c.hidden;
+    const int ql = c.n_heads / size * D * (c.attn_gate ? 2 : 1), kl = c.n_kv_heads / size * D;
+    const int oc = c.n_heads / size * D, il = c.inter / size, vl = c.vocab / size;
+    const int plan[8][4] = {{rank * ql, ql, 0, H},     {rank * kl, kl, 0, H},     {rank * kl, kl, 0, H},
+                            {0, H, rank * oc, oc},     {rank * il, il, 0, H},     {rank * il, il, 0, H},
+                            {0, H, rank * il, il},     {rank * vl, vl, 0, H}};
+    for (int i = 0; i < 8; i++)
+        for (int j = 0; j < 4; j++) r[4 * i + j] = plan[i][j];
+    return 0;
+}
+
 int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const mlxd_tensor *tensors,
                            int n_tensors) {
     if (!out || !cfg || (!tensors && n_tensors)) {
@@ -635,10 +656,8 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         set_error("quantisation group %d not supported (32 or 64)", c.qgroup);
         return -1;
     }
-    if (c.n_heads % tp || c.n_kv_heads % tp || c.inter % tp || c.vocab % tp) {
-        set_error("tensor-parallel degree %d does not divide heads/intermediate/vocab", tp);
-        return -1;
-    }
+    int plan[8][4];   // this rank's rows/columns of q, k, v, o, gate, up, down, lm_head
+    if (mlxd_cuda_tp_plan(&c, rank, tp, &plan[0][0])) return -1;
     if (c.rope_dims <= 0 || c.rope_dims > c.head_dim || (c.rope_dims & 1)) {
         set_error("invalid rope dims %d", c.rope_dims);
         return -1;
@@ -681,21 +700,22 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
             set_error("layer %d: projection shapes do not match the config", l);
             return fail();
         }
-        int ql = m->qdim, kl = m->hkv * D;
+        int ql = plan[0][1], kl = plan[1][1];
         // fused q|k|v rows (column-parallel slice by heads)
         std::vector<Piece> qkv = {
-            {q, rank * ql, ql, 0, 0, 1, 0},
-            {k, rank * kl, kl, 0, ql / 16, 1, ql},
-            {v, rank * kl, kl, 0, (ql + kl) / 16, 1, ql + kl}};
+            {q, plan[0][0], ql, 0, 0, 1, 0},
+            {k, plan[1][0], kl, 0, ql / 16, 1, ql},
+            {v, plan[2][0], kl, 0, (ql + kl) / 16, 1, ql + kl}};
         if (build_qmat(ts, L.qkv, ql + 2 * kl, c.hidden, G, qkv, st)) return fail();
         // o: row-parallel (input columns of this rank's heads)
-        int oc = m->hq * D;
-        if (build_qmat(ts, L.o, c.hidden, oc, G, {{o, 0, c.hidden, rank * oc, 0, 1, 0}}, st)) return fail();
+        int oc = plan[3][3];
+        if (build_qmat(ts, L.o, c.hidden, oc, G, {{o, 0, c.hidden, plan[3][2], 0, 1, 0}}, st)) return fail();
         // gate/up: quantized -> interleaved 16-row blocks; dense -> stacked
-        int il = m->inter_local;
-        std::vector<Piece> gu = {{gt, rank * il, il, 0, 0, 2, 0}, {up, rank * il, il, 0, 1, 2, il}};
+        int il = plan[4][1];
+        std::vector<Piece> gu = {{gt, plan[4][0], il, 0, 0, 2, 0}, {up, plan[5][0], il, 0, 1, 2, il}};
         if (build_qmat(ts, L.gateup, 2 * il, c.hidden, G, gu, st)) return fail();
-        if (build_qmat(ts, L.down, c.hidden, il, G, {{dn, 0, c.hidden, rank * il, 0, 1, 0}}, st)) return fail();
+        if (build_qmat(ts, L.down, c.hidden, plan[6][3], G, {{dn, 0, c.hidden, plan[6][2], 0, 1, 0}}, st))
+            return fail();
         if (!(L.ln1 = upload_vec(ts, p + "input_layernorm.weight", c.hidden, st))) return fail();
         if (!(L.ln2 = upload_vec(ts, p + "post_attention_layernorm.weight", c.hidden, st))) return fail();
         if (c.qk_norm) {
@@ -739,7 +759,7 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         set_error("lm_head shape does not match the config");
         return fail();
     }
-    if (build_qmat(ts, m->lm, m->vocab_local, c.hidden, G, {{lm, m->vocab_off, m->vocab_local, 0, 0, 1, 0}}, st))
+    if (build_qmat(ts, m->lm, plan[7][1], c.hidden, G, {{lm, plan[7][0], plan[7][1], 0, 0, 1, 0}}, st))
         return fail();
     if (!(m->norm = upload_vec(ts, "model.norm.weight", c.hidden, st))) return fail();
 

@@ -76,6 +76,7 @@ _SIGS = {
     "mlxd_cuda_model_decode_path": (C.c_int, [P]),
     "mlxd_cuda_model_tp_init": (C.c_int, [P, P]),
     "mlxd_cuda_nccl_unique_id": (C.c_int, [P]),
+    "mlxd_cuda_tp_plan": (C.c_int, [C.POINTER(ModelConfig), C.c_int, C.c_int, P]),
     "mlxd_cuda_kv_create": (C.c_int, [C.POINTER(P), P, C.c_int]),
     "mlxd_cuda_kv_destroy": (None, [P]),
     "mlxd_cuda_kv_offset": (C.c_int, [P, C.c_int]),
@@ -215,6 +216,15 @@ def read_checkpoint(model_dir):
     for fn in files:
         t.update(read_safetensors(os.path.join(model_dir, fn)))
     return t
+
+
+def tp_plan(cfg, rank, size):
+    """The library's tensor-parallel shard plan (host only): {name: (row0,
+    rows, col0, cols)} of this rank's part of each full projection."""
+    r = np.zeros(32, np.int32)
+    check(lib().mlxd_cuda_tp_plan(C.byref(cfg), rank, size, ptr(r)), "tp_plan")
+    names = ["q", "k", "v", "o", "gate", "up", "down", "lm_head"]
+    return {n: tuple(int(v) for v in r[4 * i:4 * i + 4]) for i, n in enumerate(names)}
 
 
 def config_from_json(cj, tp_rank=0, tp_size=1):
