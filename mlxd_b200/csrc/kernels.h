@@ -58,6 +58,12 @@ int megastep_timeouts(mlxd_model *m);
 // y[S][rows] = x[S][cols] . W^T with epilogue (STORE/RESIDUAL/SWIGLU)
 int linear_multi(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi,
                  const uint16_t *residual, float *yf, cudaStream_t st);
+// the same on tcgen05 (qgemm_tc.cu) for group-64 bf16-scale matrices with
+// rows a multiple of 128; timeouts: nonzero once a launch gave up a wait
+bool qgemm_tc_eligible(const QMat &W, int S);
+int qgemm_tc(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi, const uint16_t *res, float *yf,
+             cudaStream_t st);
+int qgemm_tc_timeouts();
 
 // ---- small ops (ops.cu)
 int embed_rows(const Embed &e, int H, int group, int vocab, const int32_t *ids, int S, uint16_t *h,

@@ -1281,6 +1281,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
         set_error("decode step gave up waiting at a grid barrier");
         rc = -1;
     }
+    if (!rc && qgemm_tc_timeouts()) {
+        set_error("prefill GEMM gave up waiting on its pipeline");
+        rc = -1;
+    }
     if (timing) {
         float pre = 0.f, dec = 0.f;
         cudaEventElapsedTime(&pre, e0, e1);

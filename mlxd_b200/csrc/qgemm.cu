@@ -272,6 +272,7 @@ int linear_multi(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi,
         set_error("qgemm: gate/up rows must pair 16-row blocks");
         return -1;
     }
+    if (qgemm_tc_eligible(W, S)) return qgemm_tc(W, x, S, y, epi, residual, yf, st);
     bool f32 = W.sdtype == MLXD_F32;
     if (W.group == 64) return f32 ? dispatch_qgemm<64, true>(W, x, S, y, epi, residual, yf, st)
                                   : dispatch_qgemm<64, false>(W, x, S, y, epi, residual, yf, st);

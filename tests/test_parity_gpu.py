@@ -70,6 +70,23 @@ def test_prefill_gemm_matches_oracle(S, rows, cols, group, f32):
     assert np.all(np.abs(g - o) <= tol), float(np.abs(g - o).max())
 
 
+@pytest.mark.parametrize("S", [130, 300])
+def test_prefill_gemm_tcgen05_large(S):
+    """The tcgen05 path at a larger shape (1024 x 4096, several 128-token
+    tiles and 64 K-steps, a partial last token tile): within 2 bf16 ulps of
+    the oracle's qmm."""
+    rows, cols = 1024, 4096
+    rng = np.random.default_rng(S)
+    w, s, b = synth_triplet(rows, cols, 64, S + 17)
+    x = rand_bf16((S, cols), rng)
+    lin = cuda.Linear(w, s, b, 64)
+    g = bf16_to_f32(lin(x))
+    o = bf16_to_f32(po.qlinear(x, w, s, b, 64, exact=False))
+    tol = 2 * 2.0 ** -8 * np.maximum(np.abs(o), 1e-3 * np.abs(o).max())
+    assert np.all(np.abs(g - o) <= tol), float(np.abs(g - o).max())
+    assert np.mean(g == o) > 0.9
+
+
 @pytest.mark.parametrize("rows,n", [(1, 64), (7, 1024), (3, 4096), (5, 128), (2, 300)])
 def test_rmsnorm_bit_exact(rows, n):
     rng = np.random.default_rng(n)
