@@ -7,6 +7,8 @@ streams its weights from HBM. Achieved GB/s = algorithmic bytes (packed
 weights + bf16 scale/bias per group + x in + y out) / mean launch time.
 
     python -m mlxd_b200.microbench [--shape gate_up] [--iters N] [--copies C]
+    python -m mlxd_b200.microbench --prefill-gemm   # tcgen05 GEMM, 24576 x 4096, 512 tokens
+    python -m mlxd_b200.microbench --attention      # decode attention, 32/8 heads, context 2048
 """
 import argparse
 import json
@@ -54,13 +56,58 @@ def measure(rows, cols, iters=None, copies=None, group=64, min_bytes=400e6):
             "gbs": round(gbs, 1), "copies": copies, "iters": iters}
 
 
+def prefill_gemm(rows=24576, cols=4096, S=512, reps=3):
+    """The prefill GEMM (mlxd_cuda_linear with S tokens) on one synthetic
+    group-64 matrix, `reps` launches; for ncu captures of the tcgen05 kernel."""
+    import numpy as np
+    w = cuda.DeviceBuffer(rows * cols // 2)
+    s = cuda.DeviceBuffer(rows * cols // 64 * 2)
+    b = cuda.DeviceBuffer(rows * cols // 64 * 2)
+    cuda.check(cuda.lib().mlxd_cuda_synth_quantized(w.ptr, s.ptr, b.ptr, rows, cols, 64, 5, 0.02, None),
+               "synth")
+    lin = cuda.Linear(w, s, b, 64, rows=rows, cols=cols)
+    x = np.random.default_rng(0).standard_normal((S, cols)).astype(np.float32)
+    xb = (x.view(np.uint32) >> 16).astype(np.uint16)
+    for _ in range(reps):
+        y = lin(xb)
+    lin.close()
+    return {"prefill_gemm": {"rows": rows, "cols": cols, "tokens": S, "launches": reps,
+                             "out_shape": list(y.shape)}}
+
+
+def decode_attention(context=2048, steps=6):
+    """Decode steps of a 2-layer model with the Qwen3-8B attention shape (32/8
+    heads, head_dim 128) after a `context`-token prefill, through
+    mlxd_cuda_forward; for ncu captures of the decode attention kernel."""
+    import numpy as np
+    cfg = cuda.synth_config(hidden=1024, layers=2, n_heads=32, n_kv_heads=8, head_dim=128, inter=1024,
+                            vocab=4096, max_pos=context + steps + 64)
+    m = cuda.Model(cfg, cuda.synth_host_tensors(cfg, seed=1))
+    kv = m.new_kv(context + steps + 64)
+    ids = np.random.default_rng(0).integers(0, cfg.vocab, context).tolist()
+    m.forward(kv, ids, want_logits=False)
+    t = 5
+    for _ in range(steps):
+        t = int(np.argmax(m.forward(kv, [t])))
+    m.close()
+    return {"decode_attention": {"context": context, "steps": steps, "last_token": t}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shape", default="all")
     ap.add_argument("--iters", type=int, default=None)
     ap.add_argument("--copies", type=int, default=None)
+    ap.add_argument("--prefill-gemm", action="store_true", help="run the tcgen05 prefill GEMM workload")
+    ap.add_argument("--attention", action="store_true", help="run the decode attention workload")
     args = ap.parse_args()
     cuda.init(0)
+    if args.prefill_gemm:
+        print(json.dumps(prefill_gemm()))
+        return
+    if args.attention:
+        print(json.dumps(decode_attention()))
+        return
     shp = shapes_of(QWEN3_8B)
     names = list(shp) if args.shape == "all" else [args.shape]
     out = {n: measure(*shp[n], iters=args.iters, copies=args.copies) for n in names}
