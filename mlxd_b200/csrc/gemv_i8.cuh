@@ -73,6 +73,7 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
         const int it = tid + k * NT;
         if (it < ni) xv[k] = *reinterpret_cast<const uint2 *>(x + i8_feature(it));
     }
+    MLXD_TRACE_T(st0_)
     float inv = 1.f;
     if (NORM) {
         const int Ta = n >= 1024 ? 256 : (n >= 256 ? 128 : 32);
@@ -95,6 +96,7 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
         for (int w = 0; w < NT / 32; w++) tot += s_red[w];
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
     }
+    MLXD_TRACE_T(st1_)
     // normalised values (bf16) of the thread's items, group sums, max |x|
     unsigned mx = 0u;
     for (int k0 = 0; k0 * NT < ni; k0 += MAXI) {
@@ -145,6 +147,7 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
     mx = 0u;
 #pragma unroll
     for (int w = 0; w < NT / 32; w++) mx = max(mx, s_max[w]);
+    MLXD_TRACE_T(st2_)
     int E = (int)(mx >> 7) - 127;            // exponent of the largest |x|
     if (E < -100) E = -100;                  // zero / subnormal: digits round to 0
     const float sc = __int_as_float((127 + 20 - E) << 23);
@@ -174,6 +177,7 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
         e[32] = p2;
     }
     __syncthreads();
+    MLXD_TRACE_REC(threadIdx.x == 0, 0x80 + (NORM ? 1 : 0), st1_ - st0_, st2_ - st1_, gtime() - st2_)
     return lscale;
 }
 
