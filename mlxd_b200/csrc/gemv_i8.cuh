@@ -57,6 +57,7 @@ MLXD_DEV int i8_feature(int it) {
     const int g = it >> 4, r = it & 15;
     return g * 64 + (r >> 3) * 32 + ((r >> 2) & 1) * 16 + (r & 3) * 4;
 }
+// s_red, s_max: NT/32 entries each, 16-byte aligned (NT a multiple of 128)
 template <int NT>
 MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float eps, uint16_t *xraw,
                         uint32_t *xbw, float *xsum4, uint32_t *zero16, float *s_red, unsigned *s_max,
@@ -93,7 +94,13 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
         __syncthreads();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < NT / 32; w++) tot += s_red[w];
+        for (int w = 0; w < NT / 32; w += 4) {   // 16-byte loads in flight together, sum in order
+            const float4 r4 = *reinterpret_cast<const float4 *>(s_red + w);
+            tot += r4.x;
+            tot += r4.y;
+            tot += r4.z;
+            tot += r4.w;
+        }
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
     }
     MLXD_TRACE_T(st1_)
@@ -146,7 +153,10 @@ MLXD_DEV float i8_stage(const uint16_t *x, const uint16_t *norm_w, int n, float 
     __syncthreads();
     mx = 0u;
 #pragma unroll
-    for (int w = 0; w < NT / 32; w++) mx = max(mx, s_max[w]);
+    for (int w = 0; w < NT / 32; w += 4) {
+        const uint4 m4 = *reinterpret_cast<const uint4 *>(s_max + w);
+        mx = max(max(mx, max(m4.x, m4.y)), max(m4.z, m4.w));
+    }
     MLXD_TRACE_T(st2_)
     int E = (int)(mx >> 7) - 127;            // exponent of the largest |x|
     if (E < -100) E = -100;                  // zero / subnormal: digits round to 0

@@ -696,8 +696,8 @@ __global__ void __launch_bounds__(MS_CT, 1) megastep_kernel(const MsCall kv, int
                                                             int pool_units) {
     using RowT = typename std::conditional<D == 128, uint2, uint32_t>::type;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ float s_red[MS_WARPS];
-    __shared__ unsigned s_max[MS_WARPS];
+    __shared__ __align__(16) float s_red[MS_WARPS];
+    __shared__ __align__(16) unsigned s_max[MS_WARPS];
     __shared__ volatile int s_dead;
     const MsSmem Lo = ms_layout(max_cols, MA.H, D, REP, pool_items, pool_units);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

@@ -896,8 +896,8 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
     static_assert(DEPTH == 1 || DEPTH == 2, "register item buffers");
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ float s_red[NW];
-    __shared__ unsigned s_max[NW];
+    __shared__ __align__(16) float s_red[NW];
+    __shared__ __align__(16) unsigned s_max[NW];
     __shared__ unsigned long long s_key[NW];
     const int nbk = a.cols / 512;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
