@@ -9,6 +9,7 @@ weights + bf16 scale/bias per group + x in + y out) / mean launch time.
     python -m mlxd_b200.microbench [--shape gate_up] [--iters N] [--copies C]
     python -m mlxd_b200.microbench --prefill-gemm   # tcgen05 GEMM, 24576 x 4096, 512 tokens
     python -m mlxd_b200.microbench --attention      # decode attention, 32/8 heads, context 2048
+    python -m mlxd_b200.microbench --sampler        # sampler, V 151936, T 0.7 k 50 p 0.9 rep 1.1
 """
 import argparse
 import json
@@ -93,6 +94,30 @@ def decode_attention(context=2048, steps=6):
     return {"decode_attention": {"context": context, "steps": steps, "last_token": t}}
 
 
+def sampler(V=151936, reps=6):
+    """The sampler (mlxd_cuda_sample) on one bf16 logits row of V entries with
+    the sampled-decode settings of the Mistral-style workload: temperature 0.7,
+    top-k 50, top-p 0.9, repetition penalty 1.1 over the last 256 context
+    tokens; `reps` draws with their device times (CUDA events)."""
+    import ctypes as C
+    import numpy as np
+    rng = np.random.default_rng(0)
+    logits = (rng.standard_normal(V).astype(np.float32) * 3.0)
+    lb = (logits.view(np.uint32) >> 16).astype(np.uint16)
+    ctx = rng.integers(0, V, 256).astype(np.int32)
+    sp = cuda.sampling(temperature=0.7, top_k=50, top_p=0.9, seed=7, repetition_penalty=1.1,
+                       repetition_context=256)
+    dl = cuda.DeviceBuffer.from_array(lb)
+    dc = cuda.DeviceBuffer.from_array(ctx)
+    tok = cuda.DeviceBuffer(4)
+    toks = []
+    for r in range(reps):
+        cuda.check(cuda.lib().mlxd_cuda_sample(dl.ptr, cuda.BF16, V, C.byref(sp), dc.ptr, len(ctx), r, tok.ptr,
+                                               None, None, None), "sample")
+        toks.append(int(tok.to_array(np.int32, (1,))[0]))
+    return {"sampler": {"V": V, "draws": reps, "tokens": toks}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shape", default="all")
@@ -100,6 +125,7 @@ def main():
     ap.add_argument("--copies", type=int, default=None)
     ap.add_argument("--prefill-gemm", action="store_true", help="run the tcgen05 prefill GEMM workload")
     ap.add_argument("--attention", action="store_true", help="run the decode attention workload")
+    ap.add_argument("--sampler", action="store_true", help="run the sampler on a 151936-entry row")
     args = ap.parse_args()
     cuda.init(0)
     if args.prefill_gemm:
@@ -107,6 +133,9 @@ def main():
         return
     if args.attention:
         print(json.dumps(decode_attention()))
+        return
+    if args.sampler:
+        print(json.dumps(sampler()))
         return
     shp = shapes_of(QWEN3_8B)
     names = list(shp) if args.shape == "all" else [args.shape]
