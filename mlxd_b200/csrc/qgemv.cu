@@ -870,9 +870,11 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
 // block of 8 groups the bias multipliers xsum4[t][j] (the group sum for even
 // t, 0 for odd t), a 16-byte zero entry, the item partials and the counters
 struct I8Smem {
-    size_t xb, xsum, zero, pool, cnt, total;
+    size_t xb, xsum, zero, pool, cnt, ring, total;
 };
-static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int pool_units) {
+// ring: one 4.6 KB item slot per warp (ring_warps of them) for the item
+// requested with cp.async before the producer is waited for
+static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int pool_units, int ring_warps = 0) {
     I8Smem L;
     const int ng = cols / 64;
     L.xb = (((size_t)cols * 2 + 15) / 16) * 16;
@@ -880,7 +882,8 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
     L.zero = L.xsum + (size_t)(ng / 8) * 64;
     L.pool = L.zero + 16;
     L.cnt = L.pool + (size_t)pool_items * 64;
-    L.total = L.cnt + (size_t)pool_units * 4;
+    L.ring = ((L.cnt + (size_t)pool_units * 4 + 15) / 16) * 16;
+    L.total = L.ring + (size_t)ring_warps * 4608;
     return L;
 }
 
@@ -889,7 +892,10 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
 // (4 KB of tiles + two 16-byte scale/bias words each) in registers while
 // computing the current one, the first DEPTH of them requested before the
 // PDL wait.
-template <int PRO, int EPI, int NW, int DEPTH>
+// SM2: each warp's second item goes to a shared-memory slot by cp.async
+// before the wait (DEPTH 1), so two items per warp stream during the wait and
+// the staging of x without costing registers
+template <int PRO, int EPI, int NW, int DEPTH, bool SM2>
 __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int pool_items) {
     MLXD_TRACE_START
     constexpr int NT = NW * 32;
@@ -907,7 +913,8 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     const int ipu = nbk * UNIT_RB;
     const int n = (u1 - u0) * ipu;
     const long long i0 = (long long)u0 * ipu;
-    const I8Smem L = i8_layout(a.cols, pool_items, (u1 - u0));
+    static_assert(!SM2 || DEPTH == 1, "the shared-memory item follows one register item");
+    const I8Smem L = i8_layout(a.cols, pool_items, (u1 - u0), SM2 ? NW : 0);
     float *pool = reinterpret_cast<float *>(smem_raw + L.pool);
     int *s_cnt = reinterpret_cast<int *>(smem_raw + L.cnt);
     for (int i = tid; i < u1 - u0; i += NT) s_cnt[i] = 0;
@@ -928,6 +935,16 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     };
 #pragma unroll
     for (int d = 0; d < DEPTH; d++) load(d, warp + d * NW);
+    unsigned char *slot = smem_raw + L.ring + (size_t)warp * 4608;
+    if constexpr (SM2) {
+        if (warp + NW < n) {
+            const uint8_t *pw = a.ti8 + (i0 + warp + NW) * 4096 + lane * 16;
+#pragma unroll
+            for (int p = 0; p < 8; p++) cp_async16(slot + p * 512 + lane * 16, pw + p * 512);
+            cp_async16(slot + 4096 + lane * 16, a.sbi + (i0 + warp + NW) * 512 + lane * 16);
+        }
+        cp_async_commit();
+    }
     l2_prefetch_share(a.pf);
     I8Pre<NT> pre;
     i8_stage_pre<NT>(pre, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols);
@@ -946,23 +963,11 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     const I8Lane IL = i8_lane(xbw, xsum4, zero16, lscale);
 
     unsigned long long best = 0ull;
-    // item k from buffer d; the buffer is refilled with item k + DEPTH*NW
-    auto process = [&](int d, int k) {
-        const int kn = k + DEPTH * NW;
-        const bool more = kn < n;
-        const uint8_t *pwn = a.ti8 + (i0 + kn) * 4096 + lane * 16;
+    // the item's 16 partial sums to the pool; the warp completing a unit
+    // adds the unit's partials in item order and runs the epilogue
+    auto finish = [&](int k, float y0, float y1) {
         const int unit = k / ipu;
         const int iu = k - unit * ipu;
-        const int bk = iu % nbk;
-        const uint4 sA = sb[d][0], sB = sb[d][1];
-        if (more) {
-            sb[d][0] = ldg_nc_v4_ef(sbl + (i0 + kn) * 512, pol);
-            sb[d][1] = ldg_nc_v4_ef(sbl + (i0 + kn) * 512 + 16, pol);
-        }
-        float y0, y1;
-        i8_item(wb[d], sA, sB, IL, bk, y0, y1, [&](int p) {
-            if (more) wb[d][p] = ldg_nc_v4_ef(pwn + p * 512, pol);
-        });
         float *ps = pool + (size_t)unit * ipu * 16;
         if (t == 0) {
             ps[iu * 16 + gq] = y0;
@@ -980,9 +985,45 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
             rb_epilogue<EPI>(a, ps, nbk, u0 + unit, lane, best);
         }
     };
-    for (int k = warp; k < n; k += DEPTH * NW) {
-        process(0, k);
-        if (DEPTH == 2 && k + NW < n) process(DEPTH - 1, k + NW);
+    // item k from register buffer d, refilled with item kn as it is read
+    auto process = [&](int d, int k, int kn) {
+        const bool more = kn < n;
+        const uint8_t *pwn = a.ti8 + (i0 + kn) * 4096 + lane * 16;
+        const int bk = (k % ipu) % nbk;
+        const uint4 sA = sb[d][0], sB = sb[d][1];
+        if (more) {
+            sb[d][0] = ldg_nc_v4_ef(sbl + (i0 + kn) * 512, pol);
+            sb[d][1] = ldg_nc_v4_ef(sbl + (i0 + kn) * 512 + 16, pol);
+        }
+        float y0, y1;
+        i8_item(wb[d], sA, sB, IL, bk, y0, y1, [&](int p) {
+            if (more) wb[d][p] = ldg_nc_v4_ef(pwn + p * 512, pol);
+        });
+        finish(k, y0, y1);
+    };
+    if constexpr (SM2) {
+        const int cnt = warp < n ? (n - warp + NW - 1) / NW : 0;
+        if (cnt > 0) process(0, warp, warp + 2 * NW);
+        if (cnt > 1) {
+            // the item in the shared-memory slot (the lanes' copies seen by all)
+            cp_async_wait<0>();
+            __syncwarp();
+            uint4 w[8];
+#pragma unroll
+            for (int p = 0; p < 8; p++) w[p] = *reinterpret_cast<const uint4 *>(slot + p * 512 + lane * 16);
+            const unsigned char *rec = slot + 4096 + (gq * 2 + (t >> 1)) * 32;
+            const uint4 sA = *reinterpret_cast<const uint4 *>(rec), sB = *reinterpret_cast<const uint4 *>(rec + 16);
+            const int k = warp + NW;
+            float y0, y1;
+            i8_item(w, sA, sB, IL, (k % ipu) % nbk, y0, y1, I8NoRefill{});
+            finish(k, y0, y1);
+        }
+        for (int i = 2; i < cnt; i++) process(0, warp + i * NW, warp + (i + 1) * NW);
+    } else {
+        for (int k = warp; k < n; k += DEPTH * NW) {
+            process(0, k, k + DEPTH * NW);
+            if (DEPTH == 2 && k + NW < n) process(DEPTH - 1, k + NW, k + NW + DEPTH * NW);
+        }
     }
     if constexpr (EPI == EPI_ARGMAX) {
 #pragma unroll
@@ -1140,17 +1181,17 @@ static int launch_gemv8r(GemvArgs a, cudaStream_t st, bool pdl) {
     return 0;
 }
 
-template <int PRO, int EPI, int NW, int DEPTH>
+template <int PRO, int EPI, int NW, int DEPTH, bool SM2>
 static int launch_gemv_i8_cfg(GemvArgs a, cudaStream_t st, bool pdl) {
-    auto kern = qgemv_i8_kernel<PRO, EPI, NW, DEPTH>;
+    auto kern = qgemv_i8_kernel<PRO, EPI, NW, DEPTH, SM2>;
     const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
     const int n_units = a.rows / 16 / unit_rb;
     int grid = num_sms();
     if (grid > n_units) grid = n_units;
     const int per = (n_units + grid - 1) / grid;
     const int pool_items = per * unit_rb * (a.cols / 512);
-    const size_t smem = i8_layout(a.cols, pool_items, per).total;
-    if (smem > 200 * 1024) {
+    const size_t smem = i8_layout(a.cols, pool_items, per, SM2 ? NW : 0).total;
+    if (smem > 220 * 1024) {
         set_error("qgemv: %d x %d needs %zu bytes of shared memory", a.rows, a.cols, smem);
         return -1;
     }
@@ -1174,10 +1215,17 @@ static int launch_gemv_i8_cfg(GemvArgs a, cudaStream_t st, bool pdl) {
 }
 
 // 16 warps with one item in registers ahead: on Qwen3-8B 608 tokens/s,
-// against 582 for 12 warps x 2 items and 479 for 16 x 2 (register spills)
+// against 582 for 12 warps x 2 items and 479 for 16 x 2 (register spills).
+// A launch without programmatic dependent launch (a projection on its own)
+// also streams each warp's second item into shared memory before staging x:
+// gate|up 15.8 -> 14.4 us, lm_head at 6.43 TB/s. Inside the PDL-chained
+// decode graph the same early traffic slows the previous kernel's tail
+// (646 -> 614 tokens/s), so chained launches keep one item; loading even that
+// one after the wait instead of before it costs 636 -> 589 tokens/s.
 template <int PRO, int EPI>
 static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
-    return launch_gemv_i8_cfg<PRO, EPI, 16, 1>(a, st, pdl);
+    if (!pdl) return launch_gemv_i8_cfg<PRO, EPI, 16, 1, true>(a, st, pdl);
+    return launch_gemv_i8_cfg<PRO, EPI, 16, 1, false>(a, st, pdl);
 }
 
 static int dispatch_gemv_i8(int pro, int epi, const GemvArgs &a, cudaStream_t st, bool pdl) {
