@@ -18,6 +18,10 @@
 //   online softmax in the log2 domain, f32, per head;
 //   O += P V      mma.m16n8k16: A = P as bf16 hi + lo (P = hi + lo to 2^-17,
 //                 so P.V keeps f32 precision), B = V rows through ldmatrix.trans.
+// A row r < REP of both MMAs is head r; rows REP..2REP-1 repeat the heads, so
+// that P's hi part (rows < REP) and lo part (the repeats) share one P.V MMA
+// and are added once after the loop (REP 8: the lo rows are 8..15, in the
+// same lanes as their hi rows).
 // The chunk holding the new position gets the new k/v rows written over its
 // (not yet appended) cache rows. Warps merge in shared memory, the cluster
 // synchronises, and CTA r merges the r-th slice of the group's outputs from
@@ -193,12 +197,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
         }
     }
     __syncwarp();
-    // A fragments of q (rows: heads gq < REP; rows gq + 8 are zero)
+    // A fragments of q: row gq holds head gq % REP for gq < 2 REP (REP 8:
+    // head gq, rows gq + 8 unused in q K^T), other rows are zero
+    constexpr bool LO8 = REP == 8;            // lo rows are gq + 8, same lane
+    const bool rowv = LO8 || gq < 2 * REP;
+    const int hrow = LO8 ? gq : gq % REP;
     uint32_t qa[NKK][2];
 #pragma unroll
     for (int kk = 0; kk < NKK; kk++) {
-        qa[kk][0] = gq < REP ? *reinterpret_cast<const uint32_t *>(sq + gq * D + 16 * kk + 2 * t) : 0u;
-        qa[kk][1] = gq < REP ? *reinterpret_cast<const uint32_t *>(sq + gq * D + 16 * kk + 8 + 2 * t) : 0u;
+        qa[kk][0] = rowv ? *reinterpret_cast<const uint32_t *>(sq + hrow * D + 16 * kk + 2 * t) : 0u;
+        qa[kk][1] = rowv ? *reinterpret_cast<const uint32_t *>(sq + hrow * D + 16 * kk + 8 + 2 * t) : 0u;
     }
 
     MLXD_TRACE_T(tr_prep_)
@@ -266,20 +274,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
         for (int n = 0; n < NTO; n++) {
             o[n][0] *= al;
             o[n][1] *= al;
+            if (LO8) {
+                o[n][2] *= al;
+                o[n][3] *= al;
+            }
         }
-        // P as bf16 hi + lo
+        // P as bf16 hi + lo: hi in rows < REP, lo in the repeated rows
         const uint32_t h0 = pack_bf2(p[0][0], p[0][1]), h1 = pack_bf2(p[1][0], p[1][1]);
         const uint32_t l0 = pack_bf2(p[0][0] - lo_bf(h0), p[0][1] - hi_bf(h0));
         const uint32_t l1 = pack_bf2(p[1][0] - lo_bf(h1), p[1][1] - hi_bf(h1));
-        const uint32_t ahi[4] = {h0, 0u, h1, 0u}, alo[4] = {l0, 0u, l1, 0u};
+        uint32_t ap[4];
+        if (LO8) {
+            ap[0] = h0, ap[1] = l0, ap[2] = h1, ap[3] = l1;
+        } else {
+            ap[0] = gq < REP ? h0 : gq < 2 * REP ? l0 : 0u;
+            ap[2] = gq < REP ? h1 : gq < 2 * REP ? l1 : 0u;
+            ap[1] = ap[3] = 0u;
+        }
 #pragma unroll
         for (int n2 = 0; n2 < NTO / 2; n2++) {
             uint32_t b[4];
             ldmatrix_x4_trans(b, vb + tc_sw<D>(((lane >> 3) & 1) * 8 + (lane & 7), 2 * n2 + (lane >> 4)));
-            mma_bf16_16816(o[2 * n2], ahi, b[0], b[1]);
-            mma_bf16_16816(o[2 * n2], alo, b[0], b[1]);
-            mma_bf16_16816(o[2 * n2 + 1], ahi, b[2], b[3]);
-            mma_bf16_16816(o[2 * n2 + 1], alo, b[2], b[3]);
+            mma_bf16_16816(o[2 * n2], ap, b[0], b[1]);
+            mma_bf16_16816(o[2 * n2 + 1], ap, b[2], b[3]);
         }
         __syncwarp();
         issue(c + TC_NBUF);
@@ -288,6 +305,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(AttnDecodeArgs a
     MLXD_TRACE_T(tr_loop_)
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
+    // O of head gq: its hi rows plus its lo rows
+#pragma unroll
+    for (int n = 0; n < NTO; n++) {
+        if (LO8) {
+            o[n][0] += o[n][2];
+            o[n][1] += o[n][3];
+        } else {
+            o[n][0] += __shfl_down_sync(0xffffffffu, o[n][0], 4 * REP);
+            o[n][1] += __shfl_down_sync(0xffffffffu, o[n][1], 4 * REP);
+        }
+    }
     // the warps' partials, then the CTA's
     if (gq < REP) {
         if (t == 0) {
@@ -431,43 +459,68 @@ static int tc_launch_cl(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
 }
 
 // clusters of 16 CTAs per kv head when hkv of them fit at once, else 8;
-// 1 when neither fits (the split-merge kernel serves)
+// -1 when neither fits (the split-merge kernel serves)
+template <int D, int REP>
+static int tc_cluster(int hkv) {
+    static int cl_for[65] = {};   // per hkv: 0 unknown, 16, 8 or -1 (none)
+    const int key = hkv <= 64 ? hkv : 64;
+    if (cl_for[key] == 0) cl_for[key] = tc_fits<D, REP, 16>(hkv) ? 16 : tc_fits<D, REP, 8>(hkv) ? 8 : -1;
+    return cl_for[key];
+}
 template <int D, int REP>
 static int tc_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
-    static int cl_for[65] = {};   // per hkv: 0 unknown, 16, 8 or -1 (none)
-    const int key = a.hkv <= 64 ? a.hkv : 64;
-    if (cl_for[key] == 0) cl_for[key] = tc_fits<D, REP, 16>(a.hkv) ? 16 : tc_fits<D, REP, 8>(a.hkv) ? 8 : -1;
-    if (cl_for[key] == 16) return tc_launch_cl<D, REP, 16>(a, st, pdl);
-    if (cl_for[key] == 8) return tc_launch_cl<D, REP, 8>(a, st, pdl);
+    const int cl = tc_cluster<D, REP>(a.hkv);
+    if (cl == 16) return tc_launch_cl<D, REP, 16>(a, st, pdl);
+    if (cl == 8) return tc_launch_cl<D, REP, 8>(a, st, pdl);
     return 1;
 }
+template <int D, int REP>
+static int tc_sms(const AttnDecodeArgs &a) {
+    const int cl = tc_cluster<D, REP>(a.hkv);
+    return cl > 0 ? cl * a.hkv : 0;
+}
 
-// 0: launched; 1: this kernel does not serve the shape (the caller falls back);
-// -1: error. MLXD_ATTN_TC=0 turns it off.
-int attention_decode_tc(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+static bool tc_on() {
     static const bool on = [] {
         const char *e = getenv("MLXD_ATTN_TC");
         return !e || atoi(e) != 0;
     }();
-    if (!on) return 1;
-    const int D = a.rope.D, rep = a.hq / a.hkv;
-    if (a.rope.rope_dims != D || a.hkv > 64) return 1;
-    if (D == 128) {
-        switch (rep) {
-        case 1: return tc_launch<128, 1>(a, st, pdl);
-        case 2: return tc_launch<128, 2>(a, st, pdl);
-        case 4: return tc_launch<128, 4>(a, st, pdl);
-        case 8: return tc_launch<128, 8>(a, st, pdl);
-        }
-    } else if (D == 64) {
-        switch (rep) {
-        case 1: return tc_launch<64, 1>(a, st, pdl);
-        case 2: return tc_launch<64, 2>(a, st, pdl);
-        case 4: return tc_launch<64, 4>(a, st, pdl);
-        case 8: return tc_launch<64, 8>(a, st, pdl);
-        }
-    }
-    return 1;
+    return on;
 }
+
+#define MLXD_TC_DISPATCH(FN, ...)                                   \
+    const int D = a.rope.D, rep = a.hq / a.hkv;                     \
+    if (a.rope.rope_dims != D || a.hkv > 64) return NONE;           \
+    if (D == 128) {                                                 \
+        switch (rep) {                                              \
+        case 1: return FN<128, 1>(__VA_ARGS__);                     \
+        case 2: return FN<128, 2>(__VA_ARGS__);                     \
+        case 4: return FN<128, 4>(__VA_ARGS__);                     \
+        case 8: return FN<128, 8>(__VA_ARGS__);                     \
+        }                                                           \
+    } else if (D == 64) {                                           \
+        switch (rep) {                                              \
+        case 1: return FN<64, 1>(__VA_ARGS__);                      \
+        case 2: return FN<64, 2>(__VA_ARGS__);                      \
+        case 4: return FN<64, 4>(__VA_ARGS__);                      \
+        case 8: return FN<64, 8>(__VA_ARGS__);                      \
+        }                                                           \
+    }                                                               \
+    return NONE;
+
+// 0: launched; 1: this kernel does not serve the shape (the caller falls back);
+// -1: error. MLXD_ATTN_TC=0 turns it off.
+int attention_decode_tc(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+    constexpr int NONE = 1;
+    if (!tc_on()) return NONE;
+    MLXD_TC_DISPATCH(tc_launch, a, st, pdl)
+}
+
+int attention_decode_tc_sms(const AttnDecodeArgs &a) {
+    constexpr int NONE = 0;
+    if (!tc_on()) return NONE;
+    MLXD_TC_DISPATCH(tc_sms, a)
+}
+#undef MLXD_TC_DISPATCH
 
 }  // namespace mlxd

@@ -35,6 +35,7 @@ struct GemvArgs {
     int *cnt;                   // per-unit arrival counters (zero between launches)
     int ws_slots;               // set by the launcher
     PfList pf;                  // weight-stream ranges this launch requests into L2
+    int grid_cap;               // at most this many CTAs (0: one per SM)
 };
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl);
 // the arrays (pointer, bytes) that the decode GEMV of W reads, in order
@@ -101,6 +102,9 @@ int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
 // the tensor-core decode kernel (one cluster per kv head): 0 launched, 1 not
 // applicable to the shape or device, -1 error
 int attention_decode_tc(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
+// SMs the decode attention kernel holds (one CTA each) for this shape; 0 when
+// the tensor-core kernel does not serve it
+int attention_decode_tc_sms(const AttnDecodeArgs &a);
 // prefill (S queries at positions pos0..): q [S][hq][D]; gate [S][qdim] or null
 int attention_prefill(const uint16_t *q, int S, int pos0, const uint16_t *kc,
                       const uint16_t *vc, int cap, int window, int hq, int hkv, int D,

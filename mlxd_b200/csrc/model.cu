@@ -460,6 +460,13 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         if (attention_decode(ad, st, pdl)) return -1;
         GemvArgs o = {};
         plan.gemv(4 * l + 1, o.pf);
+        // the o projection runs on the SMs that attention leaves free (one
+        // attention CTA per SM), its CTAs resident with their weights loaded
+        // while attention runs, instead of a third of them starting cold after it
+        if (pdl) {
+            const int att_sms = attention_decode_tc_sms(ad), sms = num_sms();
+            if (att_sms > 0 && sms - att_sms >= sms / 4) o.grid_cap = sms - att_sms;
+        }
         o.ws = m->gemv_ws;
         o.cnt = m->gemv_cnt;
         o.x = m->att;

@@ -1187,6 +1187,7 @@ static int launch_gemv_i8_cfg(GemvArgs a, cudaStream_t st, bool pdl) {
     const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
     const int n_units = a.rows / 16 / unit_rb;
     int grid = num_sms();
+    if (a.grid_cap > 0 && grid > a.grid_cap) grid = a.grid_cap;
     if (grid > n_units) grid = n_units;
     const int per = (n_units + grid - 1) / grid;
     const int pool_items = per * unit_rb * (a.cols / 512);
@@ -1222,9 +1223,12 @@ static int launch_gemv_i8_cfg(GemvArgs a, cudaStream_t st, bool pdl) {
 // decode graph the same early traffic slows the previous kernel's tail
 // (646 -> 614 tokens/s), so chained launches keep one item; loading even that
 // one after the wait instead of before it costs 636 -> 589 tokens/s.
+// A launch capped to the SMs that the running attention kernel leaves free
+// (the o projection) streams two items per warp too: its CTAs are resident
+// and idle for the whole attention step.
 template <int PRO, int EPI>
 static int launch_gemv_i8(GemvArgs a, cudaStream_t st, bool pdl) {
-    if (!pdl) return launch_gemv_i8_cfg<PRO, EPI, 16, 1, true>(a, st, pdl);
+    if (!pdl || a.grid_cap > 0) return launch_gemv_i8_cfg<PRO, EPI, 16, 1, true>(a, st, pdl);
     return launch_gemv_i8_cfg<PRO, EPI, 16, 1, false>(a, st, pdl);
 }
 

@@ -279,11 +279,15 @@ def test_persistent_step_matches_layer_kernels(monkeypatch):
 
 
 @pytest.mark.parametrize("family,kw", [(cuda.QWEN3, {}), (cuda.MISTRAL, dict(window=24)),
-                                       (cuda.QWEN3, dict(n_kv_heads=8))])
+                                       (cuda.QWEN3, dict(n_kv_heads=8)),
+                                       (cuda.QWEN3, dict(n_kv_heads=4)),
+                                       (cuda.QWEN3, dict(n_heads=16, n_kv_heads=2)),
+                                       (cuda.QWEN3, dict(head_dim=64, n_heads=8, n_kv_heads=1))])
 def test_cluster_attention_matches_oracle(monkeypatch, family, kw):
     """Decode attention with the splits of a kv head merged through
     distributed shared memory (MLXD_ATTN_CLUSTER=1) against the oracle, on a
-    plain cache, a wrapping sliding-window ring and one query head per kv head."""
+    plain cache, a wrapping sliding-window ring, and 1, 2, 4 and 8 query heads
+    per kv head (head dims 128 and 64)."""
     monkeypatch.setenv("MLXD_ATTN_CLUSTER", "1")
     cfg = qwen3_small(family=family, layers=2, **kw)
     m, o = synth_pair(cfg, seed=6)
