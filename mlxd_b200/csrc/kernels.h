@@ -36,6 +36,8 @@ struct GemvArgs {
     int ws_slots;               // set by the launcher
     PfList pf;                  // weight-stream ranges this launch requests into L2
     int grid_cap;               // at most this many CTAs (0: one per SM)
+    int res_early;              // EPI_RESIDUAL: the residual was complete before the producer of
+                                // x started, so a chained launch requests it before its wait
 };
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl);
 // the arrays (pointer, bytes) that the decode GEMV of W reads, in order

@@ -478,6 +478,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         } else {
             o.y = m->h1;
             o.residual = m->h;
+            o.res_early = 1;   // written by the previous layer's down GEMV (or the embedding)
             if (qgemv(L.o, PRO_PLAIN, EPI_RESIDUAL, o, st, pdl)) return -1;
         }
         GemvArgs gu = {};
@@ -502,6 +503,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         } else {
             dn.y = m->h;
             dn.residual = m->h1;
+            dn.res_early = 1;   // written by the o GEMV, two launches back
             if (qgemv(L.down, PRO_PLAIN, EPI_RESIDUAL, dn, st, pdl)) return -1;
         }
     }

@@ -698,9 +698,11 @@ MLXD_TRACE_BINDER(qgemv)
 
 constexpr int RB_THREADS = 512, RB_WARPS = 16;
 
+// res_s: EPI_RESIDUAL, the unit's 16 residual rows already in shared memory
+// (nullptr: read from global memory)
 template <int EPI>
 MLXD_DEV void rb_epilogue(const GemvArgs &a, const float *ps, int nbk, int unit, int lane,
-                          unsigned long long &best) {
+                          unsigned long long &best, const uint16_t *res_s = nullptr) {
     constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
     if (lane >= 16) return;
     float acc[UNIT_RB];
@@ -717,6 +719,8 @@ MLXD_DEV void rb_epilogue(const GemvArgs &a, const float *ps, int nbk, int unit,
         a.y[row] = f2bf(acc[0]);
         const unsigned long long key = argmax_key(rbf(acc[0]), a.row_offset + row);
         best = key > best ? key : best;
+    } else if (EPI == EPI_RESIDUAL && res_s) {
+        a.y[row] = f2bf(__fadd_rn(bf2f(res_s[lane]), rbf(acc[0])));
     } else {
         epilogue_row<EPI>(a, row, acc[0]);
     }
@@ -870,8 +874,9 @@ __global__ void __launch_bounds__(RB_THREADS, 1) qgemv8r_kernel(GemvArgs a, int 
 // block of 8 groups the bias multipliers xsum4[t][j] (the group sum for even
 // t, 0 for odd t), a 16-byte zero entry, the item partials and the counters
 struct I8Smem {
-    size_t xb, xsum, zero, pool, cnt, ring, total;
+    size_t xb, xsum, zero, pool, cnt, res, ring, total;
 };
+// res: the residual rows of the CTA's units (16 bf16 per unit);
 // ring: one 4.6 KB item slot per warp (ring_warps of them) for the item
 // requested with cp.async before the producer is waited for
 static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int pool_units, int ring_warps = 0) {
@@ -882,7 +887,8 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
     L.zero = L.xsum + (size_t)(ng / 8) * 64;
     L.pool = L.zero + 16;
     L.cnt = L.pool + (size_t)pool_items * 64;
-    L.ring = ((L.cnt + (size_t)pool_units * 4 + 15) / 16) * 16;
+    L.res = ((L.cnt + (size_t)pool_units * 4 + 15) / 16) * 16;
+    L.ring = L.res + (size_t)pool_units * 32;
     L.total = L.ring + (size_t)ring_warps * 4608;
     return L;
 }
@@ -918,6 +924,16 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     float *pool = reinterpret_cast<float *>(smem_raw + L.pool);
     int *s_cnt = reinterpret_cast<int *>(smem_raw + L.cnt);
     for (int i = tid; i < u1 - u0; i += NT) s_cnt[i] = 0;
+    // residual rows complete before the producer started: requested now, 16
+    // bytes (8 rows) per thread, waited for by their threads before the
+    // staging's last barrier
+    uint16_t *s_res = reinterpret_cast<uint16_t *>(smem_raw + L.res);
+    const bool res_s = EPI == EPI_RESIDUAL && a.res_early && (reinterpret_cast<uintptr_t>(a.residual) & 15) == 0;
+    const bool res_mine = res_s && tid < 2 * (u1 - u0);
+    if (res_mine) {
+        cp_async16(s_res + 8 * tid, a.residual + (size_t)u0 * 16 + 8 * tid);
+        cp_async_commit();
+    }
 
     // the warp's first items stream while the previous kernel finishes
     const uint64_t pol = l2_policy_evict_first();
@@ -950,6 +966,7 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     i8_stage_pre<NT>(pre, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols);
     pdl_wait();
     MLXD_TRACE_WAITED
+    if (res_mine) cp_async_wait<0>();
     uint16_t *xraw = reinterpret_cast<uint16_t *>(smem_raw);
     uint32_t *xbw = reinterpret_cast<uint32_t *>(smem_raw + L.xb);
     float *xsum4 = reinterpret_cast<float *>(smem_raw + L.xsum);
@@ -982,7 +999,7 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
         done = __shfl_sync(0xffffffffu, done, 0);
         if (done) {
             __threadfence_block();
-            rb_epilogue<EPI>(a, ps, nbk, u0 + unit, lane, best);
+            rb_epilogue<EPI>(a, ps, nbk, u0 + unit, lane, best, res_s ? s_res + unit * 16 : nullptr);
         }
     };
     // item k from register buffer d, refilled with item kn as it is read
