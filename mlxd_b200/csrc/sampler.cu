@@ -16,6 +16,15 @@
 // are formed from the survivors alone at their virtual positions. exp is the
 // shared Cody-Waite implementation, so candidate sets match the oracle bit for
 // bit given identical logits. Uniforms: SplitMix64 on (seed, step).
+//
+// The passes over the vocabulary run on ceil(V / 1024) CTAs of 256 threads,
+// one 1024-logit chunk each: statistics (penalty, max, argmax, partial
+// logsumexp, scaling, radix pass 0), three further radix passes for top_k,
+// then masking and candidate compaction. In each launch the CTA that arrives
+// last (an atomic ticket, no waiting) reduces the partials; only order-free
+// quantities (max, argmax key, histogram counts) decide the candidate set, so
+// it does not depend on the split. The logsumexp (logprob only) combines
+// per-chunk partial sums.
 #include <cub/cub.cuh>
 #include "common.cuh"
 #include "kernels.h"
@@ -26,12 +35,17 @@ constexpr int SAMP_THREADS = 1024;
 constexpr int SAMP_CAND = 4096;
 constexpr int SAMP_NB = 1024;
 
+constexpr int SAMP_CH = 1024;   // logits per CTA of the parallel passes
+constexpr int SAMP_PT = 256;    // threads per CTA of the parallel passes
+
 struct SampMeta {
     float m;        // max of scaled values
     float lse;      // logsumexp of the raw (penalised) logits
     float ck;       // top-k cutoff (or -inf)
     int n_surv;     // survivors after top-k
     int mode;       // 0 greedy done, 1 candidates, 2 full sort
+    uint32_t prefix;  // radix select: key bits fixed so far
+    int need;         // radix select: rank still to find below the prefix
 };
 
 struct SampWork {
@@ -45,6 +59,12 @@ struct SampWork {
     void *cub_tmp = nullptr;
     size_t cub_bytes = 0;
     SampMeta *meta = nullptr;
+    // per-CTA partials of the parallel passes ([ceil(V / SAMP_CH)])
+    float *p_max = nullptr, *p_sum = nullptr, *p_smax = nullptr;
+    unsigned long long *p_key = nullptr;
+    unsigned int *hist = nullptr;   // [256] radix histogram (zero between passes)
+    unsigned int *ctr = nullptr;    // [2] arrivals, survivors (zero between launches)
+    float *ev = nullptr;            // [V] exp(v - m) of the ascending survivors (tail)
     int V = 0;
 };
 static SampWork g_work;
@@ -76,162 +96,281 @@ MLXD_DEV float load_logit(const void *p, int i) {
     else return ((const float *)p)[i];
 }
 
-// block reductions for 1024 threads
-MLXD_DEV float block_max(float v, float *sh) {
+// reductions over the SAMP_PT threads of a CTA (result in every thread)
+MLXD_DEV float cta_max(float v, float *sh) {
     v = warp_max(v);
-    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     __syncthreads();
-    if (l == 0) sh[w] = v;
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
     __syncthreads();
     float r = -INFINITY;
-    for (int i = 0; i < (int)(blockDim.x >> 5); i++) r = fmaxf(r, sh[i]);
+#pragma unroll
+    for (int i = 0; i < SAMP_PT / 32; i++) r = fmaxf(r, sh[i]);
     return r;
 }
-MLXD_DEV float block_sum(float v, float *sh) {
+MLXD_DEV float cta_sum(float v, float *sh) {
     v = warp_sum(v);
-    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     __syncthreads();
-    if (l == 0) sh[w] = v;
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
     __syncthreads();
     float r = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); i++) r += sh[i];
+#pragma unroll
+    for (int i = 0; i < SAMP_PT / 32; i++) r += sh[i];
     return r;
 }
-
-template <typename T>
-__global__ void __launch_bounds__(SAMP_THREADS) samp_prep_kernel(
-    const void *logits, int V, mlxd_sampling sp, const int32_t *ctx, int n_ctx, SampWork w,
-    int32_t *tok, float *lp, uint8_t *keep) {
-    __shared__ float sh[32];
-    __shared__ unsigned int hist[256];
-    __shared__ uint32_t s_prefix;
-    __shared__ int s_need;
-    const int tid = threadIdx.x;
-    const bool greedy = sp.temperature < 0.01f;
-    for (int i = tid; i < V; i += SAMP_THREADS) w.xw[i] = load_logit<T>(logits, i);
-    __syncthreads();
-    if (!greedy && tid == 0 && sp.repetition_penalty > 0.f && sp.repetition_penalty != 1.0f &&
-        n_ctx > 0) {
-        int R = sp.repetition_context > 0 ? sp.repetition_context : n_ctx;
-        int start = n_ctx > R ? n_ctx - R : 0;
-        for (int i = start; i < n_ctx; i++) {
-            int id = ctx[i];
-            if (id < 0 || id >= V) continue;
-            bool dup = false;
-            for (int k = start; k < i; k++) dup |= (ctx[k] == id);
-            if (dup) continue;
-            float x = w.xw[id];
-            w.xw[id] = x > 0.f ? __fdiv_rn(x, sp.repetition_penalty) : __fmul_rn(x, sp.repetition_penalty);
-        }
+MLXD_DEV unsigned long long cta_max_u64(unsigned long long v, unsigned long long *sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+        v = other > v ? other : v;
     }
     __syncthreads();
-    // max and logsumexp of the raw values; greedy argmax (first index)
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    unsigned long long r = 0ull;
+#pragma unroll
+    for (int i = 0; i < SAMP_PT / 32; i++) r = sh[i] > r ? sh[i] : r;
+    return r;
+}
+// count one value in bin b of a shared-memory histogram: the lanes of a warp
+// that share a bin add once (logits crowd a few bins of the top key bytes)
+MLXD_DEV void hist_add(unsigned int *hist, unsigned b, bool on) {
+    const unsigned act = __ballot_sync(0xffffffffu, on);
+    if (!on) return;
+    const unsigned peers = __match_any_sync(act, b);
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[b], (unsigned)__popc(peers));
+}
+// true in every thread of the CTA that arrived last at ctr (after its
+// writes); that CTA then sees every other CTA's writes
+MLXD_DEV bool last_arrival(unsigned int *ctr, bool *s_last) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *s_last = atomicAdd(ctr, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (*s_last) __threadfence();
+    return *s_last;
+}
+// next radix digit (bits shift..shift+7 below the prefix) from the summed
+// histogram: the bin holding the need-th largest key, scanning from the top
+MLXD_DEV void radix_step(const unsigned int *hs, int shift, SampMeta *meta) {
+    uint32_t prefix = meta->prefix;
+    int need = meta->need;
+    for (int b = 255; b >= 0; b--) {
+        const int c = (int)hs[b];
+        if (c >= need) {
+            prefix |= (uint32_t)b << shift;
+            break;
+        }
+        need -= c;
+    }
+    meta->prefix = prefix;
+    meta->need = need;
+}
+
+// Pass 1 over chunk blockIdx.x: logits (repetition penalty applied), their
+// max / first-index argmax / exp-sum partials, the scaled values and the
+// histogram of their top key byte. The last CTA reduces: greedy token and
+// logprob, or the max of the scaled values, the logsumexp and radix digit 0.
+template <typename T>
+__global__ void __launch_bounds__(SAMP_PT) samp_stats_kernel(
+    const void *logits, int V, mlxd_sampling sp, const int32_t *ctx, int n_ctx, SampWork w,
+    int32_t *tok, float *lp, int topk) {
+    __shared__ float xs[SAMP_CH];
+    __shared__ int first[SAMP_CH];
+    __shared__ unsigned int hist[256];
+    __shared__ float sh[SAMP_PT / 32];
+    __shared__ unsigned long long shk[SAMP_PT / 32];
+    __shared__ bool s_last;
+    const int tid = threadIdx.x;
+    const int c0 = blockIdx.x * SAMP_CH, n = min(V - c0, SAMP_CH);
+    const bool greedy = sp.temperature < 0.01f;
+    const bool pen = !greedy && sp.repetition_penalty > 0.f && sp.repetition_penalty != 1.0f && n_ctx > 0;
+    for (int i = tid; i < n; i += SAMP_PT) {
+        xs[i] = load_logit<T>(logits, c0 + i);
+        first[i] = 0x7fffffff;
+    }
+    hist[tid] = 0u;
+    __syncthreads();
+    if (pen) {
+        // each distinct id of the last R context tokens once (its first
+        // occurrence in the window)
+        const int R = sp.repetition_context > 0 ? sp.repetition_context : n_ctx;
+        const int start = n_ctx > R ? n_ctx - R : 0;
+        for (int j = start + tid; j < n_ctx; j += SAMP_PT) {
+            const int id = ctx[j];
+            if (id >= c0 && id < c0 + n) atomicMin(&first[id - c0], j);
+        }
+        __syncthreads();
+        for (int i = tid; i < n; i += SAMP_PT)
+            if (first[i] != 0x7fffffff) {
+                const float x = xs[i];
+                xs[i] = x > 0.f ? __fdiv_rn(x, sp.repetition_penalty) : __fmul_rn(x, sp.repetition_penalty);
+            }
+    }
     float mx = -INFINITY;
-    unsigned long long best = 0;
-    for (int i = tid; i < V; i += SAMP_THREADS) {
-        float x = w.xw[i];
+    unsigned long long best = 0ull;
+    for (int i = tid; i < n; i += SAMP_PT) {
+        const float x = xs[i];
+        w.xw[c0 + i] = x;
         mx = fmaxf(mx, x);
-        unsigned long long k = ((unsigned long long)ord_key(x) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        const unsigned long long k = ((unsigned long long)ord_key(x) << 32) | (0xFFFFFFFFu - (uint32_t)(c0 + i));
         best = k > best ? k : best;
     }
-    mx = block_max(mx, sh);
+    mx = cta_max(mx, sh);
+    best = cta_max_u64(best, shk);
     float se = 0.f;
-    for (int i = tid; i < V; i += SAMP_THREADS) se += expf(w.xw[i] - mx);
-    se = block_sum(se, sh);
-    float lse = mx + logf(se);
-    if (greedy) {
-        __shared__ unsigned long long sb[32];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-            best = other > best ? other : best;
-        }
-        if ((tid & 31) == 0) sb[tid >> 5] = best;
-        __syncthreads();
-        if (tid == 0) {
-            unsigned long long b = 0;
-            for (int i = 0; i < SAMP_THREADS / 32; i++) b = sb[i] > b ? sb[i] : b;
-            int t = (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
-            *tok = t;
-            if (lp) *lp = w.xw[t] - lse;
-            w.meta->mode = 0;
-        }
-        if (keep) {
-            __syncthreads();
-            for (int i = tid; i < V; i += SAMP_THREADS) keep[i] = 0;
-            __syncthreads();
-            if (tid == 0) keep[*tok] = 1;
-        }
-        return;
-    }
-    // scaled values
-    for (int i = tid; i < V; i += SAMP_THREADS) {
-        float x = w.xw[i];
-        w.sw[i] = sp.temperature != 1.0f ? __fdiv_rn(x, sp.temperature) : x;
-    }
-    __syncthreads();
-    float m = -INFINITY;
-    for (int i = tid; i < V; i += SAMP_THREADS) m = fmaxf(m, w.sw[i]);
-    m = block_max(m, sh);
-    // top-k cutoff by radix select on order-preserving keys (MSB first)
-    float ck = -INFINITY;
-    if (sp.top_k > 0 && sp.top_k < V) {
-        if (tid == 0) {
-            s_prefix = 0;
-            s_need = sp.top_k;
-        }
-        for (int pass = 0; pass < 4; pass++) {
-            int shift = 24 - 8 * pass;
-            for (int b = tid; b < 256; b += SAMP_THREADS) hist[b] = 0;
-            __syncthreads();
-            uint32_t prefix = s_prefix;
-            uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (32 - 8 * pass));
-            for (int i = tid; i < V; i += SAMP_THREADS) {
-                uint32_t k = ord_key(w.sw[i]);
-                if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1u);
+    if (mx > -INFINITY)
+        for (int i = tid; i < n; i += SAMP_PT) se += expf(xs[i] - mx);
+    se = cta_sum(se, sh);
+    float smx = -INFINITY;
+    if (!greedy) {
+        for (int it = 0; it < SAMP_CH / SAMP_PT; it++) {
+            const int i = tid + it * SAMP_PT;
+            float v = -INFINITY;
+            if (i < n) {
+                v = sp.temperature != 1.0f ? __fdiv_rn(xs[i], sp.temperature) : xs[i];
+                w.sw[c0 + i] = v;
+                smx = fmaxf(smx, v);
             }
-            __syncthreads();
-            if (tid == 0) {
-                int need = s_need;
-                for (int b = 255; b >= 0; b--) {
-                    int c = (int)hist[b];
-                    if (c >= need) {
-                        s_prefix = prefix | ((uint32_t)b << shift);
-                        break;
-                    }
-                    need -= c;
-                }
-                s_need = need;
-            }
-            __syncthreads();
+            if (topk) hist_add(hist, ord_key(v) >> 24, i < n);
         }
-        ck = key_val(s_prefix);
-        for (int i = tid; i < V; i += SAMP_THREADS)
-            if (!(w.sw[i] >= ck)) w.sw[i] = -INFINITY;
-        __syncthreads();
+        smx = cta_max(smx, sh);
+        if (topk && hist[tid]) atomicAdd(&w.hist[tid], hist[tid]);
     }
-    // survivors
-    __shared__ int s_cnt;
-    if (tid == 0) s_cnt = 0;
-    __syncthreads();
-    for (int i = tid; i < V; i += SAMP_THREADS) {
-        float v = w.sw[i];
-        if (v > -INFINITY) {
-            int slot = atomicAdd(&s_cnt, 1);
-            if (slot < SAMP_CAND) {
-                w.cand_v[slot] = v;
-                w.cand_i[slot] = i;
-            }
-        }
+    if (tid == 0) {
+        w.p_max[blockIdx.x] = mx;
+        w.p_sum[blockIdx.x] = se;
+        w.p_key[blockIdx.x] = best;
+        w.p_smax[blockIdx.x] = smx;
+    }
+    if (!last_arrival(&w.ctr[0], &s_last)) return;
+    const int G = gridDim.x;
+    float M = -INFINITY, m = -INFINITY;
+    unsigned long long key = 0ull;
+    for (int g = tid; g < G; g += SAMP_PT) {
+        M = fmaxf(M, __ldcg(&w.p_max[g]));
+        m = fmaxf(m, __ldcg(&w.p_smax[g]));
+        const unsigned long long kg = __ldcg(&w.p_key[g]);
+        key = kg > key ? kg : key;
+    }
+    M = cta_max(M, sh);
+    m = cta_max(m, sh);
+    key = cta_max_u64(key, shk);
+    float S = 0.f;
+    for (int g = tid; g < G; g += SAMP_PT) {
+        const float pm = __ldcg(&w.p_max[g]);
+        if (pm > -INFINITY) S += __ldcg(&w.p_sum[g]) * expf(pm - M);
+    }
+    S = cta_sum(S, sh);
+    if (topk) {
+        hist[tid] = __ldcg(&w.hist[tid]);
+        w.hist[tid] = 0u;
     }
     __syncthreads();
     if (tid == 0) {
-        w.meta->m = m;
-        w.meta->lse = lse;
-        w.meta->ck = ck;
-        w.meta->n_surv = s_cnt;
-        w.meta->mode = s_cnt <= SAMP_CAND ? 1 : 2;
+        const float lse = M + logf(S);
+        if (greedy) {
+            const int t = (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+            *tok = t;
+            if (lp) *lp = __ldcg(&w.xw[t]) - lse;
+            w.meta->mode = 0;
+        } else {
+            w.meta->m = m;
+            w.meta->lse = lse;
+            w.meta->ck = -INFINITY;
+            if (topk) {
+                w.meta->prefix = 0u;
+                w.meta->need = sp.top_k;
+                radix_step(hist, 24, w.meta);
+            }
+        }
+        w.ctr[0] = 0u;
     }
+}
+
+// radix passes 1..3 of the top_k select over the scaled values; the last
+// CTA fixes the next key byte (and after pass 3 the cutoff)
+__global__ void __launch_bounds__(SAMP_PT) samp_radix_kernel(int V, int pass, SampWork w) {
+    __shared__ unsigned int hist[256];
+    __shared__ bool s_last;
+    const int tid = threadIdx.x;
+    const int c0 = blockIdx.x * SAMP_CH, n = min(V - c0, SAMP_CH);
+    const int shift = 24 - 8 * pass;
+    const uint32_t pmask = 0xFFFFFFFFu << (32 - 8 * pass);
+    const uint32_t prefix = w.meta->prefix;
+    hist[tid] = 0u;
+    __syncthreads();
+    for (int it = 0; it < SAMP_CH / SAMP_PT; it++) {
+        const int i = tid + it * SAMP_PT;
+        const uint32_t k = i < n ? ord_key(w.sw[c0 + i]) : 0u;
+        hist_add(hist, (k >> shift) & 0xFFu, i < n && (k & pmask) == prefix);
+    }
+    __syncthreads();
+    if (hist[tid]) atomicAdd(&w.hist[tid], hist[tid]);
+    if (!last_arrival(&w.ctr[0], &s_last)) return;
+    hist[tid] = __ldcg(&w.hist[tid]);
+    w.hist[tid] = 0u;
+    __syncthreads();
+    if (tid == 0) {
+        radix_step(hist, shift, w.meta);
+        if (pass == 3) w.meta->ck = key_val(w.meta->prefix);
+        w.ctr[0] = 0u;
+    }
+}
+
+// values below the top_k cutoff masked to -inf; survivors appended to the
+// candidate list (one slot reservation per CTA); the last CTA records the
+// survivor count and the path (candidates or full sort)
+__global__ void __launch_bounds__(SAMP_PT) samp_mask_kernel(int V, SampWork w, int topk) {
+    __shared__ float lv[SAMP_CH];
+    __shared__ int li[SAMP_CH];
+    __shared__ int s_cnt, s_base;
+    __shared__ bool s_last;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int c0 = blockIdx.x * SAMP_CH, n = min(V - c0, SAMP_CH);
+    const float ck = topk ? w.meta->ck : -INFINITY;
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    for (int it = 0; it < SAMP_CH / SAMP_PT; it++) {
+        const int i = tid + it * SAMP_PT;
+        float v = -INFINITY;
+        if (i < n) {
+            v = w.sw[c0 + i];
+            if (topk && !(v >= ck)) {
+                v = -INFINITY;
+                w.sw[c0 + i] = v;
+            }
+        }
+        const bool sv = i < n && v > -INFINITY;
+        const unsigned bal = __ballot_sync(0xffffffffu, sv);
+        int base = 0;
+        if (lane == 0 && bal) base = atomicAdd(&s_cnt, __popc(bal));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (sv) {
+            const int slot = base + __popc(bal & ((1u << lane) - 1u));
+            lv[slot] = v;
+            li[slot] = c0 + i;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) s_base = s_cnt ? (int)atomicAdd(&w.ctr[1], (unsigned)s_cnt) : 0;
+    __syncthreads();
+    for (int j = tid; j < s_cnt && s_base + j < SAMP_CAND; j += SAMP_PT) {
+        w.cand_v[s_base + j] = lv[j];
+        w.cand_i[s_base + j] = li[j];
+    }
+    if (!last_arrival(&w.ctr[0], &s_last)) return;
+    if (tid == 0) {
+        const int tot = (int)__ldcg(&w.ctr[1]);
+        w.meta->n_surv = tot;
+        w.meta->mode = tot <= SAMP_CAND ? 1 : 2;
+        w.ctr[1] = 0u;
+        w.ctr[0] = 0u;
+    }
+}
+
+__global__ void samp_keep_token_kernel(int V, const int32_t *tok, uint8_t *keep) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < V) keep[i] = i == *tok ? 1 : 0;
 }
 
 // Ascending (value, index) order over a candidate list in shared memory.
@@ -256,113 +395,13 @@ __device__ void bitonic_sort_asc(float *v, int *ix, int n_pow2) {
     }
 }
 
-// Final stage on an ascending list of n values (the top n of V virtual
-// positions), sequential in one thread with the blocked association.
-__device__ void finish_sequential(const float *v, const int *ix, int n, int V, float m,
-                                  const mlxd_sampling &sp, float log_mp, uint64_t step,
-                                  float *out_thr, int *out_tok) {
-    const int bs = max(1, (V + SAMP_NB - 1) / SAMP_NB);
-    const int base = V - n;
-    // softmax denominator z over the survivors
-    auto blocked_total = [&](auto val_of, int from) {
-        float prefix = 0.f, bt = 0.f;
-        int cur = -1;
-        for (int i = from; i < n; i++) {
-            int b = (base + i) / bs;
-            if (b != cur) {
-                prefix = __fadd_rn(prefix, bt);
-                bt = 0.f;
-                cur = b;
-            }
-            bt = __fadd_rn(bt, val_of(i));
-        }
-        return __fadd_rn(prefix, bt);
-    };
-    float thr = -INFINITY;
-    if (sp.top_p < 1.0f) {
-        if (sp.top_p <= 0.0f) {
-            thr = m;
-        } else {
-            float z = blocked_total([&](int i) { return own_expf(__fsub_rn(v[i], m)); }, 0);
-            float t1 = __fsub_rn(1.0f, sp.top_p);
-            float prefix = 0.f, bt = 0.f, run = 0.f;
-            int cur = -1;
-            float cut = __int_as_float(0x7f800000);
-            for (int i = 0; i < n; i++) {
-                int b = (base + i) / bs;
-                if (b != cur) {
-                    prefix = __fadd_rn(prefix, bt);
-                    bt = 0.f;
-                    run = prefix;
-                    cur = b;
-                }
-                float p = __fdiv_rn(own_expf(__fsub_rn(v[i], m)), z);
-                run = __fadd_rn(run, p);
-                bt = __fadd_rn(bt, p);
-                if (run > t1) {
-                    cut = v[i];
-                    break;
-                }
-            }
-            thr = fminf(cut, m);
-        }
-    }
-    if (sp.min_p > 0.0f) thr = fmaxf(thr, __fadd_rn(m, log_mp));
-    // kept = suffix with v >= thr
-    int first = 0;
-    while (first < n && !(v[first] >= thr)) first++;
-    int nk = n - first;
-    // categorical over the kept suffix at virtual positions V-nk..V-1
-    const int kbase = V - nk;
-    float z2;
-    {
-        float prefix = 0.f, bt = 0.f;
-        int cur = -1;
-        for (int i = 0; i < nk; i++) {
-            int b = (kbase + i) / bs;
-            if (b != cur) {
-                prefix = __fadd_rn(prefix, bt);
-                bt = 0.f;
-                cur = b;
-            }
-            bt = __fadd_rn(bt, own_expf(__fsub_rn(v[first + i], m)));
-        }
-        z2 = __fadd_rn(prefix, bt);
-    }
-    float u = draw_uniform(sp.seed < 0 ? 0 : sp.seed, step);
-    float target = __fmul_rn(u, z2);
-    int pick = n - 1;
-    {
-        float prefix = 0.f, bt = 0.f, run = 0.f;
-        int cur = -1;
-        for (int i = 0; i < nk; i++) {
-            int b = (kbase + i) / bs;
-            if (b != cur) {
-                prefix = __fadd_rn(prefix, bt);
-                bt = 0.f;
-                run = prefix;
-                cur = b;
-            }
-            float e = own_expf(__fsub_rn(v[first + i], m));
-            run = __fadd_rn(run, e);
-            bt = __fadd_rn(bt, e);
-            if (run > target && e > 0.f) {
-                pick = first + i;
-                break;
-            }
-        }
-    }
-    *out_thr = thr;
-    *out_tok = ix[pick];
-}
-
-__global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(
-    int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w, int32_t *tok, float *lp,
-    uint8_t *keep, int full_scheduled) {
+// Candidate path: the survivors sorted ascending by (value, index) in shared
+// memory and written to the tail of the sorted arrays, where the full-sort
+// path leaves its survivors too.
+__global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(int V, SampWork w, int32_t *tok,
+                                                                  int full_scheduled) {
     __shared__ float sv[SAMP_CAND];
     __shared__ int si[SAMP_CAND];
-    __shared__ float s_thr;
-    __shared__ int s_tok;
     if (w.meta->mode == 2 && !full_scheduled) {
         // more tied survivors than the candidate list holds and no full sort
         // was scheduled: report an invalid token instead of a wrong one
@@ -379,48 +418,146 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(
     }
     __syncthreads();
     bitonic_sort_asc(sv, si, np2);
-    if (threadIdx.x == 0) {
-        finish_sequential(sv, si, n, V, w.meta->m, sp, log_mp, step, &s_thr, &s_tok);
-        *tok = s_tok;
-        if (lp) *lp = w.xw[s_tok] - w.meta->lse;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        w.sorted_v[V - n + i] = sv[i];
+        w.sorted_i[V - n + i] = si[i];
     }
-    __syncthreads();
-    if (keep) {
-        float thr = s_thr;
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            float v = w.sw[i];
-            keep[i] = (v > -INFINITY && v >= thr) ? 1 : 0;
+}
+
+// exp(v - m) of the n ascending survivors at sorted positions V-n..V-1
+__global__ void samp_exp_kernel(int V, SampWork w, int full_scheduled) {
+    const int mode = w.meta->mode;
+    if (mode == 0 || (mode == 2 && !full_scheduled)) return;
+    const int n = w.meta->n_surv;
+    const float m = w.meta->m;
+    for (int i = V - n + blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x)
+        w.ev[i] = own_expf(__fsub_rn(w.sorted_v[i], m));
+}
+
+// Final stage over the ascending survivors v[V-n..V-1] (sorted position p is
+// the p-th smallest of V virtual positions). Every sum below uses the blocked
+// association: positions form blocks of bs = ceil(V/1024); a block's values
+// are summed in order starting from zero, the block totals are folded in
+// block order, and a running sum enters each block at the fold of the
+// previous blocks' totals. Thread b owns block b, so the per-block parts run
+// in parallel and only the fold over at most 1024 totals is sequential; the
+// first position where a running sum crosses its target is the smallest such
+// position over all blocks. The result equals the sequential walk bit for bit.
+//   top_p: z = sum exp(v - m); cutoff = the value where the running sum of
+//          exp(v - m) / z first exceeds 1 - top_p (clamped to the max);
+//   min_p: cutoff >= max + log(min_p);
+//   draw:  inverse CDF of exp(v - m) over the kept suffix v >= cutoff, at
+//          u * (its blocked total), u from SplitMix64 on (seed, step).
+__global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
+    int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w, int32_t *tok, float *lp,
+    uint8_t *keep, int full_scheduled) {
+    __shared__ float sbt[SAMP_NB], spre[SAMP_NB];
+    __shared__ float s_z, s_thr;
+    __shared__ int s_at, s_first;
+    const int mode = w.meta->mode;
+    if (mode == 0 || (mode == 2 && !full_scheduled)) return;
+    const int tid = threadIdx.x;
+    const int n = w.meta->n_surv;
+    const float m = w.meta->m;
+    const int base = V - n;
+    const int bs = max(1, (V + SAMP_NB - 1) / SAMP_NB);
+    const int b_lo = base / bs, b_hi = (V - 1) / bs;   // blocks holding survivors
+    const float *v = w.sorted_v, *ev = w.ev;
+    const int b = tid;
+    // this thread's block clipped to [from, V)
+    auto range = [&](int from, int &lo, int &hi) {
+        lo = max(from, b * bs);
+        hi = min(V, (b + 1) * bs);
+    };
+    // block totals of f over [from, V) into sbt, then (thread 0) the running
+    // prefixes into spre and the total into *total
+    auto blocked = [&](int from, auto f, float *total) {
+        int lo, hi;
+        range(from, lo, hi);
+        if (b < SAMP_NB) {
+            float bt = 0.f;
+            for (int i = lo; i < hi; i++) bt = __fadd_rn(bt, f(i));
+            sbt[b] = bt;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float prefix = 0.f;
+#pragma unroll 8
+            for (int k = b_lo; k <= b_hi; k++) {
+                spre[k] = prefix;
+                prefix = __fadd_rn(prefix, sbt[k]);
+            }
+            *total = prefix;
+        }
+        __syncthreads();
+    };
+    // smallest position in [from, V) where the running sum of f first
+    // exceeds target (and ok(i) holds), or INT_MAX
+    auto crossing = [&](int from, auto f, float target, auto ok) {
+        if (tid == 0) s_at = 0x7fffffff;
+        __syncthreads();
+        int lo, hi;
+        range(from, lo, hi);
+        if (b >= b_lo && b <= b_hi && lo < hi) {
+            float run = spre[b];
+            for (int i = lo; i < hi; i++) {
+                const float x = f(i);
+                run = __fadd_rn(run, x);
+                if (run > target && ok(x)) {
+                    atomicMin(&s_at, i);
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        return s_at;
+    };
+    float thr = -INFINITY;
+    if (sp.top_p < 1.0f) {
+        if (sp.top_p <= 0.0f) {
+            thr = m;
+        } else {
+            blocked(base, [&](int i) { return ev[i]; }, &s_z);
+            const float z = s_z;
+            auto pf = [&](int i) { return __fdiv_rn(ev[i], z); };
+            blocked(base, pf, &s_thr);   // block totals and prefixes of p
+            const int at = crossing(base, pf, __fsub_rn(1.0f, sp.top_p), [](float) { return true; });
+            const float cut = at != 0x7fffffff ? v[at] : __int_as_float(0x7f800000);
+            thr = fminf(cut, m);
         }
     }
+    if (sp.min_p > 0.0f) thr = fmaxf(thr, __fadd_rn(m, log_mp));
+    // kept = the suffix with v >= thr
+    if (tid == 0) s_first = V;
+    __syncthreads();
+    for (int i = base + tid; i < V; i += blockDim.x)
+        if (v[i] >= thr) {
+            atomicMin(&s_first, i);
+            break;
+        }
+    __syncthreads();
+    const int first = s_first;
+    blocked(first, [&](int i) { return ev[i]; }, &s_z);
+    const float z2 = s_z;
+    const float u = draw_uniform(sp.seed < 0 ? 0 : sp.seed, step);
+    const int at = crossing(first, [&](int i) { return ev[i]; }, __fmul_rn(u, z2),
+                            [](float e) { return e > 0.f; });
+    const int pick = at != 0x7fffffff ? at : V - 1;
+    if (tid == 0) {
+        const int t = w.sorted_i[pick];
+        *tok = t;
+        if (lp) *lp = w.xw[t] - w.meta->lse;
+    }
+    if (keep)
+        for (int i = tid; i < V; i += blockDim.x) {
+            const float x = w.sw[i];
+            keep[i] = (x > -INFINITY && x >= thr) ? 1 : 0;
+        }
 }
 
 __global__ void iota_kernel(int *p, int n) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = i;
-}
-
-// full-sort path: the ascending list lives in global memory
-__global__ void samp_full_kernel(int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w,
-                                 int32_t *tok, float *lp, uint8_t *keep) {
-    __shared__ float s_thr;
-    __shared__ int s_tok;
-    if (w.meta->mode != 2) return;
-    if (threadIdx.x == 0) {
-        // masked (-inf) entries sort first; survivors are the top n_surv
-        int n = w.meta->n_surv;
-        finish_sequential(w.sorted_v + (V - n), w.sorted_i + (V - n), n, V, w.meta->m, sp, log_mp,
-                          step, &s_thr, &s_tok);
-        *tok = s_tok;
-        if (lp) *lp = w.xw[s_tok] - w.meta->lse;
-    }
-    __syncthreads();
-    if (keep) {
-        float thr = s_thr;
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            float v = w.sw[i];
-            keep[i] = (v > -INFINITY && v >= thr) ? 1 : 0;
-        }
-    }
 }
 
 static int ensure_work(int V) {
@@ -429,6 +566,8 @@ static int ensure_work(int V) {
     dev_free(w.xw); dev_free(w.sw); dev_free(w.cand_v); dev_free(w.cand_i);
     dev_free(w.sorted_v); dev_free(w.sorted_i); dev_free(w.idx_in); dev_free(w.cub_tmp);
     dev_free(w.meta);
+    dev_free(w.p_max); dev_free(w.p_sum); dev_free(w.p_smax); dev_free(w.p_key);
+    dev_free(w.hist); dev_free(w.ctr); dev_free(w.ev);
     w = SampWork{};
     w.xw = (float *)dev_alloc(sizeof(float) * V);
     w.sw = (float *)dev_alloc(sizeof(float) * V);
@@ -438,6 +577,20 @@ static int ensure_work(int V) {
     w.sorted_i = (int *)dev_alloc(sizeof(int) * V);
     w.idx_in = (int *)dev_alloc(sizeof(int) * V);
     w.meta = (SampMeta *)dev_alloc(sizeof(SampMeta));
+    const int G = (V + SAMP_CH - 1) / SAMP_CH;
+    w.p_max = (float *)dev_alloc(sizeof(float) * G);
+    w.p_sum = (float *)dev_alloc(sizeof(float) * G);
+    w.p_smax = (float *)dev_alloc(sizeof(float) * G);
+    w.p_key = (unsigned long long *)dev_alloc(sizeof(unsigned long long) * G);
+    w.hist = (unsigned int *)dev_alloc(sizeof(unsigned int) * 256);
+    w.ctr = (unsigned int *)dev_alloc(sizeof(unsigned int) * 2);
+    w.ev = (float *)dev_alloc(sizeof(float) * V);
+    if (!w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev) return -1;
+    if (cudaMemset(w.hist, 0, sizeof(unsigned int) * 256) != cudaSuccess ||
+        cudaMemset(w.ctr, 0, sizeof(unsigned int) * 2) != cudaSuccess) {
+        set_error("sample: clearing the sampler's counters failed");
+        return -1;
+    }
     size_t tmp = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, tmp, (const float *)nullptr, (float *)nullptr,
                                     (const int *)nullptr, (int *)nullptr, V);
@@ -458,30 +611,44 @@ int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const 
     }
     if (ensure_work(V)) return -1;
     SampWork w = g_work;
+    const int G = (V + SAMP_CH - 1) / SAMP_CH;
+    const bool greedy = sp.temperature < 0.01f;
+    const int topk = !greedy && sp.top_k > 0 && sp.top_k < V;
     if (dtype == MLXD_BF16)
-        samp_prep_kernel<uint16_t><<<1, SAMP_THREADS, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, keep);
+        samp_stats_kernel<uint16_t><<<G, SAMP_PT, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, topk);
     else if (dtype == MLXD_F32)
-        samp_prep_kernel<float><<<1, SAMP_THREADS, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, keep);
+        samp_stats_kernel<float><<<G, SAMP_PT, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, topk);
     else {
         set_error("sample: logits dtype must be bf16 or f32");
         return -1;
     }
     MLXD_CHECK(cudaGetLastError());
-    if (sp.temperature < 0.01f) return 0;
+    if (greedy) {
+        if (keep) samp_keep_token_kernel<<<(V + 255) / 256, 256, 0, st>>>(V, tok, keep);
+        MLXD_CHECK(cudaGetLastError());
+        return 0;
+    }
+    if (topk)
+        for (int pass = 1; pass < 4; pass++) samp_radix_kernel<<<G, SAMP_PT, 0, st>>>(V, pass, w);
+    samp_mask_kernel<<<G, SAMP_PT, 0, st>>>(V, w, topk);
+    MLXD_CHECK(cudaGetLastError());
     float log_mp = sp.min_p > 0.0f ? logf(sp.min_p) : 0.0f;
     // With top_k <= 1024 the survivors fit the candidate list unless more than
     // 3072 values tie at the cutoff; otherwise the whole vocabulary is sorted.
     bool need_full = !(sp.top_k > 0 && sp.top_k <= 1024);
-    samp_cand_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep, need_full);
+    samp_cand_kernel<<<1, SAMP_THREADS, 0, st>>>(V, w, tok, need_full);
     MLXD_CHECK(cudaGetLastError());
     if (need_full) {
+        // ascending (value, index) over the whole vocabulary: a stable radix
+        // sort of the masked values with the indices in order
         iota_kernel<<<(V + 255) / 256, 256, 0, st>>>(w.idx_in, V);
         size_t tmp = w.cub_bytes;
         MLXD_CHECK(cub::DeviceRadixSort::SortPairs(w.cub_tmp, tmp, w.sw, w.sorted_v, w.idx_in,
                                                    w.sorted_i, V, 0, 32, st));
-        samp_full_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep);
-        MLXD_CHECK(cudaGetLastError());
     }
+    samp_exp_kernel<<<(V + 1023) / 1024, 256, 0, st>>>(V, w, need_full);
+    samp_finish_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep, need_full);
+    MLXD_CHECK(cudaGetLastError());
     return 0;
 }
 

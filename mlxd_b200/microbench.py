@@ -94,28 +94,48 @@ def decode_attention(context=2048, steps=6):
     return {"decode_attention": {"context": context, "steps": steps, "last_token": t}}
 
 
-def sampler(V=151936, reps=6):
+SAMPLER_DEFAULT = dict(temperature=0.7, top_k=50, top_p=0.9, seed=7, repetition_penalty=1.1,
+                      repetition_context=256)
+
+
+def sampler(V=151936, reps=6, timed=50, settings=None):
     """The sampler (mlxd_cuda_sample) on one bf16 logits row of V entries with
     the sampled-decode settings of the Mistral-style workload: temperature 0.7,
     top-k 50, top-p 0.9, repetition penalty 1.1 over the last 256 context
-    tokens; `reps` draws with their device times (CUDA events)."""
+    tokens (or `settings`); `reps` draws reported, then `timed` back-to-back
+    draws on the default stream between two CUDA events (the mean device time
+    per draw)."""
     import ctypes as C
     import numpy as np
+    import torch
     rng = np.random.default_rng(0)
     logits = (rng.standard_normal(V).astype(np.float32) * 3.0)
     lb = (logits.view(np.uint32) >> 16).astype(np.uint16)
     ctx = rng.integers(0, V, 256).astype(np.int32)
-    sp = cuda.sampling(temperature=0.7, top_k=50, top_p=0.9, seed=7, repetition_penalty=1.1,
-                       repetition_context=256)
+    settings = dict(SAMPLER_DEFAULT if settings is None else settings)
+    sp = cuda.sampling(**settings)
     dl = cuda.DeviceBuffer.from_array(lb)
     dc = cuda.DeviceBuffer.from_array(ctx)
     tok = cuda.DeviceBuffer(4)
+    L = cuda.lib()
+
+    def draw(step):
+        cuda.check(L.mlxd_cuda_sample(dl.ptr, cuda.BF16, V, C.byref(sp), dc.ptr, len(ctx), step, tok.ptr,
+                                      None, None, None), "sample")
     toks = []
     for r in range(reps):
-        cuda.check(cuda.lib().mlxd_cuda_sample(dl.ptr, cuda.BF16, V, C.byref(sp), dc.ptr, len(ctx), r, tok.ptr,
-                                               None, None, None), "sample")
+        draw(r)
         toks.append(int(tok.to_array(np.int32, (1,))[0]))
-    return {"sampler": {"V": V, "draws": reps, "tokens": toks}}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cuda.check(L.mlxd_cuda_synchronize(None), "sync")
+    e0.record(torch.cuda.default_stream())
+    for r in range(timed):
+        draw(reps + r)
+    e1.record(torch.cuda.default_stream())
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / timed
+    return {"sampler": {"V": V, "settings": settings, "draws": reps, "tokens": toks, "us_per_draw": round(us, 2),
+                        "timed_draws": timed}}
 
 
 def main():
@@ -126,6 +146,8 @@ def main():
     ap.add_argument("--prefill-gemm", action="store_true", help="run the tcgen05 prefill GEMM workload")
     ap.add_argument("--attention", action="store_true", help="run the decode attention workload")
     ap.add_argument("--sampler", action="store_true", help="run the sampler on a 151936-entry row")
+    ap.add_argument("--sampler-settings", default=None,
+                    help="JSON sampling settings for --sampler (default: the sampled-decode settings)")
     args = ap.parse_args()
     cuda.init(0)
     if args.prefill_gemm:
@@ -135,7 +157,7 @@ def main():
         print(json.dumps(decode_attention()))
         return
     if args.sampler:
-        print(json.dumps(sampler()))
+        print(json.dumps(sampler(settings=json.loads(args.sampler_settings) if args.sampler_settings else None)))
         return
     shp = shapes_of(QWEN3_8B)
     names = list(shp) if args.shape == "all" else [args.shape]
