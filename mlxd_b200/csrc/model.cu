@@ -1328,6 +1328,7 @@ void trace_bind_qgemv(unsigned long long *p);
 void trace_bind_attention(unsigned long long *p);
 void trace_bind_megastep(unsigned long long *p);
 void trace_bind_attention_tc(unsigned long long *p);
+void trace_bind_sampler(unsigned long long *p);
 }
 // timeline trace of the decode kernels (trace builds only): buf is a device
 // buffer of 4 + 4 * 2^20 u64, word 0 zeroed by the caller
@@ -1336,6 +1337,7 @@ extern "C" int mlxd_cuda_trace_bind(void *buf) {
     mlxd::trace_bind_attention((unsigned long long *)buf);
     mlxd::trace_bind_megastep((unsigned long long *)buf);
     mlxd::trace_bind_attention_tc((unsigned long long *)buf);
+    mlxd::trace_bind_sampler((unsigned long long *)buf);
     return 0;
 }
 #endif

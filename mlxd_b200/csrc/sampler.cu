@@ -31,6 +31,8 @@
 
 namespace mlxd {
 
+MLXD_TRACE_BINDER(sampler)
+
 constexpr int SAMP_THREADS = 1024;
 constexpr int SAMP_CAND = 4096;
 constexpr int SAMP_NB = 1024;
@@ -64,7 +66,9 @@ struct SampWork {
     unsigned long long *p_key = nullptr;
     unsigned int *hist = nullptr;   // [256] radix histogram (zero between passes)
     unsigned int *ctr = nullptr;    // [2] arrivals, survivors (zero between launches)
-    float *ev = nullptr;            // [V] exp(v - m) of the ascending survivors (tail)
+    float *ev = nullptr;            // exp(v - m) of the ascending survivors, block-transposed:
+                                    // position b*bs + j at ev[j*1024 + b] (bs = ceil(V/1024))
+    float *pv = nullptr;            // exp(v - m) / z, same layout (top_p)
     int V = 0;
 };
 static SampWork g_work;
@@ -150,20 +154,35 @@ MLXD_DEV bool last_arrival(unsigned int *ctr, bool *s_last) {
     return *s_last;
 }
 // next radix digit (bits shift..shift+7 below the prefix) from the summed
-// histogram: the bin holding the need-th largest key, scanning from the top
-MLXD_DEV void radix_step(const unsigned int *hs, int shift, SampMeta *meta) {
-    uint32_t prefix = meta->prefix;
-    int need = meta->need;
-    for (int b = 255; b >= 0; b--) {
-        const int c = (int)hs[b];
-        if (c >= need) {
-            prefix |= (uint32_t)b << shift;
-            break;
-        }
-        need -= c;
+// histogram hs (256 bins, shared memory): the bin holding the need-th largest
+// key, i.e. the first bin from the top whose running count reaches need. All
+// SAMP_PT (= 256) threads take part: thread t holds bin 255 - t and the
+// running counts come from a block scan; *prefix and *need (shared, read by
+// every thread beforehand) are updated by the thread that finds the bin.
+MLXD_DEV void radix_step(const unsigned int *hs, int shift, uint32_t *prefix, int *need, unsigned *s_wsum) {
+    const int t = threadIdx.x, lane = t & 31, wp = t >> 5;
+    const unsigned c = hs[255 - t];
+    unsigned incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
     }
-    meta->prefix = prefix;
-    meta->need = need;
+    if (lane == 31) s_wsum[wp] = incl;
+    const int nd = *need;
+    const uint32_t pf = *prefix;
+    __syncthreads();
+    unsigned before = 0;
+    for (int k = 0; k < wp; k++) before += s_wsum[k];
+    incl += before;
+    const unsigned excl = incl - c;
+    __syncthreads();
+    // the first bin (from the top) whose running count reaches need
+    if ((int)incl >= nd && (int)excl < nd) {
+        *prefix = pf | ((uint32_t)(255 - t) << shift);
+        *need = nd - (int)excl;
+    }
+    __syncthreads();
 }
 
 // Pass 1 over chunk blockIdx.x: logits (repetition penalty applied), their
@@ -261,11 +280,19 @@ __global__ void __launch_bounds__(SAMP_PT) samp_stats_kernel(
         if (pm > -INFINITY) S += __ldcg(&w.p_sum[g]) * expf(pm - M);
     }
     S = cta_sum(S, sh);
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_need;
+    __shared__ unsigned s_wsum[SAMP_PT / 32];
     if (topk) {
         hist[tid] = __ldcg(&w.hist[tid]);
         w.hist[tid] = 0u;
+        if (tid == 0) {
+            s_prefix = 0u;
+            s_need = sp.top_k;
+        }
+        __syncthreads();
+        radix_step(hist, 24, &s_prefix, &s_need, s_wsum);
     }
-    __syncthreads();
     if (tid == 0) {
         const float lse = M + logf(S);
         if (greedy) {
@@ -278,9 +305,8 @@ __global__ void __launch_bounds__(SAMP_PT) samp_stats_kernel(
             w.meta->lse = lse;
             w.meta->ck = -INFINITY;
             if (topk) {
-                w.meta->prefix = 0u;
-                w.meta->need = sp.top_k;
-                radix_step(hist, 24, w.meta);
+                w.meta->prefix = s_prefix;
+                w.meta->need = s_need;
             }
         }
         w.ctr[0] = 0u;
@@ -297,6 +323,10 @@ __global__ void __launch_bounds__(SAMP_PT) samp_radix_kernel(int V, int pass, Sa
     const int shift = 24 - 8 * pass;
     const uint32_t pmask = 0xFFFFFFFFu << (32 - 8 * pass);
     const uint32_t prefix = w.meta->prefix;
+    const int need = w.meta->need;
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_need;
+    __shared__ unsigned s_wsum[SAMP_PT / 32];
     hist[tid] = 0u;
     __syncthreads();
     for (int it = 0; it < SAMP_CH / SAMP_PT; it++) {
@@ -309,10 +339,16 @@ __global__ void __launch_bounds__(SAMP_PT) samp_radix_kernel(int V, int pass, Sa
     if (!last_arrival(&w.ctr[0], &s_last)) return;
     hist[tid] = __ldcg(&w.hist[tid]);
     w.hist[tid] = 0u;
-    __syncthreads();
     if (tid == 0) {
-        radix_step(hist, shift, w.meta);
-        if (pass == 3) w.meta->ck = key_val(w.meta->prefix);
+        s_prefix = prefix;
+        s_need = need;
+    }
+    __syncthreads();
+    radix_step(hist, shift, &s_prefix, &s_need, s_wsum);
+    if (tid == 0) {
+        w.meta->prefix = s_prefix;
+        w.meta->need = s_need;
+        if (pass == 3) w.meta->ck = key_val(s_prefix);
         w.ctr[0] = 0u;
     }
 }
@@ -424,14 +460,17 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(int V, SampWork
     }
 }
 
-// exp(v - m) of the n ascending survivors at sorted positions V-n..V-1
+// exp(v - m) of the n ascending survivors at sorted positions V-n..V-1, in
+// the block-transposed layout the final stage reads (thread b of a warp
+// walking block b reads 32 consecutive floats per step)
 __global__ void samp_exp_kernel(int V, SampWork w, int full_scheduled) {
     const int mode = w.meta->mode;
     if (mode == 0 || (mode == 2 && !full_scheduled)) return;
     const int n = w.meta->n_surv;
     const float m = w.meta->m;
+    const int bs = max(1, (V + SAMP_NB - 1) / SAMP_NB);
     for (int i = V - n + blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x)
-        w.ev[i] = own_expf(__fsub_rn(w.sorted_v[i], m));
+        w.ev[(i % bs) * SAMP_NB + i / bs] = own_expf(__fsub_rn(w.sorted_v[i], m));
 }
 
 // Final stage over the ascending survivors v[V-n..V-1] (sorted position p is
@@ -451,19 +490,23 @@ __global__ void samp_exp_kernel(int V, SampWork w, int full_scheduled) {
 __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
     int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w, int32_t *tok, float *lp,
     uint8_t *keep, int full_scheduled) {
-    __shared__ float sbt[SAMP_NB], spre[SAMP_NB];
+    __shared__ __align__(16) float sbt[SAMP_NB];
+    __shared__ __align__(16) float spre[SAMP_NB];
     __shared__ float s_z, s_thr;
     __shared__ int s_at, s_first;
     const int mode = w.meta->mode;
     if (mode == 0 || (mode == 2 && !full_scheduled)) return;
+    MLXD_TRACE_START
     const int tid = threadIdx.x;
     const int n = w.meta->n_surv;
     const float m = w.meta->m;
     const int base = V - n;
     const int bs = max(1, (V + SAMP_NB - 1) / SAMP_NB);
     const int b_lo = base / bs, b_hi = (V - 1) / bs;   // blocks holding survivors
-    const float *v = w.sorted_v, *ev = w.ev;
+    const float *v = w.sorted_v;
     const int b = tid;
+    // exp(v[i] - m) for a position i of this thread's block
+    auto ev = [&](int i) { return w.ev[(i - b * bs) * SAMP_NB + b]; };
     // this thread's block clipped to [from, V)
     auto range = [&](int from, int &lo, int &hi) {
         lo = max(from, b * bs);
@@ -475,17 +518,36 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
         int lo, hi;
         range(from, lo, hi);
         if (b < SAMP_NB) {
+            // 16 values in flight, then added in order
             float bt = 0.f;
-            for (int i = lo; i < hi; i++) bt = __fadd_rn(bt, f(i));
+            for (int i0 = lo; i0 < hi; i0 += 16) {
+                float x[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) x[j] = i0 + j < hi ? f(i0 + j) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (i0 + j < hi) bt = __fadd_rn(bt, x[j]);
+            }
             sbt[b] = bt;
         }
         __syncthreads();
         if (tid == 0) {
+            // the fold over the block totals of blocks b_lo..b_hi, in groups of
+            // 8 (blocks without positions in range hold +0, which leaves the
+            // non-negative prefix as it is); only the additions are serial
             float prefix = 0.f;
-#pragma unroll 8
-            for (int k = b_lo; k <= b_hi; k++) {
-                spre[k] = prefix;
-                prefix = __fadd_rn(prefix, sbt[k]);
+            for (int k0 = b_lo & ~7; k0 <= b_hi; k0 += 8) {
+                const float4 q0 = *reinterpret_cast<const float4 *>(sbt + k0);
+                const float4 q1 = *reinterpret_cast<const float4 *>(sbt + k0 + 4);
+                const float in[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                float out[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    out[j] = prefix;
+                    prefix = __fadd_rn(prefix, in[j]);
+                }
+                *reinterpret_cast<float4 *>(spre + k0) = make_float4(out[0], out[1], out[2], out[3]);
+                *reinterpret_cast<float4 *>(spre + k0 + 4) = make_float4(out[4], out[5], out[6], out[7]);
             }
             *total = prefix;
         }
@@ -500,13 +562,20 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
         range(from, lo, hi);
         if (b >= b_lo && b <= b_hi && lo < hi) {
             float run = spre[b];
-            for (int i = lo; i < hi; i++) {
-                const float x = f(i);
-                run = __fadd_rn(run, x);
-                if (run > target && ok(x)) {
-                    atomicMin(&s_at, i);
-                    break;
-                }
+            bool found = false;
+            for (int i0 = lo; i0 < hi && !found; i0 += 16) {
+                float x[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) x[j] = i0 + j < hi ? f(i0 + j) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (!found && i0 + j < hi) {
+                        run = __fadd_rn(run, x[j]);
+                        if (run > target && ok(x[j])) {
+                            atomicMin(&s_at, i0 + j);
+                            found = true;
+                        }
+                    }
             }
         }
         __syncthreads();
@@ -517,42 +586,72 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
         if (sp.top_p <= 0.0f) {
             thr = m;
         } else {
-            blocked(base, [&](int i) { return ev[i]; }, &s_z);
+            blocked(base, ev, &s_z);
+            MLXD_TRACE_T(tr_z_)
             const float z = s_z;
-            auto pf = [&](int i) { return __fdiv_rn(ev[i], z); };
+            // p = exp(v - m) / z, kept for the crossing pass (each thread
+            // reads back only its own block)
+            auto pf = [&](int i) {
+                const float pi = __fdiv_rn(ev(i), z);
+                w.pv[(i - b * bs) * SAMP_NB + b] = pi;
+                return pi;
+            };
+            auto pc = [&](int i) { return w.pv[(i - b * bs) * SAMP_NB + b]; };
             blocked(base, pf, &s_thr);   // block totals and prefixes of p
-            const int at = crossing(base, pf, __fsub_rn(1.0f, sp.top_p), [](float) { return true; });
+            MLXD_TRACE_T(tr_p_)
+            const int at = crossing(base, pc, __fsub_rn(1.0f, sp.top_p), [](float) { return true; });
+            MLXD_TRACE_T(tr_c_)
+            MLXD_TRACE_REC(tid == 0, 0x90, tr_z_, tr_p_, tr_c_)
             const float cut = at != 0x7fffffff ? v[at] : __int_as_float(0x7f800000);
             thr = fminf(cut, m);
         }
     }
     if (sp.min_p > 0.0f) thr = fmaxf(thr, __fadd_rn(m, log_mp));
-    // kept = the suffix with v >= thr
+    // kept = the suffix with v >= thr: the smallest such position, 16
+    // positions (a warp's 16 coalesced rows) in flight per step
     if (tid == 0) s_first = V;
     __syncthreads();
-    for (int i = base + tid; i < V; i += blockDim.x)
-        if (v[i] >= thr) {
-            atomicMin(&s_first, i);
+    for (int i0 = base + tid; i0 < V; i0 += 16 * SAMP_THREADS) {
+        bool hit[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int i = i0 + j * SAMP_THREADS;
+            hit[j] = i < V && v[i] >= thr;
+        }
+        int f = 0x7fffffff;
+#pragma unroll
+        for (int j = 15; j >= 0; j--)
+            if (hit[j]) f = i0 + j * SAMP_THREADS;
+        if (f != 0x7fffffff) {
+            atomicMin(&s_first, f);
             break;
         }
+    }
     __syncthreads();
     const int first = s_first;
-    blocked(first, [&](int i) { return ev[i]; }, &s_z);
+    MLXD_TRACE_T(tr_f_)
+    blocked(first, ev, &s_z);
+    MLXD_TRACE_T(tr_z2_)
     const float z2 = s_z;
     const float u = draw_uniform(sp.seed < 0 ? 0 : sp.seed, step);
-    const int at = crossing(first, [&](int i) { return ev[i]; }, __fmul_rn(u, z2),
+    const int at = crossing(first, ev, __fmul_rn(u, z2),
                             [](float e) { return e > 0.f; });
     const int pick = at != 0x7fffffff ? at : V - 1;
+    MLXD_TRACE_T(tr_d_)
+    MLXD_TRACE_REC(tid == 0, 0x91, tr_f_, tr_z2_, tr_d_)
     if (tid == 0) {
         const int t = w.sorted_i[pick];
         *tok = t;
         if (lp) *lp = w.xw[t] - w.meta->lse;
     }
     if (keep)
+#pragma unroll 8
         for (int i = tid; i < V; i += blockDim.x) {
             const float x = w.sw[i];
             keep[i] = (x > -INFINITY && x >= thr) ? 1 : 0;
         }
+    MLXD_TRACE_WAITED
+    MLXD_TRACE_END(0x92)
 }
 
 __global__ void iota_kernel(int *p, int n) {
@@ -567,7 +666,7 @@ static int ensure_work(int V) {
     dev_free(w.sorted_v); dev_free(w.sorted_i); dev_free(w.idx_in); dev_free(w.cub_tmp);
     dev_free(w.meta);
     dev_free(w.p_max); dev_free(w.p_sum); dev_free(w.p_smax); dev_free(w.p_key);
-    dev_free(w.hist); dev_free(w.ctr); dev_free(w.ev);
+    dev_free(w.hist); dev_free(w.ctr); dev_free(w.ev); dev_free(w.pv);
     w = SampWork{};
     w.xw = (float *)dev_alloc(sizeof(float) * V);
     w.sw = (float *)dev_alloc(sizeof(float) * V);
@@ -584,8 +683,9 @@ static int ensure_work(int V) {
     w.p_key = (unsigned long long *)dev_alloc(sizeof(unsigned long long) * G);
     w.hist = (unsigned int *)dev_alloc(sizeof(unsigned int) * 256);
     w.ctr = (unsigned int *)dev_alloc(sizeof(unsigned int) * 2);
-    w.ev = (float *)dev_alloc(sizeof(float) * V);
-    if (!w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev) return -1;
+    w.ev = (float *)dev_alloc(sizeof(float) * ((V + SAMP_NB - 1) / SAMP_NB) * SAMP_NB);
+    w.pv = (float *)dev_alloc(sizeof(float) * ((V + SAMP_NB - 1) / SAMP_NB) * SAMP_NB);
+    if (!w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev || !w.pv) return -1;
     if (cudaMemset(w.hist, 0, sizeof(unsigned int) * 256) != cudaSuccess ||
         cudaMemset(w.ctr, 0, sizeof(unsigned int) * 2) != cudaSuccess) {
         set_error("sample: clearing the sampler's counters failed");
