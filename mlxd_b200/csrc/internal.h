@@ -99,9 +99,14 @@ struct mlxd_model {
     int32_t *ctx = nullptr;     // context ids (prompt + generated)
     int32_t *n_ctx = nullptr;
     int ctx_cap = 0;
-    void *graph_exec = nullptr; // cudaGraphExec_t of one greedy decode step
+    unsigned long long *d_step = nullptr;   // sampled decoding: the draw's step
+    void *graph_exec = nullptr; // cudaGraphExec_t of one decode step (greedy or sampled)
     const void *graph_kv = nullptr;
+    unsigned long long graph_kv_serial = 0;   // a cache freed and another created at the same
+                                              // address must not replay the old graph
     bool graph_lp = false;
+    bool graph_sampled = false;
+    mlxd_sampling graph_sp = {};   // the settings a sampled graph was captured with
     // prefill scratch (grown on demand)
     int pre_cap = 0;
     uint16_t *p_h = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_q = nullptr, *p_att = nullptr,
@@ -122,4 +127,5 @@ struct mlxd_kv {
     int offset;                 // absolute positions written (host mirror)
     uint16_t *k = nullptr, *v = nullptr;   // [L][hkv][cap][d]
     int32_t *d_pos = nullptr;   // device copy of offset (position of the next token)
+    unsigned long long serial = 0;   // unique per created cache (keys the decode graph)
 };

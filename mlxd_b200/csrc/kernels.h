@@ -113,8 +113,13 @@ int attention_prefill(const uint16_t *q, int S, int pos0, const uint16_t *kc,
                       const uint16_t *gate_src, int qdim, uint16_t *out, cudaStream_t st);
 
 // ---- sampler (sampler.cu)
+// d_nctx / d_step (optional): the context length and the draw's step read
+// from device memory instead of n_ctx / step, so that the launches can be
+// replayed from a CUDA graph; sample_reserve(V) then runs before the capture
 int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const int32_t *ctx,
-           int n_ctx, uint64_t step, int32_t *tok, float *lp, uint8_t *keep, cudaStream_t st);
+           int n_ctx, uint64_t step, int32_t *tok, float *lp, uint8_t *keep, cudaStream_t st,
+           const int32_t *d_nctx = nullptr, const unsigned long long *d_step = nullptr);
+int sample_reserve(int V);
 int argmax_decode(const unsigned long long *amax, int32_t *tok, cudaStream_t st);
 
 }  // namespace mlxd

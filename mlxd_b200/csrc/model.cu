@@ -4,6 +4,8 @@
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
+
+#include <atomic>
 #include <chrono>
 #include <string>
 #include <unordered_map>
@@ -40,6 +42,15 @@ __global__ void step_finish_kernel(int32_t *d_pos, unsigned long long *amax, int
 }
 
 __global__ void append_token_kernel(int32_t *ctx, int idx, const int32_t *token) { ctx[idx] = *token; }
+
+// sampled decoding inside a CUDA graph: append the drawn token to the
+// context list and advance the context length and the draw's step
+__global__ void sampled_step_kernel(int32_t *ctx, int32_t *n_ctx, const int32_t *token,
+                                    unsigned long long *d_step) {
+    ctx[*n_ctx] = *token;
+    *n_ctx += 1;
+    *d_step += 1;
+}
 
 __global__ void add_partial_kernel(uint16_t *h_out, const uint16_t *h_in, const float *part, int n) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -886,7 +897,7 @@ void mlxd_cuda_model_destroy(mlxd_model *m) {
                     (void *)m->logits, (void *)m->part, (void *)m->att_count, (void *)m->amax,
                     (void *)m->token, (void *)m->part_h, (void *)m->p_h, (void *)m->p_x, (void *)m->p_qkv,
                     (void *)m->p_q, (void *)m->p_att, (void *)m->p_act, (void *)m->p_tmp, (void *)m->p_ids,
-                    (void *)m->p_part, (void *)m->ctx, (void *)m->n_ctx, (void *)m->lp,
+                    (void *)m->p_part, (void *)m->ctx, (void *)m->n_ctx, (void *)m->d_step, (void *)m->lp,
                     (void *)m->gemv_ws, (void *)m->gemv_cnt})
         dev_free(p);
     if (m->nccl) ncclCommDestroy((ncclComm_t)m->nccl);
@@ -926,7 +937,9 @@ int mlxd_cuda_kv_create(mlxd_kv **out, const mlxd_model *m, int capacity) {
         set_error("kv_create: bad arguments");
         return -1;
     }
+    static std::atomic<unsigned long long> kv_serial{0};
     mlxd_kv *kv = new mlxd_kv();
+    kv->serial = ++kv_serial;
     kv->layers = m->c.layers;
     kv->hkv = m->hkv;
     kv->d = m->c.head_dim;
@@ -1161,6 +1174,8 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
         if (!m->n_ctx) m->n_ctx = (int32_t *)dev_alloc(4);
         if (!m->n_ctx) return -1;
     }
+    if (!m->d_step) m->d_step = (unsigned long long *)dev_alloc(8);
+    if (!m->d_step) return -1;
     int32_t *pin = nullptr;
     MLXD_CHECK(cudaMallocHost(&pin, sizeof(int32_t) * (size_t)(n + 8) + sizeof(float) * 8));
     float *pin_lp = (float *)(pin + n + 8);
@@ -1172,6 +1187,7 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     MLXD_CHECK(cudaMemcpyAsync(m->ctx, pin, sizeof(int32_t) * (size_t)n, cudaMemcpyHostToDevice, st));
     int32_t nctx_h = n;
     MLXD_CHECK(cudaMemcpyAsync(m->n_ctx, &nctx_h, 4, cudaMemcpyHostToDevice, st));
+    MLXD_CHECK(cudaMemsetAsync(m->d_step, 0, 8, st));
 
     cudaEvent_t e0, e1, e2;
     cudaEventCreate(&e0);
@@ -1201,14 +1217,27 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     // one decode step (forward of m->token, then the token choice), enqueued
     auto enqueue_step = [&](int e) -> int {
         if (check_room(m, kv, 1)) return -1;
-        if (fast && greedy) {
-            if (!m->graph_exec || m->graph_kv != kv || m->graph_lp != (logprobs != nullptr)) {
+        // one CUDA graph per step: the greedy step, or (one GPU) the sampled
+        // step with the sampler reading the context length and the draw's
+        // step from device counters
+        const bool sampled = !greedy;
+        if (fast && (greedy || m->c.tp_size == 1)) {
+            if (!m->graph_exec || m->graph_kv != kv || m->graph_kv_serial != kv->serial ||
+                m->graph_lp != (logprobs != nullptr) ||
+                m->graph_sampled != sampled || (sampled && memcmp(&m->graph_sp, sp, sizeof *sp) != 0)) {
                 if (m->graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
                 m->graph_exec = nullptr;
+                if (sampled && sample_reserve(m->vocab_local)) return -1;
                 cudaGraph_t g;
                 MLXD_CHECK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-                int r = decode_step(m, kv, m->token, true, m->logits, true, st, true);
-                if (!r && logprobs) logprob_kernel<<<1, 1024, 0, st>>>(m->logits, m->vocab_local, m->token, m->lp);
+                int r = decode_step(m, kv, m->token, true, m->logits, !sampled, st, true);
+                if (!r && sampled) {
+                    r = sample(m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, 0, 0, m->token,
+                               logprobs ? m->lp : nullptr, nullptr, st, m->n_ctx, m->d_step);
+                    if (!r) sampled_step_kernel<<<1, 1, 0, st>>>(m->ctx, m->n_ctx, m->token, m->d_step);
+                } else if (!r && logprobs) {
+                    logprob_kernel<<<1, 1024, 0, st>>>(m->logits, m->vocab_local, m->token, m->lp);
+                }
                 cudaError_t ce = cudaStreamEndCapture(st, &g);
                 if (r || ce != cudaSuccess) {
                     if (!r) set_error("graph capture: %s", cudaGetErrorString(ce));
@@ -1219,7 +1248,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
                 cudaGraphDestroy(g);
                 m->graph_exec = ge;
                 m->graph_kv = kv;
+                m->graph_kv_serial = kv->serial;
                 m->graph_lp = logprobs != nullptr;
+                m->graph_sampled = sampled;
+                m->graph_sp = *sp;
             }
             MLXD_CHECK(cudaGraphLaunch((cudaGraphExec_t)m->graph_exec, st));
         } else {

@@ -192,7 +192,7 @@ MLXD_DEV void radix_step(const unsigned int *hs, int shift, uint32_t *prefix, in
 template <typename T>
 __global__ void __launch_bounds__(SAMP_PT) samp_stats_kernel(
     const void *logits, int V, mlxd_sampling sp, const int32_t *ctx, int n_ctx, SampWork w,
-    int32_t *tok, float *lp, int topk) {
+    int32_t *tok, float *lp, int topk, const int32_t *d_nctx) {
     __shared__ float xs[SAMP_CH];
     __shared__ int first[SAMP_CH];
     __shared__ unsigned int hist[256];
@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(SAMP_PT) samp_stats_kernel(
     const int tid = threadIdx.x;
     const int c0 = blockIdx.x * SAMP_CH, n = min(V - c0, SAMP_CH);
     const bool greedy = sp.temperature < 0.01f;
+    if (d_nctx) n_ctx = *d_nctx;
     const bool pen = !greedy && sp.repetition_penalty > 0.f && sp.repetition_penalty != 1.0f && n_ctx > 0;
     for (int i = tid; i < n; i += SAMP_PT) {
         xs[i] = load_logit<T>(logits, c0 + i);
@@ -489,7 +490,7 @@ __global__ void samp_exp_kernel(int V, SampWork w, int full_scheduled) {
 //          u * (its blocked total), u from SplitMix64 on (seed, step).
 __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
     int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w, int32_t *tok, float *lp,
-    uint8_t *keep, int full_scheduled) {
+    uint8_t *keep, int full_scheduled, const unsigned long long *d_step) {
     __shared__ __align__(16) float sbt[SAMP_NB];
     __shared__ __align__(16) float spre[SAMP_NB];
     __shared__ float s_z, s_thr;
@@ -633,7 +634,7 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
     blocked(first, ev, &s_z);
     MLXD_TRACE_T(tr_z2_)
     const float z2 = s_z;
-    const float u = draw_uniform(sp.seed < 0 ? 0 : sp.seed, step);
+    const float u = draw_uniform(sp.seed < 0 ? 0 : sp.seed, d_step ? *d_step : step);
     const int at = crossing(first, ev, __fmul_rn(u, z2),
                             [](float e) { return e > 0.f; });
     const int pick = at != 0x7fffffff ? at : V - 1;
@@ -703,8 +704,11 @@ static int ensure_work(int V) {
     return 0;
 }
 
+int sample_reserve(int V) { return V > 0 ? ensure_work(V) : 0; }
+
 int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const int32_t *ctx,
-           int n_ctx, uint64_t step, int32_t *tok, float *lp, uint8_t *keep, cudaStream_t st) {
+           int n_ctx, uint64_t step, int32_t *tok, float *lp, uint8_t *keep, cudaStream_t st,
+           const int32_t *d_nctx, const unsigned long long *d_step) {
     if (V <= 0 || !tok) {
         set_error("sample: bad arguments");
         return -1;
@@ -715,9 +719,9 @@ int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const 
     const bool greedy = sp.temperature < 0.01f;
     const int topk = !greedy && sp.top_k > 0 && sp.top_k < V;
     if (dtype == MLXD_BF16)
-        samp_stats_kernel<uint16_t><<<G, SAMP_PT, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, topk);
+        samp_stats_kernel<uint16_t><<<G, SAMP_PT, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, topk, d_nctx);
     else if (dtype == MLXD_F32)
-        samp_stats_kernel<float><<<G, SAMP_PT, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, topk);
+        samp_stats_kernel<float><<<G, SAMP_PT, 0, st>>>(logits, V, sp, ctx, n_ctx, w, tok, lp, topk, d_nctx);
     else {
         set_error("sample: logits dtype must be bf16 or f32");
         return -1;
@@ -747,7 +751,7 @@ int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const 
                                                    w.sorted_i, V, 0, 32, st));
     }
     samp_exp_kernel<<<(V + 1023) / 1024, 256, 0, st>>>(V, w, need_full);
-    samp_finish_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep, need_full);
+    samp_finish_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep, need_full, d_step);
     MLXD_CHECK(cudaGetLastError());
     return 0;
 }

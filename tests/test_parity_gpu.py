@@ -358,6 +358,33 @@ def test_sampled_generate_runs_and_respects_candidates():
     assert np.all(lpa <= 0) and np.array_equal(lpa, lpb)
 
 
+def test_sampled_generate_graph_matches_step_loop():
+    """Sampled generation replays one captured decode step (forward, sampler
+    with device-side context length and step, token append); the tokens and
+    logprobs equal a loop of forward + mlxd_cuda_sample with the context list
+    and step passed from the host."""
+    cfg = qwen3_small(layers=2)
+    m, _ = synth_pair(cfg, seed=7)
+    sp = cuda.sampling(temperature=0.7, top_k=50, top_p=0.9, repetition_penalty=1.1,
+                       repetition_context=16, seed=4)
+    prompt = cuda.synth_prompt(20, cfg.vocab, 2)
+    toks, lps, _ = m.generate(prompt, 12, sp=sp, logprobs=True)
+    kv = m.new_kv(64)
+    m.forward(kv, prompt[:-1].tolist(), want_logits=False)
+    ctx, t, out, outlp = list(prompt), int(prompt[-1]), [], []
+    for e in range(12):
+        tok, lp, _ = cuda.sample(m.forward(kv, [t]), sp, ctx=np.array(ctx, np.int32), step=e)
+        out.append(tok)
+        outlp.append(lp)
+        ctx.append(tok)
+        t = tok
+    assert out == toks.tolist()
+    assert np.array_equal(np.array(outlp, np.float32), lps)
+    # a second call replays the same graph from fresh counters
+    toks2, _, _ = m.generate(prompt, 12, sp=sp)
+    assert np.array_equal(toks2, toks)
+
+
 def test_edge_cases():
     cfg = qwen3_small(layers=1, max_pos=64)
     m, o = synth_pair(cfg)
