@@ -233,6 +233,9 @@ def main():
     ap.add_argument("--cpu-prompt", type=int, default=8)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--roofline", type=int, default=1)
+    ap.add_argument("--sampled", type=int, default=1,
+                    help="also time sampled decoding (one GPU; temperature 0.7, top-k 50, top-p 0.9, "
+                         "repetition penalty 1.1 over 256 tokens)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -248,7 +251,9 @@ def main():
         P = args.prompt
     K, W = args.steps, args.warmup
     total = W + K
-    cfg = cuda.synth_config(**kw, max_pos=P + total + 8, tp_rank=rank, tp_size=world)
+    SAMPLED_STEPS, SAMPLED_WARMUP = 256, 16
+    room = max(total, SAMPLED_STEPS + SAMPLED_WARMUP) + 8   # positions past the prompt
+    cfg = cuda.synth_config(**kw, max_pos=P + room, tp_rank=rank, tp_size=world)
     t0 = time.time()
     dev = cuda.synth_device_tensors(cfg, seed=0)
     model = cuda.Model(cfg, dev, on_device=True)
@@ -265,7 +270,7 @@ def main():
         dist.broadcast(t, 0)
         model.tp_init(t.numpy().tobytes())
     prompt = cuda.synth_prompt(P, cfg.vocab, seed=0)
-    kv = model.new_kv(P + total + 8)
+    kv = model.new_kv(P + room)
     # untimed warm-up of the whole path (graph capture, allocator)
     model.generate(prompt[:64], 4, kv=kv)
     if dist:
@@ -312,6 +317,21 @@ def main():
                              (1 + 5 * kw["layers"] + 2 + (4 * kw["layers"] + 1 if world > 1 else 0))),
         "clocks": clk,
     }
+    if args.sampled and world == 1:
+        # sampled decoding (the Mistral-style workload's settings) on the same
+        # model and prompt: one captured step (forward, sampler, append) per
+        # token, device time between the first and last timed step
+        sp = cuda.sampling(temperature=0.7, top_k=50, top_p=0.9, repetition_penalty=1.1,
+                           repetition_context=256, seed=1)
+        ns, ws = SAMPLED_STEPS, SAMPLED_WARMUP
+        model.generate(prompt[:64], 4, sp=sp, kv=kv)
+        stoks, _, stm = model.generate(prompt, ws + ns, sp=sp, kv=kv)
+        if len(stoks) == ws + ns:
+            se = stm["step_end_ms"]
+            line["config"]["sampled_decode"] = {
+                "tokens_per_s": round(ns / (float(se[ws + ns - 1] - se[ws - 1]) / 1e3), 2),
+                "steps": ns, "warmup": ws,
+                "settings": "temperature 0.7, top_k 50, top_p 0.9, repetition_penalty 1.1 (last 256)"}
     if args.roofline and rank == 0:
         g = gemv_roofline(kw, peak)
         dom = g["gate_up"]
@@ -325,7 +345,7 @@ def main():
             "peak_source": peak_src, "shapes": g}
     if args.cpu_baseline and rank == 0 and world == 1:
         try:
-            host = host_weights_from_gpu(cuda, cuda.synth_config(**kw, max_pos=P + total + 8))
+            host = host_weights_from_gpu(cuda, cuda.synth_config(**kw, max_pos=P + room))
             line["cpu_baseline"] = oracle_sample(kw, host, args.cpu_prompt, kw["vocab"],
                                                  args.cpu_budget)
             del host
