@@ -79,8 +79,20 @@ def test_tp2_matches_tp1():
         assert tp.shape == (2 * V2,)
         ok, mx, mr = logits_close(tp, f)
         assert ok, (i, mx, mr)
-    # the greedy token is identical on both ranks; against TP=1 a flip is only
-    # allowed where TP=1's top-2 margin is a near-tie
+    # the greedy token is identical on both ranks; against TP=1 the first flip
+    # is only allowed where TP=1's logits hold the two tokens within two bf16
+    # ulps (the row-parallel sums round in a different order); TP=1's logits
+    # at that step come from the same decode steps, one token at a time
     assert np.array_equal(res[0][1], res[1][1])
-    assert np.array_equal(res[0][1], np.asarray(toks1)) or \
-        np.argmax(res[0][1] != np.asarray(toks1)) > 8
+    t2, t1 = np.asarray(res[0][1]), np.asarray(toks1)
+    diff = np.nonzero(t2 != t1)[0]
+    if len(diff):
+        d = int(diff[0])
+        kv2 = m.new_kv(64)
+        m.forward(kv2, ids[:15], want_logits=False)
+        lg = bf16_to_f32(m.forward(kv2, [ids[15]]))
+        for t in t1[:d]:
+            lg = bf16_to_f32(m.forward(kv2, [int(t)]))
+        a, b = float(lg[t1[d]]), float(lg[t2[d]])
+        assert int(np.argmax(lg)) == int(t1[d])
+        assert a - b <= 2 * 2.0 ** -8 * max(abs(a), 1.0), (d, a, b)
