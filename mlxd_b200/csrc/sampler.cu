@@ -435,8 +435,14 @@ __device__ void bitonic_sort_asc(float *v, int *ix, int n_pow2) {
 // Candidate path: the survivors sorted ascending by (value, index) in shared
 // memory and written to the tail of the sorted arrays, where the full-sort
 // path leaves its survivors too.
-__global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(int V, SampWork w, int32_t *tok,
-                                                                  int full_scheduled) {
+__device__ void finish_stage(int V, const mlxd_sampling &sp, float log_mp, uint64_t step, const SampWork &w,
+                             int32_t *tok, float *lp, uint8_t *keep, const unsigned long long *d_step);
+
+// finish_here (no full sort scheduled): the exp values and the final stage
+// follow in the same CTA
+__global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(
+    int V, SampWork w, int32_t *tok, int full_scheduled, mlxd_sampling sp, float log_mp, uint64_t step,
+    float *lp, uint8_t *keep, const unsigned long long *d_step, int finish_here) {
     __shared__ float sv[SAMP_CAND];
     __shared__ int si[SAMP_CAND];
     if (w.meta->mode == 2 && !full_scheduled) {
@@ -459,6 +465,16 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(int V, SampWork
         w.sorted_v[V - n + i] = sv[i];
         w.sorted_i[V - n + i] = si[i];
     }
+    if (!finish_here) return;
+    // exp(v - m) in the final stage's block-transposed layout
+    const float m = w.meta->m;
+    const int bs = max(1, (V + SAMP_NB - 1) / SAMP_NB);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const int i = V - n + j;
+        w.ev[(i % bs) * SAMP_NB + i / bs] = own_expf(__fsub_rn(sv[j], m));
+    }
+    __syncthreads();   // the CTA's global writes above, seen by every thread
+    finish_stage(V, sp, log_mp, step, w, tok, lp, keep, d_step);
 }
 
 // exp(v - m) of the n ascending survivors at sorted positions V-n..V-1, in
@@ -488,15 +504,13 @@ __global__ void samp_exp_kernel(int V, SampWork w, int full_scheduled) {
 //   min_p: cutoff >= max + log(min_p);
 //   draw:  inverse CDF of exp(v - m) over the kept suffix v >= cutoff, at
 //          u * (its blocked total), u from SplitMix64 on (seed, step).
-__global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
-    int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w, int32_t *tok, float *lp,
-    uint8_t *keep, int full_scheduled, const unsigned long long *d_step) {
+// (run by all SAMP_THREADS threads of one CTA)
+__device__ void finish_stage(int V, const mlxd_sampling &sp, float log_mp, uint64_t step, const SampWork &w,
+                             int32_t *tok, float *lp, uint8_t *keep, const unsigned long long *d_step) {
     __shared__ __align__(16) float sbt[SAMP_NB];
     __shared__ __align__(16) float spre[SAMP_NB];
     __shared__ float s_z, s_thr;
     __shared__ int s_at, s_first;
-    const int mode = w.meta->mode;
-    if (mode == 0 || (mode == 2 && !full_scheduled)) return;
     MLXD_TRACE_START
     const int tid = threadIdx.x;
     const int n = w.meta->n_surv;
@@ -655,6 +669,15 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
     MLXD_TRACE_END(0x92)
 }
 
+// the final stage after the full-vocabulary sort
+__global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
+    int V, mlxd_sampling sp, float log_mp, uint64_t step, SampWork w, int32_t *tok, float *lp,
+    uint8_t *keep, int full_scheduled, const unsigned long long *d_step) {
+    const int mode = w.meta->mode;
+    if (mode == 0 || (mode == 2 && !full_scheduled)) return;
+    finish_stage(V, sp, log_mp, step, w, tok, lp, keep, d_step);
+}
+
 __global__ void iota_kernel(int *p, int n) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = i;
@@ -740,9 +763,11 @@ int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const 
     // With top_k <= 1024 the survivors fit the candidate list unless more than
     // 3072 values tie at the cutoff; otherwise the whole vocabulary is sorted.
     bool need_full = !(sp.top_k > 0 && sp.top_k <= 1024);
-    samp_cand_kernel<<<1, SAMP_THREADS, 0, st>>>(V, w, tok, need_full);
+    samp_cand_kernel<<<1, SAMP_THREADS, 0, st>>>(V, w, tok, need_full, sp, log_mp, step, lp, keep, d_step,
+                                                 !need_full);
     MLXD_CHECK(cudaGetLastError());
-    if (need_full) {
+    if (!need_full) return 0;   // the candidate kernel finished the draw
+    {
         // ascending (value, index) over the whole vocabulary: a stable radix
         // sort of the masked values with the indices in order
         iota_kernel<<<(V + 255) / 256, 256, 0, st>>>(w.idx_in, V);
