@@ -313,8 +313,7 @@ def main():
         "step_roofline": {"bytes_per_token": round(bpt / world), "achieved_gbs": round(step_gbs, 1),
                           "peak_gbs": peak, "peak_source": peak_src,
                           "frac": round(step_gbs / peak, 4), "mean_context": mean_ctx},
-        "gpu_launches": K * (1 if model.decode_path() == 1 else
-                             (1 + 5 * kw["layers"] + 2 + (4 * kw["layers"] + 1 if world > 1 else 0))),
+        "gpu_launches": K * (1 + 5 * kw["layers"] + 2 + (2 * kw["layers"] if world > 1 else 0)),
         "clocks": clk,
     }
     if args.sampled and world == 1:

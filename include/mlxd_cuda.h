@@ -85,11 +85,6 @@ int  mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg,
                             const mlxd_tensor *tensors, int n_tensors);
 void mlxd_cuda_model_destroy(mlxd_model *m);
 size_t mlxd_cuda_model_weight_bytes(const mlxd_model *m);
-/* Decode path the model runs (no reference counterpart): 1 = the whole step
-   as one persistent kernel (opt-in: MLXD_MEGASTEP=1 in the environment when
-   the model is created; 4-bit group-64 bf16-scale checkpoints on one GPU),
-   0 = one kernel per projection / attention (default). */
-int  mlxd_cuda_model_decode_path(const mlxd_model *m);
 /* Tensor parallel: bind an NCCL communicator (unique id bytes from rank 0,
    128 bytes) before the first forward when tp_size > 1. */
 int  mlxd_cuda_model_tp_init(mlxd_model *m, const void *nccl_unique_id);
@@ -134,22 +129,25 @@ int  mlxd_cuda_linear_create(mlxd_linear **out, const uint32_t *w, const void *s
                              const void *biases, int sdtype, int rows, int cols,
                              int group, int on_device);
 void mlxd_cuda_linear_destroy(mlxd_linear *l);
-/* y[S][out] (bf16) = x[S][in] (bf16) . deq(W)^T; S == 1 uses the decode GEMV
-   (exact f32 dequantised product), S > 1 the prefill GEMM (bf16-rounded
-   dequantised weights, the mlx qmm tile semantics). Device pointers. */
+/* y[S][out] (bf16) = x[S][in] (bf16) . deq(W)^T in the library's projection
+   arithmetic (each group of 64 or 32 inputs in fixed point on its largest
+   magnitude's grid, exact integer group sums, f64 combination, one rounding
+   to bf16): S == 1 on the decode kernel, S > 1 on the chunk kernels, with
+   identical bits per row. Device pointers. */
 int  mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *stream);
 /* One-token y[out] = x[in] . deq(W)^T that allocates nothing (no counterpart
-   in the reference): same decode GEMV and result as mlxd_cuda_linear with
+   in the reference): the same projection and bits as mlxd_cuda_linear with
    S == 1, for callers that cannot allocate device memory when they call it:
    code inside a caching allocator's callback (allocating would re-enter it)
    and serving loops that hold all HBM under a fixed plan (a cudaMalloc there
-   can fail, and it synchronises the device). Its split partial sums live in
-   one static device array of 2 MiB + 64 KiB shared by every call on a
-   device; a matrix
-   needing more (over 262144 rows, or over 2^19 workspace floats) is rejected
-   with -1 and a message. The first call on each device looks the array up
-   and should come before any stream capture. Calls whose kernels can overlap
-   on the GPU (unordered streams) race on the array. Device pointers. */
+   can fail, and it synchronises the device). The workspace of the generic
+   kernel (the input staged in per-group fixed point, 4 bytes per column plus
+   16 per group) lives in one static device array of 2 MiB + 64 KiB, held by
+   every GPU that loads the library and shared by every call on it; an input
+   wider than 262144 columns is rejected with -1 and a message. The first
+   call on each device looks the array up and should come before any stream
+   capture. Calls whose kernels can overlap on the GPU (unordered streams)
+   race on the array. Device pointers. */
 int  mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void *stream);
 /* qGEMV measurement (no reference counterpart; the survey's qmv microbench):
    launches the decode GEMV of n projections round-robin, iters rounds, on an

@@ -206,31 +206,6 @@ MLXD_DEV unsigned smid_() {
 #define MLXD_TRACE_T(var)
 #endif
 
-// ---- L2 prefetch of upcoming weights. A decode kernel is handed byte ranges
-// of the weight stream that later kernels of the step will read; each CTA
-// requests its share into L2 with cp.async.bulk.prefetch.L2 before waiting on
-// its producer, so HBM keeps streaming across kernel boundaries. Ranges and
-// sizes are multiples of 16 bytes (cudaMalloc'd arrays of 16-byte records).
-// (PfList: internal.h)
-MLXD_DEV void l2_prefetch_bulk(const void *p, unsigned int bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-// this CTA's share of every range, 64 KB per request, spread over its warps
-MLXD_DEV void l2_prefetch_share(const mlxd::PfList &pf) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    if (lane != 0) return;
-    const unsigned G = gridDim.x * gridDim.y, c = blockIdx.x + blockIdx.y * gridDim.x;
-    constexpr unsigned CH = 64u * 1024u;
-    for (int r = 0; r < pf.n; r++) {
-        const unsigned long long n16 = pf.bytes[r] >> 4;
-        const unsigned long long b0 = (n16 * c / G) << 4, b1 = (n16 * (c + 1) / G) << 4;
-        for (unsigned long long o = b0 + (unsigned long long)warp * CH; o < b1; o += (unsigned long long)nw * CH) {
-            const unsigned long long len = b1 - o < CH ? b1 - o : CH;
-            l2_prefetch_bulk(pf.p[r] + o, (unsigned int)len);
-        }
-    }
-}
-
 // Programmatic dependent launch: wait for the producer grid / let the
 // consumer grid be scheduled. No-ops when the launch has no PDL attribute.
 MLXD_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

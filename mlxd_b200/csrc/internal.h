@@ -14,45 +14,38 @@ void set_error(const char *fmt, ...);
 bool cuda_ok(cudaError_t e, const char *what);
 #define MLXD_CHECK(call) do { if (!::mlxd::cuda_ok((call), #call)) return -1; } while (0)
 
-// Byte ranges of the weight stream that one decode launch requests into L2
-// (multiples of 16 bytes, 16-byte aligned); n = 0: none.
-constexpr int PF_MAX = 8;
-struct PfList {
-    const unsigned char *p[PF_MAX];
-    unsigned int bytes[PF_MAX];
-    int n;
-};
-
 void *dev_alloc(size_t bytes);      // tracked cudaMalloc (nullptr + error on failure)
 void dev_free(void *p);
 
-// A projection in device memory. Quantized matrices live in the tile layout
-// written by repack: for row block rb (16 rows) and group g, 32 lanes of
-// group/4 bytes each (tiles), plus 8 scale/bias records per tile (sb).
+// A projection in device memory. Every quantized matrix keeps its MLX
+// arrays (w u32 [rows][cols/8], scales/biases [rows][cols/group] of sdtype);
+// a fused gate|up matrix stores alternating 64-row blocks of gate and up
+// rows. Matrices of the fast format (group 64, bf16 scales, cols a multiple
+// of 512) also carry the decode layout: ti8, tiles of 16 rows x 64 columns
+// whose lane words are the u8 A fragments of two mma.m16n8k32 (low nibbles:
+// columns 0-31, high nibbles: 32-63), and sbi, per (16 rows, 8 groups) 16
+// records of 32 B: (s, b) of rows g, g+8 for the four groups 2j + h that
+// lanes (g, 2h) and (g, 2h+1) scale. Dense matrices keep bf16 [rows][cols].
 struct QMat {
-    int rows = 0, cols = 0;     // out, in (rows a multiple of 16)
+    int rows = 0, cols = 0;     // out, in
     int group = 64;
     int sdtype = MLXD_BF16;     // scale/bias dtype
     bool quant = true;
-    uint8_t *tiles = nullptr;
-    uint8_t *sb = nullptr;
-    // decode fast path (group 64, bf16 scales, cols/64 a multiple of 8): the
-    // same scales/biases regrouped per row block and block of 8 groups, one
-    // 16-byte record per lane: (s,b) of rows g, g+8 x groups 2t, 2t+1
-    uint8_t *sb8 = nullptr;
-    // integer-MMA decode layout (same eligibility as sb8): tiles whose lane
-    // words carry the u8 A fragments of two m16n8k32 MMAs (low nibbles: group
-    // columns 0-31, high nibbles: 32-63), and per (row block, block of 8
-    // groups) 16 records of 32 B: (s, b) of rows g, g+8 for the four groups
-    // 2j + h (j = 0..3) that lanes (g, 2h) and (g, 2h+1) scale
-    uint8_t *ti8 = nullptr;
-    uint8_t *sbi = nullptr;
-    uint16_t *dense = nullptr;  // [rows][cols] bf16 when !quant
-    size_t tile_bytes() const { return (size_t)rows / 16 * (cols / group) * 32 * (group / 4); }
-    size_t sb_bytes() const {
-        return (size_t)rows / 16 * (cols / group) * 8 * (sdtype == MLXD_F32 ? 16 : 8);
+    uint32_t *w = nullptr;
+    void *s = nullptr, *b = nullptr;
+    uint8_t *ti8 = nullptr, *sbi = nullptr;
+    uint16_t *dense = nullptr;
+    bool fast() const {
+        return quant && group == 64 && sdtype == MLXD_BF16 && cols % 512 == 0 && rows % 16 == 0;
     }
-    bool fast8() const { return quant && group == 64 && sdtype == MLXD_BF16 && (cols / 64) % 8 == 0; }
+    size_t w_bytes() const { return quant ? (size_t)rows * cols / 2 : (size_t)rows * cols * 2; }
+    size_t sb_bytes() const {   // scales + biases
+        return quant ? (size_t)rows * (cols / group) * (sdtype == MLXD_F32 ? 8 : 4) : 0;
+    }
+    size_t ti8_bytes() const { return (size_t)rows * cols / 2; }
+    size_t sbi_bytes() const { return (size_t)rows * cols / 16; }
+    // bytes one decode step streams from HBM for this matrix
+    size_t stream_bytes() const { return ti8 ? ti8_bytes() + sbi_bytes() : w_bytes() + sb_bytes(); }
 };
 
 struct Layer {
@@ -71,6 +64,10 @@ struct Embed {
 
 }  // namespace mlxd
 
+namespace mlxd {
+struct SampWork;
+}
+
 struct mlxd_model {
     mlxd_model_config c;
     int hq, hkv, qdim;          // local heads, q rows per token (x2 with gate)
@@ -84,17 +81,15 @@ struct mlxd_model {
     // decode scratch
     uint16_t *h = nullptr, *h1 = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr;
     uint16_t *logits = nullptr;
-    float *part = nullptr;      // attention split partials
-    int *att_count = nullptr;   // per kv head split completion counters
     unsigned long long *amax = nullptr;  // fused argmax key
     int32_t *token = nullptr;   // device token slot
     float *lp = nullptr;        // device logprob slot
-    float *part_h = nullptr;    // [hidden] f32 partial (tensor parallel)
-    float *gemv_ws = nullptr;   // decode GEMV split row-block partials
-    int *gemv_cnt = nullptr;    // decode GEMV per-unit counters
+    double *part_h = nullptr;   // [tp_size][hidden] f64 partials (tensor parallel)
+    void *gws = nullptr;        // generic projection workspace (decode)
+    size_t gws_bytes = 0;
     float *rope_cs = nullptr;   // [positions][rope_dims/2][2] cos/sin
     int rope_positions = 0;
-    int nsplit = 16;
+    mlxd::SampWork *samp = nullptr;   // sampler scratch of this model
     // generate loop state
     int32_t *ctx = nullptr;     // context ids (prompt + generated)
     int32_t *n_ctx = nullptr;
@@ -112,10 +107,12 @@ struct mlxd_model {
     uint16_t *p_h = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_q = nullptr, *p_att = nullptr,
              *p_act = nullptr, *p_tmp = nullptr;
     int32_t *p_ids = nullptr;
-    float *p_part = nullptr;
+    double *p_part = nullptr;   // [S][hidden] f64 partials (tensor parallel)
+    void *p_ws = nullptr;       // projection workspace of a chunk
+    size_t p_ws_bytes = 0;
+    float *p_scr = nullptr;     // attention scratch of a chunk
+    size_t p_scr_floats = 0;
     cudaStream_t stream = nullptr;
-    // persistent single-kernel decode step (megastep.cu) when eligible
-    void *mega = nullptr;
     // tensor parallel
     void *nccl = nullptr;       // ncclComm_t when tp_size > 1
     size_t weight_bytes = 0;

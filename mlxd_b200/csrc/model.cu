@@ -7,6 +7,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -26,18 +27,12 @@ namespace mlxd {
 __global__ void set_pos_kernel(int32_t *d_pos, int v) { *d_pos = v; }
 
 // end of one decode step: advance the position; with the fused argmax, turn
-// the winning key into the token id and clear the key for the next step;
-// append the token to the context list used by the repetition penalty.
-__global__ void step_finish_kernel(int32_t *d_pos, unsigned long long *amax, int32_t *token,
-                                   int32_t *ctx, int32_t *n_ctx) {
+// the winning key into the token id and clear the key for the next step
+__global__ void step_finish_kernel(int32_t *d_pos, unsigned long long *amax, int32_t *token) {
     *d_pos += 1;
     if (amax) {
         *token = (int32_t)(0xFFFFFFFFu - (uint32_t)(*amax & 0xFFFFFFFFull));
         *amax = 0ull;
-    }
-    if (ctx) {
-        ctx[*n_ctx] = *token;
-        *n_ctx += 1;
     }
 }
 
@@ -50,13 +45,6 @@ __global__ void sampled_step_kernel(int32_t *ctx, int32_t *n_ctx, const int32_t 
     ctx[*n_ctx] = *token;
     *n_ctx += 1;
     *d_step += 1;
-}
-
-__global__ void add_partial_kernel(uint16_t *h_out, const uint16_t *h_in, const float *part, int n) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) h_out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(
-                   __fadd_rn(__uint_as_float((uint32_t)h_in[i] << 16),
-                             __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(part[i])) << 16))));
 }
 
 // raw logprob of the chosen token: x[tok] - logsumexp(x)
@@ -88,8 +76,8 @@ __global__ void logprob_kernel(const uint16_t *logits, int V, const int32_t *tok
 
 struct mlxd_linear {
     QMat W;
-    float *ws = nullptr;
-    int *cnt = nullptr;
+    void *ws = nullptr;   // generic-path workspace
+    size_t ws_bytes = 0;
 };
 
 // ---------------------------------------------------------------- helpers
@@ -98,26 +86,9 @@ namespace {
 
 struct TensorSet {
     std::unordered_map<std::string, const mlxd_tensor *> by_name;
-    std::vector<void *> temps;   // uploaded host tensors, freed after create
     const mlxd_tensor *get(const std::string &n) const {
         auto it = by_name.find(n);
         return it == by_name.end() ? nullptr : it->second;
-    }
-    const void *dev(const mlxd_tensor *t, size_t bytes, cudaStream_t st) {
-        if (t->on_device) return t->data;
-        void *p = dev_alloc(bytes);
-        if (!p) return nullptr;
-        if (cudaMemcpyAsync(p, t->data, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
-            set_error("upload of %s failed", t->name);
-            dev_free(p);
-            return nullptr;
-        }
-        temps.push_back(p);
-        return p;
-    }
-    ~TensorSet() {
-        cudaDeviceSynchronize();
-        for (void *p : temps) dev_free(p);
     }
 };
 
@@ -162,8 +133,8 @@ int get_triplet(const TensorSet &ts, const std::string &base, int group, Triplet
         }
         out.cols = (int)out.w->shape[1] * 8;
         if (out.s->dtype != out.b->dtype || (out.s->dtype != MLXD_BF16 && out.s->dtype != MLXD_F32) ||
-            out.s->shape[0] != out.rows || out.s->shape[1] * group != out.cols ||
-            out.b->shape[0] != out.rows || out.b->shape[1] != out.s->shape[1]) {
+            out.s->ndim != 2 || out.b->ndim != 2 || out.s->shape[0] != out.rows ||
+            out.s->shape[1] * group != out.cols || out.b->shape[0] != out.rows || out.b->shape[1] != out.s->shape[1]) {
             set_error("%s: scales/biases shape or dtype mismatch", base.c_str());
             return -1;
         }
@@ -177,72 +148,96 @@ int get_triplet(const TensorSet &ts, const std::string &base, int group, Triplet
     return 0;
 }
 
-// one source block of rows [r0, r0+nr) x cols [c0, c0+nc) into a matrix
+// one source block of rows [r0, r0+nr) x cols [c0, c0+ncols of the matrix)
+// into a matrix: at destination rows dst_row0.. (il = 0), or as the gate
+// (il = 1) / up (il = 2) rows of a fused gate|up matrix (64-row blocks of
+// gate and up alternate)
 struct Piece {
     Triplet t;
     int r0, nr, c0;
-    int dst_rb0, dst_rb_stride;   // quant: destination row blocks
-    int dst_row0;                 // dense: destination first row
+    int dst_row0;
+    int il;
 };
 
-int build_qmat(TensorSet &ts, QMat &M, int rows, int cols, int group, const std::vector<Piece> &pcs,
+int copy_rows(void *dst, size_t dst_pitch, const void *src, size_t src_pitch, size_t width, int rows,
+              cudaStream_t st) {
+    MLXD_CHECK(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width, rows, cudaMemcpyDefault, st));
+    return 0;
+}
+
+int place_piece(QMat &M, const Piece &p, cudaStream_t st) {
+    const int G = M.group;
+    const int ng = M.quant ? M.cols / G : 0, sng = M.quant ? p.t.cols / G : 0;
+    const size_t es = M.quant ? dt_size(M.sdtype) : 2;
+    auto copy_block = [&](int src_row, int dst_row, int n) -> int {
+        if (M.quant) {
+            if (copy_rows(M.w + (size_t)dst_row * (M.cols / 8), (size_t)M.cols / 2,
+                          (const uint32_t *)p.t.w->data + (size_t)src_row * (p.t.cols / 8) + p.c0 / 8,
+                          (size_t)p.t.cols / 2, (size_t)M.cols / 2, n, st) ||
+                copy_rows((char *)M.s + (size_t)dst_row * ng * es, ng * es,
+                          (const char *)p.t.s->data + ((size_t)src_row * sng + p.c0 / G) * es, sng * es, ng * es, n,
+                          st) ||
+                copy_rows((char *)M.b + (size_t)dst_row * ng * es, ng * es,
+                          (const char *)p.t.b->data + ((size_t)src_row * sng + p.c0 / G) * es, sng * es, ng * es, n,
+                          st))
+                return -1;
+        } else {
+            if (copy_rows(M.dense + (size_t)dst_row * M.cols, (size_t)M.cols * 2,
+                          (const uint16_t *)p.t.w->data + (size_t)src_row * p.t.cols + p.c0, (size_t)p.t.cols * 2,
+                          (size_t)M.cols * 2, n, st))
+                return -1;
+        }
+        return 0;
+    };
+    if (p.il == 0) return copy_block(p.r0, p.dst_row0, p.nr);
+    if (p.nr % 64) {
+        set_error("gate/up shard of %d rows is not a multiple of 64", p.nr);
+        return -1;
+    }
+    for (int c = 0; c < p.nr / 64; c++)
+        if (copy_block(p.r0 + 64 * c, 128 * c + (p.il == 2 ? 64 : 0), 64)) return -1;
+    return 0;
+}
+
+int build_qmat(QMat &M, int rows, int cols, int group, const std::vector<Piece> &pcs, bool gateup,
                cudaStream_t st) {
     M.rows = rows;
     M.cols = cols;
     M.group = group;
     M.quant = pcs[0].t.quant;
-    for (auto &p : pcs) {
+    for (auto &p : pcs)
         if (p.t.quant != M.quant) {
             set_error("mixed quantized and dense projections in one fused matrix");
             return -1;
         }
-    }
     if (M.quant) {
         M.sdtype = pcs[0].t.s->dtype;
-        if (rows % 16 || cols % group) {
-            set_error("projection %dx%d does not tile (16 rows, group %d)", rows, cols, group);
-            return -1;
-        }
-        M.tiles = (uint8_t *)dev_alloc(M.tile_bytes());
-        M.sb = (uint8_t *)dev_alloc(M.sb_bytes());
-        if (!M.tiles || !M.sb) return -1;
-        if (M.fast8()) {
-            M.sb8 = (uint8_t *)dev_alloc(M.sb_bytes() * 2);   // 16 B per lane record
-            M.ti8 = (uint8_t *)dev_alloc(M.tile_bytes());
-            M.sbi = (uint8_t *)dev_alloc(M.sb_bytes());
-            if (!M.sb8 || !M.ti8 || !M.sbi) return -1;
-        }
-        for (auto &p : pcs) {
+        for (auto &p : pcs)
             if (p.t.s->dtype != M.sdtype) {
                 set_error("mixed scale dtypes in one fused matrix");
                 return -1;
             }
-            size_t wb = tensor_elems(p.t.w) * 4, sbb = tensor_elems(p.t.s) * dt_size(M.sdtype);
-            const uint32_t *w = (const uint32_t *)ts.dev(p.t.w, wb, st);
-            const void *s = ts.dev(p.t.s, sbb, st);
-            const void *b = ts.dev(p.t.b, sbb, st);
-            if (!w || !s || !b) return -1;
-            if (repack_quant(M, w, s, b, M.sdtype, p.t.cols / 8, p.t.cols / group, p.r0, p.nr, p.c0,
-                             p.dst_rb0, p.dst_rb_stride, st))
-                return -1;
+        if (cols % group || cols % 8) {
+            set_error("projection %dx%d does not split into groups of %d", rows, cols, group);
+            return -1;
         }
+        M.w = (uint32_t *)dev_alloc(M.w_bytes());
+        M.s = dev_alloc(M.sb_bytes() / 2);
+        M.b = dev_alloc(M.sb_bytes() / 2);
+        if (!M.w || !M.s || !M.b) return -1;
     } else {
-        M.dense = (uint16_t *)dev_alloc((size_t)rows * cols * 2);
+        M.dense = (uint16_t *)dev_alloc(M.w_bytes());
         if (!M.dense) return -1;
-        for (auto &p : pcs) {
-            const uint16_t *src = (const uint16_t *)p.t.w->data + (size_t)p.r0 * p.t.cols + p.c0;
-            cudaMemcpyKind kind = p.t.w->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-            MLXD_CHECK(cudaMemcpy2DAsync(M.dense + (size_t)p.dst_row0 * cols, (size_t)cols * 2, src,
-                                         (size_t)p.t.cols * 2, (size_t)cols * 2, p.nr, kind, st));
-        }
     }
-    return 0;
+    for (auto &p : pcs)
+        if (place_piece(M, p, st)) return -1;
+    return build_decode_layout(M, gateup, st);
 }
 
 void free_qmat(QMat &M) {
-    dev_free(M.tiles);
-    dev_free(M.sb);
-    dev_free(M.sb8);
+    dev_free(M.w);
+    dev_free(M.s);
+    dev_free(M.b);
     dev_free(M.ti8);
     dev_free(M.sbi);
     dev_free(M.dense);
@@ -257,8 +252,7 @@ uint16_t *upload_vec(TensorSet &ts, const std::string &name, int n, cudaStream_t
     }
     uint16_t *p = (uint16_t *)dev_alloc((size_t)n * 2);
     if (!p) return nullptr;
-    if (cudaMemcpyAsync(p, t->data, (size_t)n * 2,
-                        t->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st) != cudaSuccess) {
+    if (cudaMemcpyAsync(p, t->data, (size_t)n * 2, cudaMemcpyDefault, st) != cudaSuccess) {
         set_error("upload of %s failed", name.c_str());
         return nullptr;
     }
@@ -288,35 +282,53 @@ int llama3_freqs(const mlxd_model_config &c, std::vector<float> &out) {
     return 0;
 }
 
+// the one-kernel-per-op decode step serves head dims 64/128 with 1, 2, 4
+// or 8 query heads per kv head; other models decode through the generic
+// forward (one position)
 bool fast_decode_ok(const mlxd_model *m) {
-    int D = m->c.head_dim;
-    if (!(D == 64 || D == 128)) return false;
-    int rep = m->hq / m->hkv;
-    if (!(rep == 1 || rep == 2 || rep == 4 || rep == 8)) return false;
-    if (m->c.rope_dims != D) {
-        // partial rotary is handled by the shared norm+rope helper as well
-    }
-    for (auto &L : m->L)
-        if (!L.qkv.quant || !L.o.quant || !L.gateup.quant || !L.down.quant) return false;
-    return m->lm.quant;
+    return attention_decode_supported(m->c.head_dim, m->hq / m->hkv, m->c.rope_dims);
 }
 
 ncclComm_t comm_of(mlxd_model *m) { return (ncclComm_t)m->nccl; }
 
-int allreduce_f32(mlxd_model *m, float *buf, size_t n, cudaStream_t st) {
-    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, comm_of(m), st);
+// the row-parallel projection's f64 partials summed over the ranks (in
+// place), then h_out = bf16(h_in + bf16(sum)): the sum of exact partials of
+// the group-exact arithmetic, so the result equals one GPU's bit for bit
+int reduce_partials(mlxd_model *m, double *part, size_t n, uint16_t *h_out, const uint16_t *h_in, cudaStream_t st) {
+    ncclResult_t r = ncclAllReduce(part, part, n, ncclFloat64, ncclSum, comm_of(m), st);
     if (r != ncclSuccess) {
         set_error("ncclAllReduce: %s", ncclGetErrorString(r));
         return -1;
     }
-    return 0;
+    return add_partials(h_out, h_in, part, 1, n, n, st);
+}
+
+size_t proj_ws_bytes(const mlxd_model *m, int S) {
+    size_t b = 0;
+    auto need = [&](const QMat &W) {
+        size_t x = generic_ws_bytes(W, S, PRO_PLAIN);
+        if (x > b) b = x;
+    };
+    for (auto &L : m->L) {
+        need(L.qkv);
+        need(L.o);
+        need(L.gateup);
+        need(L.down);
+    }
+    need(m->lm);
+    return b;
 }
 
 int ensure_prefill(mlxd_model *m, int S) {
     if (S <= m->pre_cap) return 0;
     dev_free(m->p_h); dev_free(m->p_x); dev_free(m->p_qkv); dev_free(m->p_q);
     dev_free(m->p_att); dev_free(m->p_act); dev_free(m->p_tmp); dev_free(m->p_ids);
-    dev_free(m->p_part);
+    dev_free(m->p_part); dev_free(m->p_ws);
+    m->p_h = m->p_x = m->p_qkv = m->p_q = m->p_att = m->p_act = m->p_tmp = nullptr;
+    m->p_ids = nullptr;
+    m->p_part = nullptr;
+    m->p_ws = nullptr;
+    m->pre_cap = 0;
     const mlxd_model_config &c = m->c;
     int D = c.head_dim;
     size_t qkvw = (size_t)m->qdim + 2 * (size_t)m->hkv * D;
@@ -328,28 +340,39 @@ int ensure_prefill(mlxd_model *m, int S) {
     m->p_act = (uint16_t *)dev_alloc((size_t)S * m->inter_local * 2);
     m->p_tmp = (uint16_t *)dev_alloc((size_t)S * c.hidden * 2);
     m->p_ids = (int32_t *)dev_alloc((size_t)S * 4);
-    m->p_part = c.tp_size > 1 ? (float *)dev_alloc((size_t)S * c.hidden * 4) : nullptr;
+    m->p_part = c.tp_size > 1 ? (double *)dev_alloc((size_t)S * c.hidden * 8) : nullptr;
+    m->p_ws_bytes = proj_ws_bytes(m, S);
+    m->p_ws = dev_alloc(m->p_ws_bytes);
     if (!m->p_h || !m->p_x || !m->p_qkv || !m->p_q || !m->p_att || !m->p_act || !m->p_tmp || !m->p_ids ||
-        (c.tp_size > 1 && !m->p_part))
+        (c.tp_size > 1 && !m->p_part) || !m->p_ws)
         return -1;
     m->pre_cap = S;
     return 0;
 }
 
-// y = W x for S tokens (S == 1 & quantized: decode GEMV semantics)
-int linear_any(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi, const uint16_t *res,
-               float *yf, float *ws, int *cnt, cudaStream_t st) {
-    if (W.quant && S == 1) {
-        GemvArgs a = {};
-        a.x = x;
-        a.y = y;
-        a.yf = yf;
-        a.residual = res;
-        a.ws = ws;
-        a.cnt = cnt;
+int ensure_attn_scratch(mlxd_model *m, int S, int pos0, int window) {
+    const size_t need = attention_prefill_scratch(S, pos0, window, m->hq, m->c.head_dim);
+    if (need <= m->p_scr_floats) return 0;
+    dev_free(m->p_scr);
+    m->p_scr = (float *)dev_alloc(need * 4);
+    m->p_scr_floats = m->p_scr ? need : 0;
+    return m->p_scr ? 0 : -1;
+}
+
+// y[S] = W x[S] with the epilogue; S == 1 on the decode kernels
+int linear_any(mlxd_model *m, const QMat &W, const uint16_t *x, int S, int epi, uint16_t *y, const uint16_t *res,
+               double *yf, cudaStream_t st) {
+    GemvArgs a = {};
+    a.x = x;
+    a.y = y;
+    a.yf = yf;
+    a.residual = res;
+    if (S == 1) {
+        a.gws = m->gws;
+        a.gws_bytes = m->gws_bytes;
         return qgemv(W, PRO_PLAIN, epi, a, st, false);
     }
-    return linear_multi(W, x, S, y, epi, res, yf, st);
+    return qgemm_generic(W, PRO_PLAIN, epi, a, S, m->p_ws, m->p_ws_bytes, st);
 }
 
 }  // namespace
@@ -358,92 +381,19 @@ int linear_any(const QMat &W, const uint16_t *x, int S, uint16_t *y, int epi, co
 
 namespace mlxd {
 
-// The decode step's weight stream: the arrays each decode GEMV reads, in
-// launch order (per layer q|k|v, o, gate|up, down; then lm_head). Launch k
-// requests stream bytes [C_k + LA, C_(k+1) + LA) into L2 (C_k: offset of its
-// own first byte), so the next LA bytes are in flight while it runs; the
-// lm_head launch requests the first LA bytes of the next step. LA is set in MB
-// by MLXD_PF_MB; it is off by default: on Qwen3-8B the step measured 532
-// tokens/s without it, 515 at 32 MB and 499 at 64 MB (the kernels' time is
-// in their prologues and waits, not in their weight loads).
-struct StreamSeg {
-    const unsigned char *p;
-    size_t n, off;
-};
-static size_t pf_lookahead() {
-    static const size_t v = [] {
-        const char *e = getenv("MLXD_PF_MB");
-        return (size_t)(e ? atoi(e) : 0) << 20;
-    }();
-    return v;
-}
-static void pf_window(const std::vector<StreamSeg> &segs, size_t lo, size_t hi, PfList &pf) {
-    pf.n = 0;
-    for (const StreamSeg &g : segs) {
-        const size_t a = std::max(lo, g.off), b = std::min(hi, g.off + g.n);
-        if (a >= b) continue;
-        if (pf.n == PF_MAX) return;
-        const size_t a16 = (a - g.off) & ~(size_t)15, b16 = std::min(g.n, ((b - g.off) + 15) & ~(size_t)15);
-        pf.p[pf.n] = g.p + a16;
-        pf.bytes[pf.n] = (unsigned)(b16 - a16);
-        pf.n++;
-    }
-}
-struct StreamPlan {
-    std::vector<StreamSeg> segs;
-    std::vector<size_t> start;   // per matrix in launch order, then the total
-    size_t la = 0;
-    void build(const mlxd_model *m) {
-        std::vector<std::pair<const unsigned char *, size_t>> arr;
-        auto add = [&](const QMat &q) {
-            start.push_back(segs.empty() ? 0 : segs.back().off + segs.back().n);
-            arr.clear();
-            qgemv_stream(q, arr);
-            for (auto &x : arr) {
-                const size_t off = segs.empty() ? 0 : segs.back().off + segs.back().n;
-                segs.push_back(StreamSeg{x.first, x.second, off});
-            }
-        };
-        for (const Layer &L : m->L) {
-            add(L.qkv);
-            add(L.o);
-            add(L.gateup);
-            add(L.down);
-        }
-        add(m->lm);
-        start.push_back(segs.empty() ? 0 : segs.back().off + segs.back().n);
-        la = pf_lookahead();
-    }
-    // the window of the GEMV of matrix k (launch order)
-    void gemv(size_t k, PfList &pf) const {
-        pf.n = 0;
-        if (!la) return;
-        const size_t K = start.size() - 1;
-        if (k + 1 == K) {   // lm_head: the head of the next step's stream
-            pf_window(segs, 0, std::min(la, start[K]), pf);
-            return;
-        }
-        pf_window(segs, start[k] + la, std::min(start[k + 1] + la, start[K]), pf);
-    }
-};
-
 // one token through every layer with the fused decode kernels
 static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool want_logits,
                        uint16_t *logits_out, bool argmax, cudaStream_t st, bool pdl) {
     const mlxd_model_config &c = m->c;
     int H = c.hidden, D = c.head_dim;
     bool tp = c.tp_size > 1;
-    if (want_logits && megastep_ready(m, kv)) return megastep_launch(m, kv, ids_dev, logits_out, argmax, st);
     if (embed_rows(m->embed, H, c.qgroup, c.vocab, ids_dev, 1, m->h, st)) return -1;
     size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
-    StreamPlan plan;
-    plan.build(m);
     for (int l = 0; l < c.layers; l++) {
         Layer &L = m->L[l];
         GemvArgs a = {};
-        plan.gemv(4 * l, a.pf);
-        a.ws = m->gemv_ws;
-        a.cnt = m->gemv_cnt;
+        a.gws = m->gws;
+        a.gws_bytes = m->gws_bytes;
         a.x = m->h;
         a.norm_w = L.ln1;
         a.eps = c.eps;
@@ -464,28 +414,23 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         ad.d_pos = kv->d_pos;
         ad.hq = m->hq;
         ad.hkv = m->hkv;
-        ad.part = m->part;
-        ad.count = m->att_count;
-        ad.nsplit = m->nsplit;
         ad.out = m->att;
         if (attention_decode(ad, st, pdl)) return -1;
         GemvArgs o = {};
-        plan.gemv(4 * l + 1, o.pf);
         // the o projection runs on the SMs that attention leaves free (one
         // attention CTA per SM), its CTAs resident with their weights loaded
         // while attention runs, instead of a third of them starting cold after it
         if (pdl) {
-            const int att_sms = attention_decode_tc_sms(ad), sms = num_sms();
+            const int att_sms = attention_decode_sms(ad), sms = num_sms();
             if (att_sms > 0 && sms - att_sms >= sms / 4) o.grid_cap = sms - att_sms;
         }
-        o.ws = m->gemv_ws;
-        o.cnt = m->gemv_cnt;
+        o.gws = m->gws;
+        o.gws_bytes = m->gws_bytes;
         o.x = m->att;
         if (tp) {
             o.yf = m->part_h;
-            if (qgemv(L.o, PRO_PLAIN, EPI_PARTIAL_F32, o, st, pdl)) return -1;
-            if (allreduce_f32(m, m->part_h, H, st)) return -1;
-            add_partial_kernel<<<(H + 255) / 256, 256, 0, st>>>(m->h1, m->h, m->part_h, H);
+            if (qgemv(L.o, PRO_PLAIN, EPI_PARTIAL, o, st, pdl)) return -1;
+            if (reduce_partials(m, m->part_h, H, m->h1, m->h, st)) return -1;
         } else {
             o.y = m->h1;
             o.residual = m->h;
@@ -493,24 +438,21 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
             if (qgemv(L.o, PRO_PLAIN, EPI_RESIDUAL, o, st, pdl)) return -1;
         }
         GemvArgs gu = {};
-        plan.gemv(4 * l + 2, gu.pf);
-        gu.ws = m->gemv_ws;
-        gu.cnt = m->gemv_cnt;
+        gu.gws = m->gws;
+        gu.gws_bytes = m->gws_bytes;
         gu.x = m->h1;
         gu.norm_w = L.ln2;
         gu.eps = c.eps;
         gu.y = m->act;
         if (qgemv(L.gateup, PRO_RMSNORM, EPI_SWIGLU, gu, st, pdl)) return -1;
         GemvArgs dn = {};
-        plan.gemv(4 * l + 3, dn.pf);
-        dn.ws = m->gemv_ws;
-        dn.cnt = m->gemv_cnt;
+        dn.gws = m->gws;
+        dn.gws_bytes = m->gws_bytes;
         dn.x = m->act;
         if (tp) {
             dn.yf = m->part_h;
-            if (qgemv(L.down, PRO_PLAIN, EPI_PARTIAL_F32, dn, st, pdl)) return -1;
-            if (allreduce_f32(m, m->part_h, H, st)) return -1;
-            add_partial_kernel<<<(H + 255) / 256, 256, 0, st>>>(m->h, m->h1, m->part_h, H);
+            if (qgemv(L.down, PRO_PLAIN, EPI_PARTIAL, dn, st, pdl)) return -1;
+            if (reduce_partials(m, m->part_h, H, m->h, m->h1, st)) return -1;
         } else {
             dn.y = m->h;
             dn.residual = m->h1;
@@ -520,9 +462,8 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
     }
     if (want_logits) {
         GemvArgs lg = {};
-        plan.gemv(4 * (size_t)c.layers, lg.pf);
-        lg.ws = m->gemv_ws;
-        lg.cnt = m->gemv_cnt;
+        lg.gws = m->gws;
+        lg.gws_bytes = m->gws_bytes;
         lg.x = m->h;
         lg.norm_w = m->norm;
         lg.eps = c.eps;
@@ -538,13 +479,13 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
             }
         }
     }
-    step_finish_kernel<<<1, 1, 0, st>>>(kv->d_pos, argmax ? m->amax : nullptr, m->token, nullptr,
-                                        nullptr);
+    step_finish_kernel<<<1, 1, 0, st>>>(kv->d_pos, argmax ? m->amax : nullptr, m->token);
     MLXD_CHECK(cudaGetLastError());
     return 0;
 }
 
-// S tokens through the generic kernels (prefill chunks; dense checkpoints)
+// S tokens through the generic kernels (prefill chunks; models the decode
+// kernels do not serve)
 static int generic_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, int S, bool want_logits,
                            uint16_t *logits_out, cudaStream_t st) {
     const mlxd_model_config &c = m->c;
@@ -552,41 +493,40 @@ static int generic_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, i
     bool tp = c.tp_size > 1;
     if (ensure_prefill(m, S)) return -1;
     int pos0 = kv->offset;
+    if (ensure_attn_scratch(m, S, pos0, kv->window)) return -1;
     if (embed_rows(m->embed, H, c.qgroup, c.vocab, ids_dev, S, m->p_h, st)) return -1;
     size_t layer_elems = (size_t)kv->hkv * kv->cap * D;
     for (int l = 0; l < c.layers; l++) {
         Layer &L = m->L[l];
         uint16_t *kc = kv->k + (size_t)l * layer_elems, *vc = kv->v + (size_t)l * layer_elems;
         if (rmsnorm_rows(m->p_h, S, H, L.ln1, c.eps, m->p_x, st)) return -1;
-        if (linear_any(L.qkv, m->p_x, S, m->p_qkv, EPI_STORE, nullptr, nullptr, m->gemv_ws, m->gemv_cnt, st)) return -1;
+        if (linear_any(m, L.qkv, m->p_x, S, EPI_STORE, m->p_qkv, nullptr, nullptr, st)) return -1;
         if (qk_rope_append(m->p_qkv, S, m->qdim, m->hq, m->hkv, c.attn_gate, c.qk_norm ? L.qn : nullptr,
                            c.qk_norm ? L.kn : nullptr, c.eps, RopeArgs{D, c.rope_dims, m->rope_cs}, pos0,
                            m->p_q, kc, vc, kv->cap, st))
             return -1;
         if (attention_prefill(m->p_q, S, pos0, kc, vc, kv->cap, kv->window, m->hq, m->hkv, D,
-                              c.attn_gate ? m->p_qkv : nullptr, m->qdim, m->p_att, st))
+                              c.attn_gate ? m->p_qkv : nullptr, m->qdim, m->p_att, m->p_scr, m->p_scr_floats, st))
             return -1;
         if (tp) {
-            if (linear_any(L.o, m->p_att, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, m->gemv_ws, m->gemv_cnt, st)) return -1;
-            if (allreduce_f32(m, m->p_part, (size_t)S * H, st)) return -1;
-            add_partial_kernel<<<(S * H + 255) / 256, 256, 0, st>>>(m->p_h, m->p_h, m->p_part, S * H);
-        } else if (linear_any(L.o, m->p_att, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, m->gemv_ws, m->gemv_cnt, st)) {
+            if (linear_any(m, L.o, m->p_att, S, EPI_PARTIAL, nullptr, nullptr, m->p_part, st)) return -1;
+            if (reduce_partials(m, m->p_part, (size_t)S * H, m->p_h, m->p_h, st)) return -1;
+        } else if (linear_any(m, L.o, m->p_att, S, EPI_RESIDUAL, m->p_h, m->p_h, nullptr, st)) {
             return -1;
         }
         if (rmsnorm_rows(m->p_h, S, H, L.ln2, c.eps, m->p_x, st)) return -1;
-        if (linear_any(L.gateup, m->p_x, S, m->p_act, EPI_SWIGLU, nullptr, nullptr, m->gemv_ws, m->gemv_cnt, st)) return -1;
+        if (linear_any(m, L.gateup, m->p_x, S, EPI_SWIGLU, m->p_act, nullptr, nullptr, st)) return -1;
         if (tp) {
-            if (linear_any(L.down, m->p_act, S, nullptr, EPI_PARTIAL_F32, nullptr, m->p_part, m->gemv_ws, m->gemv_cnt, st)) return -1;
-            if (allreduce_f32(m, m->p_part, (size_t)S * H, st)) return -1;
-            add_partial_kernel<<<(S * H + 255) / 256, 256, 0, st>>>(m->p_h, m->p_h, m->p_part, S * H);
-        } else if (linear_any(L.down, m->p_act, S, m->p_h, EPI_RESIDUAL, m->p_h, nullptr, m->gemv_ws, m->gemv_cnt, st)) {
+            if (linear_any(m, L.down, m->p_act, S, EPI_PARTIAL, nullptr, nullptr, m->p_part, st)) return -1;
+            if (reduce_partials(m, m->p_part, (size_t)S * H, m->p_h, m->p_h, st)) return -1;
+        } else if (linear_any(m, L.down, m->p_act, S, EPI_RESIDUAL, m->p_h, m->p_h, nullptr, st)) {
             return -1;
         }
     }
     if (want_logits) {
         const uint16_t *last = m->p_h + (size_t)(S - 1) * H;
         if (rmsnorm_rows(last, 1, H, m->norm, c.eps, m->p_x, st)) return -1;
-        if (linear_any(m->lm, m->p_x, 1, logits_out, EPI_STORE, nullptr, nullptr, m->gemv_ws, m->gemv_cnt, st)) return -1;
+        if (linear_any(m, m->lm, m->p_x, 1, EPI_STORE, logits_out, nullptr, nullptr, st)) return -1;
     }
     set_pos_kernel<<<1, 1, 0, st>>>(kv->d_pos, pos0 + S);
     MLXD_CHECK(cudaGetLastError());
@@ -682,6 +622,10 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         set_error("invalid rope dims %d", c.rope_dims);
         return -1;
     }
+    if ((c.inter / tp) % 64) {
+        set_error("intermediate shard %d is not a multiple of 64", c.inter / tp);
+        return -1;
+    }
     mlxd_model *m = new mlxd_model();
     m->c = c;
     m->c.tp_size = tp;
@@ -698,6 +642,7 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
     TensorSet ts;
     for (int i = 0; i < n_tensors; i++) ts.by_name[tensors[i].name] = &tensors[i];
     auto fail = [&]() {
+        cudaDeviceSynchronize();
         mlxd_cuda_model_destroy(m);
         return -1;
     };
@@ -720,21 +665,20 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
             set_error("layer %d: projection shapes do not match the config", l);
             return fail();
         }
-        int ql = plan[0][1], kl = plan[1][1];
+        const int ql = plan[0][1], kl = plan[1][1];
         // fused q|k|v rows (column-parallel slice by heads)
-        std::vector<Piece> qkv = {
-            {q, plan[0][0], ql, 0, 0, 1, 0},
-            {k, plan[1][0], kl, 0, ql / 16, 1, ql},
-            {v, plan[2][0], kl, 0, (ql + kl) / 16, 1, ql + kl}};
-        if (build_qmat(ts, L.qkv, ql + 2 * kl, c.hidden, G, qkv, st)) return fail();
+        if (build_qmat(L.qkv, ql + 2 * kl, c.hidden, G,
+                       {{q, plan[0][0], ql, 0, 0, 0}, {k, plan[1][0], kl, 0, ql, 0}, {v, plan[2][0], kl, 0, ql + kl, 0}},
+                       false, st))
+            return fail();
         // o: row-parallel (input columns of this rank's heads)
-        int oc = plan[3][3];
-        if (build_qmat(ts, L.o, c.hidden, oc, G, {{o, 0, c.hidden, plan[3][2], 0, 1, 0}}, st)) return fail();
-        // gate/up: quantized -> interleaved 16-row blocks; dense -> stacked
-        int il = plan[4][1];
-        std::vector<Piece> gu = {{gt, plan[4][0], il, 0, 0, 2, 0}, {up, plan[5][0], il, 0, 1, 2, il}};
-        if (build_qmat(ts, L.gateup, 2 * il, c.hidden, G, gu, st)) return fail();
-        if (build_qmat(ts, L.down, c.hidden, plan[6][3], G, {{dn, 0, c.hidden, plan[6][2], 0, 1, 0}}, st))
+        if (build_qmat(L.o, c.hidden, plan[3][3], G, {{o, 0, c.hidden, plan[3][2], 0, 0}}, false, st)) return fail();
+        // gate/up: alternating 64-row blocks
+        const int il = plan[4][1];
+        if (build_qmat(L.gateup, 2 * il, c.hidden, G, {{gt, plan[4][0], il, 0, 0, 1}, {up, plan[5][0], il, 0, 0, 2}},
+                       true, st))
+            return fail();
+        if (build_qmat(L.down, c.hidden, plan[6][3], G, {{dn, 0, c.hidden, plan[6][2], 0, 0}}, false, st))
             return fail();
         if (!(L.ln1 = upload_vec(ts, p + "input_layernorm.weight", c.hidden, st))) return fail();
         if (!(L.ln2 = upload_vec(ts, p + "post_attention_layernorm.weight", c.hidden, st))) return fail();
@@ -758,18 +702,15 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         m->embed.s = dev_alloc(sbb);
         m->embed.b = dev_alloc(sbb);
         if (!m->embed.w || !m->embed.s || !m->embed.b) return fail();
-        cudaMemcpyKind kind = emb.w->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-        if (!cuda_ok(cudaMemcpyAsync(m->embed.w, emb.w->data, wb, kind, st), "embed upload") ||
-            !cuda_ok(cudaMemcpyAsync(m->embed.s, emb.s->data, sbb, kind, st), "embed upload") ||
-            !cuda_ok(cudaMemcpyAsync(m->embed.b, emb.b->data, sbb, kind, st), "embed upload"))
+        if (!cuda_ok(cudaMemcpyAsync(m->embed.w, emb.w->data, wb, cudaMemcpyDefault, st), "embed upload") ||
+            !cuda_ok(cudaMemcpyAsync(m->embed.s, emb.s->data, sbb, cudaMemcpyDefault, st), "embed upload") ||
+            !cuda_ok(cudaMemcpyAsync(m->embed.b, emb.b->data, sbb, cudaMemcpyDefault, st), "embed upload"))
             return fail();
     } else {
         size_t b = tensor_elems(emb.w) * 2;
         m->embed.dense = (uint16_t *)dev_alloc(b);
         if (!m->embed.dense) return fail();
-        if (!cuda_ok(cudaMemcpyAsync(m->embed.dense, emb.w->data, b,
-                                     emb.w->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st),
-                     "embed upload"))
+        if (!cuda_ok(cudaMemcpyAsync(m->embed.dense, emb.w->data, b, cudaMemcpyDefault, st), "embed upload"))
             return fail();
     }
     Triplet lm;
@@ -779,8 +720,7 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         set_error("lm_head shape does not match the config");
         return fail();
     }
-    if (build_qmat(ts, m->lm, plan[7][1], c.hidden, G, {{lm, plan[7][0], plan[7][1], 0, 0, 1, 0}}, st))
-        return fail();
+    if (build_qmat(m->lm, plan[7][1], c.hidden, G, {{lm, plan[7][0], plan[7][1], 0, 0, 0}}, false, st)) return fail();
     if (!(m->norm = upload_vec(ts, "model.norm.weight", c.hidden, st))) return fail();
 
     // RoPE cos/sin table, computed exactly as mlx_fast_rope's angle
@@ -797,9 +737,9 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         for (int i = 0; i < half; i++)
             inv[i] = c.rope_llama3 ? 1.0f / fr[i] : exp2f(-((float)i / (float)half) * lb);
         for (int p = 0; p < npos; p++) {
-            float L = (float)p;
+            float Lp = (float)p;
             for (int i = 0; i < half; i++) {
-                float th = L * inv[i];
+                float th = Lp * inv[i];
                 cs[((size_t)p * half + i) * 2] = cosf(th);
                 cs[((size_t)p * half + i) * 2 + 1] = sinf(th);
             }
@@ -811,35 +751,25 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         m->rope_positions = npos;
     }
 
-    // decode GEMV workspace: the largest need over this model's matrices
+    // decode scratch
     {
-        size_t ws = 0;
-        int units = 0;
-        auto need = [&](const QMat &M, int epi) {
-            if (!M.quant) return;
-            int u = 0;
-            size_t f = gemv_workspace_floats(M.rows, M.cols, M.group, epi, num_sms(), &u);
-            if (f > ws) ws = f;
-            if (u > units) units = u;
+        size_t g = 0;
+        auto need = [&](const QMat &W) {
+            if (W.ti8) return;
+            size_t x = generic_ws_bytes(W, 1, PRO_RMSNORM);
+            if (x > g) g = x;
         };
         for (auto &L : m->L) {
-            need(L.qkv, EPI_STORE);
-            need(L.o, EPI_RESIDUAL);
-            need(L.gateup, EPI_SWIGLU);
-            need(L.down, EPI_RESIDUAL);
+            need(L.qkv);
+            need(L.o);
+            need(L.gateup);
+            need(L.down);
         }
-        need(m->lm, EPI_ARGMAX);
-        m->gemv_ws = (float *)dev_alloc((ws ? ws : 16) * 4);
-        m->gemv_cnt = (int *)dev_alloc((size_t)(units ? units : 4) * 4);
-        if (!m->gemv_ws || !m->gemv_cnt) return fail();
-        if (!cuda_ok(cudaMemset(m->gemv_cnt, 0, (size_t)(units ? units : 4) * 4), "memset")) return fail();
+        need(m->lm);
+        m->gws_bytes = g ? g : 256;
+        m->gws = dev_alloc(m->gws_bytes);
+        if (!m->gws) return fail();
     }
-    // decode scratch
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int ns = (2 * sms + m->hkv - 1) / m->hkv;
-    m->nsplit = ns < 1 ? 1 : (ns > 64 ? 64 : ns);
     size_t qkvw = (size_t)m->qdim + 2 * (size_t)m->hkv * D;
     m->h = (uint16_t *)dev_alloc((size_t)c.hidden * 2);
     m->h1 = (uint16_t *)dev_alloc((size_t)c.hidden * 2);
@@ -847,35 +777,27 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
     m->att = (uint16_t *)dev_alloc((size_t)m->hq * D * 2);
     m->act = (uint16_t *)dev_alloc((size_t)m->inter_local * 2);
     m->logits = (uint16_t *)dev_alloc((size_t)m->vocab_local * 2);
-    m->part = (float *)dev_alloc((size_t)m->hq * m->nsplit * (D + 2) * 4);
-    m->att_count = (int *)dev_alloc((size_t)m->hkv * 4);
     m->amax = (unsigned long long *)dev_alloc(8);
     m->token = (int32_t *)dev_alloc(4);
-    m->part_h = (float *)dev_alloc((size_t)c.hidden * 4);
+    m->part_h = (double *)dev_alloc((size_t)c.hidden * 8 * tp);
     m->lp = (float *)dev_alloc(4);
-    if (!m->lp || !m->h || !m->h1 || !m->qkv || !m->att || !m->act || !m->logits || !m->part || !m->att_count ||
-        !m->amax || !m->token || !m->part_h)
+    if (!m->lp || !m->h || !m->h1 || !m->qkv || !m->att || !m->act || !m->logits || !m->amax || !m->token ||
+        !m->part_h)
         return fail();
-    if (!cuda_ok(cudaMemset(m->att_count, 0, (size_t)m->hkv * 4), "memset") ||
-        !cuda_ok(cudaMemset(m->amax, 0, 8), "memset"))
-        return fail();
+    if (!cuda_ok(cudaMemset(m->amax, 0, 8), "memset")) return fail();
+    if (!(m->samp = samp_work_create(m->vocab_local))) return fail();
     if (!cuda_ok(cudaDeviceSynchronize(), "model upload")) return fail();
-    if (megastep_setup(m)) return fail();
     for (auto &L : m->L)
-        m->weight_bytes += L.qkv.tile_bytes() + L.qkv.sb_bytes() + L.o.tile_bytes() + L.o.sb_bytes() +
-                           L.gateup.tile_bytes() + L.gateup.sb_bytes() + L.down.tile_bytes() + L.down.sb_bytes();
-    m->weight_bytes += m->lm.tile_bytes() + m->lm.sb_bytes();
+        m->weight_bytes += L.qkv.stream_bytes() + L.o.stream_bytes() + L.gateup.stream_bytes() + L.down.stream_bytes();
+    m->weight_bytes += m->lm.stream_bytes();
     *out = m;
     return 0;
 }
-
-int mlxd_cuda_model_decode_path(const mlxd_model *m) { return m && m->mega ? 1 : 0; }
 
 void mlxd_cuda_model_destroy(mlxd_model *m) {
     if (!m) return;
     cudaDeviceSynchronize();
     if (m->graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
-    megastep_free(m);
     for (auto &L : m->L) {
         free_qmat(L.qkv);
         free_qmat(L.o);
@@ -894,12 +816,13 @@ void mlxd_cuda_model_destroy(mlxd_model *m) {
     dev_free(m->norm);
     dev_free(m->rope_cs);
     for (void *p : {(void *)m->h, (void *)m->h1, (void *)m->qkv, (void *)m->att, (void *)m->act,
-                    (void *)m->logits, (void *)m->part, (void *)m->att_count, (void *)m->amax,
-                    (void *)m->token, (void *)m->part_h, (void *)m->p_h, (void *)m->p_x, (void *)m->p_qkv,
-                    (void *)m->p_q, (void *)m->p_att, (void *)m->p_act, (void *)m->p_tmp, (void *)m->p_ids,
-                    (void *)m->p_part, (void *)m->ctx, (void *)m->n_ctx, (void *)m->d_step, (void *)m->lp,
-                    (void *)m->gemv_ws, (void *)m->gemv_cnt})
+                    (void *)m->logits, (void *)m->amax, (void *)m->token, (void *)m->part_h, (void *)m->p_h,
+                    (void *)m->p_x, (void *)m->p_qkv, (void *)m->p_q, (void *)m->p_att, (void *)m->p_act,
+                    (void *)m->p_tmp, (void *)m->p_ids, (void *)m->p_part, (void *)m->p_ws, (void *)m->p_scr,
+                    (void *)m->ctx, (void *)m->n_ctx, (void *)m->d_step, (void *)m->lp, (void *)m->gws})
         dev_free(p);
+    samp_work_destroy(m->samp);
+    if (m->stream) cudaStreamDestroy(m->stream);
     if (m->nccl) ncclCommDestroy((ncclComm_t)m->nccl);
     delete m;
 }
@@ -1021,10 +944,9 @@ int mlxd_cuda_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids, int n, int
     cudaStream_t st = (cudaStream_t)stream;
     if (ensure_prefill(m, n)) return -1;
     if (!ids_on_device) {
-        std::vector<int32_t> chk(ids, ids + n);
         for (int i = 0; i < n; i++)
-            if (chk[i] < 0 || chk[i] >= m->c.vocab) {
-                set_error("token id %d out of range", chk[i]);
+            if (ids[i] < 0 || ids[i] >= m->c.vocab) {
+                set_error("token id %d out of range", ids[i]);
                 return -1;
             }
     }
@@ -1037,11 +959,14 @@ int mlxd_cuda_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids, int n, int
 
 int mlxd_cuda_linear_create(mlxd_linear **out, const uint32_t *w, const void *scales, const void *biases,
                             int sdtype, int rows, int cols, int group, int on_device) {
-    if (!out || !w || !scales || !biases) return -1;
+    if (!out || !w || !scales || !biases || rows <= 0 || cols <= 0 || (group != 32 && group != 64) ||
+        cols % group || (sdtype != MLXD_BF16 && sdtype != MLXD_F32)) {
+        set_error("linear_create: bad arguments");
+        return -1;
+    }
     mlxd_tensor tw = {"w", MLXD_U32, 2, {rows, cols / 8}, w, on_device};
     mlxd_tensor tsc = {"w.scales", sdtype, 2, {rows, cols / group}, scales, on_device};
     mlxd_tensor tb = {"w.biases", sdtype, 2, {rows, cols / group}, biases, on_device};
-    TensorSet ts;
     Triplet t;
     t.w = &tw;
     t.s = &tsc;
@@ -1050,22 +975,15 @@ int mlxd_cuda_linear_create(mlxd_linear **out, const uint32_t *w, const void *sc
     t.rows = rows;
     t.cols = cols;
     mlxd_linear *l = new mlxd_linear();
-    if (build_qmat(ts, l->W, rows, cols, group, {{t, 0, rows, 0, 0, 1, 0}}, nullptr)) {
-        free_qmat(l->W);
-        delete l;
-        return -1;
-    }
-    int units = 0;
-    size_t wsf = gemv_workspace_floats(rows, cols, group, EPI_STORE, num_sms(), &units);
-    l->ws = (float *)dev_alloc((wsf ? wsf : 16) * 4);
-    l->cnt = (int *)dev_alloc((size_t)(units ? units : 4) * 4);
-    if (!l->ws || !l->cnt || !cuda_ok(cudaMemset(l->cnt, 0, (size_t)(units ? units : 4) * 4), "memset")) {
+    if (build_qmat(l->W, rows, cols, group, {{t, 0, rows, 0, 0, 0}}, false, nullptr)) {
+        cudaDeviceSynchronize();
         mlxd_cuda_linear_destroy(l);
         return -1;
     }
-    if (!cuda_ok(cudaDeviceSynchronize(), "linear upload")) {
-        free_qmat(l->W);
-        delete l;
+    l->ws_bytes = generic_ws_bytes(l->W, 1, PRO_PLAIN);
+    l->ws = dev_alloc(l->ws_bytes);
+    if (!l->ws || !cuda_ok(cudaDeviceSynchronize(), "linear upload")) {
+        mlxd_cuda_linear_destroy(l);
         return -1;
     }
     *out = l;
@@ -1077,14 +995,32 @@ void mlxd_cuda_linear_destroy(mlxd_linear *l) {
     cudaDeviceSynchronize();
     free_qmat(l->W);
     dev_free(l->ws);
-    dev_free(l->cnt);
     delete l;
 }
 
 int mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *stream) {
-    if (!l || !x || !y || S <= 0) return -1;
-    return linear_any(l->W, (const uint16_t *)x, S, (uint16_t *)y, EPI_STORE, nullptr, nullptr, l->ws,
-                      l->cnt, (cudaStream_t)stream);
+    if (!l || !x || !y || S <= 0) {
+        set_error("linear: bad arguments");
+        return -1;
+    }
+    mlxd_linear *ml = const_cast<mlxd_linear *>(l);
+    GemvArgs a = {};
+    a.x = (const uint16_t *)x;
+    a.y = (uint16_t *)y;
+    if (S == 1) {
+        a.gws = ml->ws;
+        a.gws_bytes = ml->ws_bytes;
+        return qgemv(ml->W, PRO_PLAIN, EPI_STORE, a, (cudaStream_t)stream, false);
+    }
+    const size_t need = generic_ws_bytes(ml->W, S, PRO_PLAIN);
+    if (need > ml->ws_bytes) {
+        MLXD_CHECK(cudaStreamSynchronize((cudaStream_t)stream));
+        dev_free(ml->ws);
+        ml->ws = dev_alloc(need);
+        ml->ws_bytes = ml->ws ? need : 0;
+        if (!ml->ws) return -1;
+    }
+    return qgemm_generic(ml->W, PRO_PLAIN, EPI_STORE, a, S, ml->ws, ml->ws_bytes, (cudaStream_t)stream);
 }
 
 int mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void *stream) {
@@ -1104,14 +1040,18 @@ int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const
     cudaEventCreate(&a);
     cudaEventCreate(&b);
     int rc = 0;
-    for (int i = 0; i < n && !rc; i++)   // warm-up
-        rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr,
-                        ls[i]->ws, ls[i]->cnt, st);
+    auto one = [&](int i) {
+        GemvArgs g = {};
+        g.x = (const uint16_t *)x;
+        g.y = (uint16_t *)y;
+        g.gws = ls[i]->ws;
+        g.gws_bytes = ls[i]->ws_bytes;
+        return qgemv(ls[i]->W, PRO_PLAIN, EPI_STORE, g, st, false);
+    };
+    for (int i = 0; i < n && !rc; i++) rc = one(i);   // warm-up
     cudaEventRecord(a, st);
     for (int it = 0; it < iters && !rc; it++)
-        for (int i = 0; i < n && !rc; i++)
-            rc = linear_any(ls[i]->W, (const uint16_t *)x, 1, (uint16_t *)y, EPI_STORE, nullptr, nullptr,
-                            ls[i]->ws, ls[i]->cnt, st);
+        for (int i = 0; i < n && !rc; i++) rc = one(i);
     cudaEventRecord(b, st);
     if (!rc && cuda_ok(cudaEventSynchronize(b), "linear_timed")) {
         float ms = 0.f;
@@ -1134,8 +1074,39 @@ int mlxd_cuda_rmsnorm(const void *x, int rows, int n, const void *w, float eps, 
 int mlxd_cuda_sample(const void *logits_dev, int dtype, int V, const mlxd_sampling *sp, const int32_t *ctx_dev,
                      int n_ctx, uint64_t step, int32_t *tok_dev, float *logprob_dev, uint8_t *keep_dev,
                      void *stream) {
-    if (!sp) return -1;
-    return sample(logits_dev, dtype, V, *sp, ctx_dev, n_ctx, step, tok_dev, logprob_dev, keep_dev,
+    if (!sp || V <= 0) {
+        set_error("sample: bad arguments");
+        return -1;
+    }
+    // scratch per device for the one-off entry point, sized up as needed
+    static std::mutex mu;
+    static std::vector<std::pair<int, SampWork *>> works;
+    int dev = 0;
+    MLXD_CHECK(cudaGetDevice(&dev));
+    SampWork *w = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (auto &e : works)
+            if (e.first == dev) w = e.second;
+        if (!w || samp_work_capacity(w) < V) {
+            if (w) {
+                MLXD_CHECK(cudaDeviceSynchronize());
+                samp_work_destroy(w);
+                for (auto &e : works)
+                    if (e.first == dev) e.second = nullptr;
+            }
+            w = samp_work_create(V);
+            if (!w) return -1;
+            bool placed = false;
+            for (auto &e : works)
+                if (e.first == dev) {
+                    e.second = w;
+                    placed = true;
+                }
+            if (!placed) works.push_back({dev, w});
+        }
+    }
+    return sample(w, logits_dev, dtype, V, *sp, ctx_dev, n_ctx, step, tok_dev, logprob_dev, keep_dev,
                   (cudaStream_t)stream);
 }
 
@@ -1158,24 +1129,35 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
             set_error("prompt token id %d out of range", prompt[i]);
             return -1;
         }
+    if (m->c.tp_size > 1 && !(sp->temperature < 0.01f && !(sp->repetition_penalty > 0.f && sp->repetition_penalty != 1.f))) {
+        set_error("sampled decoding and the repetition penalty are not supported with tensor parallelism");
+        return -1;
+    }
     cudaStream_t st = m->stream;
     if (!st) {
         MLXD_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
         m->stream = st;
     }
     if (mlxd_cuda_kv_reset(kv)) return -1;
-    // context list for the repetition penalty (prompt + generated)
+    // context list for the repetition penalty (prompt + generated); a
+    // captured decode graph holds these buffers, so it goes when they do
     int ctx_cap = n + max_new + 1;
-    if (ctx_cap > m->ctx_cap) {
+    if (ctx_cap > m->ctx_cap || !m->n_ctx || !m->d_step) {
+        if (m->graph_exec) {
+            cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
+            m->graph_exec = nullptr;
+        }
         dev_free(m->ctx);
         m->ctx = (int32_t *)dev_alloc((size_t)ctx_cap * 4);
-        if (!m->ctx) return -1;
+        if (!m->ctx) {
+            m->ctx_cap = 0;
+            return -1;
+        }
         m->ctx_cap = ctx_cap;
         if (!m->n_ctx) m->n_ctx = (int32_t *)dev_alloc(4);
-        if (!m->n_ctx) return -1;
+        if (!m->d_step) m->d_step = (unsigned long long *)dev_alloc(8);
+        if (!m->n_ctx || !m->d_step) return -1;
     }
-    if (!m->d_step) m->d_step = (unsigned long long *)dev_alloc(8);
-    if (!m->d_step) return -1;
     int32_t *pin = nullptr;
     MLXD_CHECK(cudaMallocHost(&pin, sizeof(int32_t) * (size_t)(n + 8) + sizeof(float) * 8));
     float *pin_lp = (float *)(pin + n + 8);
@@ -1208,8 +1190,11 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     }
     cudaEventRecord(e1, st);
     nvtxRangePop();
-    bool greedy = sp->temperature < 0.01f;
-    bool fast = fast_decode_ok(m);
+    // the fused greedy argmax needs the raw logits: a repetition penalty
+    // (applied before greedy draws too) goes through the sampler
+    const bool penalty = sp->repetition_penalty > 0.f && sp->repetition_penalty != 1.0f;
+    const bool greedy = sp->temperature < 0.01f && !penalty;
+    const bool fast = fast_decode_ok(m);
     // device token slot starts as the last prompt token (the seed forward)
     MLXD_CHECK(cudaMemcpyAsync(m->token, m->ctx + n - 1, 4, cudaMemcpyDeviceToDevice, st));
     int emitted = 0;
@@ -1217,22 +1202,21 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     // one decode step (forward of m->token, then the token choice), enqueued
     auto enqueue_step = [&](int e) -> int {
         if (check_room(m, kv, 1)) return -1;
-        // one CUDA graph per step: the greedy step, or (one GPU) the sampled
-        // step with the sampler reading the context length and the draw's
-        // step from device counters
+        // one CUDA graph per step: the greedy step, or the sampled step with
+        // the sampler reading the context length and the draw's step from
+        // device counters
         const bool sampled = !greedy;
-        if (fast && (greedy || m->c.tp_size == 1)) {
+        if (fast) {
             if (!m->graph_exec || m->graph_kv != kv || m->graph_kv_serial != kv->serial ||
-                m->graph_lp != (logprobs != nullptr) ||
-                m->graph_sampled != sampled || (sampled && memcmp(&m->graph_sp, sp, sizeof *sp) != 0)) {
+                m->graph_lp != (logprobs != nullptr) || m->graph_sampled != sampled ||
+                (sampled && memcmp(&m->graph_sp, sp, sizeof *sp) != 0)) {
                 if (m->graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)m->graph_exec);
                 m->graph_exec = nullptr;
-                if (sampled && sample_reserve(m->vocab_local)) return -1;
                 cudaGraph_t g;
                 MLXD_CHECK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
                 int r = decode_step(m, kv, m->token, true, m->logits, !sampled, st, true);
                 if (!r && sampled) {
-                    r = sample(m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, 0, 0, m->token,
+                    r = sample(m->samp, m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, 0, 0, m->token,
                                logprobs ? m->lp : nullptr, nullptr, st, m->n_ctx, m->d_step);
                     if (!r) sampled_step_kernel<<<1, 1, 0, st>>>(m->ctx, m->n_ctx, m->token, m->d_step);
                 } else if (!r && logprobs) {
@@ -1241,11 +1225,13 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
                 cudaError_t ce = cudaStreamEndCapture(st, &g);
                 if (r || ce != cudaSuccess) {
                     if (!r) set_error("graph capture: %s", cudaGetErrorString(ce));
+                    if (ce == cudaSuccess) cudaGraphDestroy(g);
                     return -1;
                 }
                 cudaGraphExec_t ge;
-                MLXD_CHECK(cudaGraphInstantiate(&ge, g, 0));
+                cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
                 cudaGraphDestroy(g);
+                if (!cuda_ok(ie, "cudaGraphInstantiate")) return -1;
                 m->graph_exec = ge;
                 m->graph_kv = kv;
                 m->graph_kv_serial = kv->serial;
@@ -1255,16 +1241,8 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
             }
             MLXD_CHECK(cudaGraphLaunch((cudaGraphExec_t)m->graph_exec, st));
         } else {
-            if (fast) {
-                if (decode_step(m, kv, m->token, true, m->logits, false, st, false)) return -1;
-            } else {
-                if (generic_forward(m, kv, m->token, 1, true, m->logits, st)) return -1;
-            }
-            if (m->c.tp_size > 1) {
-                set_error("sampled decoding with tensor parallelism is not supported");
-                return -1;
-            }
-            if (sample(m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, n + e, (uint64_t)e, m->token,
+            if (generic_forward(m, kv, m->token, 1, true, m->logits, st)) return -1;
+            if (sample(m->samp, m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, n + e, (uint64_t)e, m->token,
                        logprobs ? m->lp : nullptr, nullptr, st))
                 return -1;
             append_token_kernel<<<1, 1, 0, st>>>(m->ctx, n + e, m->token);
@@ -1274,7 +1252,6 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
         if (logprobs) MLXD_CHECK(cudaMemcpyAsync(pin_lp + (e & 1), m->lp, 4, cudaMemcpyDeviceToHost, st));
         return 0;
     };
-    (void)nctx_h;
     std::chrono::steady_clock::time_point t0;
     bool decode_range = false;
     std::vector<cudaEvent_t> evs(2);
@@ -1318,12 +1295,8 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     }
     cudaEventRecord(e2, st);
     if (!cuda_ok(cudaStreamSynchronize(st), "generate")) rc = -1;
-    if (!rc && megastep_timeouts(m)) {
-        set_error("decode step gave up waiting at a grid barrier");
-        rc = -1;
-    }
-    if (!rc && qgemm_tc_timeouts()) {
-        set_error("prefill GEMM gave up waiting on its pipeline");
+    if (!rc && attention_timeouts()) {
+        set_error("decode attention: a launch was sized for fewer positions than it met");
         rc = -1;
     }
     if (timing) {
@@ -1353,23 +1326,3 @@ done:
 }
 
 }  // extern "C"
-
-#ifdef MLXD_TRACE
-namespace mlxd {
-void trace_bind_qgemv(unsigned long long *p);
-void trace_bind_attention(unsigned long long *p);
-void trace_bind_megastep(unsigned long long *p);
-void trace_bind_attention_tc(unsigned long long *p);
-void trace_bind_sampler(unsigned long long *p);
-}
-// timeline trace of the decode kernels (trace builds only): buf is a device
-// buffer of 4 + 4 * 2^20 u64, word 0 zeroed by the caller
-extern "C" int mlxd_cuda_trace_bind(void *buf) {
-    mlxd::trace_bind_qgemv((unsigned long long *)buf);
-    mlxd::trace_bind_attention((unsigned long long *)buf);
-    mlxd::trace_bind_megastep((unsigned long long *)buf);
-    mlxd::trace_bind_attention_tc((unsigned long long *)buf);
-    mlxd::trace_bind_sampler((unsigned long long *)buf);
-    return 0;
-}
-#endif

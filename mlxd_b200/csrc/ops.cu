@@ -1,6 +1,7 @@
 // Small per-token ops: embedding gather, RMSNorm rows, prefill q/k norm +
 // RoPE + KV append, residual add.
 #include "common.cuh"
+#include "gemv_i8.cuh"
 #include "kernels.h"
 
 namespace mlxd {
@@ -140,13 +141,21 @@ int qk_rope_append(const uint16_t *qkv, int S, int qdim, int hq, int hkv, int ga
     return 0;
 }
 
-__global__ void add_residual_kernel(uint16_t *h, const uint16_t *y, size_t n) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) h[i] = f2bf(__fadd_rn(bf2f(h[i]), bf2f(y[i])));
+// tensor parallelism: the row-parallel projection's value is the sum of the
+// ranks' f64 partials (exact terms of the group-exact arithmetic, added in
+// rank order), rounded once to bf16, then added to the residual in bf16
+__global__ void add_partials_kernel(uint16_t *h_out, const uint16_t *h_in, const double *part, int nranks,
+                                    size_t stride, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    double v = 0.0;
+    for (int r = 0; r < nranks; r++) v += part[(size_t)r * stride + i];
+    h_out[i] = f2bf(__fadd_rn(bf2f(h_in[i]), bf2f(d2bf(v))));
 }
 
-int add_residual(uint16_t *h, const uint16_t *y, size_t n, cudaStream_t st) {
-    add_residual_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(h, y, n);
+int add_partials(uint16_t *h_out, const uint16_t *h_in, const double *part, int nranks, size_t stride, size_t n,
+                 cudaStream_t st) {
+    add_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(h_out, h_in, part, nranks, stride, n);
     MLXD_CHECK(cudaGetLastError());
     return 0;
 }

@@ -71,7 +71,6 @@ struct SampWork {
     float *pv = nullptr;            // exp(v - m) / z, same layout (top_p)
     int V = 0;
 };
-static SampWork g_work;
 
 MLXD_DEV uint32_t ord_key(float v) {
     uint32_t u = __float_as_uint(v);
@@ -203,7 +202,7 @@ __global__ void __launch_bounds__(SAMP_PT) samp_stats_kernel(
     const int c0 = blockIdx.x * SAMP_CH, n = min(V - c0, SAMP_CH);
     const bool greedy = sp.temperature < 0.01f;
     if (d_nctx) n_ctx = *d_nctx;
-    const bool pen = !greedy && sp.repetition_penalty > 0.f && sp.repetition_penalty != 1.0f && n_ctx > 0;
+    const bool pen = sp.repetition_penalty > 0.f && sp.repetition_penalty != 1.0f && n_ctx > 0;
     for (int i = tid; i < n; i += SAMP_PT) {
         xs[i] = load_logit<T>(logits, c0 + i);
         first[i] = 0x7fffffff;
@@ -683,15 +682,27 @@ __global__ void iota_kernel(int *p, int n) {
     if (i < n) p[i] = i;
 }
 
-static int ensure_work(int V) {
-    if (g_work.V >= V) return 0;
-    SampWork &w = g_work;
-    dev_free(w.xw); dev_free(w.sw); dev_free(w.cand_v); dev_free(w.cand_i);
-    dev_free(w.sorted_v); dev_free(w.sorted_i); dev_free(w.idx_in); dev_free(w.cub_tmp);
-    dev_free(w.meta);
-    dev_free(w.p_max); dev_free(w.p_sum); dev_free(w.p_smax); dev_free(w.p_key);
-    dev_free(w.hist); dev_free(w.ctr); dev_free(w.ev); dev_free(w.pv);
-    w = SampWork{};
+void samp_work_destroy(SampWork *w) {
+    if (!w) return;
+    dev_free(w->xw); dev_free(w->sw); dev_free(w->cand_v); dev_free(w->cand_i);
+    dev_free(w->sorted_v); dev_free(w->sorted_i); dev_free(w->idx_in); dev_free(w->cub_tmp);
+    dev_free(w->meta);
+    dev_free(w->p_max); dev_free(w->p_sum); dev_free(w->p_smax); dev_free(w->p_key);
+    dev_free(w->hist); dev_free(w->ctr); dev_free(w->ev); dev_free(w->pv);
+    delete w;
+}
+
+int samp_work_capacity(const SampWork *w) { return w ? w->V : 0; }
+
+// scratch for rows of up to V logits on the current device (its caller owns
+// it: one per model, so that a captured decode graph keeps valid pointers)
+SampWork *samp_work_create(int V) {
+    if (V <= 0) {
+        set_error("sample: bad vocabulary size %d", V);
+        return nullptr;
+    }
+    SampWork *pw = new SampWork();
+    SampWork &w = *pw;
     w.xw = (float *)dev_alloc(sizeof(float) * V);
     w.sw = (float *)dev_alloc(sizeof(float) * V);
     w.cand_v = (float *)dev_alloc(sizeof(float) * SAMP_CAND);
@@ -709,35 +720,38 @@ static int ensure_work(int V) {
     w.ctr = (unsigned int *)dev_alloc(sizeof(unsigned int) * 2);
     w.ev = (float *)dev_alloc(sizeof(float) * ((V + SAMP_NB - 1) / SAMP_NB) * SAMP_NB);
     w.pv = (float *)dev_alloc(sizeof(float) * ((V + SAMP_NB - 1) / SAMP_NB) * SAMP_NB);
-    if (!w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev || !w.pv) return -1;
-    if (cudaMemset(w.hist, 0, sizeof(unsigned int) * 256) != cudaSuccess ||
-        cudaMemset(w.ctr, 0, sizeof(unsigned int) * 2) != cudaSuccess) {
-        set_error("sample: clearing the sampler's counters failed");
-        return -1;
-    }
     size_t tmp = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, tmp, (const float *)nullptr, (float *)nullptr,
                                     (const int *)nullptr, (int *)nullptr, V);
     w.cub_tmp = dev_alloc(tmp);
     w.cub_bytes = tmp;
-    if (!w.xw || !w.sw || !w.cand_v || !w.cand_i || !w.sorted_v || !w.sorted_i || !w.idx_in ||
-        !w.meta || !w.cub_tmp)
-        return -1;
+    if (!w.xw || !w.sw || !w.cand_v || !w.cand_i || !w.sorted_v || !w.sorted_i || !w.idx_in || !w.meta ||
+        !w.cub_tmp || !w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev || !w.pv) {
+        samp_work_destroy(pw);
+        return nullptr;
+    }
+    if (cudaMemset(w.hist, 0, sizeof(unsigned int) * 256) != cudaSuccess ||
+        cudaMemset(w.ctr, 0, sizeof(unsigned int) * 2) != cudaSuccess) {
+        set_error("sample: clearing the sampler's counters failed");
+        samp_work_destroy(pw);
+        return nullptr;
+    }
     w.V = V;
-    return 0;
+    return pw;
 }
 
-int sample_reserve(int V) { return V > 0 ? ensure_work(V) : 0; }
-
-int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const int32_t *ctx,
+int sample(SampWork *pw, const void *logits, int dtype, int V, const mlxd_sampling &sp, const int32_t *ctx,
            int n_ctx, uint64_t step, int32_t *tok, float *lp, uint8_t *keep, cudaStream_t st,
            const int32_t *d_nctx, const unsigned long long *d_step) {
-    if (V <= 0 || !tok) {
+    if (V <= 0 || !tok || !pw) {
         set_error("sample: bad arguments");
         return -1;
     }
-    if (ensure_work(V)) return -1;
-    SampWork w = g_work;
+    if (pw->V < V) {
+        set_error("sample: scratch for %d logits, row of %d", pw->V, V);
+        return -1;
+    }
+    const SampWork &w = *pw;
     const int G = (V + SAMP_CH - 1) / SAMP_CH;
     const bool greedy = sp.temperature < 0.01f;
     const int topk = !greedy && sp.top_k > 0 && sp.top_k < V;
@@ -777,16 +791,6 @@ int sample(const void *logits, int dtype, int V, const mlxd_sampling &sp, const 
     }
     samp_exp_kernel<<<(V + 1023) / 1024, 256, 0, st>>>(V, w, need_full);
     samp_finish_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep, need_full, d_step);
-    MLXD_CHECK(cudaGetLastError());
-    return 0;
-}
-
-__global__ void argmax_decode_kernel(const unsigned long long *amax, int32_t *tok) {
-    *tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(*amax & 0xFFFFFFFFull));
-}
-
-int argmax_decode(const unsigned long long *amax, int32_t *tok, cudaStream_t st) {
-    argmax_decode_kernel<<<1, 1, 0, st>>>(amax, tok);
     MLXD_CHECK(cudaGetLastError());
     return 0;
 }

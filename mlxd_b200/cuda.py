@@ -73,7 +73,6 @@ _SIGS = {
                                          C.POINTER(Tensor), C.c_int]),
     "mlxd_cuda_model_destroy": (None, [P]),
     "mlxd_cuda_model_weight_bytes": (C.c_size_t, [P]),
-    "mlxd_cuda_model_decode_path": (C.c_int, [P]),
     "mlxd_cuda_model_tp_init": (C.c_int, [P, P]),
     "mlxd_cuda_nccl_unique_id": (C.c_int, [P]),
     "mlxd_cuda_tp_plan": (C.c_int, [C.POINTER(ModelConfig), C.c_int, C.c_int, P]),
@@ -321,11 +320,6 @@ class Model:
     def from_dir(cls, model_dir, tp_rank=0, tp_size=1):
         cj = json.load(open(os.path.join(model_dir, "config.json")))
         return cls(config_from_json(cj, tp_rank, tp_size), read_checkpoint(model_dir))
-
-    def decode_path(self):
-        """1: one persistent kernel per decode step (opt-in, MLXD_MEGASTEP=1
-        at creation); 0: one kernel per op (default)."""
-        return lib().mlxd_cuda_model_decode_path(self.m)
 
     def weight_bytes(self):
         return lib().mlxd_cuda_model_weight_bytes(self.m)

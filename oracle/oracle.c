@@ -395,17 +395,71 @@ void orc_dequantize_row(const uint32_t *w, const void *s, const void *b,
     }
 }
 
-/* f32 dot product with a fixed association: eight interleaved partial sums
-   (lane i takes elements i, i+8, ...) combined pairwise. mlx's own summation
-   order is not observable, so any fixed order is as faithful; this one lets
-   the compiler keep eight independent add chains in flight. */
-static float dot8(const float *a, const float *b, int n) {
-    float p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    int j = 0;
-    for (; j + 8 <= n; j += 8)
-        for (int t = 0; t < 8; t++) p[t] += a[j + t] * b[j + t];
-    for (int t = 0; j < n; j++, t++) p[t] += a[j] * b[j];
-    return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+/* f64 -> bf16 with one correct rounding (to nearest, ties to even): the
+   value is first cut to f32 by rounding toward zero with the lowest bit set
+   when anything was cut (round to odd, 24 >= 8 + 2 bits), then rounded to
+   bf16; this equals the direct rounding of the f64 value. */
+static uint16_t d2bf(double d) {
+    if (isnan(d)) return 0x7fc0;
+    float f = (float)d;
+    if (fabs((double)f) > fabs(d)) f = nextafterf(f, 0.0f);
+    if ((double)f != d) {
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        u |= 1u;
+        memcpy(&f, &u, 4);
+    }
+    return f2bf(f);
+}
+
+/* The projection arithmetic shared with the CUDA kernels (decode GEMV,
+   prefill GEMM, tensor-parallel shards): mlx's quantized_matmul
+   (forward.c:17-32, cast to bf16 :46-54) computes per output row
+       sum over groups g of  s_g * sum_k(x_k q_k) + b_g * sum_k(x_k)
+   (qmv) in f32 with an order of its own, which is not observable. Here the
+   order is taken out of the result:
+   - each group's 64 (or 32) inputs are written in fixed point on the grid of
+     their largest magnitude: E_g = exponent of max|x_k| over the group
+     (clamped at -100), X_k = round-to-nearest-even(x_k * 2^(20 - E_g)),
+     |X_k| < 2^21; a bf16 input within 13 binades of its group's largest is
+     exact, a smaller one is rounded at 2^(E_g - 21) (below the rounding of
+     an f32 sum of the products);
+   - P_g = sum_k q_k X_k and T_g = sum_k X_k are exact integers;
+   - the row's value sum_g (s_g P_g + b_g T_g) 2^(E_g - 20) is summed in f64,
+     where every product is exact (bf16 scales) and the sum is exact while it
+     spans at most 53 bits (otherwise correct to 2^-53, so the order of the
+     sum shows only in outputs within 2^-52 of a bf16 rounding boundary);
+   - the row value is rounded once to bf16 (d2bf).
+   The grid depends on the group only, so a shard of whole groups (the
+   row-parallel projections of tensor parallelism) gives the same integers,
+   and prefill (S > 1) and decode (S = 1) give the same bits. A group
+   holding a non-finite input gives NaN. Dense bf16 weights: the f64 sum of
+   the exact products x_k w_k, rounded once. */
+static void fixed_point_groups(const float *xf, int n, int G, int32_t *X, double *pf, int64_t *T,
+                               uint8_t *bad) {
+    int ng = n / G;
+    for (int g = 0; g < ng; g++) {
+        const float *xg = xf + (size_t)g * G;
+        uint32_t eb = 0;
+        for (int k = 0; k < G; k++) {
+            uint32_t u;
+            memcpy(&u, &xg[k], 4);
+            uint32_t e = (u >> 23) & 0xffu;
+            if (e > eb) eb = e;
+        }
+        bad[g] = eb == 0xffu;
+        int E = (int)eb - 127;
+        if (E < -100) E = -100;
+        float sc = ldexpf(1.0f, 20 - E);
+        int64_t t = 0;
+        for (int k = 0; k < G; k++) {
+            int32_t v = bad[g] ? 0 : (int32_t)nearbyintf(xg[k] * sc);
+            X[(size_t)g * G + k] = v;
+            t += v;
+        }
+        T[g] = t;
+        pf[g] = ldexp(1.0, E - 20);
+    }
 }
 
 typedef struct {
@@ -414,11 +468,16 @@ typedef struct {
     const linear_t *W;
     int group, exact;
     uint16_t *y;
+    /* per token: fixed-point inputs [S][in], group factors/sums [S][ng] */
+    const int32_t *X;
+    const double *pf;
+    const int64_t *T;
+    const uint8_t *bad;
 } lin_ctx;
 
-/* mlx_quantized_matmul(transpose=true, "affine") (forward.c:17-32) and the
-   bf16 cast (forward.c:46-54). exact: y = sum_g s_g*sum(x*q) + b_g*sum(x)
-   (qmv). !exact: dequantised weights rounded to bf16, then f32 dot (qmm). */
+/* exact: the arithmetic above. !exact: mlx's qmm tile semantics (weights
+   dequantized and rounded to bf16, f32 dot in element order), kept for the
+   quantized-matmul known-answer test only. */
 static void lin_rows(void *vc, int r0, int r1) {
     lin_ctx *c = vc;
     const linear_t *W = c->W;
@@ -426,70 +485,105 @@ static void lin_rows(void *vc, int r0, int r1) {
     int ng = W->quant ? in / G : 0;
     float *wrow = malloc(sizeof(float) * (size_t)in);
     float *xf = malloc(sizeof(float) * (size_t)in * (size_t)c->S);
-    float *xs = W->quant ? malloc(sizeof(float) * (size_t)ng * (size_t)c->S) : NULL;
-    for (int s = 0; s < c->S; s++) {
+    int32_t *q = malloc(sizeof(int32_t) * (size_t)in);
+    for (int s = 0; s < c->S; s++)
         for (int j = 0; j < in; j++) xf[(size_t)s * in + j] = bf2f(c->x[(size_t)s * in + j]);
-        if (xs)
-            for (int g = 0; g < ng; g++) {
-                float a = 0.f;
-                for (int j = 0; j < G; j++) a += xf[(size_t)s * in + g * G + j];
-                xs[(size_t)s * ng + g] = a;
-            }
-    }
     for (int r = r0; r < r1; r++) {
+        if (W->quant && c->exact) {
+            const uint32_t *wr = W->w + (size_t)r * (in / 8);
+            for (int j = 0; j < in; j++) q[j] = (int32_t)((wr[j >> 3] >> ((j & 7) * 4)) & 0xFu);
+            for (int s = 0; s < c->S; s++) {
+                const int32_t *X = c->X + (size_t)s * in;
+                const double *pf = c->pf + (size_t)s * ng;
+                const int64_t *T = c->T + (size_t)s * ng;
+                const uint8_t *bad = c->bad + (size_t)s * ng;
+                double acc = 0.0;
+                int nan = 0;
+                for (int g = 0; g < ng; g++) {
+                    int32_t P = 0;
+                    for (int k = 0; k < G; k++) P += q[g * G + k] * X[g * G + k];
+                    double sc = (double)sdt_get(W->s, W->sdtype, (size_t)r * ng + g);
+                    double bi = (double)sdt_get(W->b, W->sdtype, (size_t)r * ng + g);
+                    acc += sc * ((double)P * pf[g]);
+                    acc += bi * ((double)T[g] * pf[g]);
+                    nan |= bad[g];
+                }
+                c->y[(size_t)s * c->out + r] = nan ? 0x7fc0 : d2bf(acc);
+            }
+            continue;
+        }
         if (W->quant) {
             const uint32_t *wr = W->w + (size_t)r * (in / 8);
-            if (c->exact) {
-                for (int j = 0; j < in; j++) wrow[j] = (float)((wr[j >> 3] >> ((j & 7) * 4)) & 0xFu);
-                for (int s = 0; s < c->S; s++) {
-                    const float *xv = xf + (size_t)s * in;
-                    float acc = 0.f;
-                    for (int g = 0; g < ng; g++) {
-                        float a = dot8(xv + g * G, wrow + g * G, G);
-                        float sc = sdt_get(W->s, W->sdtype, (size_t)r * ng + g);
-                        float bi = sdt_get(W->b, W->sdtype, (size_t)r * ng + g);
-                        acc += sc * a + bi * xs[(size_t)s * ng + g];
-                    }
-                    c->y[(size_t)s * c->out + r] = f2bf(acc);
-                }
-                continue;
-            }
             orc_dequantize_row(wr, (const char *)W->s + (size_t)r * ng * dtype_size(W->sdtype),
                                (const char *)W->b + (size_t)r * ng * dtype_size(W->sdtype),
                                W->sdtype, in, G, wrow);
             for (int j = 0; j < in; j++) wrow[j] = rbf(wrow[j]);
-        } else {
-            for (int j = 0; j < in; j++) wrow[j] = bf2f(W->dense[(size_t)r * in + j]);
+            for (int s = 0; s < c->S; s++) {
+                float acc = 0.f;
+                for (int j = 0; j < in; j++) acc = fmaf(xf[(size_t)s * in + j], wrow[j], acc);
+                c->y[(size_t)s * c->out + r] = f2bf(acc);
+            }
+            continue;
         }
         for (int s = 0; s < c->S; s++) {
-            float acc = dot8(xf + (size_t)s * in, wrow, in);
-            c->y[(size_t)s * c->out + r] = f2bf(acc);
+            double acc = 0.0;
+            for (int j = 0; j < in; j++)
+                acc += (double)xf[(size_t)s * in + j] * (double)bf2f(W->dense[(size_t)r * in + j]);
+            c->y[(size_t)s * c->out + r] = d2bf(acc);
         }
     }
     free(wrow);
     free(xf);
-    free(xs);
+    free(q);
 }
 
-static void linear(const linear_t *W, const uint16_t *x, int S, int group,
-                   uint16_t *y) {
-    lin_ctx c = {x, S, W->cols, W->rows, W, group, S == 1, y};
+static void run_linear(const linear_t *W, const uint16_t *x, int S, int group, int exact,
+                       uint16_t *y) {
+    lin_ctx c = {x, S, W->cols, W->rows, W, group, exact, y, NULL, NULL, NULL, NULL};
+    int32_t *X = NULL;
+    double *pf = NULL;
+    int64_t *T = NULL;
+    uint8_t *bad = NULL;
+    if (W->quant && exact) {
+        int in = W->cols, ng = in / group;
+        X = malloc(sizeof(int32_t) * (size_t)S * in);
+        pf = malloc(sizeof(double) * (size_t)S * ng);
+        T = malloc(sizeof(int64_t) * (size_t)S * ng);
+        bad = malloc((size_t)S * ng);
+        float *xf = malloc(sizeof(float) * (size_t)in);
+        for (int s = 0; s < S; s++) {
+            for (int j = 0; j < in; j++) xf[j] = bf2f(x[(size_t)s * in + j]);
+            fixed_point_groups(xf, in, group, X + (size_t)s * in, pf + (size_t)s * ng,
+                               T + (size_t)s * ng, bad + (size_t)s * ng);
+        }
+        free(xf);
+        c.X = X;
+        c.pf = pf;
+        c.T = T;
+        c.bad = bad;
+    }
     parallel_for(W->rows, 16, lin_rows, &c);
+    free(X);
+    free(pf);
+    free(T);
+    free(bad);
+}
+
+static void linear(const linear_t *W, const uint16_t *x, int S, int group, uint16_t *y) {
+    run_linear(W, x, S, group, 1, y);
 }
 
 void orc_qlinear(const uint16_t *x, int S, int in, int out, const uint32_t *w,
                  const void *scales, const void *biases, int sdtype, int group,
                  int exact_dequant, uint16_t *y) {
     linear_t W = {1, out, in, sdtype, w, scales, biases, NULL};
-    lin_ctx c = {x, S, in, out, &W, group, exact_dequant, y};
-    parallel_for(out, 16, lin_rows, &c);
+    run_linear(&W, x, S, group, exact_dequant, y);
 }
 
 void orc_dense_linear(const uint16_t *x, int S, int in, int out,
                       const uint16_t *w, uint16_t *y) {
     linear_t W = {0, out, in, 0, NULL, NULL, NULL, w};
-    lin_ctx c = {x, S, in, out, &W, 0, 0, y};
-    parallel_for(out, 16, lin_rows, &c);
+    run_linear(&W, x, S, 0, 1, y);
 }
 
 /* ------------------------------------------------------------- norm, rope */
@@ -602,6 +696,24 @@ int orc_window_mask(int q_len, int kv_len, int window, uint8_t *out) {
     return 0;
 }
 
+/* Attention arithmetic shared with the CUDA kernels (decode and prefill).
+   Fused head dims (mlx sdpa_vector / steel attention keep scores, softmax
+   and the accumulator in f32; their order is not observable, so one is
+   fixed here):
+     q_d' = f32(scale * q_d), scale = 1/sqrtf(D);
+     z_j  = fmaf chain over d = 0..D-1 of q_d' * k_jd (one rounding per step);
+     m    = max_j z_j over the attended keys;
+     p_j  = own exp(z_j - m);
+     keys are cut into blocks of 64 absolute positions [64b, 64b + 64); in a
+     block, l_b = in-order f32 sum of p_j and o_bd = fmaf chain of p_j v_jd
+     in key order; L = sum_b l_b and O_d = sum_b o_bd in f64 (exact while
+     the sum spans 53 bits, otherwise correct to 2^-53);
+     out_d = bf16(O_d / L), the f64 quotient rounded once.
+   The blocks are absolute positions, so a decode step and a prefill row at
+   the same position give the same bits. Other head dims take mlx's composed
+   fallback: q scaled in bf16, bf16 scores (fmaf chain rounded once), precise
+   softmax (in-order f32 sum) rounded to bf16, bf16 output of an fmaf chain
+   over the keys. */
 static void att_heads(void *vc, int h0, int h1) {
     att_ctx *c = vc;
     const orc_config *cf = &c->m->c;
@@ -611,6 +723,7 @@ static void att_heads(void *vc, int h0, int h1) {
     float *sc = malloc(sizeof(float) * (size_t)T);
     float *qf = malloc(sizeof(float) * (size_t)D);
     float *o = malloc(sizeof(float) * (size_t)D);
+    double *O = malloc(sizeof(double) * (size_t)D);
     for (int h = h0; h < h1; h++) {
         int kh = h / rep;
         const uint16_t *K = c->kv->k[c->layer] + (size_t)kh * c->kv->cap * D;
@@ -628,28 +741,49 @@ static void att_heads(void *vc, int h0, int h1) {
             float mx = -INFINITY;
             for (int j = j0; j < j1; j++) {
                 float a = 0.f;
-                for (int d = 0; d < D; d++) a += qf[d] * bf2f(K[(size_t)j * D + d]);
+                for (int d = 0; d < D; d++) a = fmaf(qf[d], bf2f(K[(size_t)j * D + d]), a);
                 if (c->composed) a = rbf(a);
                 sc[j] = a;
                 if (a > mx) mx = a;
             }
-            float l = 0.f;
-            for (int j = j0; j < j1; j++) {
-                sc[j] = orc_expf(sc[j] - mx);
-                l += sc[j];
-            }
-            for (int d = 0; d < D; d++) o[d] = 0.f;
-            for (int j = j0; j < j1; j++) {
-                float p = c->composed ? rbf(sc[j] / l) : sc[j];
-                for (int d = 0; d < D; d++) o[d] += p * bf2f(V[(size_t)j * D + d]);
-            }
             uint16_t *dst = c->out + ((size_t)i * Hq + h) * D;
-            for (int d = 0; d < D; d++) dst[d] = f2bf(c->composed ? o[d] : o[d] / l);
+            if (c->composed) {
+                float l = 0.f;
+                for (int j = j0; j < j1; j++) {
+                    sc[j] = orc_expf(sc[j] - mx);
+                    l += sc[j];
+                }
+                for (int d = 0; d < D; d++) o[d] = 0.f;
+                for (int j = j0; j < j1; j++) {
+                    float p = rbf(sc[j] / l);
+                    for (int d = 0; d < D; d++) o[d] = fmaf(p, bf2f(V[(size_t)j * D + d]), o[d]);
+                }
+                for (int d = 0; d < D; d++) dst[d] = f2bf(o[d]);
+                continue;
+            }
+            double L = 0.0;
+            for (int d = 0; d < D; d++) O[d] = 0.0;
+            for (int b0 = j0; b0 < j1;) {
+                int b1 = (b0 / 64 + 1) * 64;
+                if (b1 > j1) b1 = j1;
+                float l = 0.f;
+                for (int d = 0; d < D; d++) o[d] = 0.f;
+                for (int j = b0; j < b1; j++) {
+                    float p = orc_expf(sc[j] - mx);
+                    l += p;
+                    for (int d = 0; d < D; d++) o[d] = fmaf(p, bf2f(V[(size_t)j * D + d]), o[d]);
+                }
+                L += (double)l;
+                for (int d = 0; d < D; d++) O[d] += (double)o[d];
+                b0 = b1;
+            }
+            for (int d = 0; d < D; d++) dst[d] = d2bf(O[d] / L);
         }
     }
     free(sc);
     free(qf);
     free(o);
+    free(O);
 }
 
 static int fused_head_dim(int D) { return D == 64 || D == 96 || D == 128 || D == 256; }
@@ -966,11 +1100,13 @@ static float draw_uniform(int seed, uint64_t step) {
     return (float)(r >> 40) * (1.0f / 16777216.0f);
 }
 
-/* sampler_sample_lazy (sampler.c:269-380). Greedy below T=0.01: first
-   maximum; logprob from the raw logits. Otherwise: repetition penalty
+/* sampler_sample_lazy (sampler.c:269-380). Repetition penalty first
    (build-defined; the reference has none: mlx-lm's rule, x>0 ? x/p : x*p
-   over the distinct ids among the last R context tokens, on the raw
-   logits), logits/T in f32, top_k, top_p, min_p, then a categorical draw by
+   over the distinct ids among the last R context tokens, on the raw logits,
+   applied before greedy and sampled draws alike as mlx-lm's logits
+   processors are). Greedy below T=0.01: first maximum; logprob from the
+   (penalised) raw logits. Otherwise logits/T in f32, top_k, top_p, min_p,
+   then a categorical draw by
    inverse CDF over the ascending order (blocked sums, SplitMix64 uniform).
    mlx's categorical RNG stream is not reproducible here; the candidate set
    is. Logprob = x[tok] - logsumexp(x) on the (penalised) raw logits. */
@@ -980,8 +1116,7 @@ int orc_sample(const float *logits, int V, const orc_sampling *sp,
     float *x = malloc(sizeof(float) * (size_t)V);
     memcpy(x, logits, sizeof(float) * (size_t)V);
     int greedy = sp->temperature < 0.01f;
-    if (!greedy && sp->repetition_penalty > 0.f && sp->repetition_penalty != 1.0f &&
-        ctx && n_ctx > 0) {
+    if (sp->repetition_penalty > 0.f && sp->repetition_penalty != 1.0f && ctx && n_ctx > 0) {
         int R = sp->repetition_context > 0 ? sp->repetition_context : n_ctx;
         int start = n_ctx > R ? n_ctx - R : 0;
         uint8_t *seen = calloc((size_t)V, 1);
