@@ -40,63 +40,131 @@ MLXD_DEV int blk_off(int r, int c) {
 //
 // One cluster of CL CTAs (8 warps) per kv head; the attended blocks
 // (lo/64 .. pos/64) are split into CL contiguous ranges, one per CTA. A CTA
-// streams its K blocks, then its V blocks, through a 4-slot shared-memory
-// ring (cp.async, the first four requested before waiting on the q|k|v
-// projection; the cached rows do not depend on it). After the wait every CTA
-// normalises and rotates the group's q heads, and the CTA holding the new
-// position also the new k, whose row (and v's) replaces the not yet appended
-// cache row in its ring slot. Phase 1: scores (thread = (position, head)).
-// The cluster exchanges the per-head maxima through distributed shared
-// memory. Phase 2: p, then per block the f32 chains (thread = (head, pair of
-// features)), added into f64 partials. CTA r merges the r-th slice of the
-// group's outputs from all CTAs' partials, and the CTA of the new position
-// appends its k/v rows to the cache.
-constexpr int DA_THREADS = 256, DA_RING = 4;
+// streams its K blocks (padded to an even count), then its V blocks, through
+// a 4-slot shared-memory ring (cp.async; the first four loads, the norm
+// weights and this position's cos/sin are requested before waiting on the
+// q|k|v projection, on which none of them depends). After the wait warp h
+// normalises and rotates q head h in registers (lane l holds features
+// l, l + 32, ...: the oracle's per-head RMSNorm association, and rotation
+// pairs i, i + D/2 in one lane), and the CTA holding the new position also
+// the new k, whose row (and v's) replaces the not yet appended cache row in
+// its ring slot. Phase 1, two blocks at a time: scores (thread = (position,
+// head)). Each CTA pushes its per-head maxima into every CTA's inbox through
+// distributed shared memory; one cluster barrier. Phase 2, two blocks at a
+// time: p, then per block the f32 chains (thread = (head, feature pair)),
+// added into f64 partials, which are pushed into the inbox of the CTA owning
+// that slice of the outputs; one cluster barrier; each CTA adds its slice
+// locally. Remote accesses are stores only, all before a barrier.
+constexpr int DA_THREADS = 256;
+constexpr int DA_BS1 = DA_THREADS / AB;   // blocks per round in phase 1 (thread = position)
+
+template <int D>
+struct DaConst {
+    static constexpr int NP = D / 2;                 // feature pairs
+    static constexpr int BS2 = DA_THREADS / NP;      // blocks per round in phase 2
+};
 
 struct DaLayout {
-    size_t ring, qs, stage, newkv, sc, P, hmax, gmax, O, L, total;
+    size_t ring, qs, stage, newkv, sc, P, red, gmax, inmax, inO, inL, total;
 };
-static __host__ __device__ inline DaLayout da_layout(int D, int REP, int scap) {
+// nslots: K and V block slots (resident: 2 * scap/64; streaming: 2 * DA_BS1)
+static __host__ __device__ inline DaLayout da_layout(int D, int REP, int scap, int CL, int nslots) {
+    const int BS2 = DA_THREADS / (D / 2);
     DaLayout l;
     l.ring = 0;
-    l.qs = l.ring + (size_t)DA_RING * AB * D * 2;
+    l.qs = l.ring + (size_t)nslots * AB * D * 2;
     l.stage = l.qs + (size_t)REP * D * 4;
     l.newkv = l.stage + (size_t)8 * D * 4;
     l.sc = l.newkv + (size_t)2 * D * 2;
     l.P = l.sc + (size_t)REP * scap * 4;
-    l.hmax = l.P + (size_t)REP * AB * 4;
-    l.gmax = l.hmax + 64;
-    l.O = l.gmax + 64;
-    l.L = l.O + (size_t)REP * D * 8;
-    l.total = l.L + 64;
+    l.red = l.P + (size_t)BS2 * AB * REP * 4;
+    l.gmax = l.red + (size_t)8 * REP * 4;
+    l.inmax = l.gmax + 64;
+    l.inO = l.inmax + (((size_t)CL * REP * 4 + 15) / 16) * 16;
+    l.inL = l.inO + (size_t)BS2 * REP * D * 8;
+    l.total = l.inL + (size_t)CL * BS2 * REP * 8;
     return l;
 }
 
 static __device__ int g_attn_err;
 
-template <int D, int REP, int CL>
+// One head vector (warp-wide, DS = D/32 features per lane at d = lane + 32 i):
+// optional RMSNorm (fmaf partials in element order per lane, butterfly,
+// precise 1/sqrt), RoPE with rotation pairs (i, i + DS/2) in the lane, every
+// result rounded to bf16 as the oracle rounds it.
+template <int DS>
+MLXD_DEV void norm_rope_regs(float (&v)[DS], const float (&nw)[DS], bool norm, float eps, const float (&c)[DS / 2],
+                             const float (&sn)[DS / 2], int D) {
+    if (norm) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < DS; i++) acc = fmaf(v[i], v[i], acc);
+        acc = warp_sum(acc);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)D), eps)));
+#pragma unroll
+        for (int i = 0; i < DS; i++) v[i] = rbf(__fmul_rn(nw[i], rbf(__fmul_rn(v[i], inv))));
+    }
+#pragma unroll
+    for (int i = 0; i < DS / 2; i++) {
+        const float x1 = v[i], x2 = v[i + DS / 2];
+        v[i] = rbf(__fsub_rn(__fmul_rn(x1, c[i]), __fmul_rn(x2, sn[i])));
+        v[i + DS / 2] = rbf(__fadd_rn(__fmul_rn(x1, sn[i]), __fmul_rn(x2, c[i])));
+    }
+}
+
+// REP consecutive floats from shared memory
+template <int REP>
+MLXD_DEV void lds_rep(float (&o)[REP], const float *p) {
+    if constexpr (REP % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < REP; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(p + i);
+            o[i] = v.x;
+            o[i + 1] = v.y;
+            o[i + 2] = v.z;
+            o[i + 3] = v.w;
+        }
+    } else if constexpr (REP == 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(p);
+        o[0] = v.x;
+        o[1] = v.y;
+    } else {
+#pragma unroll
+        for (int i = 0; i < REP; i++) o[i] = p[i];
+    }
+}
+
+// RES: every K and V block of the CTA resident in shared memory (all K rows
+// requested as one commit group, all V rows as a second, before the wait);
+// otherwise rounds of DA_BS1 K blocks (then V blocks) in a ring of
+// 2 * DA_BS1 slots, the first round of each requested before the wait.
+template <int D, int REP, int CL, bool RES>
 __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeArgs a, int scap) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     constexpr int NCH = D / 8;               // 16-byte chunks per row
-    constexpr int HS = DA_THREADS / AB;       // head slots in phase 1 (4)
-    constexpr int NP = D / 2;                 // feature pairs
-    constexpr int HS2 = DA_THREADS / NP;      // head slots in phase 2
+    constexpr int NP = DaConst<D>::NP, BS2 = DaConst<D>::BS2;
+    constexpr int DS = D / 32;
+    constexpr int E = REP * D, ES = E / CL;   // outputs of the group, per owner CTA
+    static_assert(ES % 2 == 0, "output slices hold whole feature pairs");
     const int rank = (int)cluster.block_rank();
     const int kh = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     extern __shared__ __align__(128) unsigned char sm[];
-    const DaLayout Ly = da_layout(D, REP, scap);
+    const int NB = scap / AB;
+    const int NSLOT = RES ? 2 * NB : 2 * DA_BS1;
+    const DaLayout Ly = da_layout(D, REP, scap, CL, NSLOT);
     unsigned char *ring = sm + Ly.ring;
-    float *qs = reinterpret_cast<float *>(sm + Ly.qs);
+    float *qs = reinterpret_cast<float *>(sm + Ly.qs);          // [D][REP], scaled
     float *stage = reinterpret_cast<float *>(sm + Ly.stage) + (size_t)warp * D;
     uint16_t *newk = reinterpret_cast<uint16_t *>(sm + Ly.newkv), *newv = newk + D;
-    float *sc = reinterpret_cast<float *>(sm + Ly.sc);
-    float *P = reinterpret_cast<float *>(sm + Ly.P);
-    float *hmax = reinterpret_cast<float *>(sm + Ly.hmax);
+    float *sc = reinterpret_cast<float *>(sm + Ly.sc);          // [scap][REP]
+    float *P = reinterpret_cast<float *>(sm + Ly.P);            // [BS2][AB][REP]
+    float *red = reinterpret_cast<float *>(sm + Ly.red);        // [8 warps][REP]
     float *gmax = reinterpret_cast<float *>(sm + Ly.gmax);
-    double *O = reinterpret_cast<double *>(sm + Ly.O);
-    double *Ls = reinterpret_cast<double *>(sm + Ly.L);
+    float *inmax = reinterpret_cast<float *>(sm + Ly.inmax);    // [CL][REP]
+    double *inO = reinterpret_cast<double *>(sm + Ly.inO);      // [CL][BS2][ES]
+    double *inL = reinterpret_cast<double *>(sm + Ly.inL);      // [CL][BS2][REP]
 
     const int pos = *a.d_pos;
     const int T = pos + 1;
@@ -104,7 +172,7 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     const int bfirst = lo / AB, blast = pos / AB, nbt = blast - bfirst + 1;
     const int mb0 = bfirst + (int)((long long)nbt * rank / CL), mb1 = bfirst + (int)((long long)nbt * (rank + 1) / CL);
     int nbm = mb1 - mb0;
-    if (nbm * AB > scap) {   // cannot happen for a launch sized by the host; report and do no work
+    if (nbm > NB) {   // cannot happen for a launch sized by the host; report and do no work
         if (tid == 0) atomicExch(&g_attn_err, 1);
         nbm = 0;
     }
@@ -112,187 +180,247 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     const uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
     const uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
 
-    // load i of the stream: K block i (i < nbm) or V block i - nbm, rows
-    // outside [lo, pos) zero-filled; one commit group per call
-    auto issue = [&](int i) {
-        if (i < 2 * nbm) {
-            const bool isv = i >= nbm;
-            const int b = mb0 + (isv ? i - nbm : i);
-            unsigned char *dst = ring + (size_t)(i % DA_RING) * AB * D * 2;
-            const uint16_t *src = isv ? vc : kc;
-            for (int e = tid; e < AB * NCH; e += DA_THREADS) {
-                const int r = e / NCH, c = e % NCH;
-                const int j = b * AB + r;
-                const bool valid = j >= lo && j < pos;
-                const int jj = valid ? j : lo;
-                cp_async16_zfill(dst + blk_off<D>(r, c), src + (size_t)(jj % a.cap) * D + c * 8, valid);
-            }
+    // block i (< nbm) of K (isv 0) or V into slot `slot`; rows outside
+    // [lo, pos) zero-filled (the new position's row comes from this step)
+    auto load_block = [&](int i, bool isv, int slot) {
+        if (i >= nbm) return;
+        const int b = mb0 + i;
+        unsigned char *dst = ring + (size_t)slot * AB * D * 2;
+        const uint16_t *src = isv ? vc : kc;
+        const int slot0 = (b * AB) % a.cap;   // cache slot of the block's first position
+        for (int e = tid; e < AB * NCH; e += DA_THREADS) {
+            const int r = e / NCH, c = e % NCH;
+            const int j = b * AB + r;
+            const bool valid = j >= lo && j < pos;
+            int sl = slot0 + r;
+            if (sl >= a.cap) sl -= a.cap;
+            cp_async16_zfill(dst + blk_off<D>(r, c), src + (size_t)(valid ? sl : 0) * D + c * 8, valid);
         }
-        cp_async_commit();
     };
-#pragma unroll
-    for (int i = 0; i < DA_RING; i++) issue(i);
+    auto kslot = [&](int i) { return RES ? i : i % DA_BS1; };
+    auto vslot = [&](int i) { return RES ? NB + i : DA_BS1 + i % DA_BS1; };
+    if (RES) {
+        for (int i = 0; i < nbm; i++) load_block(i, false, kslot(i));
+        cp_async_commit();
+        for (int i = 0; i < nbm; i++) load_block(i, true, vslot(i));
+        cp_async_commit();
+    } else {
+        for (int i = 0; i < DA_BS1; i++) load_block(i, false, kslot(i));
+        cp_async_commit();
+        for (int i = 0; i < DA_BS1; i++) load_block(i, true, vslot(i));
+        cp_async_commit();
+    }
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+    // per-warp head work: q heads h = warp, warp + 8; the new k after them
+    const bool regs_rope = a.rope.rope_dims == D;
+    float nwq[DS], nwk[DS], rc[DS / 2], rs[DS / 2];
+    if (regs_rope) {
+        const float *cs = a.rope.cs + (size_t)pos * (D / 2) * 2;
+#pragma unroll
+        for (int i = 0; i < DS; i++) {
+            nwq[i] = a.qn ? bf2f(a.qn[lane + 32 * i]) : 1.f;
+            nwk[i] = a.kn ? bf2f(a.kn[lane + 32 * i]) : 1.f;
+        }
+#pragma unroll
+        for (int i = 0; i < DS / 2; i++) {
+            rc[i] = cs[2 * (lane + 32 * i)];
+            rs[i] = cs[2 * (lane + 32 * i) + 1];
+        }
+    }
     pdl_trigger();
     pdl_wait();
 
-    // q heads (warp h) and the new k (warp REP % 8, after its q head when
-    // REP = 8): RMSNorm + RoPE with the oracle's rounding points
     const int qstride = D * (a.gate ? 2 : 1);
     for (int h = warp; h < REP + 1; h += 8) {
         const bool isk = h == REP;
         if (isk && !has_new) continue;
         const uint16_t *src = isk ? a.qkv + a.qdim + (size_t)kh * D : a.qkv + (size_t)(kh * REP + h) * qstride;
-        for (int d = lane; d < D; d += 32) stage[d] = bf2f(src[d]);
-        __syncwarp();
-        head_norm_rope(stage, D, isk ? a.kn : a.qn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
-        if (isk) {
-            const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
-            for (int d = lane; d < D; d += 32) {
-                newk[d] = f2bf(stage[d]);
-                newv[d] = vsrc[d];
+        if (regs_rope) {
+            float v[DS];
+#pragma unroll
+            for (int i = 0; i < DS; i++) v[i] = bf2f(src[lane + 32 * i]);
+            norm_rope_regs<DS>(v, isk ? nwk : nwq, isk ? a.kn != nullptr : a.qn != nullptr, a.eps, rc, rs, D);
+            if (isk) {
+                const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
+#pragma unroll
+                for (int i = 0; i < DS; i++) {
+                    newk[lane + 32 * i] = f2bf(v[i]);
+                    newv[lane + 32 * i] = vsrc[lane + 32 * i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < DS; i++) qs[(lane + 32 * i) * REP + h] = __fmul_rn(scale, v[i]);
             }
         } else {
-            for (int d = lane; d < D; d += 32) qs[h * D + d] = __fmul_rn(scale, stage[d]);
+            for (int d = lane; d < D; d += 32) stage[d] = bf2f(src[d]);
+            __syncwarp();
+            head_norm_rope(stage, D, isk ? a.kn : a.qn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
+            if (isk) {
+                const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
+                for (int d = lane; d < D; d += 32) {
+                    newk[d] = f2bf(stage[d]);
+                    newv[d] = vsrc[d];
+                }
+            } else {
+                for (int d = lane; d < D; d += 32) qs[d * REP + h] = __fmul_rn(scale, stage[d]);
+            }
+            __syncwarp();
         }
-        __syncwarp();
     }
-    __syncthreads();
 
-    // phase 1: scores of (position p, heads hs, hs + HS, ...)
-    const int pp = tid & (AB - 1), hs = tid / AB;
-    float lmax[(REP + HS - 1) / HS];
+    // phase 1: thread (position pp, block slot s1) scores all REP heads of
+    // blocks s1, s1 + DA_BS1, ... (one fmaf chain over d per head)
+    const int pp = tid % AB, s1 = tid / AB;
+    float lmax[REP];
 #pragma unroll
-    for (int u = 0; u < (REP + HS - 1) / HS; u++) lmax[u] = -INFINITY;
-    for (int i = 0; i < nbm; i++) {
-        cp_async_wait<DA_RING - 1>();
-        __syncthreads();
-        const int b = mb0 + i;
-        unsigned char *blk = ring + (size_t)(i % DA_RING) * AB * D * 2;
-        if (has_new && b == blast) {
-            const int r = pos - b * AB;
+    for (int h = 0; h < REP; h++) lmax[h] = -INFINITY;
+    for (int r0 = 0; r0 < nbm; r0 += DA_BS1) {
+        if (r0 == 0) cp_async_wait<1>();   // the first K round (V may still be in flight)
+        else if (!RES) cp_async_wait<0>();  // the K round requested after the previous one
+        __syncthreads();   // (first round: also orders the q and new-k stores)
+        if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + DA_BS1) {
+            unsigned char *blk = ring + (size_t)kslot(blast - mb0) * AB * D * 2;
+            const int r = pos - blast * AB;
             for (int c = tid; c < NCH; c += DA_THREADS)
                 *reinterpret_cast<uint4 *>(blk + blk_off<D>(r, c)) = *reinterpret_cast<const uint4 *>(newk + c * 8);
             __syncthreads();
         }
-        const int j = b * AB + pp;
-        const bool valid = j >= lo && j <= pos;
+        const int i = r0 + s1;
+        if (i < nbm) {
+            const unsigned char *blk = ring + (size_t)kslot(i) * AB * D * 2;
+            float acc[REP];
 #pragma unroll
-        for (int u = 0; u < (REP + HS - 1) / HS; u++) {
-            const int h = hs + u * HS;
-            if (h < REP) {
-                const float *q = qs + h * D;
-                float acc = 0.f;
-#pragma unroll 4
-                for (int c = 0; c < NCH; c++) {
-                    const uint4 kv = *reinterpret_cast<const uint4 *>(blk + blk_off<D>(pp, c));
-                    const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-                    const float4 q0 = *reinterpret_cast<const float4 *>(q + c * 8);
-                    const float4 q1 = *reinterpret_cast<const float4 *>(q + c * 8 + 4);
-                    acc = __fmaf_rn(q0.x, lo_bf(kw[0]), acc);
-                    acc = __fmaf_rn(q0.y, hi_bf(kw[0]), acc);
-                    acc = __fmaf_rn(q0.z, lo_bf(kw[1]), acc);
-                    acc = __fmaf_rn(q0.w, hi_bf(kw[1]), acc);
-                    acc = __fmaf_rn(q1.x, lo_bf(kw[2]), acc);
-                    acc = __fmaf_rn(q1.y, hi_bf(kw[2]), acc);
-                    acc = __fmaf_rn(q1.z, lo_bf(kw[3]), acc);
-                    acc = __fmaf_rn(q1.w, hi_bf(kw[3]), acc);
+            for (int h = 0; h < REP; h++) acc[h] = 0.f;
+#pragma unroll 2
+            for (int c = 0; c < NCH; c++) {
+                const uint4 kv = *reinterpret_cast<const uint4 *>(blk + blk_off<D>(pp, c));
+                const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float kf = (e & 1) ? hi_bf(kw[e >> 1]) : lo_bf(kw[e >> 1]);
+                    float q[REP];
+                    lds_rep<REP>(q, qs + (c * 8 + e) * REP);
+#pragma unroll
+                    for (int h = 0; h < REP; h++) acc[h] = __fmaf_rn(q[h], kf, acc[h]);
                 }
-                const float z = valid ? acc : -INFINITY;
-                sc[h * scap + i * AB + pp] = z;
-                lmax[u] = fmaxf(lmax[u], z);
+            }
+            const int j = (mb0 + i) * AB + pp;
+            const bool valid = j >= lo && j <= pos;
+#pragma unroll
+            for (int h = 0; h < REP; h++) {
+                const float z = valid ? acc[h] : -INFINITY;
+                sc[(i * AB + pp) * REP + h] = z;
+                lmax[h] = fmaxf(lmax[h], z);
             }
         }
-        __syncthreads();
-        issue(i + DA_RING);
+        if (!RES && r0 + DA_BS1 < nbm) {
+            __syncthreads();
+            for (int s = 0; s < DA_BS1; s++) load_block(r0 + DA_BS1 + s, false, kslot(r0 + DA_BS1 + s));
+            cp_async_commit();
+        }
     }
-    // per-head maxima of the CTA, then of the cluster
+    // per-head maxima of the CTA, pushed into every CTA's inbox
 #pragma unroll
-    for (int u = 0; u < (REP + HS - 1) / HS; u++) {
-        float v = lmax[u];
-        v = warp_max(v);
-        // the AB threads of a head slot are warps 2hs, 2hs + 1
-        if (lane == 0) P[(hs + u * HS) * 2 + (warp & 1)] = v;   // P as scratch (REP*AB floats >= 2*REP)
+    for (int h = 0; h < REP; h++) {
+        const float v = warp_max(lmax[h]);
+        if (lane == 0) red[warp * REP + h] = v;
     }
     __syncthreads();
-    if (tid < REP) hmax[tid] = fmaxf(P[tid * 2], P[tid * 2 + 1]);
+    if (tid < CL * REP) {
+        const int dst = tid / REP, h = tid % REP;
+        float m = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; w++) m = fmaxf(m, red[w * REP + h]);
+        *cluster.map_shared_rank(inmax + rank * REP + h, dst) = m;
+    }
     cluster.sync();
     if (tid < REP) {
         float m = -INFINITY;
-        for (int r = 0; r < CL; r++) m = fmaxf(m, *cluster.map_shared_rank(hmax + tid, r));
+#pragma unroll
+        for (int r = 0; r < CL; r++) m = fmaxf(m, inmax[r * REP + tid]);
         gmax[tid] = m;
     }
-    __syncthreads();
 
-    // phase 2: p and the block chains; thread = (feature pair dp, heads
-    // hh, hh + HS2, ...)
-    const int dp = tid % NP, hh = tid / NP;
-    constexpr int NU2 = (REP + HS2 - 1) / HS2;
-    double Oacc[NU2][2], Lacc[NU2];
+    // phase 2: per round of BS2 blocks, p of the round's blocks (thread =
+    // position), then thread (feature pair dp, block slot s2) runs the
+    // 2 * REP chains of block s2 (v pair unpacked once for all heads) and
+    // l for all heads (dp == 0), added into f64 partials of its slot
+    const int dp = tid % NP, s2 = tid / NP;
+    double Oa[REP][2], La[REP];
 #pragma unroll
-    for (int u = 0; u < NU2; u++) Oacc[u][0] = Oacc[u][1] = Lacc[u] = 0.0;
-    for (int i = 0; i < nbm; i++) {
-        cp_async_wait<DA_RING - 1>();
-        __syncthreads();
-        const int b = mb0 + i;
-        unsigned char *blk = ring + (size_t)((nbm + i) % DA_RING) * AB * D * 2;
-        if (has_new && b == blast) {
-            const int r = pos - b * AB;
+    for (int h = 0; h < REP; h++) Oa[h][0] = Oa[h][1] = La[h] = 0.0;
+    if (RES) cp_async_wait<0>();
+    for (int r0 = 0; r0 < nbm; r0 += BS2) {
+        if (!RES) cp_async_wait<0>();
+        __syncthreads();   // (first round: also orders gmax and the V rows)
+        if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + BS2) {
+            unsigned char *blk = ring + (size_t)vslot(blast - mb0) * AB * D * 2;
+            const int r = pos - blast * AB;
             for (int c = tid; c < NCH; c += DA_THREADS)
                 *reinterpret_cast<uint4 *>(blk + blk_off<D>(r, c)) = *reinterpret_cast<const uint4 *>(newv + c * 8);
         }
+        for (int e = tid; e < BS2 * AB; e += DA_THREADS) {
+            const int s = e / AB, q = e % AB, i = r0 + s;
 #pragma unroll
-        for (int u = 0; u < (REP + HS - 1) / HS; u++) {
-            const int h = hs + u * HS;
-            if (h < REP) {
-                const float z = sc[h * scap + i * AB + pp];
-                P[h * AB + pp] = z == -INFINITY ? 0.f : own_expf(__fsub_rn(z, gmax[h]));
+            for (int h = 0; h < REP; h++) {
+                const float z = i < nbm ? sc[(i * AB + q) * REP + h] : -INFINITY;
+                P[(s * AB + q) * REP + h] = z == -INFINITY ? 0.f : own_expf(__fsub_rn(z, gmax[h]));
             }
         }
         __syncthreads();
+        const int i = r0 + s2;
+        if (i < nbm) {
+            const unsigned char *blk = ring + (size_t)vslot(i) * AB * D * 2;
+            const float *ps = P + (size_t)s2 * AB * REP;
+            const int c = dp >> 2, off = (dp & 3) * 4;
+            // l of head lh (threads dp < REP; the others' chain is unused)
+            const int lh = dp < REP ? dp : 0;
+            float o0[REP], o1[REP], l = 0.f;
 #pragma unroll
-        for (int u = 0; u < NU2; u++) {
-            const int h = hh + u * HS2;
-            if (h < REP) {
-                const float *ph = P + h * AB;
-                float o0 = 0.f, o1 = 0.f, l = 0.f;
-                const int c = dp >> 2, off = (dp & 3) * 4;
-#pragma unroll 8
-                for (int r = 0; r < AB; r++) {
-                    const float pv = ph[r];
-                    const uint32_t v2 = *reinterpret_cast<const uint32_t *>(blk + blk_off<D>(r, c) + off);
-                    o0 = __fmaf_rn(pv, lo_bf(v2), o0);
-                    o1 = __fmaf_rn(pv, hi_bf(v2), o1);
-                    l = __fadd_rn(l, pv);
+            for (int h = 0; h < REP; h++) o0[h] = o1[h] = 0.f;
+#pragma unroll 4
+            for (int q = 0; q < AB; q++) {
+                float pv[REP];
+                lds_rep<REP>(pv, ps + q * REP);
+                const uint32_t v2 = *reinterpret_cast<const uint32_t *>(blk + blk_off<D>(q, c) + off);
+                const float va = lo_bf(v2), vb = hi_bf(v2);
+#pragma unroll
+                for (int h = 0; h < REP; h++) {
+                    o0[h] = __fmaf_rn(pv[h], va, o0[h]);
+                    o1[h] = __fmaf_rn(pv[h], vb, o1[h]);
                 }
-                Oacc[u][0] += (double)o0;
-                Oacc[u][1] += (double)o1;
-                Lacc[u] += (double)l;
+                l = __fadd_rn(l, ps[q * REP + lh]);
             }
+#pragma unroll
+            for (int h = 0; h < REP; h++) {
+                Oa[h][0] += (double)o0[h];
+                Oa[h][1] += (double)o1[h];
+            }
+            if (dp < REP) La[dp] += (double)l;
         }
-        __syncthreads();
-        issue(nbm + i + DA_RING);
+        if (!RES && r0 + BS2 < nbm) {
+            __syncthreads();
+            for (int s = 0; s < BS2; s++) load_block(r0 + BS2 + s, true, vslot(r0 + BS2 + s));
+            cp_async_commit();
+        }
     }
     cp_async_wait<0>();
+    // the slot partials into the inbox of the CTA owning each output slice
 #pragma unroll
-    for (int u = 0; u < NU2; u++) {
-        const int h = hh + u * HS2;
-        if (h < REP) {
-            O[h * D + 2 * dp] = Oacc[u][0];
-            O[h * D + 2 * dp + 1] = Oacc[u][1];
-            if (dp == 0) Ls[h] = Lacc[u];
-        }
+    for (int h = 0; h < REP; h++) {
+        const int e = h * D + 2 * dp, dst = e / ES;
+        *reinterpret_cast<double2 *>(cluster.map_shared_rank(inO + ((size_t)rank * BS2 + s2) * ES + (e - dst * ES), dst)) =
+            make_double2(Oa[h][0], Oa[h][1]);
     }
+    if (dp < REP)
+        for (int r = 0; r < CL; r++) *cluster.map_shared_rank(inL + ((size_t)rank * BS2 + s2) * REP + dp, r) = La[dp];
     cluster.sync();
-    // merge the r-th slice of the REP*D outputs over the cluster
-    constexpr int E = REP * D;
-    const int e0 = (int)((long long)E * rank / CL), e1 = (int)((long long)E * (rank + 1) / CL);
-    for (int e = e0 + tid; e < e1; e += DA_THREADS) {
-        const int h = e / D, d = e % D;
+    for (int el = tid; el < ES; el += DA_THREADS) {
+        const int e = rank * ES + el, h = e / D, d = e % D;
         double os = 0.0, ls = 0.0;
-        for (int r = 0; r < CL; r++) {
-            os += *cluster.map_shared_rank(O + e, r);
-            ls += *cluster.map_shared_rank(Ls + h, r);
+        for (int r = 0; r < CL * BS2; r++) {
+            os += inO[(size_t)r * ES + el];
+            ls += inL[(size_t)r * REP + h];
         }
         const int hg = kh * REP + h;
         uint16_t val = d2bf(os / ls);
@@ -311,7 +439,6 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
             vd[d] = newv[d];
         }
     }
-    cluster.sync();
 }
 
 // blocks one CTA may hold for a cache of `cap` slots (window: at most
@@ -326,38 +453,44 @@ static int da_scap(const AttnDecodeArgs &a, int CL) {
 // attention CTAs on one SM the projections that follow ran slower on those
 // SMs for the rest of the step.
 template <int D, int REP>
-static size_t da_smem(int scap) {
-    const size_t t = da_layout(D, REP, scap).total;
+static size_t da_smem(int scap, int CL, bool res) {
+    const size_t t = da_layout(D, REP, scap, CL, res ? 2 * (scap / AB) : 2 * DA_BS1).total;
     return t > 116 * 1024 ? t : 116 * 1024;
 }
+// every block resident when it fits in a CTA's shared memory
+template <int D, int REP>
+static bool da_resident(int scap, int CL) {
+    return da_layout(D, REP, scap, CL, 2 * (scap / AB)).total <= 220 * 1024;
+}
 
-template <int D, int REP, int CL>
-static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
-    auto kern = attn_decode_kernel<D, REP, CL>;
-    const int scap = da_scap(a, CL);
-    const size_t smem = da_smem<D, REP>(scap);
-    if (smem > 227 * 1024) {
-        set_error("decode attention: a cache of %d slots needs %zu bytes of shared memory per CTA", a.cap, smem);
-        return -1;
-    }
-    if (!smem_allowed((const void *)kern, smem)) return -1;
-    static std::mutex mu;
-    static bool np[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
+template <int D, int REP, int CL, bool RES>
+static bool da_prepare(const AttnDecodeArgs &a, size_t smem) {
+    auto kern = attn_decode_kernel<D, REP, CL, RES>;
+    if (!smem_allowed((const void *)kern, smem)) return false;
     if (CL > 8) {
+        static std::mutex mu;
+        static bool np[64] = {};   // per instantiation and device
+        int dev = 0;
+        cudaGetDevice(&dev);
         std::lock_guard<std::mutex> lock(mu);
         if (dev >= 0 && dev < 64 && !np[dev]) {
-            MLXD_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+            if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                         "cluster attribute"))
+                return false;
             np[dev] = true;
         }
     }
+    return true;
+}
+
+template <int D, int REP, int CL>
+static cudaLaunchConfig_t da_config(const AttnDecodeArgs &a, size_t smem, cudaLaunchAttribute *attr, bool pdl,
+                                    cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(CL, a.hkv);
     cfg.blockDim = dim3(DA_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = CL;
     attr[0].val.clusterDim.y = 1;
@@ -366,37 +499,108 @@ static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a, scap));
+    return cfg;
+}
+
+// whether `hkv` clusters of CL CTAs are resident at once on this device
+template <int D, int REP, int CL>
+static bool da_fits(const AttnDecodeArgs &a) {
+    const int scap = da_scap(a, CL);
+    const bool res = da_resident<D, REP>(scap, CL);
+    const size_t smem = da_smem<D, REP>(scap, CL, res);
+    if (smem > 227 * 1024 || !(res ? da_prepare<D, REP, CL, true>(a, smem) : da_prepare<D, REP, CL, false>(a, smem))) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = da_config<D, REP, CL>(a, smem, attr, false, nullptr);
+    int n = 0;
+    cudaError_t e = res ? cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<D, REP, CL, true>, &cfg)
+                        : cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<D, REP, CL, false>, &cfg);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return n >= a.hkv;
+}
+
+// cluster size per (device, kv heads, cache span): 16 when hkv clusters of
+// 16 are resident at once, else 8
+template <int D, int REP>
+static int da_cluster(const AttnDecodeArgs &a) {
+    static std::mutex mu;
+    static std::vector<std::pair<std::pair<int, long long>, int>> memo;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const long long key = ((long long)a.hkv << 32) | (unsigned)da_scap(a, 8);
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto &m : memo)
+        if (m.first.first == dev && m.first.second == key) return m.second;
+    const int cl = da_fits<D, REP, 16>(a) ? 16 : 8;
+    memo.push_back({{dev, key}, cl});
+    return cl;
+}
+
+template <int D, int REP, int CL>
+static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+    const int scap = da_scap(a, CL);
+    const bool res = da_resident<D, REP>(scap, CL);
+    const size_t smem = da_smem<D, REP>(scap, CL, res);
+    if (smem > 227 * 1024) {
+        set_error("decode attention: a cache of %d slots needs %zu bytes of shared memory per CTA", a.cap, smem);
+        return -1;
+    }
+    if (!(res ? da_prepare<D, REP, CL, true>(a, smem) : da_prepare<D, REP, CL, false>(a, smem))) return -1;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = da_config<D, REP, CL>(a, smem, attr, pdl, st);
+    if (res) MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, REP, CL, true>, a, scap));
+    else MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, REP, CL, false>, a, scap));
     return 0;
 }
 
-// clusters of 16 CTAs when the device holds hkv of them at once, else 8
-static int da_cluster(int hkv) { return 16 * hkv <= num_sms() ? 16 : 8; }
-
 template <int D, int REP>
 static int da_dispatch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
-    return da_cluster(a.hkv) == 16 ? da_launch<D, REP, 16>(a, st, pdl) : da_launch<D, REP, 8>(a, st, pdl);
+    return da_cluster<D, REP>(a) == 16 ? da_launch<D, REP, 16>(a, st, pdl) : da_launch<D, REP, 8>(a, st, pdl);
+}
+
+template <int D, int REP>
+static int da_sms(const AttnDecodeArgs &a) {
+    return da_cluster<D, REP>(a) * a.hkv;
 }
 
 bool attention_decode_supported(int D, int rep, int rope_dims) {
     return (D == 64 || D == 128) && (rep == 1 || rep == 2 || rep == 4 || rep == 8) && rope_dims <= D;
 }
 
+#define MLXD_DA_DISPATCH(FN, ...)                                                       \
+    switch (D * 16 + rep) {                                                             \
+    case 128 * 16 + 1: return FN<128, 1>(__VA_ARGS__);                                  \
+    case 128 * 16 + 2: return FN<128, 2>(__VA_ARGS__);                                  \
+    case 128 * 16 + 4: return FN<128, 4>(__VA_ARGS__);                                  \
+    case 128 * 16 + 8: return FN<128, 8>(__VA_ARGS__);                                  \
+    case 64 * 16 + 1: return FN<64, 1>(__VA_ARGS__);                                    \
+    case 64 * 16 + 2: return FN<64, 2>(__VA_ARGS__);                                    \
+    case 64 * 16 + 4: return FN<64, 4>(__VA_ARGS__);                                    \
+    case 64 * 16 + 8: return FN<64, 8>(__VA_ARGS__);                                    \
+    }
+
 int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
     const int D = a.rope.D, rep = a.hq / a.hkv;
-    if (!attention_decode_supported(D, rep, a.rope.rope_dims) || a.hkv * 8 > num_sms() * 8) {
+    if (!attention_decode_supported(D, rep, a.rope.rope_dims)) {
         set_error("decode attention: head dim %d with %d query heads per kv head not supported", D, rep);
         return -1;
     }
-#define MLXD_DA(DD, R) \
-    if (D == DD && rep == R) return da_dispatch<DD, R>(a, st, pdl);
-    MLXD_DA(128, 1) MLXD_DA(128, 2) MLXD_DA(128, 4) MLXD_DA(128, 8)
-    MLXD_DA(64, 1) MLXD_DA(64, 2) MLXD_DA(64, 4) MLXD_DA(64, 8)
-#undef MLXD_DA
+    MLXD_DA_DISPATCH(da_dispatch, a, st, pdl)
     return -1;
 }
 
-int attention_decode_sms(const AttnDecodeArgs &a) { return da_cluster(a.hkv) * a.hkv; }
+int attention_decode_sms(const AttnDecodeArgs &a) {
+    const int D = a.rope.D, rep = a.hq / a.hkv;
+    if (!attention_decode_supported(D, rep, a.rope.rope_dims)) return 0;
+    MLXD_DA_DISPATCH(da_sms, a)
+    return 0;
+}
+#undef MLXD_DA_DISPATCH
 
 int attention_timeouts() {
     int v = 0, z = 0;
