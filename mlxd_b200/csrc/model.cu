@@ -306,7 +306,7 @@ int reduce_partials(mlxd_model *m, double *part, size_t n, uint16_t *h_out, cons
 size_t proj_ws_bytes(const mlxd_model *m, int S) {
     size_t b = 0;
     auto need = [&](const QMat &W) {
-        size_t x = generic_ws_bytes(W, S, PRO_PLAIN);
+        size_t x = qgemm_tc_eligible(W, S, EPI_STORE) ? qgemm_tc_ws_bytes(S, W.cols) : generic_ws_bytes(W, S, PRO_PLAIN);
         if (x > b) b = x;
     };
     for (auto &L : m->L) {
@@ -372,6 +372,7 @@ int linear_any(mlxd_model *m, const QMat &W, const uint16_t *x, int S, int epi, 
         a.gws_bytes = m->gws_bytes;
         return qgemv(W, PRO_PLAIN, epi, a, st, false);
     }
+    if (qgemm_tc_eligible(W, S, epi)) return qgemm_tc(W, x, S, epi, res, y, yf, m->p_ws, m->p_ws_bytes, st);
     return qgemm_generic(W, PRO_PLAIN, epi, a, S, m->p_ws, m->p_ws_bytes, st);
 }
 
@@ -1012,7 +1013,8 @@ int mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *
         a.gws_bytes = ml->ws_bytes;
         return qgemv(ml->W, PRO_PLAIN, EPI_STORE, a, (cudaStream_t)stream, false);
     }
-    const size_t need = generic_ws_bytes(ml->W, S, PRO_PLAIN);
+    const bool tc = qgemm_tc_eligible(ml->W, S, EPI_STORE);
+    const size_t need = tc ? qgemm_tc_ws_bytes(S, ml->W.cols) : generic_ws_bytes(ml->W, S, PRO_PLAIN);
     if (need > ml->ws_bytes) {
         MLXD_CHECK(cudaStreamSynchronize((cudaStream_t)stream));
         dev_free(ml->ws);
@@ -1020,6 +1022,8 @@ int mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void *
         ml->ws_bytes = ml->ws ? need : 0;
         if (!ml->ws) return -1;
     }
+    if (tc)
+        return qgemm_tc(ml->W, a.x, S, EPI_STORE, nullptr, a.y, nullptr, ml->ws, ml->ws_bytes, (cudaStream_t)stream);
     return qgemm_generic(ml->W, PRO_PLAIN, EPI_STORE, a, S, ml->ws, ml->ws_bytes, (cudaStream_t)stream);
 }
 
@@ -1297,6 +1301,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     if (!cuda_ok(cudaStreamSynchronize(st), "generate")) rc = -1;
     if (!rc && attention_timeouts()) {
         set_error("decode attention: a launch was sized for fewer positions than it met");
+        rc = -1;
+    }
+    if (!rc && qgemm_tc_timeouts()) {
+        set_error("prefill GEMM gave up waiting on its pipeline");
         rc = -1;
     }
     if (timing) {
