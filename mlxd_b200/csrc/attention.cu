@@ -676,22 +676,36 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
         qp[a] = pos0 + qt0 + 4 * tq + a;
         j0r[a] = window > 0 ? max(0, qp[a] - window + 1) : 0;
     }
+    // the rows of a key or value block, 16 B per (row r, chunk c), thread
+    // share e = tid + 256 x, c = e / 64, r = e % 64: requested one block
+    // ahead into registers
+    constexpr int NPF = AB * D / 8 / PF_T;   // 16-byte pieces per thread (4 for D = 128)
+    auto fetch_rows = [&](const uint16_t *base, int b, uint4 (&buf)[NPF]) {
+#pragma unroll
+        for (int x = 0; x < NPF; x++) {
+            const int e = tid + PF_T * x, c = e / AB, r = e % AB;
+            const int j = b * AB + r;
+            buf[x] = j < jhi ? *reinterpret_cast<const uint4 *>(base + (size_t)(j % cap) * D + c * 8)
+                             : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    uint4 kpre[NPF];
+    fetch_rows(K, b0, kpre);
     for (int bi = 0; bi < nb; bi++) {
         const int b = b0 + bi;
         __syncthreads();
         // k block transposed to f32: kT[d][r]
-        for (int e = tid; e < AB * D / 8; e += PF_T) {
-            const int c = e / AB, r = e % AB;
-            const int j = b * AB + r;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (j < jhi) v = *reinterpret_cast<const uint4 *>(K + (size_t)(j % cap) * D + c * 8);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int x = 0; x < 4; x++) {
-                kT[(c * 8 + 2 * x) * AB + r] = lo_bf(w[x]);
-                kT[(c * 8 + 2 * x + 1) * AB + r] = hi_bf(w[x]);
+        for (int x = 0; x < NPF; x++) {
+            const int e = tid + PF_T * x, c = e / AB, r = e % AB;
+            const uint32_t w[4] = {kpre[x].x, kpre[x].y, kpre[x].z, kpre[x].w};
+#pragma unroll
+            for (int y = 0; y < 4; y++) {
+                kT[(c * 8 + 2 * y) * AB + r] = lo_bf(w[y]);
+                kT[(c * 8 + 2 * y + 1) * AB + r] = hi_bf(w[y]);
             }
         }
+        if (bi + 1 < nb) fetch_rows(K, b + 1, kpre);
         __syncthreads();
         float acc[4][4] = {};
 #pragma unroll 4
@@ -740,21 +754,40 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
 #pragma unroll
         for (int y = 0; y < 8; y++) O[x][y] = 0.0;
     }
+    // scores of a block (16 per thread: 4 float4 of key r, queries 4i4..)
+    // and its value rows, requested one block ahead into registers
+    float4 zpre[4];
+    uint4 vpre[NPF];
+    auto fetch_scores = [&](int bi) {
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            const int e = tid + PF_T * x, r = e / (PF_Q / 4), i4 = e % (PF_Q / 4);
+            zpre[x] = __ldcg(reinterpret_cast<const float4 *>(myscr + (size_t)(bi * AB + r) * PF_Q) + i4);
+        }
+    };
+    fetch_scores(0);
+    fetch_rows(V, b0, vpre);
     for (int bi = 0; bi < nb; bi++) {
-        const int b = b0 + bi;
         __syncthreads();
         // p tile (transposed: pT[key][query]) and the v block
-        for (int e = tid; e < PF_Q * AB; e += PF_T) {
-            const int r = e / PF_Q, i = e % PF_Q;
-            const float z = __ldcg(myscr + (size_t)(bi * AB + r) * PF_Q + i);
-            pT[r * PF_Q + i] = z == -INFINITY ? 0.f : own_expf(__fsub_rn(z, smx[i]));
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            const int e = tid + PF_T * x, r = e / (PF_Q / 4), i4 = e % (PF_Q / 4);
+            const float z[4] = {zpre[x].x, zpre[x].y, zpre[x].z, zpre[x].w};
+            float4 pv;
+            float *pp = &pv.x;
+#pragma unroll
+            for (int k = 0; k < 4; k++) pp[k] = z[k] == -INFINITY ? 0.f : own_expf(__fsub_rn(z[k], smx[4 * i4 + k]));
+            *reinterpret_cast<float4 *>(pT + r * PF_Q + 4 * i4) = pv;
         }
-        for (int e = tid; e < AB * D / 8; e += PF_T) {
-            const int r = e / (D / 8), c = e % (D / 8);
-            const int j = b * AB + r;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (j < jhi) v = *reinterpret_cast<const uint4 *>(V + (size_t)(j % cap) * D + c * 8);
-            *reinterpret_cast<uint4 *>(vb + r * D + c * 8) = v;
+#pragma unroll
+        for (int x = 0; x < NPF; x++) {
+            const int e = tid + PF_T * x, c = e / AB, r = e % AB;
+            *reinterpret_cast<uint4 *>(vb + r * D + c * 8) = vpre[x];
+        }
+        if (bi + 1 < nb) {
+            fetch_scores(bi + 1);
+            fetch_rows(V, b0 + bi + 1, vpre);
         }
         __syncthreads();
         float o[QPT][8] = {}, l[QPT] = {};

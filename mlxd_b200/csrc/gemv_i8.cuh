@@ -37,7 +37,7 @@ struct GTab {
 // (2^52 + 2^31 + v) * 2^k minus (2^52 + 2^31) * 2^k (both exact, Sterbenz).
 // k in [-1000, 1000].
 MLXD_DEV double int_times_pow2(int v, int k) {
-    const int hi = 0x43300000 + (k << 20);
+    const int hi = 0x43300000 + k * (1 << 20);
     return __hiloint2double(hi, v ^ (int)0x80000000) - __hiloint2double(hi, (int)0x80000000);
 }
 

@@ -37,7 +37,7 @@
 namespace mlxd {
 
 constexpr int XG_BM = 128, XG_TOK = 64, XG_BN = 3 * XG_TOK, XG_BK = 128, XG_NS = 3;
-constexpr int XG_THREADS = 384;
+constexpr int XG_THREADS = 640;   // 4 warps (TMA, 2 producers, MMA) + 16 epilogue warps
 constexpr int XG_ABYTES = XG_BM * XG_BK;             // 16 KB of u8 weights
 constexpr int XG_BBYTES = XG_BN * XG_BK;             // 24 KB of digits
 constexpr int XG_TBYTES = 2 * XG_TOK * 16;           // 2 KB of table entries
@@ -46,6 +46,14 @@ constexpr int XG_STAGE = XG_ABYTES + XG_BBYTES + XG_TBYTES + XG_SBYTES;
 constexpr size_t XG_SMEM = 1024 + (size_t)XG_NS * XG_STAGE + 256 + (size_t)XG_BM * XG_TOK / 2 * 8;
 
 static __device__ int g_xgemm_err;
+
+// per (group, token) entry of the GEMM's input table: tf = T_g * 2^(E_g - 20)
+// (NaN for a non-finite group) and E_g
+struct XTab {
+    double tf;
+    int e;
+    int pad;
+};
 
 // K-major operand with 128-byte rows in the 128B swizzle: 8-row atoms of
 // 1024 B (stride byte offset), leading offset unused (1), descriptor version 1
@@ -92,7 +100,7 @@ MLXD_DEV uint2 widen_nibbles(uint32_t w) {
 // Inputs in per-group fixed point for the GEMM: one warp per (token, group);
 // xd [S_pad][3][cols] int8 digits (rows past S are zero), tab [ng][S_pad]
 __global__ void xq_kernel(const uint16_t *__restrict__ x, int S, int S_pad, int cols, int8_t *__restrict__ xd,
-                          GTab *__restrict__ tab) {
+                          XTab *__restrict__ tab) {
     const int ng = cols / 64;
     const int wg = (int)(((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
@@ -128,7 +136,7 @@ __global__ void xq_kernel(const uint16_t *__restrict__ x, int S, int S_pad, int 
         *reinterpret_cast<uint16_t *>(xd + ((size_t)s * 3 + d) * cols + (size_t)g * 64 + 2 * lane) = (uint16_t)b2;
     }
     if (lane == 0) {
-        GTab e;
+        XTab e;
         e.tf = bad ? __longlong_as_double(0x7ff8000000000000ll) : int_times_pow2(tsum, E - 20);
         e.e = E;
         e.pad = 0;
@@ -139,14 +147,14 @@ __global__ void xq_kernel(const uint16_t *__restrict__ x, int S, int S_pad, int 
 template <int EPI>
 __global__ void __launch_bounds__(XG_THREADS, 1)
     qgemm_x_kernel(const __grid_constant__ CUtensorMap tmd, const uint32_t *__restrict__ w, const uint16_t *__restrict__ sg,
-                   const uint16_t *__restrict__ bg, const GTab *__restrict__ tab, int rows, int cols, int S, int S_pad,
+                   const uint16_t *__restrict__ bg, const XTab *__restrict__ tab, int rows, int cols, int S, int S_pad,
                    uint16_t *__restrict__ y, const uint16_t *__restrict__ residual, double *__restrict__ yf) {
     extern __shared__ __align__(1024) unsigned char xsm_raw[];
     unsigned char *xsm = reinterpret_cast<unsigned char *>(((uintptr_t)xsm_raw + 1023) & ~(uintptr_t)1023);
     // stage s: [A 16 KB][B 24 KB][tables 2 KB][scale/bias 1 KB]
     auto stA = [&](int s) { return xsm + (size_t)s * XG_STAGE; };
     auto stB = [&](int s) { return xsm + (size_t)s * XG_STAGE + XG_ABYTES; };
-    auto stT = [&](int s) { return reinterpret_cast<GTab *>(xsm + (size_t)s * XG_STAGE + XG_ABYTES + XG_BBYTES); };
+    auto stT = [&](int s) { return reinterpret_cast<XTab *>(xsm + (size_t)s * XG_STAGE + XG_ABYTES + XG_BBYTES); };
     auto stS = [&](int s) {
         return reinterpret_cast<uint32_t *>(xsm + (size_t)s * XG_STAGE + XG_ABYTES + XG_BBYTES + XG_TBYTES);
     };
@@ -164,11 +172,11 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < XG_NS; s++) {
             mbar_init(&full[s], 1 + 64);
-            mbar_init(&empty[s], 1 + 8);   // the MMAs done and the 8 epilogue warps' reads of the stage
+            mbar_init(&empty[s], 1 + 16);   // the MMAs done and the 16 epilogue warps' reads of the stage
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], 8);
+            mbar_init(&acce[b], 16);
         }
         s_fail = 0;
         fence_mbar_init();
@@ -202,29 +210,32 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
             }
         }
     } else if (warp == 1 || warp == 2) {
-        // thread i of 64: rows i and i + 64 of the tile
+        // thread i of 64: rows i and i + 64 of the tile; the global loads of
+        // stage kb + 2 are issued while stage kb is written (two register sets)
         const int i = tid - 32;
-        bool failed = false;
-        for (int kb = 0; kb < nkb && !failed; kb++) {
-            const int s = kb % XG_NS, u = kb / XG_NS;
-            uint4 wv[2][4];
-            uint32_t sb[2][2];
+        uint4 wv0[2][4], wv1[2][4];
+        uint32_t sb0[2][2], sb1[2][2];
+        auto fetch = [&](int kb, uint4 (&wv)[2][4], uint32_t (&sb)[2][2]) {
+            if (kb >= nkb) return;
 #pragma unroll
             for (int rr = 0; rr < 2; rr++) {
                 const int r = row0 + i + 64 * rr;
                 const uint4 *src = reinterpret_cast<const uint4 *>(w + (size_t)r * (cols / 8) + (size_t)kb * 16);
 #pragma unroll
                 for (int q = 0; q < 4; q++) wv[rr][q] = ldg_nc_v4(src + q);
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const size_t gi = (size_t)r * ng + 2 * kb + h;
-                    sb[rr][h] = (uint32_t)sg[gi] | ((uint32_t)bg[gi] << 16);
-                }
+                const size_t gi = (size_t)r * ng + 2 * kb;
+                const uint32_t s2 = *reinterpret_cast<const uint32_t *>(sg + gi);   // groups 2kb, 2kb+1
+                const uint32_t b2 = *reinterpret_cast<const uint32_t *>(bg + gi);
+                sb[rr][0] = (s2 & 0xffffu) | (b2 << 16);
+                sb[rr][1] = (s2 >> 16) | (b2 & 0xffff0000u);
             }
+        };
+        // stage kb from one register set, then that set refilled with kb + 2
+        auto put = [&](int kb, uint4 (&wv)[2][4], uint32_t (&sb)[2][2]) -> bool {
+            const int s = kb % XG_NS, u = kb / XG_NS;
             if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1)) {
                 s_fail = 1;
-                failed = true;
-                break;
+                return false;
             }
             unsigned char *A = stA(s);
 #pragma unroll
@@ -245,6 +256,14 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
             }
             fence_proxy_async();
             mbar_arrive(&full[s]);
+            fetch(kb + 2, wv, sb);
+            return true;
+        };
+        fetch(0, wv0, sb0);
+        fetch(1, wv1, sb1);
+        for (int kb = 0; kb < nkb; kb += 2) {
+            if (!put(kb, wv0, sb0)) break;
+            if (kb + 1 < nkb && !put(kb + 1, wv1, sb1)) break;
         }
     } else if (warp == 3) {
         if (lane == 0) {
@@ -281,12 +300,12 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
             }
         }
     } else {
-        // epilogue warps 4-11: rows 32 (warp % 4) .. + 31, tokens 32 wg .. + 31
-        const int q = warp & 3, wg = (warp - 4) >> 2;
+        // epilogue warps 4-19: rows 32 (warp % 4) .. + 31, tokens 16 tq .. + 15
+        const int q = warp & 3, tq = (warp - 4) >> 2;
         const int trow = q * 32 + lane;
-        double acc[32];
+        double acc[16];
 #pragma unroll
-        for (int t = 0; t < 32; t++) acc[t] = 0.0;
+        for (int t = 0; t < 16; t++) acc[t] = 0.0;
         bool ok = true;
         for (int g = 0; g < ng; g++) {
             const int kb = g >> 1, s = kb % XG_NS, b = g & 1, ub = g >> 1;
@@ -298,20 +317,23 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
             tc_fence_after();
             const uint32_t sbw = stS(s)[(g & 1) * XG_BM + trow];
             const double sc = (double)lo_bf(sbw), bi = (double)hi_bf(sbw);
-            const GTab *tb = stT(s) + (g & 1) * XG_TOK + wg * 32;
-            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 256 + wg * 96);
+            const XTab *tb = stT(s) + (g & 1) * XG_TOK + tq * 16;
+            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 256 + tq * 48);
 #pragma unroll
-            for (int tc = 0; tc < 4; tc++) {
-                uint32_t v16[16], v8[8];
-                tmem_ld16(v16, ta + tc * 24);
-                tmem_ld8(v8, ta + tc * 24 + 16);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            for (int tp = 0; tp < 2; tp++) {
+                // 8 tokens (24 columns) per TMEM round trip
                 uint32_t v[24];
+                {
+                    uint32_t a16[16], a8[8];
+                    tmem_ld16(a16, ta + tp * 24);
+                    tmem_ld8(a8, ta + tp * 24 + 16);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int k = 0; k < 16; k++) v[k] = v16[k];
+                    for (int k = 0; k < 16; k++) v[k] = a16[k];
 #pragma unroll
-                for (int k = 0; k < 8; k++) v[16 + k] = v8[k];
-                if (tc == 3) {
+                    for (int k = 0; k < 8; k++) v[16 + k] = a8[k];
+                }
+                if (tp == 1) {
                     // the buffer is read: the MMA warp may overwrite it
                     tc_fence_before();
                     __syncwarp();
@@ -319,9 +341,9 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                 }
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
-                    const int t = tc * 8 + k;
+                    const int t = tp * 8 + k;
                     const int P = (int)v[3 * k] + ((int)v[3 * k + 1] << 7) + ((int)v[3 * k + 2] << 14);
-                    const GTab e = tb[t];
+                    const XTab e = tb[t];
                     acc[t] = fma(sc, int_times_pow2(P, e.e - 20), acc[t]);
                     acc[t] = fma(bi, e.tf, acc[t]);
                 }
@@ -340,24 +362,24 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                 // the same 64 outputs (alternating 64-row blocks)
                 if (q >= 2) {
 #pragma unroll
-                    for (int t = 0; t < 32; t++) xch[(size_t)(wg * 32 + t) * 64 + (trow - 64)] = acc[t];
+                    for (int t = 0; t < 16; t++) xch[(size_t)(tq * 16 + t) * 64 + (trow - 64)] = acc[t];
                 }
-                asm volatile("bar.sync 1, 256;" ::: "memory");
+                asm volatile("bar.sync 1, 512;" ::: "memory");
                 if (q < 2) {
                     const int pairs = rows / 2, pr = (row0 / 128) * 64 + trow;
 #pragma unroll
-                    for (int t = 0; t < 32; t++) {
-                        const int tok = tok0 + wg * 32 + t;
+                    for (int t = 0; t < 16; t++) {
+                        const int tok = tok0 + tq * 16 + t;
                         if (tok < S) {
-                            const double up = xch[(size_t)(wg * 32 + t) * 64 + trow];
+                            const double up = xch[(size_t)(tq * 16 + t) * 64 + trow];
                             y[(size_t)tok * pairs + pr] = f2bf(swiglu_bf16(bf2f(d2bf(acc[t])), bf2f(d2bf(up))));
                         }
                     }
                 }
             } else {
 #pragma unroll
-                for (int t = 0; t < 32; t++) {
-                    const int tok = tok0 + wg * 32 + t;
+                for (int t = 0; t < 16; t++) {
+                    const int tok = tok0 + tq * 16 + t;
                     if (tok >= S) continue;
                     const size_t o = (size_t)tok * rows + row;
                     if constexpr (EPI == EPI_RESIDUAL) y[o] = f2bf(__fadd_rn(bf2f(residual[o]), bf2f(d2bf(acc[t]))));
@@ -366,7 +388,7 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                 }
             }
         } else if (EPI == EPI_SWIGLU) {
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            asm volatile("bar.sync 1, 512;" ::: "memory");
         }
     }
     tc_fence_before();
@@ -425,11 +447,11 @@ bool qgemm_tc_eligible(const QMat &W, int S, int epi) {
 
 size_t qgemm_tc_ws_bytes(int S, int cols) {
     const size_t S_pad = ((size_t)S + XG_TOK - 1) / XG_TOK * XG_TOK;
-    return ((S_pad * 3 * cols + 255) / 256) * 256 + S_pad * (cols / 64) * sizeof(GTab) + 256;
+    return ((S_pad * 3 * cols + 255) / 256) * 256 + S_pad * (cols / 64) * sizeof(XTab) + 256;
 }
 
 template <int EPI>
-static int launch_x(const QMat &W, const CUtensorMap &m, const GTab *tab, int S, int S_pad, uint16_t *y,
+static int launch_x(const QMat &W, const CUtensorMap &m, const XTab *tab, int S, int S_pad, uint16_t *y,
                     const uint16_t *res, double *yf, cudaStream_t st) {
     auto kern = qgemm_x_kernel<EPI>;
     if (!smem_allowed((const void *)kern, XG_SMEM)) return -1;
@@ -452,7 +474,7 @@ int qgemm_tc(const QMat &W, const uint16_t *x, int S, int epi, const uint16_t *r
     }
     const int S_pad = (S + XG_TOK - 1) / XG_TOK * XG_TOK;
     int8_t *xd = (int8_t *)ws;
-    GTab *tab = reinterpret_cast<GTab *>((unsigned char *)ws + (((size_t)S_pad * 3 * W.cols + 255) / 256) * 256);
+    XTab *tab = reinterpret_cast<XTab *>((unsigned char *)ws + (((size_t)S_pad * 3 * W.cols + 255) / 256) * 256);
     const int ng = W.cols / 64;
     const size_t warps = (size_t)ng * S_pad;
     xq_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(x, S, S_pad, W.cols, xd, tab);
