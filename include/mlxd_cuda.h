@@ -80,13 +80,21 @@ typedef struct mlxd_kv mlxd_kv;
 
 /* engine_model_load's upload half (emodel.c:176-211): validates the tensor
    set like weights_get_triplet (weights.c:1053-1088), repacks quantized
-   projections into the kernel tile layout and keeps only this rank's shard. */
+   projections into the kernels' layouts (decode row blocks, prefill GEMM
+   tiles) and keeps only this rank's shard. */
 int  mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg,
                             const mlxd_tensor *tensors, int n_tensors);
 void mlxd_cuda_model_destroy(mlxd_model *m);
 size_t mlxd_cuda_model_weight_bytes(const mlxd_model *m);
 /* Tensor parallel: bind an NCCL communicator (unique id bytes from rank 0,
-   128 bytes) before the first forward when tp_size > 1. */
+   128 bytes) before the first forward when tp_size > 1. Collective: every
+   rank calls it. It also maps every rank's exchange mailbox into every
+   other rank (CUDA IPC): one-token steps combine their row-parallel partials,
+   greedy argmax keys and, for sampling, the logits shards through those
+   mailboxes inside the step, with no NCCL call; chunked prefill uses NCCL.
+   A one-token step whose peer does not arrive within about a second per
+   exchange fails (-1, "gave up waiting for a peer GPU"); forward then
+   synchronises its stream to report it. */
 int  mlxd_cuda_model_tp_init(mlxd_model *m, const void *nccl_unique_id);
 int  mlxd_cuda_nccl_unique_id(void *out128);
 /* Tensor-parallel shard plan, host only (no device call). The reference has
@@ -193,6 +201,35 @@ int mlxd_cuda_sample(const void *logits_dev, int dtype, int V, const mlxd_sampli
 int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
                        int max_new, const mlxd_sampling *sp, int chunk,
                        int32_t *out, float *logprobs, double *timing);
+
+/* Cancellation and hooks of handle_generate_real (engine_gen_hooks_t,
+   engine.h:96-120; poll sites engine.c:406-470). shutdown and cancelled are
+   ints read with acquire loads (the layout of C11 atomic_int); NULL is never
+   set. At every site: poll -> hook -> re-poll -> work. Sites: before each
+   prefill chunk (on_prefill_chunk(ud, pos, chunk_len), pos = absolute token
+   index), after the prefill before the seed step (on_before_seed), and
+   before each decode step is enqueued (on_decode_step(ud, step), step = the
+   count of tokens chosen before it). A set flag ends the request at that
+   site: steps already enqueued finish and their tokens are emitted (a stop
+   at step s's site leaves s tokens), `stopped` becomes 1 and the emitted
+   count is returned. Hooks run on the calling thread and may block; they
+   must not call this library for the same model. Under tensor parallelism
+   every rank must stop at the same site (a hook can agree the decision
+   across ranks); a rank that stops alone makes its peers' next step fail
+   after the exchange's bounded wait. */
+typedef struct {
+    const int *shutdown;
+    const int *cancelled;
+    void (*on_prefill_chunk)(void *ud, int pos, int chunk_len);
+    void (*on_decode_step)(void *ud, int step);
+    void (*on_before_seed)(void *ud);
+    void *ud;
+    int stopped;               /* out */
+} mlxd_gen_control;
+int mlxd_cuda_generate_ctl(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
+                           int max_new, const mlxd_sampling *sp, int chunk,
+                           int32_t *out, float *logprobs, double *timing,
+                           mlxd_gen_control *ctl);
 
 /* ---- synthetic MLX-format weights (bench and tests) ---------------------
    Fills w (u32 [rows][cols/8]), scales, biases (bf16 [rows][cols/group]) in

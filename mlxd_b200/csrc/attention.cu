@@ -7,16 +7,19 @@
 // aligned; with a window w, positions (i - w, i]),
 //   q_d' = f32(scale * q_d), scale = 1/sqrtf(D);
 //   z_j  = fmaf chain over d = 0..D-1 of q_d' * k_jd;
-//   m    = max_j z_j;  p_j = own_expf(z_j - m)  (exactly 0 for masked keys);
-//   per block of 64 absolute positions [64b, 64b + 64): l_b = in-order f32
-//   sum of p_j, o_bd = fmaf chain of p_j v_jd in key order;
-//   out_d = bf16(sum_b o_bd / sum_b l_b), the sums and the quotient in f64
-//   (exact while a sum spans 53 bits), rounded once.
-// Blocks are absolute positions, so a decode step and the prefill row at the
-// same position give the same bits, whatever the split of the keys over
-// CTAs. Head dims other than 64/128 take mlx's composed fallback (q scaled
-// in bf16, bf16 scores, precise softmax rounded to bf16, bf16 output).
-#include <cooperative_groups.h>
+//   per block of 64 absolute positions [64b, 64b + 64) holding attended
+//   keys: m_b = max z_j, p_j = own_expf(z_j - m_b), l_b = in-order f32 sum
+//   of p_j, o_bd = fmaf chain of p_j v_jd in key order;
+//   the blocks merge in key order into f64 (M, L, O_d): the first sets
+//   them; a block with m_b > M first scales by s = own_expf(M - m_b):
+//   L = fma(L, s, l_b), O_d = fma(O_d, s, o_bd), M = m_b; any other adds
+//   with e = own_expf(m_b - M): L = fma(l_b, e, L), O_d = fma(o_bd, e, O_d);
+//   out_d = bf16(O_d / L), rounded once.
+// A block is finished before the merge reads it, so a decode step splits the
+// blocks over CTAs with no exchange between them, a prefill tile walks the
+// keys once, and both give the same bits at the same position. Head dims
+// other than 64/128 take mlx's composed fallback (q scaled in bf16, bf16
+// scores, precise softmax rounded to bf16, bf16 output).
 #include <mutex>
 #include <stdlib.h>
 
@@ -38,51 +41,37 @@ MLXD_DEV int blk_off(int r, int c) {
 
 // ======================================================== decode (S = 1)
 //
-// One cluster of CL CTAs (8 warps) per kv head; the attended blocks
-// (lo/64 .. pos/64) are split into CL contiguous ranges, one per CTA. A CTA
-// streams its K blocks (padded to an even count), then its V blocks, through
-// a 4-slot shared-memory ring (cp.async; the first four loads, the norm
-// weights and this position's cos/sin are requested before waiting on the
-// q|k|v projection, on which none of them depends). After the wait warp h
-// normalises and rotates q head h in registers (lane l holds features
-// l, l + 32, ...: the oracle's per-head RMSNorm association, and rotation
-// pairs i, i + D/2 in one lane), and the CTA holding the new position also
-// the new k, whose row (and v's) replaces the not yet appended cache row in
-// its ring slot. Phase 1, two blocks at a time: scores (thread = (position,
-// head)). Each CTA pushes its per-head maxima into every CTA's inbox through
-// distributed shared memory; one cluster barrier. Phase 2, two blocks at a
-// time: p, then per block the f32 chains (thread = (head, feature pair)),
-// added into f64 partials, which are pushed into the inbox of the CTA owning
-// that slice of the outputs; one cluster barrier; each CTA adds its slice
-// locally. Remote accesses are stores only, all before a barrier.
+// Grid (NS, hkv): CTA (r, kh) takes a contiguous share of the attended
+// blocks (lo/64 .. pos/64) of kv head kh. Its K and V blocks stream through
+// rings of DR slots (cp.async); the first round is requested before waiting
+// on the q|k|v projection, on which none of it depends, so the cache streams
+// while the projection finishes. After the wait, warp h normalises and
+// rotates q head h in registers (lane l holds features l, l + 32, ...: the
+// oracle's per-head RMSNorm association, and rotation pairs i, i + D/2 in
+// one lane); the CTA holding the new position also does the new k, whose
+// row (and v's) replaces the not yet appended cache row in its slot. Per
+// round of DR blocks: thread (position, slot) runs the REP score chains;
+// per (block, head) the maximum; p in place; thread (feature pair, slot)
+// runs the 2 REP o chains and one l chain of its block. Each block's
+// (m_b, l_b, o_b) goes to the cache's step partials in global memory; the
+// last CTA of the kv head to finish (a counter) merges the group's blocks
+// in key order and writes the outputs. No CTA waits for another.
 constexpr int DA_THREADS = 256;
-constexpr int DA_BS1 = DA_THREADS / AB;   // blocks per round in phase 1 (thread = position)
-
-template <int D>
-struct DaConst {
-    static constexpr int NP = D / 2;                 // feature pairs
-    static constexpr int BS2 = DA_THREADS / NP;      // blocks per round in phase 2
-};
+constexpr int DR = DA_THREADS / AB;   // blocks per round (thread = position in phase A)
 
 struct DaLayout {
-    size_t ring, qs, stage, newkv, sc, P, red, gmax, inmax, inO, inL, total;
+    size_t kring, vring, qs, stage, newkv, sc, red, total;
 };
-// nslots: K and V block slots (resident: 2 * scap/64; streaming: 2 * DA_BS1)
-static __host__ __device__ inline DaLayout da_layout(int D, int REP, int scap, int CL, int nslots) {
-    const int BS2 = DA_THREADS / (D / 2);
+static __host__ __device__ inline DaLayout da_layout(int D, int REP) {
     DaLayout l;
-    l.ring = 0;
-    l.qs = l.ring + (size_t)nslots * AB * D * 2;
+    l.kring = 0;
+    l.vring = l.kring + (size_t)DR * AB * D * 2;
+    l.qs = l.vring + (size_t)DR * AB * D * 2;
     l.stage = l.qs + (size_t)REP * D * 4;
     l.newkv = l.stage + (size_t)8 * D * 4;
     l.sc = l.newkv + (size_t)2 * D * 2;
-    l.P = l.sc + (size_t)REP * scap * 4;
-    l.red = l.P + (size_t)BS2 * AB * REP * 4;
-    l.gmax = l.red + (size_t)8 * REP * 4;
-    l.inmax = l.gmax + 64;
-    l.inO = l.inmax + (((size_t)CL * REP * 4 + 15) / 16) * 16;
-    l.inL = l.inO + (size_t)BS2 * REP * D * 8;
-    l.total = l.inL + (size_t)CL * BS2 * REP * 8;
+    l.red = l.sc + (size_t)DR * AB * REP * 4;
+    l.total = l.red + (size_t)8 * REP * 4 + 16;
     return l;
 }
 
@@ -134,45 +123,51 @@ MLXD_DEV void lds_rep(float (&o)[REP], const float *p) {
     }
 }
 
-// RES: every K and V block of the CTA resident in shared memory (all K rows
-// requested as one commit group, all V rows as a second, before the wait);
-// otherwise rounds of DA_BS1 K blocks (then V blocks) in a ring of
-// 2 * DA_BS1 slots, the first round of each requested before the wait.
-template <int D, int REP, int CL, bool RES>
-__global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeArgs a, int scap) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
+// one block's result into the f64 running merge (M, L, O0, O1)
+MLXD_DEV void merge_block(float mb, float l, float o0, float o1, float &M, double &L, double &O0, double &O1) {
+    if (M == -INFINITY) {
+        M = mb;
+        L = (double)l;
+        O0 = (double)o0;
+        O1 = (double)o1;
+    } else if (mb > M) {
+        const double s = (double)own_expf(__fsub_rn(M, mb));
+        M = mb;
+        L = __fma_rn(L, s, (double)l);
+        O0 = __fma_rn(O0, s, (double)o0);
+        O1 = __fma_rn(O1, s, (double)o1);
+    } else {
+        const double e = (double)own_expf(__fsub_rn(mb, M));
+        L = __fma_rn((double)l, e, L);
+        O0 = __fma_rn((double)o0, e, O0);
+        O1 = __fma_rn((double)o1, e, O1);
+    }
+}
+
+template <int D, int REP>
+__global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeArgs a) {
     constexpr int NCH = D / 8;               // 16-byte chunks per row
-    constexpr int NP = DaConst<D>::NP, BS2 = DaConst<D>::BS2;
+    constexpr int NP = D / 2;                // feature pairs
     constexpr int DS = D / 32;
-    constexpr int E = REP * D, ES = E / CL;   // outputs of the group, per owner CTA
-    static_assert(ES % 2 == 0, "output slices hold whole feature pairs");
-    const int rank = (int)cluster.block_rank();
-    const int kh = blockIdx.y;
+    const int NS = gridDim.x, rank = blockIdx.x, kh = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     extern __shared__ __align__(128) unsigned char sm[];
-    const int NB = scap / AB;
-    const int NSLOT = RES ? 2 * NB : 2 * DA_BS1;
-    const DaLayout Ly = da_layout(D, REP, scap, CL, NSLOT);
-    unsigned char *ring = sm + Ly.ring;
+    const DaLayout Ly = da_layout(D, REP);
+    unsigned char *kring = sm + Ly.kring, *vring = sm + Ly.vring;
     float *qs = reinterpret_cast<float *>(sm + Ly.qs);          // [D][REP], scaled
     float *stage = reinterpret_cast<float *>(sm + Ly.stage) + (size_t)warp * D;
     uint16_t *newk = reinterpret_cast<uint16_t *>(sm + Ly.newkv), *newv = newk + D;
-    float *sc = reinterpret_cast<float *>(sm + Ly.sc);          // [scap][REP]
-    float *P = reinterpret_cast<float *>(sm + Ly.P);            // [BS2][AB][REP]
+    float *sc = reinterpret_cast<float *>(sm + Ly.sc);          // [DR][AB][REP]: z, then p
     float *red = reinterpret_cast<float *>(sm + Ly.red);        // [8 warps][REP]
-    float *gmax = reinterpret_cast<float *>(sm + Ly.gmax);
-    float *inmax = reinterpret_cast<float *>(sm + Ly.inmax);    // [CL][REP]
-    double *inO = reinterpret_cast<double *>(sm + Ly.inO);      // [CL][BS2][ES]
-    double *inL = reinterpret_cast<double *>(sm + Ly.inL);      // [CL][BS2][REP]
+    int *s_last = reinterpret_cast<int *>(red + 8 * REP);
 
     const int pos = *a.d_pos;
     const int T = pos + 1;
     const int lo = a.window > 0 ? max(0, T - a.window) : 0;
     const int bfirst = lo / AB, blast = pos / AB, nbt = blast - bfirst + 1;
-    const int mb0 = bfirst + (int)((long long)nbt * rank / CL), mb1 = bfirst + (int)((long long)nbt * (rank + 1) / CL);
+    const int mb0 = bfirst + (int)((long long)nbt * rank / NS), mb1 = bfirst + (int)((long long)nbt * (rank + 1) / NS);
     int nbm = mb1 - mb0;
-    if (nbm > NB) {   // cannot happen for a launch sized by the host; report and do no work
+    if (nbt > a.nbmax) {   // cannot happen for a cache sized by the host; report and do no work
         if (tid == 0) atomicExch(&g_attn_err, 1);
         nbm = 0;
     }
@@ -180,12 +175,12 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     const uint16_t *kc = a.kc + (size_t)kh * a.cap * D;
     const uint16_t *vc = a.vc + (size_t)kh * a.cap * D;
 
-    // block i (< nbm) of K (isv 0) or V into slot `slot`; rows outside
+    // block i (< nbm) of K (isv 0) or V into ring slot i % DR; rows outside
     // [lo, pos) zero-filled (the new position's row comes from this step)
-    auto load_block = [&](int i, bool isv, int slot) {
+    auto load_block = [&](int i, bool isv) {
         if (i >= nbm) return;
         const int b = mb0 + i;
-        unsigned char *dst = ring + (size_t)slot * AB * D * 2;
+        unsigned char *dst = (isv ? vring : kring) + (size_t)(i % DR) * AB * D * 2;
         const uint16_t *src = isv ? vc : kc;
         const int slot0 = (b * AB) % a.cap;   // cache slot of the block's first position
         for (int e = tid; e < AB * NCH; e += DA_THREADS) {
@@ -197,21 +192,11 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
             cp_async16_zfill(dst + blk_off<D>(r, c), src + (size_t)(valid ? sl : 0) * D + c * 8, valid);
         }
     };
-    auto kslot = [&](int i) { return RES ? i : i % DA_BS1; };
-    auto vslot = [&](int i) { return RES ? NB + i : DA_BS1 + i % DA_BS1; };
-    if (RES) {
-        for (int i = 0; i < nbm; i++) load_block(i, false, kslot(i));
-        cp_async_commit();
-        for (int i = 0; i < nbm; i++) load_block(i, true, vslot(i));
-        cp_async_commit();
-    } else {
-        for (int i = 0; i < DA_BS1; i++) load_block(i, false, kslot(i));
-        cp_async_commit();
-        for (int i = 0; i < DA_BS1; i++) load_block(i, true, vslot(i));
-        cp_async_commit();
-    }
+    for (int i = 0; i < DR; i++) load_block(i, false);
+    cp_async_commit();
+    for (int i = 0; i < DR; i++) load_block(i, true);
+    cp_async_commit();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
-    // per-warp head work: q heads h = warp, warp + 8; the new k after them
     const bool regs_rope = a.rope.rope_dims == D;
     float nwq[DS], nwk[DS], rc[DS / 2], rs[DS / 2];
     if (regs_rope) {
@@ -230,64 +215,65 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     pdl_trigger();
     pdl_wait();
 
+    // q heads (and the new k) of the group: warp h takes heads h, h + 8, ...
     const int qstride = D * (a.gate ? 2 : 1);
-    for (int h = warp; h < REP + 1; h += 8) {
-        const bool isk = h == REP;
-        if (isk && !has_new) continue;
-        const uint16_t *src = isk ? a.qkv + a.qdim + (size_t)kh * D : a.qkv + (size_t)(kh * REP + h) * qstride;
-        if (regs_rope) {
-            float v[DS];
+    if (nbm > 0) {
+        for (int h = warp; h < REP + 1; h += 8) {
+            const bool isk = h == REP;
+            if (isk && !has_new) continue;
+            const uint16_t *src = isk ? a.qkv + a.qdim + (size_t)kh * D : a.qkv + (size_t)(kh * REP + h) * qstride;
+            if (regs_rope) {
+                float v[DS];
 #pragma unroll
-            for (int i = 0; i < DS; i++) v[i] = bf2f(src[lane + 32 * i]);
-            norm_rope_regs<DS>(v, isk ? nwk : nwq, isk ? a.kn != nullptr : a.qn != nullptr, a.eps, rc, rs, D);
-            if (isk) {
-                const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
+                for (int i = 0; i < DS; i++) v[i] = bf2f(src[lane + 32 * i]);
+                norm_rope_regs<DS>(v, isk ? nwk : nwq, isk ? a.kn != nullptr : a.qn != nullptr, a.eps, rc, rs, D);
+                if (isk) {
+                    const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
 #pragma unroll
-                for (int i = 0; i < DS; i++) {
-                    newk[lane + 32 * i] = f2bf(v[i]);
-                    newv[lane + 32 * i] = vsrc[lane + 32 * i];
+                    for (int i = 0; i < DS; i++) {
+                        newk[lane + 32 * i] = f2bf(v[i]);
+                        newv[lane + 32 * i] = vsrc[lane + 32 * i];
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < DS; i++) qs[(lane + 32 * i) * REP + h] = __fmul_rn(scale, v[i]);
                 }
             } else {
-#pragma unroll
-                for (int i = 0; i < DS; i++) qs[(lane + 32 * i) * REP + h] = __fmul_rn(scale, v[i]);
-            }
-        } else {
-            for (int d = lane; d < D; d += 32) stage[d] = bf2f(src[d]);
-            __syncwarp();
-            head_norm_rope(stage, D, isk ? a.kn : a.qn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
-            if (isk) {
-                const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
-                for (int d = lane; d < D; d += 32) {
-                    newk[d] = f2bf(stage[d]);
-                    newv[d] = vsrc[d];
+                for (int d = lane; d < D; d += 32) stage[d] = bf2f(src[d]);
+                __syncwarp();
+                head_norm_rope(stage, D, isk ? a.kn : a.qn, a.eps, a.rope.cs, a.rope.rope_dims, pos);
+                if (isk) {
+                    const uint16_t *vsrc = a.qkv + a.qdim + (size_t)(a.hkv + kh) * D;
+                    for (int d = lane; d < D; d += 32) {
+                        newk[d] = f2bf(stage[d]);
+                        newv[d] = vsrc[d];
+                    }
+                } else {
+                    for (int d = lane; d < D; d += 32) qs[d * REP + h] = __fmul_rn(scale, stage[d]);
                 }
-            } else {
-                for (int d = lane; d < D; d += 32) qs[d * REP + h] = __fmul_rn(scale, stage[d]);
+                __syncwarp();
             }
-            __syncwarp();
         }
     }
 
-    // phase 1: thread (position pp, block slot s1) scores all REP heads of
-    // blocks s1, s1 + DA_BS1, ... (one fmaf chain over d per head)
-    const int pp = tid % AB, s1 = tid / AB;
-    float lmax[REP];
-#pragma unroll
-    for (int h = 0; h < REP; h++) lmax[h] = -INFINITY;
-    for (int r0 = 0; r0 < nbm; r0 += DA_BS1) {
-        if (r0 == 0) cp_async_wait<1>();   // the first K round (V may still be in flight)
-        else if (!RES) cp_async_wait<0>();  // the K round requested after the previous one
-        __syncthreads();   // (first round: also orders the q and new-k stores)
-        if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + DA_BS1) {
-            unsigned char *blk = ring + (size_t)kslot(blast - mb0) * AB * D * 2;
+    const int pp = tid % AB, s1 = tid / AB;      // phase A: (position, slot)
+    const int dp = tid % NP, s2 = tid / NP;      // phase B: (feature pair, slot)
+    const size_t gbase = (size_t)kh * a.nbmax;   // the head group's block results
+    for (int r0 = 0; r0 < nbm; r0 += DR) {
+        cp_async_wait<1>();   // this round's K (V may still be in flight)
+        __syncthreads();      // (first round: also orders the q and new-k stores)
+        if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + DR) {
+            unsigned char *blk = kring + (size_t)((blast - mb0) % DR) * AB * D * 2;
             const int r = pos - blast * AB;
             for (int c = tid; c < NCH; c += DA_THREADS)
                 *reinterpret_cast<uint4 *>(blk + blk_off<D>(r, c)) = *reinterpret_cast<const uint4 *>(newk + c * 8);
             __syncthreads();
         }
+        // phase A: scores of position pp of block r0 + s1, all REP heads
         const int i = r0 + s1;
+        float z[REP];
         if (i < nbm) {
-            const unsigned char *blk = ring + (size_t)kslot(i) * AB * D * 2;
+            const unsigned char *blk = kring + (size_t)s1 * AB * D * 2;
             float acc[REP];
 #pragma unroll
             for (int h = 0; h < REP; h++) acc[h] = 0.f;
@@ -307,73 +293,44 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
             const int j = (mb0 + i) * AB + pp;
             const bool valid = j >= lo && j <= pos;
 #pragma unroll
-            for (int h = 0; h < REP; h++) {
-                const float z = valid ? acc[h] : -INFINITY;
-                sc[(i * AB + pp) * REP + h] = z;
-                lmax[h] = fmaxf(lmax[h], z);
-            }
+            for (int h = 0; h < REP; h++) z[h] = valid ? acc[h] : -INFINITY;
+        } else {
+#pragma unroll
+            for (int h = 0; h < REP; h++) z[h] = -INFINITY;
         }
-        if (!RES && r0 + DA_BS1 < nbm) {
-            __syncthreads();
-            for (int s = 0; s < DA_BS1; s++) load_block(r0 + DA_BS1 + s, false, kslot(r0 + DA_BS1 + s));
-            cp_async_commit();
+        // block maxima: the two warps of a slot
+#pragma unroll
+        for (int h = 0; h < REP; h++) {
+            const float v = warp_max(z[h]);
+            if (lane == 0) red[warp * REP + h] = v;
         }
-    }
-    // per-head maxima of the CTA, pushed into every CTA's inbox
+        __syncthreads();
+        // the K ring is free: the next round's K blocks stream during the rest
+        if (r0 + DR < nbm) {
+            for (int s = 0; s < DR; s++) load_block(r0 + DR + s, false);
+        }
+        cp_async_commit();
 #pragma unroll
-    for (int h = 0; h < REP; h++) {
-        const float v = warp_max(lmax[h]);
-        if (lane == 0) red[warp * REP + h] = v;
-    }
-    __syncthreads();
-    if (tid < CL * REP) {
-        const int dst = tid / REP, h = tid % REP;
-        float m = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < 8; w++) m = fmaxf(m, red[w * REP + h]);
-        *cluster.map_shared_rank(inmax + rank * REP + h, dst) = m;
-    }
-    cluster.sync();
-    if (tid < REP) {
-        float m = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < CL; r++) m = fmaxf(m, inmax[r * REP + tid]);
-        gmax[tid] = m;
-    }
-
-    // phase 2: per round of BS2 blocks, p of the round's blocks (thread =
-    // position), then thread (feature pair dp, block slot s2) runs the
-    // 2 * REP chains of block s2 (v pair unpacked once for all heads) and
-    // l for all heads (dp == 0), added into f64 partials of its slot
-    const int dp = tid % NP, s2 = tid / NP;
-    double Oa[REP][2], La[REP];
-#pragma unroll
-    for (int h = 0; h < REP; h++) Oa[h][0] = Oa[h][1] = La[h] = 0.0;
-    if (RES) cp_async_wait<0>();
-    for (int r0 = 0; r0 < nbm; r0 += BS2) {
-        if (!RES) cp_async_wait<0>();
-        __syncthreads();   // (first round: also orders gmax and the V rows)
-        if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + BS2) {
-            unsigned char *blk = ring + (size_t)vslot(blast - mb0) * AB * D * 2;
+        for (int h = 0; h < REP; h++) {
+            const float mb = fmaxf(red[(2 * s1) * REP + h], red[(2 * s1 + 1) * REP + h]);
+            sc[(s1 * AB + pp) * REP + h] = z[h] == -INFINITY ? 0.f : own_expf(__fsub_rn(z[h], mb));
+        }
+        cp_async_wait<1>();   // this round's V
+        __syncthreads();
+        if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + DR) {
+            unsigned char *blk = vring + (size_t)((blast - mb0) % DR) * AB * D * 2;
             const int r = pos - blast * AB;
             for (int c = tid; c < NCH; c += DA_THREADS)
                 *reinterpret_cast<uint4 *>(blk + blk_off<D>(r, c)) = *reinterpret_cast<const uint4 *>(newv + c * 8);
+            __syncthreads();
         }
-        for (int e = tid; e < BS2 * AB; e += DA_THREADS) {
-            const int s = e / AB, q = e % AB, i = r0 + s;
-#pragma unroll
-            for (int h = 0; h < REP; h++) {
-                const float z = i < nbm ? sc[(i * AB + q) * REP + h] : -INFINITY;
-                P[(s * AB + q) * REP + h] = z == -INFINITY ? 0.f : own_expf(__fsub_rn(z, gmax[h]));
-            }
-        }
-        __syncthreads();
-        const int i = r0 + s2;
-        if (i < nbm) {
-            const unsigned char *blk = ring + (size_t)vslot(i) * AB * D * 2;
-            const float *ps = P + (size_t)s2 * AB * REP;
+        // phase B: thread (dp, s2) runs the o chains of feature pair dp of
+        // block r0 + s2 for all heads, and the l chain of head dp (dp < REP)
+        const int ib = r0 + s2;
+        if (s2 < DR && ib < nbm) {
+            const unsigned char *blk = vring + (size_t)s2 * AB * D * 2;
+            const float *ps = sc + (size_t)s2 * AB * REP;
             const int c = dp >> 2, off = (dp & 3) * 4;
-            // l of head lh (threads dp < REP; the others' chain is unused)
             const int lh = dp < REP ? dp : 0;
             float o0[REP], o1[REP], l = 0.f;
 #pragma unroll
@@ -391,45 +348,22 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
                 }
                 l = __fadd_rn(l, ps[q * REP + lh]);
             }
+            const size_t gb = (gbase + (size_t)(mb0 + ib - bfirst)) * REP;
 #pragma unroll
-            for (int h = 0; h < REP; h++) {
-                Oa[h][0] += (double)o0[h];
-                Oa[h][1] += (double)o1[h];
+            for (int h = 0; h < REP; h++)
+                *reinterpret_cast<float2 *>(a.part_o + (gb + h) * D + 2 * dp) = make_float2(o0[h], o1[h]);
+            if (dp < REP) {
+                a.part_l[gb + dp] = l;
+                a.part_m[gb + dp] = fmaxf(red[(2 * s2) * REP + dp], red[(2 * s2 + 1) * REP + dp]);
             }
-            if (dp < REP) La[dp] += (double)l;
         }
-        if (!RES && r0 + BS2 < nbm) {
-            __syncthreads();
-            for (int s = 0; s < BS2; s++) load_block(r0 + BS2 + s, true, vslot(r0 + BS2 + s));
-            cp_async_commit();
+        __syncthreads();
+        if (r0 + DR < nbm) {
+            for (int s = 0; s < DR; s++) load_block(r0 + DR + s, true);
         }
+        cp_async_commit();
     }
     cp_async_wait<0>();
-    // the slot partials into the inbox of the CTA owning each output slice
-#pragma unroll
-    for (int h = 0; h < REP; h++) {
-        const int e = h * D + 2 * dp, dst = e / ES;
-        *reinterpret_cast<double2 *>(cluster.map_shared_rank(inO + ((size_t)rank * BS2 + s2) * ES + (e - dst * ES), dst)) =
-            make_double2(Oa[h][0], Oa[h][1]);
-    }
-    if (dp < REP)
-        for (int r = 0; r < CL; r++) *cluster.map_shared_rank(inL + ((size_t)rank * BS2 + s2) * REP + dp, r) = La[dp];
-    cluster.sync();
-    for (int el = tid; el < ES; el += DA_THREADS) {
-        const int e = rank * ES + el, h = e / D, d = e % D;
-        double os = 0.0, ls = 0.0;
-        for (int r = 0; r < CL * BS2; r++) {
-            os += inO[(size_t)r * ES + el];
-            ls += inL[(size_t)r * REP + h];
-        }
-        const int hg = kh * REP + h;
-        uint16_t val = d2bf(os / ls);
-        if (a.gate) {
-            const float gv = bf2f(a.qkv[(size_t)hg * qstride + D + d]);
-            val = f2bf(__fmul_rn(bf2f(val), sigmoid_bf16(gv)));
-        }
-        a.out[(size_t)hg * D + d] = val;
-    }
     // the new position's k/v rows into the cache
     if (has_new) {
         uint16_t *kd = a.kc + ((size_t)kh * a.cap + pos % a.cap) * D;
@@ -439,133 +373,78 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
             vd[d] = newv[d];
         }
     }
-}
-
-// blocks one CTA may hold for a cache of `cap` slots (window: at most
-// `window` attended positions)
-static int da_scap(const AttnDecodeArgs &a, int CL) {
-    const int span = a.window > 0 && a.window < a.cap ? a.window : a.cap;
-    const int nbt = span / AB + 2;
-    return ((nbt + CL - 1) / CL) * AB;
-}
-
-// One CTA per SM (dynamic shared memory above half of an SM's): with two
-// attention CTAs on one SM the projections that follow ran slower on those
-// SMs for the rest of the step.
-template <int D, int REP>
-static size_t da_smem(int scap, int CL, bool res) {
-    const size_t t = da_layout(D, REP, scap, CL, res ? 2 * (scap / AB) : 2 * DA_BS1).total;
-    return t > 116 * 1024 ? t : 116 * 1024;
-}
-// every block resident when it fits in a CTA's shared memory
-template <int D, int REP>
-static bool da_resident(int scap, int CL) {
-    return da_layout(D, REP, scap, CL, 2 * (scap / AB)).total <= 220 * 1024;
-}
-
-template <int D, int REP, int CL, bool RES>
-static bool da_prepare(const AttnDecodeArgs &a, size_t smem) {
-    auto kern = attn_decode_kernel<D, REP, CL, RES>;
-    if (!smem_allowed((const void *)kern, smem)) return false;
-    if (CL > 8) {
-        static std::mutex mu;
-        static bool np[64] = {};   // per instantiation and device
-        int dev = 0;
-        cudaGetDevice(&dev);
-        std::lock_guard<std::mutex> lock(mu);
-        if (dev >= 0 && dev < 64 && !np[dev]) {
-            if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
-                         "cluster attribute"))
-                return false;
-            np[dev] = true;
+    // the last CTA of the head group merges its blocks
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *s_last = atomicAdd(a.cnt + kh, 1) == NS - 1;
+    __syncthreads();
+    if (!*s_last) return;
+    __threadfence();
+    const int nmerge = nbt <= a.nbmax ? nbt : 0;
+    for (int e = tid; e < REP * NP; e += DA_THREADS) {
+        const int h = e / NP, fp = e % NP;
+        float M = -INFINITY;
+        double L = 0.0, O0 = 0.0, O1 = 0.0;
+#pragma unroll 4
+        for (int b = 0; b < nmerge; b++) {
+            const size_t gb = (gbase + b) * REP + h;
+            const float2 o = __ldcg(reinterpret_cast<const float2 *>(a.part_o + gb * D + 2 * fp));
+            merge_block(__ldcg(a.part_m + gb), __ldcg(a.part_l + gb), o.x, o.y, M, L, O0, O1);
         }
+        const int hg = kh * REP + h;
+        uint16_t v0 = d2bf(O0 / L), v1 = d2bf(O1 / L);
+        if (a.gate) {
+            const uint16_t *gp = a.qkv + (size_t)hg * qstride + D + 2 * fp;
+            v0 = f2bf(__fmul_rn(bf2f(v0), sigmoid_bf16(bf2f(gp[0]))));
+            v1 = f2bf(__fmul_rn(bf2f(v1), sigmoid_bf16(bf2f(gp[1]))));
+        }
+        *reinterpret_cast<uint32_t *>(a.out + (size_t)hg * D + 2 * fp) = (uint32_t)v0 | ((uint32_t)v1 << 16);
     }
-    return true;
+    if (tid == 0) a.cnt[kh] = 0;   // ready for the next launch
 }
 
-template <int D, int REP, int CL>
-static cudaLaunchConfig_t da_config(const AttnDecodeArgs &a, size_t smem, cudaLaunchAttribute *attr, bool pdl,
-                                    cudaStream_t st) {
+// CTAs per kv head: about DR blocks each over the cache's attended span,
+// all kv heads' CTAs on distinct SMs
+static int da_splits(const AttnDecodeArgs &a) {
+    const int sms = num_sms();
+    int ns = (a.nbmax + DR - 1) / DR;
+    const int cap_ns = sms / a.hkv > 0 ? sms / a.hkv : 1;
+    if (ns > cap_ns) ns = cap_ns;
+    return ns < 1 ? 1 : ns;
+}
+
+template <int D, int REP>
+static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+    auto kern = attn_decode_kernel<D, REP>;
+    // one CTA per SM (dynamic shared memory above half of an SM's): with two
+    // attention CTAs on one SM the projections that follow ran slower on
+    // those SMs for the rest of the step
+    size_t smem = da_layout(D, REP).total;
+    if (smem < 116 * 1024) smem = 116 * 1024;
+    if (!smem_allowed((const void *)kern, smem)) return -1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(CL, a.hkv);
+    cfg.gridDim = dim3(da_splits(a), a.hkv);
     cfg.blockDim = dim3(DA_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CL;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
-    return cfg;
-}
-
-// whether `hkv` clusters of CL CTAs are resident at once on this device
-template <int D, int REP, int CL>
-static bool da_fits(const AttnDecodeArgs &a) {
-    const int scap = da_scap(a, CL);
-    const bool res = da_resident<D, REP>(scap, CL);
-    const size_t smem = da_smem<D, REP>(scap, CL, res);
-    if (smem > 227 * 1024 || !(res ? da_prepare<D, REP, CL, true>(a, smem) : da_prepare<D, REP, CL, false>(a, smem))) {
-        cudaGetLastError();
-        return false;
-    }
-    cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = da_config<D, REP, CL>(a, smem, attr, false, nullptr);
-    int n = 0;
-    cudaError_t e = res ? cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<D, REP, CL, true>, &cfg)
-                        : cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<D, REP, CL, false>, &cfg);
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    return n >= a.hkv;
-}
-
-// cluster size per (device, kv heads, cache span): 16 when hkv clusters of
-// 16 are resident at once, else 8
-template <int D, int REP>
-static int da_cluster(const AttnDecodeArgs &a) {
-    static std::mutex mu;
-    static std::vector<std::pair<std::pair<int, long long>, int>> memo;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const long long key = ((long long)a.hkv << 32) | (unsigned)da_scap(a, 8);
-    std::lock_guard<std::mutex> lock(mu);
-    for (auto &m : memo)
-        if (m.first.first == dev && m.first.second == key) return m.second;
-    const int cl = da_fits<D, REP, 16>(a) ? 16 : 8;
-    memo.push_back({{dev, key}, cl});
-    return cl;
-}
-
-template <int D, int REP, int CL>
-static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
-    const int scap = da_scap(a, CL);
-    const bool res = da_resident<D, REP>(scap, CL);
-    const size_t smem = da_smem<D, REP>(scap, CL, res);
-    if (smem > 227 * 1024) {
-        set_error("decode attention: a cache of %d slots needs %zu bytes of shared memory per CTA", a.cap, smem);
-        return -1;
-    }
-    if (!(res ? da_prepare<D, REP, CL, true>(a, smem) : da_prepare<D, REP, CL, false>(a, smem))) return -1;
-    cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = da_config<D, REP, CL>(a, smem, attr, pdl, st);
-    if (res) MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, REP, CL, true>, a, scap));
-    else MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, REP, CL, false>, a, scap));
+    cfg.numAttrs = pdl ? 1 : 0;
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
     return 0;
 }
 
 template <int D, int REP>
-static int da_dispatch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
-    return da_cluster<D, REP>(a) == 16 ? da_launch<D, REP, 16>(a, st, pdl) : da_launch<D, REP, 8>(a, st, pdl);
+static int da_sms(const AttnDecodeArgs &a) {
+    return da_splits(a) * a.hkv;
 }
 
-template <int D, int REP>
-static int da_sms(const AttnDecodeArgs &a) {
-    return da_cluster<D, REP>(a) * a.hkv;
+// result floats per kv head of a cache whose attended span holds at most
+// nbmax blocks: (m, l, o[D]) per (block, query head of the group)
+size_t attention_decode_part_floats(int nbmax, int hkv, int rep, int D) {
+    return (size_t)hkv * nbmax * rep * (D + 2);
 }
 
 bool attention_decode_supported(int D, int rep, int rope_dims) {
@@ -590,7 +469,11 @@ int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
         set_error("decode attention: head dim %d with %d query heads per kv head not supported", D, rep);
         return -1;
     }
-    MLXD_DA_DISPATCH(da_dispatch, a, st, pdl)
+    if (!a.part_o || !a.part_l || !a.part_m || !a.cnt || a.nbmax <= 0) {
+        set_error("decode attention: the cache has no step partials");
+        return -1;
+    }
+    MLXD_DA_DISPATCH(da_launch, a, st, pdl)
     return -1;
 }
 
@@ -611,18 +494,17 @@ int attention_timeouts() {
 
 // ======================================================= prefill (S > 1)
 //
-// CTA = (64 queries, one q head), 256 threads. Keys are walked in blocks of
-// 64 absolute positions over the union of the tile's key ranges.
-//   pass 1: the 64 x 64 score tile of a block on CUDA cores, thread (tq, tk)
-//           holding queries 4tq.. and keys 4tk.. (16 fmaf chains stepping
-//           through d together; q' and k transposed to f32 in shared memory
-//           so that each step is two 16-byte loads); scores go to the CTA's
-//           own region of a global scratch (read back from L2) and the
-//           per-query maxima are kept;
-//   pass 2: per block, p = own_expf(z - m) into shared memory, then thread
-//           (tq, td) runs the chains of queries 4tq.. x features 8td.. over
-//           the block's keys and adds them into f64 registers; l_b by the
-//           threads with td = 0.
+// CTA = (64 queries, one q head), 256 threads, one pass over the keys in
+// blocks of 64 absolute positions (the union of the tile's key ranges):
+//   the 64 x 64 score tile on CUDA cores, thread (tq, tk) holding queries
+//   4tq.. and keys 4tk.. (16 fmaf chains stepping through d together; q'
+//   and k transposed to f32 in shared memory so that each step is two
+//   16-byte loads); per query the block maximum (the 16 threads of a tq);
+//   p = own_expf(z - m_b) into shared memory; thread (tq, td) runs the
+//   chains of queries 4tq.. x features 8td.. over the block's keys (l_b by
+//   every td, the same chain) and merges the block into its f64 running
+//   sums. The next block's key and value rows are requested into registers
+//   while the current one is computed.
 constexpr int PF_T = 256, PF_Q = 64;
 
 template <int D>
@@ -631,8 +513,8 @@ struct PfLayout {
     static constexpr size_t kT = qT + (size_t)D * PF_Q * 4;        // [D][64] f32
     static constexpr size_t pT = kT + (size_t)D * AB * 4;          // [64 keys][64 q] f32
     static constexpr size_t vb = pT + (size_t)AB * PF_Q * 4;       // [64][D] bf16
-    static constexpr size_t mx = vb + (size_t)AB * D * 2;          // [64] f32 + red
-    static constexpr size_t total = mx + (size_t)PF_Q * 4 * 16;
+    static constexpr size_t mx = vb + (size_t)AB * D * 2;          // [64] f32 block maxima
+    static constexpr size_t total = mx + (size_t)PF_Q * 4;
 };
 
 template <int D>
@@ -640,8 +522,7 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
                                                            const uint16_t *__restrict__ kc,
                                                            const uint16_t *__restrict__ vc, int cap, int window,
                                                            int hq, int hkv, const uint16_t *__restrict__ gate_src,
-                                                           int row_stride, uint16_t *__restrict__ out,
-                                                           float *__restrict__ scr, int span_max) {
+                                                           int row_stride, uint16_t *__restrict__ out) {
     using L = PfLayout<D>;
     extern __shared__ __align__(128) unsigned char sm[];
     float *qT = reinterpret_cast<float *>(sm + L::qT);
@@ -659,7 +540,6 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
     const int jhi = qpos_hi + 1;   // exclusive
     const int b0 = jlo / AB, b1 = (jhi - 1) / AB;
     const int nb = b1 - b0 + 1;
-    float *myscr = scr + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * PF_Q * (size_t)span_max;
     const uint16_t *K = kc + (size_t)kh * cap * D;
     const uint16_t *V = vc + (size_t)kh * cap * D;
 
@@ -668,13 +548,26 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
         const int d = e / PF_Q, i = e % PF_Q;
         qT[d * PF_Q + i] = i < nq ? __fmul_rn(scale, bf2f(q[((size_t)(qt0 + i) * hq + h) * D + d])) : 0.f;
     }
-    const int tq = tid >> 4, tk = tid & 15;   // pass 1: queries 4tq.., keys 4tk..
-    float rmax[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    const int tq = tid >> 4, tk = tid & 15;   // scores: queries 4tq.., keys 4tk..
     int qp[4], j0r[4];
 #pragma unroll
     for (int a = 0; a < 4; a++) {
         qp[a] = pos0 + qt0 + 4 * tq + a;
         j0r[a] = window > 0 ? max(0, qp[a] - window + 1) : 0;
+    }
+    // o/l chains: thread (tq2, td): queries QPT tq2.., features 8td..
+    constexpr int FT = D / 8;           // feature groups
+    constexpr int QT = PF_T / FT;       // query groups (16 for D=128, 32 for D=64)
+    constexpr int QPT = PF_Q / QT;      // queries per thread (4 or 2)
+    const int td = tid % FT, tq2 = tid / FT;
+    float Mq[QPT];
+    double O[QPT][8], Lq[QPT];
+#pragma unroll
+    for (int x = 0; x < QPT; x++) {
+        Mq[x] = -INFINITY;
+        Lq[x] = 0.0;
+#pragma unroll
+        for (int y = 0; y < 8; y++) O[x][y] = 0.0;
     }
     // the rows of a key or value block, 16 B per (row r, chunk c), thread
     // share e = tid + 256 x, c = e / 64, r = e % 64: requested one block
@@ -689,12 +582,13 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
                              : make_uint4(0u, 0u, 0u, 0u);
         }
     };
-    uint4 kpre[NPF];
+    uint4 kpre[NPF], vpre[NPF];
     fetch_rows(K, b0, kpre);
+    fetch_rows(V, b0, vpre);
     for (int bi = 0; bi < nb; bi++) {
         const int b = b0 + bi;
-        __syncthreads();
-        // k block transposed to f32: kT[d][r]
+        __syncthreads();   // the previous block's kT, pT, vb and maxima are consumed
+        // k block transposed to f32: kT[d][r]; the v block as it is
 #pragma unroll
         for (int x = 0; x < NPF; x++) {
             const int e = tid + PF_T * x, c = e / AB, r = e % AB;
@@ -704,8 +598,12 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
                 kT[(c * 8 + 2 * y) * AB + r] = lo_bf(w[y]);
                 kT[(c * 8 + 2 * y + 1) * AB + r] = hi_bf(w[y]);
             }
+            *reinterpret_cast<uint4 *>(vb + r * D + c * 8) = vpre[x];
         }
-        if (bi + 1 < nb) fetch_rows(K, b + 1, kpre);
+        if (bi + 1 < nb) {
+            fetch_rows(K, b + 1, kpre);
+            fetch_rows(V, b + 1, vpre);
+        }
         __syncthreads();
         float acc[4][4] = {};
 #pragma unroll 4
@@ -718,76 +616,35 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
 #pragma unroll
                 for (int y = 0; y < 4; y++) acc[x][y] = __fmaf_rn(qa[x], ka[y], acc[x][y]);
         }
+        // masks and the per-query block maxima (16 consecutive lanes per tq)
+        float mrow[4];
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            float v = -INFINITY;
+#pragma unroll
+            for (int y = 0; y < 4; y++) {
+                const int j = b * AB + 4 * tk + y;
+                const bool ok = 4 * tq + x < nq && j >= j0r[x] && j <= qp[x];
+                acc[x][y] = ok ? acc[x][y] : -INFINITY;
+                v = fmaxf(v, acc[x][y]);
+            }
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+            mrow[x] = v;
+        }
+        if (tk == 0) {
+#pragma unroll
+            for (int x = 0; x < 4; x++) smx[4 * tq + x] = mrow[x];
+        }
+        // p tile, transposed: pT[key][query]
 #pragma unroll
         for (int y = 0; y < 4; y++) {
-            const int j = b * AB + 4 * tk + y;
-            float4 o;
-            float *ov = &o.x;
-#pragma unroll
-            for (int x = 0; x < 4; x++) {
-                const bool ok = 4 * tq + x < nq && j >= j0r[x] && j <= qp[x];
-                ov[x] = ok ? acc[x][y] : -INFINITY;
-                rmax[x] = fmaxf(rmax[x], ov[x]);
-            }
-            *reinterpret_cast<float4 *>(myscr + (size_t)(bi * AB + 4 * tk + y) * PF_Q + 4 * tq) = o;
-        }
-    }
-    // per-query maxima: the 16 threads of a tq (consecutive lanes) reduce
-#pragma unroll
-    for (int x = 0; x < 4; x++) {
-        float v = rmax[x];
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (tk == 0) smx[4 * tq + x] = v;
-    }
-    __syncthreads();   // also orders the score stores before pass 2 reads them
-
-    // pass 2: thread (tq, td): queries 4tq.., features 8td.. (D = 128: td < 16)
-    constexpr int FT = D / 8;           // feature groups
-    constexpr int QT = PF_T / FT;       // query groups (16 for D=128, 32 for D=64)
-    constexpr int QPT = PF_Q / QT;      // queries per thread (4 or 2)
-    const int td = tid % FT, tq2 = tid / FT;
-    double O[QPT][8], Lq[QPT];
-#pragma unroll
-    for (int x = 0; x < QPT; x++) {
-        Lq[x] = 0.0;
-#pragma unroll
-        for (int y = 0; y < 8; y++) O[x][y] = 0.0;
-    }
-    // scores of a block (16 per thread: 4 float4 of key r, queries 4i4..)
-    // and its value rows, requested one block ahead into registers
-    float4 zpre[4];
-    uint4 vpre[NPF];
-    auto fetch_scores = [&](int bi) {
-#pragma unroll
-        for (int x = 0; x < 4; x++) {
-            const int e = tid + PF_T * x, r = e / (PF_Q / 4), i4 = e % (PF_Q / 4);
-            zpre[x] = __ldcg(reinterpret_cast<const float4 *>(myscr + (size_t)(bi * AB + r) * PF_Q) + i4);
-        }
-    };
-    fetch_scores(0);
-    fetch_rows(V, b0, vpre);
-    for (int bi = 0; bi < nb; bi++) {
-        __syncthreads();
-        // p tile (transposed: pT[key][query]) and the v block
-#pragma unroll
-        for (int x = 0; x < 4; x++) {
-            const int e = tid + PF_T * x, r = e / (PF_Q / 4), i4 = e % (PF_Q / 4);
-            const float z[4] = {zpre[x].x, zpre[x].y, zpre[x].z, zpre[x].w};
             float4 pv;
             float *pp = &pv.x;
 #pragma unroll
-            for (int k = 0; k < 4; k++) pp[k] = z[k] == -INFINITY ? 0.f : own_expf(__fsub_rn(z[k], smx[4 * i4 + k]));
-            *reinterpret_cast<float4 *>(pT + r * PF_Q + 4 * i4) = pv;
-        }
-#pragma unroll
-        for (int x = 0; x < NPF; x++) {
-            const int e = tid + PF_T * x, c = e / AB, r = e % AB;
-            *reinterpret_cast<uint4 *>(vb + r * D + c * 8) = vpre[x];
-        }
-        if (bi + 1 < nb) {
-            fetch_scores(bi + 1);
-            fetch_rows(V, b0 + bi + 1, vpre);
+            for (int x = 0; x < 4; x++)
+                pp[x] = acc[x][y] == -INFINITY ? 0.f : own_expf(__fsub_rn(acc[x][y], mrow[x]));
+            *reinterpret_cast<float4 *>(pT + (4 * tk + y) * PF_Q + 4 * tq) = pv;
         }
         __syncthreads();
         float o[QPT][8] = {}, l[QPT] = {};
@@ -816,11 +673,28 @@ __global__ void __launch_bounds__(PF_T) attn_prefill_kernel(const uint16_t *__re
                 l[x] = __fadd_rn(l[x], pv[x]);
             }
         }
+        // merge the block (queries with attended keys in it)
 #pragma unroll
         for (int x = 0; x < QPT; x++) {
-            Lq[x] += (double)l[x];
+            const float mb = smx[QPT * tq2 + x];
+            if (mb == -INFINITY) continue;
+            if (Mq[x] == -INFINITY) {
+                Mq[x] = mb;
+                Lq[x] = (double)l[x];
 #pragma unroll
-            for (int y = 0; y < 8; y++) O[x][y] += (double)o[x][y];
+                for (int y = 0; y < 8; y++) O[x][y] = (double)o[x][y];
+            } else if (mb > Mq[x]) {
+                const double s = (double)own_expf(__fsub_rn(Mq[x], mb));
+                Mq[x] = mb;
+                Lq[x] = __fma_rn(Lq[x], s, (double)l[x]);
+#pragma unroll
+                for (int y = 0; y < 8; y++) O[x][y] = __fma_rn(O[x][y], s, (double)o[x][y]);
+            } else {
+                const double e = (double)own_expf(__fsub_rn(mb, Mq[x]));
+                Lq[x] = __fma_rn((double)l[x], e, Lq[x]);
+#pragma unroll
+                for (int y = 0; y < 8; y++) O[x][y] = __fma_rn((double)o[x][y], e, O[x][y]);
+            }
         }
     }
 #pragma unroll
@@ -891,15 +765,10 @@ __global__ void attn_small_kernel(const uint16_t *__restrict__ q, int S, int pos
     }
 }
 
-// scratch floats a prefill launch needs
+// scratch floats a prefill launch needs (the composed path for other head
+// dims keeps its scores there; head dims 64 and 128 need none)
 size_t attention_prefill_scratch(int S, int pos0, int window, int hq, int D) {
-    if (D == 64 || D == 128) {
-        const int ntile = (S + PF_Q - 1) / PF_Q;
-        int span = (pos0 + S) + AB;   // keys of a tile, rounded out to blocks
-        if (window > 0 && span > window + PF_Q + 2 * AB) span = window + PF_Q + 2 * AB;
-        span = ((span + AB - 1) / AB) * AB;
-        return (size_t)ntile * hq * PF_Q * span;
-    }
+    if (D == 64 || D == 128) return 0;
     int tmax = pos0 + S;
     if (window > 0 && tmax > window + S) tmax = window + S;
     return (size_t)S * hq * tmax;
@@ -909,28 +778,27 @@ int attention_prefill(const uint16_t *q, int S, int pos0, const uint16_t *kc, co
                       int window, int hq, int hkv, int D, const uint16_t *gate_src, int qdim, uint16_t *out,
                       float *scr, size_t scr_floats, cudaStream_t st) {
     const int row_stride = qdim + 2 * hkv * D;
-    const size_t need = attention_prefill_scratch(S, pos0, window, hq, D);
-    if (!scr || scr_floats < need) {
-        set_error("prefill attention: scratch of %zu floats too small (%zu needed)", scr_floats, need);
-        return -1;
-    }
     if (D == 64 || D == 128) {
         const int ntile = (S + PF_Q - 1) / PF_Q;
-        const int span_max = (int)(need / ((size_t)ntile * hq * PF_Q));
         dim3 grid(ntile, hq);
         if (D == 128) {
             const size_t smem = PfLayout<128>::total;
             if (!smem_allowed((const void *)attn_prefill_kernel<128>, smem)) return -1;
             attn_prefill_kernel<128><<<grid, PF_T, smem, st>>>(q, S, pos0, kc, vc, cap, window, hq, hkv, gate_src,
-                                                               row_stride, out, scr, span_max);
+                                                               row_stride, out);
         } else {
             const size_t smem = PfLayout<64>::total;
             if (!smem_allowed((const void *)attn_prefill_kernel<64>, smem)) return -1;
             attn_prefill_kernel<64><<<grid, PF_T, smem, st>>>(q, S, pos0, kc, vc, cap, window, hq, hkv, gate_src,
-                                                              row_stride, out, scr, span_max);
+                                                              row_stride, out);
         }
         MLXD_CHECK(cudaGetLastError());
         return 0;
+    }
+    const size_t need = attention_prefill_scratch(S, pos0, window, hq, D);
+    if (!scr || scr_floats < need) {
+        set_error("prefill attention: scratch of %zu floats too small (%zu needed)", scr_floats, need);
+        return -1;
     }
     int tmax = pos0 + S;
     if (window > 0 && tmax > window + S) tmax = window + S;

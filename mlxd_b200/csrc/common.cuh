@@ -107,7 +107,7 @@ MLXD_DEV void put_pair(uint32_t *xp, int G, int XW, int k, uint32_t v) {
     xp[(gi * 4 + tt) * XW + j * 2 + hi] = v;
 }
 
-// ---- bulk copies (cp.async.bulk, no multicast) and mbarriers
+// ---- bulk copies (cp.async.bulk into this CTA's own shared memory) and mbarriers
 MLXD_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 MLXD_DEV void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

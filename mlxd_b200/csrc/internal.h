@@ -115,6 +115,7 @@ struct mlxd_model {
     cudaStream_t stream = nullptr;
     // tensor parallel
     void *nccl = nullptr;       // ncclComm_t when tp_size > 1
+    void *tp = nullptr;         // NVLink mailboxes of the decode step's exchanges (tp.cu)
     size_t weight_bytes = 0;
 };
 
@@ -125,4 +126,8 @@ struct mlxd_kv {
     uint16_t *k = nullptr, *v = nullptr;   // [L][hkv][cap][d]
     int32_t *d_pos = nullptr;   // device copy of offset (position of the next token)
     unsigned long long serial = 0;   // unique per created cache (keys the decode graph)
+    // decode attention's per-step block results and arrival counters
+    float *att_part = nullptr;
+    int *att_cnt = nullptr;
+    int att_nbmax = 0, att_rep = 0;
 };

@@ -69,6 +69,24 @@ int qk_rope_append(const uint16_t *qkv, int S, int qdim, int hq, int hkv, int ga
 int add_partials(uint16_t *h_out, const uint16_t *h_in, const double *part, int nranks, size_t stride,
                  size_t n, cudaStream_t st);
 
+// ---- tensor parallel exchanges of the decode step (tp.cu)
+int tp_setup(mlxd_model *m);       // collective over the model's NCCL communicator
+void tp_free(mlxd_model *m);
+// out = bf16(res + bf16(sum of the ranks' f64 partials)); idx: the exchange's
+// index in the step (0 .. 2L-1)
+int tp_sum(mlxd_model *m, const double *part, const uint16_t *res, uint16_t *out, int idx, cudaStream_t st,
+           bool pdl);
+// greedy: the largest of the ranks' argmax keys -> token; position + 1,
+// step counter + 1
+int tp_argmax(mlxd_model *m, unsigned long long *amax, int32_t *d_pos, int32_t *token, cudaStream_t st, bool pdl);
+// every rank's logits shard into every rank's full row (tp_full_logits)
+int tp_gather_logits(mlxd_model *m, const uint16_t *logits, cudaStream_t st, bool pdl);
+uint16_t *tp_full_logits(mlxd_model *m);
+// device step counter: every one-token step that is not greedy-fused
+// advances it in its final kernel
+unsigned *tp_seq(mlxd_model *m);
+int tp_timeouts(mlxd_model *m);
+
 // ---- attention (attention.cu)
 struct AttnDecodeArgs {
     const uint16_t *qkv;     // [qdim + 2*hkv*D]
@@ -81,7 +99,13 @@ struct AttnDecodeArgs {
     const int32_t *d_pos;
     int hq, hkv;
     uint16_t *out;           // [hq*D]
+    // the step's block results ([hkv][nbmax][rep] (m, l) and [..][D] o) and
+    // one arrival counter per kv head (zero between launches)
+    float *part_o, *part_l, *part_m;
+    int *cnt;
+    int nbmax;               // blocks the attended span can touch
 };
+size_t attention_decode_part_floats(int nbmax, int hkv, int rep, int D);
 bool attention_decode_supported(int D, int rep, int rope_dims);
 int attention_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
 // SMs the decode attention kernel holds (one CTA each)

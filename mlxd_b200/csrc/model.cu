@@ -28,8 +28,9 @@ __global__ void set_pos_kernel(int32_t *d_pos, int v) { *d_pos = v; }
 
 // end of one decode step: advance the position; with the fused argmax, turn
 // the winning key into the token id and clear the key for the next step
-__global__ void step_finish_kernel(int32_t *d_pos, unsigned long long *amax, int32_t *token) {
+__global__ void step_finish_kernel(int32_t *d_pos, unsigned long long *amax, int32_t *token, unsigned *tp_seq) {
     *d_pos += 1;
+    if (tp_seq) *tp_seq += 1u;
     if (amax) {
         *token = (int32_t)(0xFFFFFFFFu - (uint32_t)(*amax & 0xFFFFFFFFull));
         *amax = 0ull;
@@ -416,6 +417,18 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         ad.hq = m->hq;
         ad.hkv = m->hkv;
         ad.out = m->att;
+        if (kv->att_rep != m->hq / m->hkv || kv->d != D) {
+            set_error("KV cache made for another model shape");
+            return -1;
+        }
+        {
+            const size_t per = (size_t)kv->hkv * kv->att_nbmax * kv->att_rep;
+            ad.part_o = kv->att_part;
+            ad.part_l = kv->att_part + per * D;
+            ad.part_m = ad.part_l + per;
+            ad.cnt = kv->att_cnt;
+            ad.nbmax = kv->att_nbmax;
+        }
         if (attention_decode(ad, st, pdl)) return -1;
         GemvArgs o = {};
         // the o projection runs on the SMs that attention leaves free (one
@@ -431,7 +444,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         if (tp) {
             o.yf = m->part_h;
             if (qgemv(L.o, PRO_PLAIN, EPI_PARTIAL, o, st, pdl)) return -1;
-            if (reduce_partials(m, m->part_h, H, m->h1, m->h, st)) return -1;
+            if (tp_sum(m, m->part_h, m->h, m->h1, 2 * l, st, pdl)) return -1;
         } else {
             o.y = m->h1;
             o.residual = m->h;
@@ -453,7 +466,7 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         if (tp) {
             dn.yf = m->part_h;
             if (qgemv(L.down, PRO_PLAIN, EPI_PARTIAL, dn, st, pdl)) return -1;
-            if (reduce_partials(m, m->part_h, H, m->h, m->h1, st)) return -1;
+            if (tp_sum(m, m->part_h, m->h1, m->h, 2 * l + 1, st, pdl)) return -1;
         } else {
             dn.y = m->h;
             dn.residual = m->h1;
@@ -472,15 +485,10 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         lg.amax = m->amax;
         lg.row_offset = m->vocab_off;
         if (qgemv(m->lm, PRO_RMSNORM, argmax ? EPI_ARGMAX : EPI_STORE, lg, st, pdl)) return -1;
-        if (argmax && tp) {
-            ncclResult_t r = ncclAllReduce(m->amax, m->amax, 1, ncclUint64, ncclMax, comm_of(m), st);
-            if (r != ncclSuccess) {
-                set_error("ncclAllReduce(max): %s", ncclGetErrorString(r));
-                return -1;
-            }
-        }
+        // greedy over the vocabulary shards: the largest key of all ranks
+        if (argmax && tp) return tp_argmax(m, m->amax, kv->d_pos, m->token, st, pdl);
     }
-    step_finish_kernel<<<1, 1, 0, st>>>(kv->d_pos, argmax ? m->amax : nullptr, m->token);
+    step_finish_kernel<<<1, 1, 0, st>>>(kv->d_pos, argmax ? m->amax : nullptr, m->token, tp ? tp_seq(m) : nullptr);
     MLXD_CHECK(cudaGetLastError());
     return 0;
 }
@@ -786,7 +794,7 @@ int mlxd_cuda_model_create(mlxd_model **out, const mlxd_model_config *cfg, const
         !m->part_h)
         return fail();
     if (!cuda_ok(cudaMemset(m->amax, 0, 8), "memset")) return fail();
-    if (!(m->samp = samp_work_create(m->vocab_local))) return fail();
+    if (!(m->samp = samp_work_create(c.vocab))) return fail();   // full rows (gathered under TP)
     if (!cuda_ok(cudaDeviceSynchronize(), "model upload")) return fail();
     for (auto &L : m->L)
         m->weight_bytes += L.qkv.stream_bytes() + L.o.stream_bytes() + L.gateup.stream_bytes() + L.down.stream_bytes();
@@ -823,6 +831,7 @@ void mlxd_cuda_model_destroy(mlxd_model *m) {
                     (void *)m->ctx, (void *)m->n_ctx, (void *)m->d_step, (void *)m->lp, (void *)m->gws})
         dev_free(p);
     samp_work_destroy(m->samp);
+    tp_free(m);
     if (m->stream) cudaStreamDestroy(m->stream);
     if (m->nccl) ncclCommDestroy((ncclComm_t)m->nccl);
     delete m;
@@ -853,7 +862,7 @@ int mlxd_cuda_model_tp_init(mlxd_model *m, const void *uid) {
         return -1;
     }
     m->nccl = comm;
-    return 0;
+    return tp_setup(m);
 }
 
 int mlxd_cuda_kv_create(mlxd_kv **out, const mlxd_model *m, int capacity) {
@@ -879,11 +888,20 @@ int mlxd_cuda_kv_create(mlxd_kv **out, const mlxd_model *m, int capacity) {
     kv->k = (uint16_t *)dev_alloc(n * 2);
     kv->v = (uint16_t *)dev_alloc(n * 2);
     kv->d_pos = (int32_t *)dev_alloc(4);
-    if (!kv->k || !kv->v || !kv->d_pos) {
+    // decode attention's block results: a step attends at most `span`
+    // positions, which touch at most span/64 + 2 blocks
+    const int span = kv->window > 0 && kv->window < kv->cap ? kv->window : kv->cap;
+    kv->att_nbmax = span / 64 + 2;
+    kv->att_rep = m->hq / m->hkv;
+    const size_t pf = attention_decode_part_floats(kv->att_nbmax, kv->hkv, kv->att_rep, kv->d);
+    kv->att_part = (float *)dev_alloc(pf * 4);
+    kv->att_cnt = (int *)dev_alloc((size_t)kv->hkv * 4);
+    if (!kv->k || !kv->v || !kv->d_pos || !kv->att_part || !kv->att_cnt) {
         mlxd_cuda_kv_destroy(kv);
         return -1;
     }
-    if (!cuda_ok(cudaMemset(kv->d_pos, 0, 4), "memset")) {
+    if (!cuda_ok(cudaMemset(kv->d_pos, 0, 4), "memset") ||
+        !cuda_ok(cudaMemset(kv->att_cnt, 0, (size_t)kv->hkv * 4), "memset")) {
         mlxd_cuda_kv_destroy(kv);
         return -1;
     }
@@ -897,6 +915,8 @@ void mlxd_cuda_kv_destroy(mlxd_kv *kv) {
     dev_free(kv->k);
     dev_free(kv->v);
     dev_free(kv->d_pos);
+    dev_free(kv->att_part);
+    dev_free(kv->att_cnt);
     delete kv;
 }
 
@@ -953,7 +973,17 @@ int mlxd_cuda_forward(mlxd_model *m, mlxd_kv *kv, const int32_t *ids, int n, int
     }
     MLXD_CHECK(cudaMemcpyAsync(m->p_ids, ids, (size_t)n * 4,
                                ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
-    return forward_dev(m, kv, m->p_ids, n, want_logits != 0, (uint16_t *)logits_dev, st);
+    if (forward_dev(m, kv, m->p_ids, n, want_logits != 0, (uint16_t *)logits_dev, st)) return -1;
+    // tensor parallel: the step waits for its exchanges, so that a peer that
+    // never arrived is reported here rather than as wrong numbers
+    if (m->tp) {
+        if (!cuda_ok(cudaStreamSynchronize(st), "forward")) return -1;
+        if (tp_timeouts(m)) {
+            set_error("tensor-parallel exchange gave up waiting for a peer GPU");
+            return -1;
+        }
+    }
+    return 0;
 }
 
 // ---- single ops
@@ -1118,6 +1148,26 @@ int mlxd_cuda_sample(const void *logits_dev, int dtype, int V, const mlxd_sampli
 
 int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n, int max_new,
                        const mlxd_sampling *sp, int chunk, int32_t *out, float *logprobs, double *timing) {
+    return mlxd_cuda_generate_ctl(m, kv, prompt, n, max_new, sp, chunk, out, logprobs, timing, nullptr);
+}
+
+int mlxd_cuda_generate_ctl(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n, int max_new,
+                           const mlxd_sampling *sp, int chunk, int32_t *out, float *logprobs, double *timing,
+                           mlxd_gen_control *ctl) {
+    if (ctl) ctl->stopped = 0;
+    // poll -> hook -> re-poll at each site (engine.c:406-470): true when a
+    // flag ends the request there
+    auto flagged = [ctl]() -> bool {
+        return (ctl->shutdown && __atomic_load_n(ctl->shutdown, __ATOMIC_ACQUIRE)) ||
+               (ctl->cancelled && __atomic_load_n(ctl->cancelled, __ATOMIC_ACQUIRE));
+    };
+    auto site = [&](auto &&hook) -> bool {
+        if (!ctl) return false;
+        if (flagged()) return ctl->stopped = 1, true;
+        hook();
+        if (flagged()) return ctl->stopped = 1, true;
+        return false;
+    };
     if (!m || !kv || !prompt || !sp || !out) {
         set_error("generate: null argument");
         return -1;
@@ -1133,8 +1183,8 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
             set_error("prompt token id %d out of range", prompt[i]);
             return -1;
         }
-    if (m->c.tp_size > 1 && !(sp->temperature < 0.01f && !(sp->repetition_penalty > 0.f && sp->repetition_penalty != 1.f))) {
-        set_error("sampled decoding and the repetition penalty are not supported with tensor parallelism");
+    if (m->c.tp_size > 1 && !m->tp) {
+        set_error("tensor-parallel model: mlxd_cuda_model_tp_init has not run");
         return -1;
     }
     cudaStream_t st = m->stream;
@@ -1184,6 +1234,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     // chunked prefill of prompt[:-1]
     for (int pos = 0; pos < n - 1; pos += chunk) {
         int len = (n - 1 - pos) < chunk ? (n - 1 - pos) : chunk;
+        if (site([&] {
+                if (ctl->on_prefill_chunk) ctl->on_prefill_chunk(ctl->ud, pos, len);
+            }))
+            break;
         if (ensure_prefill(m, len) ||
             !cuda_ok(cudaMemcpyAsync(m->p_ids, m->ctx + pos, (size_t)len * 4, cudaMemcpyDeviceToDevice, st),
                      "prefill ids") ||
@@ -1197,7 +1251,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     // the fused greedy argmax needs the raw logits: a repetition penalty
     // (applied before greedy draws too) goes through the sampler
     const bool penalty = sp->repetition_penalty > 0.f && sp->repetition_penalty != 1.0f;
-    const bool greedy = sp->temperature < 0.01f && !penalty;
+    const bool tp = m->c.tp_size > 1;
+    // tensor parallel: logprobs need the whole row, so they go through the
+    // gathered row and the sampler too
+    const bool greedy = sp->temperature < 0.01f && !penalty && !(tp && logprobs);
     const bool fast = fast_decode_ok(m);
     // device token slot starts as the last prompt token (the seed forward)
     MLXD_CHECK(cudaMemcpyAsync(m->token, m->ctx + n - 1, 4, cudaMemcpyDeviceToDevice, st));
@@ -1220,8 +1277,14 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
                 MLXD_CHECK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
                 int r = decode_step(m, kv, m->token, true, m->logits, !sampled, st, true);
                 if (!r && sampled) {
-                    r = sample(m->samp, m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, 0, 0, m->token,
-                               logprobs ? m->lp : nullptr, nullptr, st, m->n_ctx, m->d_step);
+                    const uint16_t *row = m->logits;
+                    if (tp) {
+                        r = tp_gather_logits(m, m->logits, st, true);
+                        row = tp_full_logits(m);
+                    }
+                    if (!r)
+                        r = sample(m->samp, row, MLXD_BF16, m->c.vocab, *sp, m->ctx, 0, 0, m->token,
+                                   logprobs ? m->lp : nullptr, nullptr, st, m->n_ctx, m->d_step);
                     if (!r) sampled_step_kernel<<<1, 1, 0, st>>>(m->ctx, m->n_ctx, m->token, m->d_step);
                 } else if (!r && logprobs) {
                     logprob_kernel<<<1, 1024, 0, st>>>(m->logits, m->vocab_local, m->token, m->lp);
@@ -1245,6 +1308,10 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
             }
             MLXD_CHECK(cudaGraphLaunch((cudaGraphExec_t)m->graph_exec, st));
         } else {
+            if (tp) {
+                set_error("tensor parallelism needs the one-token decode kernels (head dim 64 or 128)");
+                return -1;
+            }
             if (generic_forward(m, kv, m->token, 1, true, m->logits, st)) return -1;
             if (sample(m->samp, m->logits, MLXD_BF16, m->vocab_local, *sp, m->ctx, n + e, (uint64_t)e, m->token,
                        logprobs ? m->lp : nullptr, nullptr, st))
@@ -1272,12 +1339,25 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
     t0 = std::chrono::steady_clock::now();
     nvtxRangePushA("decode");
     decode_range = true;
+    if (ctl && ctl->stopped) goto stopped;   // during the prefill
+    if (site([&] {
+            if (ctl->on_before_seed) ctl->on_before_seed(ctl->ud);
+        }) ||
+        site([&] {
+            if (ctl->on_decode_step) ctl->on_decode_step(ctl->ud, 0);
+        }))
+        goto stopped;
     if (enqueue_step(0)) { rc = -1; goto done; }
     cudaEventRecord(evs[0], st);
     if (timing) cudaEventRecord(tev[0], st);
     for (int e = 0; e < max_new; e++) {
         // lookahead: enqueue step e+1 before reading token e
         bool more = e + 1 < max_new;
+        // the site of step e + 1; a stop there still emits token e
+        if (more && site([&] {
+                if (ctl->on_decode_step) ctl->on_decode_step(ctl->ud, e + 1);
+            }))
+            more = false;
         if (more) {
             if (enqueue_step(e + 1)) { rc = -1; goto done; }
             cudaEventRecord(evs[(e + 1) & 1], st);
@@ -1296,11 +1376,17 @@ int mlxd_cuda_generate(mlxd_model *m, mlxd_kv *kv, const int32_t *prompt, int n,
         out[emitted] = tok;
         if (logprobs) logprobs[emitted] = pin_lp[e & 1];
         emitted++;
+        if (ctl && ctl->stopped) break;
     }
+stopped:
     cudaEventRecord(e2, st);
     if (!cuda_ok(cudaStreamSynchronize(st), "generate")) rc = -1;
     if (!rc && attention_timeouts()) {
         set_error("decode attention: a launch was sized for fewer positions than it met");
+        rc = -1;
+    }
+    if (!rc && tp_timeouts(m)) {
+        set_error("tensor-parallel exchange gave up waiting for a peer GPU");
         rc = -1;
     }
     if (!rc && qgemm_tc_timeouts()) {

@@ -53,6 +53,32 @@ def sampling(temperature=1.0, top_p=1.0, top_k=-1, min_p=0.0, seed=-1,
                     repetition_context)
 
 
+PREFILL_HOOK = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_int)
+STEP_HOOK = C.CFUNCTYPE(None, C.c_void_p, C.c_int)
+SEED_HOOK = C.CFUNCTYPE(None, C.c_void_p)
+
+
+class GenControl(C.Structure):
+    """mlxd_gen_control: cancel/shutdown flags and the three generate hooks
+    (engine_gen_hooks_t)."""
+    _fields_ = [("shutdown", C.POINTER(C.c_int)), ("cancelled", C.POINTER(C.c_int)),
+                ("on_prefill_chunk", PREFILL_HOOK), ("on_decode_step", STEP_HOOK),
+                ("on_before_seed", SEED_HOOK), ("ud", C.c_void_p), ("stopped", C.c_int)]
+
+
+def gen_control(on_prefill_chunk=None, on_decode_step=None, on_before_seed=None):
+    """A control block with its own flags (ctl.flags = (shutdown, cancelled),
+    c_int objects the caller sets) and Python hooks."""
+    sd, cn = C.c_int(0), C.c_int(0)
+    ctl = GenControl(C.pointer(sd), C.pointer(cn),
+                     PREFILL_HOOK(lambda ud, pos, n: on_prefill_chunk(pos, n)) if on_prefill_chunk
+                     else PREFILL_HOOK(),
+                     STEP_HOOK(lambda ud, step: on_decode_step(step)) if on_decode_step else STEP_HOOK(),
+                     SEED_HOOK(lambda ud: on_before_seed()) if on_before_seed else SEED_HOOK(), None, 0)
+    ctl.flags = (sd, cn)
+    return ctl
+
+
 # symbol -> (restype, argtypes)
 P = C.c_void_p
 _SIGS = {
@@ -95,6 +121,8 @@ _SIGS = {
                                    C.c_uint64, P, P, P, P]),
     "mlxd_cuda_generate": (C.c_int, [P, P, P, C.c_int, C.c_int, C.POINTER(Sampling), C.c_int,
                                      P, P, P]),
+    "mlxd_cuda_generate_ctl": (C.c_int, [P, P, P, C.c_int, C.c_int, C.POINTER(Sampling), C.c_int,
+                                         P, P, P, C.POINTER(GenControl)]),
     "mlxd_cuda_synth_quantized": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_uint64,
                                             C.c_float, P]),
     "mlxd_cuda_synth_bf16": (C.c_int, [P, C.c_size_t, C.c_uint64, C.c_float, C.c_float, P]),
@@ -344,8 +372,9 @@ class Model:
             return logits.to_array(np.uint16, (self.vocab_local,))
         return None
 
-    def generate(self, prompt, max_new, sp=None, chunk=512, kv=None, logprobs=False):
-        """handle_generate_real: returns (tokens, logprobs or None, timing dict)."""
+    def generate(self, prompt, max_new, sp=None, chunk=512, kv=None, logprobs=False, control=None):
+        """handle_generate_real: returns (tokens, logprobs or None, timing dict).
+        control: a gen_control() block (cancel/shutdown flags and hooks)."""
         sp = sp or sampling(temperature=0.0)
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)
         own_kv = kv is None
@@ -354,9 +383,10 @@ class Model:
         out = np.zeros(max_new, dtype=np.int32)
         lps = np.zeros(max_new, dtype=np.float32) if logprobs else None
         timing = np.zeros(4 + max_new, dtype=np.float64)
-        n = lib().mlxd_cuda_generate(self.m, kv.kv, ptr(prompt), len(prompt), max_new,
-                                     C.byref(sp), chunk, ptr(out),
-                                     ptr(lps) if logprobs else None, ptr(timing))
+        n = lib().mlxd_cuda_generate_ctl(self.m, kv.kv, ptr(prompt), len(prompt), max_new,
+                                         C.byref(sp), chunk, ptr(out),
+                                         ptr(lps) if logprobs else None, ptr(timing),
+                                         C.byref(control) if control is not None else None)
         if n < 0:
             check(-1, "generate")
         t = {"prefill_ms": timing[0], "decode_ms": timing[1], "decode_steps": timing[2],

@@ -20,11 +20,14 @@ QWEN3_8B = dict(hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, inter=12288
                 vocab=151936)
 
 
-def shapes_of(kw):
+def shapes_of(kw, tp=1):
+    """Decode projection shapes (rows, cols) of one rank at tensor-parallel
+    degree tp: q/k/v, gate/up and lm_head split by rows, o and down by
+    columns."""
     H, D = kw["hidden"], kw["head_dim"]
-    q, kv = kw["n_heads"] * D, kw["n_kv_heads"] * D
-    return {"qkv": (q + 2 * kv, H), "o_proj": (H, q), "gate_up": (2 * kw["inter"], H),
-            "down": (H, kw["inter"]), "lm_head": (kw["vocab"], H)}
+    q, kv = kw["n_heads"] * D // tp, kw["n_kv_heads"] * D // tp
+    return {"qkv": (q + 2 * kv, H), "o_proj": (H, q), "gate_up": (2 * kw["inter"] // tp, H),
+            "down": (H, kw["inter"] // tp), "lm_head": (kw["vocab"] // tp, H)}
 
 
 def gemv_bytes(rows, cols, group=64):

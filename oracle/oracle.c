@@ -702,13 +702,19 @@ int orc_window_mask(int q_len, int kv_len, int window, uint8_t *out) {
    fixed here):
      q_d' = f32(scale * q_d), scale = 1/sqrtf(D);
      z_j  = fmaf chain over d = 0..D-1 of q_d' * k_jd (one rounding per step);
-     m    = max_j z_j over the attended keys;
-     p_j  = own exp(z_j - m);
-     keys are cut into blocks of 64 absolute positions [64b, 64b + 64); in a
-     block, l_b = in-order f32 sum of p_j and o_bd = fmaf chain of p_j v_jd
-     in key order; L = sum_b l_b and O_d = sum_b o_bd in f64 (exact while
-     the sum spans 53 bits, otherwise correct to 2^-53);
+     keys are cut into blocks of 64 absolute positions [64b, 64b + 64); a
+     block with attended keys has m_b = max z_j over them, p_j = own
+     exp(z_j - m_b), l_b = in-order f32 sum of p_j and o_bd = fmaf chain of
+     p_j v_jd in key order;
+     the blocks merge in key order into f64 (M, L, O_d): the first sets
+     M = m_b, L = l_b, O_d = o_bd; a block with m_b > M scales the sums by
+     s = own exp(M - m_b) (f32) first: L = fma(L, s, l_b), O_d = fma(O_d, s,
+     o_bd), M = m_b; any other adds with e = own exp(m_b - M): L = fma(l_b,
+     e, L), O_d = fma(o_bd, e, O_d);
      out_d = bf16(O_d / L), the f64 quotient rounded once.
+   Every block is complete before the merge sees it, so a decode step can
+   split the blocks over CTAs and merge their results in one place, and a
+   prefill tile needs one pass over the keys.
    The blocks are absolute positions, so a decode step and a prefill row at
    the same position give the same bits. Other head dims take mlx's composed
    fallback: q scaled in bf16, bf16 scores (fmaf chain rounded once), precise
@@ -761,20 +767,37 @@ static void att_heads(void *vc, int h0, int h1) {
                 for (int d = 0; d < D; d++) dst[d] = f2bf(o[d]);
                 continue;
             }
+            /* blocks of 64 absolute positions in key order, each with its
+               own maximum, merged into f64 running sums */
             double L = 0.0;
+            float M = -INFINITY;
             for (int d = 0; d < D; d++) O[d] = 0.0;
             for (int b0 = j0; b0 < j1;) {
                 int b1 = (b0 / 64 + 1) * 64;
                 if (b1 > j1) b1 = j1;
+                float mb = -INFINITY;
+                for (int j = b0; j < b1; j++) mb = sc[j] > mb ? sc[j] : mb;
                 float l = 0.f;
                 for (int d = 0; d < D; d++) o[d] = 0.f;
                 for (int j = b0; j < b1; j++) {
-                    float p = orc_expf(sc[j] - mx);
+                    float p = orc_expf(sc[j] - mb);
                     l += p;
                     for (int d = 0; d < D; d++) o[d] = fmaf(p, bf2f(V[(size_t)j * D + d]), o[d]);
                 }
-                L += (double)l;
-                for (int d = 0; d < D; d++) O[d] += (double)o[d];
+                if (M == -INFINITY) {
+                    M = mb;
+                    L = (double)l;
+                    for (int d = 0; d < D; d++) O[d] = (double)o[d];
+                } else if (mb > M) {
+                    double s = (double)orc_expf(M - mb);
+                    M = mb;
+                    L = fma(L, s, (double)l);
+                    for (int d = 0; d < D; d++) O[d] = fma(O[d], s, (double)o[d]);
+                } else {
+                    double e = (double)orc_expf(mb - M);
+                    L = fma((double)l, e, L);
+                    for (int d = 0; d < D; d++) O[d] = fma((double)o[d], e, O[d]);
+                }
                 b0 = b1;
             }
             for (int d = 0; d < D; d++) dst[d] = d2bf(O[d] / L);
@@ -1227,4 +1250,106 @@ done:
     free(ctx);
     orc_kv_free(kv);
     return rc;
+}
+
+/* ------------------------------------------------------ synthetic weights */
+/* The benchmark's seeded MLX-format weights, restated here so the CPU
+   baseline can build them without the CUDA library: element e of stream
+   `seed` is the Irwin-Hall sum of 12 uniforms (24-bit halves of six
+   SplitMix64 outputs, Steele/Lea/Flood 2014) scaled to N(0, std) and rounded
+   to bf16; each group is MLX affine-quantized (mlx ops.cpp affine_quantize:
+   the larger-magnitude edge maps exactly to a level). The CUDA library's
+   generator produces the same bits (a test compares them). */
+static uint64_t syn_mix(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static uint16_t syn_value(uint64_t seed, uint64_t e, float std) {
+    uint64_t base = syn_mix(seed ^ 0x5EED5EED5EEDull) + e * 6ull;
+    uint32_t sum = 0;
+    for (int i = 0; i < 6; i++) {
+        uint64_t r = syn_mix(base + (uint64_t)i);
+        sum += (uint32_t)(r >> 40) + (uint32_t)((r >> 16) & 0xFFFFFFu);
+    }
+    float z = (float)sum * (1.0f / 16777216.0f) - 6.0f;
+    return f2bf(z * std);
+}
+
+typedef struct {
+    uint32_t *w;
+    uint16_t *s, *b;
+    int cols, G;
+    uint64_t seed;
+    float std;
+} syn_ctx;
+
+static void syn_rows(void *vc, int r0, int r1) {
+    syn_ctx *c = vc;
+    const int G = c->G, ng = c->cols / G;
+    float v[64];
+    for (int r = r0; r < r1; r++)
+        for (int g = 0; g < ng; g++) {
+            float mx = -INFINITY, mn = INFINITY;
+            for (int j = 0; j < G; j++) {
+                v[j] = bf2f(syn_value(c->seed, (uint64_t)r * c->cols + (uint64_t)g * G + j, c->std));
+                mx = v[j] > mx ? v[j] : mx;
+                mn = v[j] < mn ? v[j] : mn;
+            }
+            int neg_edge = fabsf(mn) > fabsf(mx);
+            float sc = (mx - mn) / 15.0f;
+            if (sc < 1e-7f) sc = 1e-7f;
+            if (!neg_edge) sc = -sc;
+            float edge = neg_edge ? mn : mx;
+            float q0 = nearbyintf(edge / sc);
+            if (q0 != 0.0f) sc = edge / q0;
+            float bi = q0 == 0.0f ? 0.0f : edge;
+            uint32_t *wo = c->w + (size_t)r * (c->cols / 8) + (size_t)g * (G / 8);
+            for (int k8 = 0; k8 < G / 8; k8++) {
+                uint32_t word = 0;
+                for (int k = 0; k < 8; k++) {
+                    float q = nearbyintf((v[k8 * 8 + k] - bi) / sc);
+                    q = q < 0.f ? 0.f : (q > 15.f ? 15.f : q);
+                    word |= ((uint32_t)q & 0xFu) << (4 * k);
+                }
+                wo[k8] = word;
+            }
+            c->s[(size_t)r * ng + g] = f2bf(sc);
+            c->b[(size_t)r * ng + g] = f2bf(bi);
+        }
+}
+
+int orc_synth_quantized(uint32_t *w, uint16_t *scales, uint16_t *biases, int rows, int cols,
+                        int group, uint64_t seed, float std) {
+    if ((group != 32 && group != 64) || cols % group || rows <= 0) return -1;
+    syn_ctx c = {w, scales, biases, cols, group, seed, std};
+    parallel_for(rows, 16, syn_rows, &c);
+    return 0;
+}
+
+void orc_synth_bf16(uint16_t *out, size_t n, uint64_t seed, float std, float constant) {
+    for (size_t i = 0; i < n; i++) out[i] = std > 0.f ? syn_value(seed, i, std) : f2bf(constant);
+}
+
+/* Benchmark helper: stand in for a prefill of n positions by filling the
+   cache with seeded N(0, 1) keys and values (ring slot p % capacity) and
+   setting every layer's offset to n, so decode can be timed at context n
+   without the prefill's CPU time. */
+int orc_kv_fill_synth(orc_kv *kv, int n, uint64_t seed) {
+    if (!kv || n < 0) return -1;
+    for (int l = 0; l < kv->layers; l++) {
+        for (int h = 0; h < kv->hkv; h++)
+            for (int p = 0; p < n; p++) {
+                size_t row = ((size_t)h * kv->cap + (size_t)(p % kv->cap)) * kv->d;
+                uint64_t e = (((uint64_t)l * kv->hkv + h) * (uint64_t)n + p) * (uint64_t)kv->d;
+                for (int j = 0; j < kv->d; j++) {
+                    kv->k[l][row + j] = syn_value(seed, 2 * (e + j), 1.0f);
+                    kv->v[l][row + j] = syn_value(seed, 2 * (e + j) + 1, 1.0f);
+                }
+            }
+        kv->off[l] = n;
+    }
+    return 0;
 }

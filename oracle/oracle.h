@@ -135,6 +135,15 @@ int orc_generate(orc_model *m, const int32_t *prompt, int n, int max_new,
                  const orc_sampling *sp, int prefill_chunk,
                  int32_t *out, float *logprobs, float *margins);
 
+/* seeded synthetic MLX-format weights (the benchmark's generator, restated
+   so the CPU baseline needs no CUDA library); same bits as libmlxd_cuda's */
+int  orc_synth_quantized(uint32_t *w, uint16_t *scales, uint16_t *biases, int rows, int cols,
+                         int group, uint64_t seed, float std);
+void orc_synth_bf16(uint16_t *out, size_t n, uint64_t seed, float std, float constant);
+/* stands in for a prefill of n positions (seeded N(0,1) keys/values): decode
+   timing at context n */
+int  orc_kv_fill_synth(orc_kv *kv, int n, uint64_t seed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,6 +68,10 @@ def lib():
         L.orc_kv_offset.argtypes = [P, C.c_int]
         L.orc_kv_read.argtypes = [P, C.c_int, C.c_int, P]
         L.orc_forward.argtypes = [P, P, P, C.c_int, C.c_int, P]
+        L.orc_synth_quantized.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_float]
+        L.orc_synth_bf16.argtypes = [P, C.c_size_t, C.c_uint64, C.c_float, C.c_float]
+        L.orc_synth_bf16.restype = None
+        L.orc_kv_fill_synth.argtypes = [P, C.c_int, C.c_uint64]
         L.orc_forward_hidden.argtypes = [P, P, P, C.c_int, P]
         L.orc_qlinear.argtypes = [P, C.c_int, C.c_int, C.c_int, P, P, P, C.c_int, C.c_int, C.c_int, P]
         L.orc_dense_linear.argtypes = [P, C.c_int, C.c_int, C.c_int, P, P]
@@ -350,3 +354,24 @@ def top_p(x, p):
 
 def min_p(x, mp):
     return _filter(lib().orc_min_p, x, mp)
+
+
+def synth_host_tensors(specs, group, seed=0, std=0.02):
+    """The benchmark's seeded weights built on the host by the oracle's copy of
+    the generator. specs: (name, kind, rows, cols) as the library's
+    synth_tensor_specs gives them; kind "n" is a norm weight of ones."""
+    L = lib()
+    out = {}
+    for i, (name, kind, rows, cols) in enumerate(specs):
+        if kind == "n":
+            a = np.zeros(rows, np.uint16)
+            L.orc_synth_bf16(ptr(a), rows, 0, 0.0, 1.0)
+            out[name] = a
+            continue
+        w = np.zeros((rows, cols // 8), np.uint32)
+        s = np.zeros((rows, cols // group), np.uint16)
+        b = np.zeros((rows, cols // group), np.uint16)
+        if L.orc_synth_quantized(ptr(w), ptr(s), ptr(b), rows, cols, group, seed * 1000003 + i, std):
+            raise RuntimeError("orc_synth_quantized: bad shape %s" % name)
+        out[name + ".weight"], out[name + ".scales"], out[name + ".biases"] = w, s, b
+    return out

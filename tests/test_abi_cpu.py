@@ -100,3 +100,25 @@ def test_synth_prompt_uniform():
     assert p.min() >= 0 and p.max() < 151936
     assert np.array_equal(p, cuda.synth_prompt(20000, 151936, seed=3))
     assert abs(p.mean() / 151936 - 0.5) < 0.02
+
+
+def test_oracle_synth_matches_library_synth():
+    """The CPU baseline builds its weights with the oracle's copy of the
+    generator (no CUDA library in that process): same bits as the library's."""
+    cfg = cuda.synth_config(hidden=128, layers=1, n_heads=2, n_kv_heads=1, head_dim=64, inter=256,
+                            vocab=512)
+    specs = cuda.synth_tensor_specs(cfg)
+    a = cuda.synth_host_tensors(cfg, seed=5)
+    b = po.synth_host_tensors(specs, cfg.qgroup, seed=5)
+    assert a.keys() == b.keys()
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+    L = cuda.lib()
+    for group in (32, 64):
+        w = np.zeros((48, 320 // 8), np.uint32)
+        s = np.zeros((48, 320 // group), np.uint16)
+        bb = np.zeros_like(s)
+        L.mlxd_host_synth_quantized(cuda.ptr(w), cuda.ptr(s), cuda.ptr(bb), 48, 320, group, 99, 0.06)
+        w2, s2, b2 = np.zeros_like(w), np.zeros_like(s), np.zeros_like(bb)
+        po.lib().orc_synth_quantized(po.ptr(w2), po.ptr(s2), po.ptr(b2), 48, 320, group, 99, 0.06)
+        assert np.array_equal(w, w2) and np.array_equal(s, s2) and np.array_equal(bb, b2)
