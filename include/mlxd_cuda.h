@@ -121,6 +121,17 @@ int  mlxd_cuda_kv_reset(mlxd_kv *kv);
 int  mlxd_cuda_kv_read(mlxd_kv *kv, int layer, int is_value, uint16_t *host_out,
                        int *n_out);
 
+/* kvcache_update / kvcache_view (kvcache.c:98-180) for callers that drive
+   layers themselves: rows [pos, pos + n) of one layer (ring slots
+   (pos + i) % capacity) from / to contiguous device arrays [Hkv][n][D]
+   (bf16), enqueued on `stream`. kv_set_offset sets the position the next
+   forward appends at (every layer). */
+int  mlxd_cuda_kv_write(mlxd_kv *kv, int layer, int pos, int n, const void *k_dev,
+                        const void *v_dev, void *stream);
+int  mlxd_cuda_kv_gather(mlxd_kv *kv, int layer, int is_value, int pos, int n,
+                         void *dst_dev, void *stream);
+int  mlxd_cuda_kv_set_offset(mlxd_kv *kv, int offset, void *stream);
+
 /* ---- forward (model_forward, emodel.c:221-337) --------------------------
    ids: n token ids (host or device memory). Appends n positions to kv.
    want_logits: write the last position's logits (bf16 [V]) to logits_dev
@@ -187,6 +198,22 @@ int mlxd_cuda_sample(const void *logits_dev, int dtype, int V, const mlxd_sampli
                      const int32_t *ctx_dev, int n_ctx, uint64_t step,
                      int32_t *tok_dev, float *logprob_dev, uint8_t *keep_dev,
                      void *stream);
+
+/* The pipelined decode loop's pair (engine.c:470-560 over
+   mlxbridge_async_eval_n + mlxbridge_item_int32, mlxbridge.c:88-124):
+   step_async enqueues on `stream` the forward of the token in tok_in_dev
+   (device int32) at the cache's next position and the choice of the next
+   token (the sampler with sp, context ctx_dev[n_ctx] for the repetition
+   penalty and draw index `step`; temperature < 0.01 is greedy) into
+   tok_out_dev, with its raw logprob when logprob_dev is given, and returns
+   without waiting; it may be called again with tok_out_dev as the next input
+   before the token is read. read_token waits for the stream's work up to the
+   call and reads one token into host memory. */
+int mlxd_cuda_step_async(mlxd_model *m, mlxd_kv *kv, const int32_t *tok_in_dev,
+                         const mlxd_sampling *sp, const int32_t *ctx_dev, int n_ctx,
+                         uint64_t step, int32_t *tok_out_dev, float *logprob_dev,
+                         void *stream);
+int mlxd_cuda_read_token(const int32_t *tok_dev, int32_t *out, void *stream);
 
 /* ---- generate (handle_generate_real, engine.c:360-602) ------------------
    Chunked prefill of prompt[:-1] (chunk tokens per forward), seed forward of

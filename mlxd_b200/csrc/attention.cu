@@ -123,27 +123,6 @@ MLXD_DEV void lds_rep(float (&o)[REP], const float *p) {
     }
 }
 
-// one block's result into the f64 running merge (M, L, O0, O1)
-MLXD_DEV void merge_block(float mb, float l, float o0, float o1, float &M, double &L, double &O0, double &O1) {
-    if (M == -INFINITY) {
-        M = mb;
-        L = (double)l;
-        O0 = (double)o0;
-        O1 = (double)o1;
-    } else if (mb > M) {
-        const double s = (double)own_expf(__fsub_rn(M, mb));
-        M = mb;
-        L = __fma_rn(L, s, (double)l);
-        O0 = __fma_rn(O0, s, (double)o0);
-        O1 = __fma_rn(O1, s, (double)o1);
-    } else {
-        const double e = (double)own_expf(__fsub_rn(mb, M));
-        L = __fma_rn((double)l, e, L);
-        O0 = __fma_rn((double)o0, e, O0);
-        O1 = __fma_rn((double)o1, e, O1);
-    }
-}
-
 template <int D, int REP>
 __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeArgs a) {
     constexpr int NCH = D / 8;               // 16-byte chunks per row
@@ -381,18 +360,90 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     if (!*s_last) return;
     __threadfence();
     const int nmerge = nbt <= a.nbmax ? nbt : 0;
-    for (int e = tid; e < REP * NP; e += DA_THREADS) {
-        const int h = e / NP, fp = e % NP;
-        float M = -INFINITY;
-        double L = 0.0, O0 = 0.0, O1 = 0.0;
-#pragma unroll 4
-        for (int b = 0; b < nmerge; b++) {
-            const size_t gb = (gbase + b) * REP + h;
-            const float2 o = __ldcg(reinterpret_cast<const float2 *>(a.part_o + gb * D + 2 * fp));
-            merge_block(__ldcg(a.part_m + gb), __ldcg(a.part_l + gb), o.x, o.y, M, L, O0, O1);
+    // The merge runs in chunks of MCH blocks staged in shared memory (the
+    // rings are free): the blocks' results are loaded together, each
+    // (block, head) gets its factor from the running maximum before it (a
+    // prefix maximum, in parallel), then thread (head, feature pair) runs its
+    // f64 chain over the chunk in key order.
+    constexpr int MCH = (2 * DR * AB * D * 2 - REP * 4) / (REP * (D + 4) * 4);
+    constexpr int NE = (REP * NP + DA_THREADS - 1) / DA_THREADS;
+    float *o_s = reinterpret_cast<float *>(sm);                 // [MCH][REP][D]
+    float *m_s = o_s + (size_t)MCH * REP * D;                    // [MCH][REP]
+    float *l_s = m_s + MCH * REP;
+    float *f_s = l_s + MCH * REP;
+    int *g_s = reinterpret_cast<int *>(f_s + MCH * REP);         // 0 first, 1 new maximum, 2 other
+    float *Mrun = reinterpret_cast<float *>(g_s + MCH * REP);    // [REP]
+    double L[NE], O0[NE], O1[NE];
+#pragma unroll
+    for (int q = 0; q < NE; q++) L[q] = O0[q] = O1[q] = 0.0;
+    if (tid < REP) Mrun[tid] = -INFINITY;
+    for (int c0 = 0; c0 < nmerge; c0 += MCH) {
+        const int nb = min(MCH, nmerge - c0);
+        __syncthreads();   // the previous chunk is consumed (first: Mrun is set)
+        const size_t r0 = (gbase + c0) * REP;
+        const float4 *src = reinterpret_cast<const float4 *>(a.part_o + r0 * D);
+        for (int i = tid; i < nb * REP * D / 4; i += DA_THREADS) reinterpret_cast<float4 *>(o_s)[i] = __ldcg(src + i);
+        for (int i = tid; i < nb * REP; i += DA_THREADS) {
+            m_s[i] = __ldcg(a.part_m + r0 + i);
+            l_s[i] = __ldcg(a.part_l + r0 + i);
         }
+        __syncthreads();
+        for (int i = tid; i < nb * REP; i += DA_THREADS) {
+            const int b = i / REP, h = i % REP;
+            float mp = Mrun[h];
+            for (int bb = 0; bb < b; bb++) mp = fmaxf(mp, m_s[bb * REP + h]);
+            const float mb = m_s[i];
+            int g = 0;
+            float f = 1.f;
+            if (mp != -INFINITY) {
+                g = mb > mp ? 1 : 2;
+                f = own_expf(g == 1 ? __fsub_rn(mp, mb) : __fsub_rn(mb, mp));
+            }
+            g_s[i] = g;
+            f_s[i] = f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < NE; q++) {
+            const int e = tid + q * DA_THREADS;
+            if (e < REP * NP) {
+                const int h = e / NP, fp = e % NP;
+#pragma unroll 4
+                for (int b = 0; b < nb; b++) {
+                    const int i = b * REP + h;
+                    const float2 o = *reinterpret_cast<const float2 *>(o_s + (size_t)i * D + 2 * fp);
+                    const double l = (double)l_s[i], f = (double)f_s[i];
+                    const int g = g_s[i];
+                    if (g == 0) {
+                        L[q] = l;
+                        O0[q] = (double)o.x;
+                        O1[q] = (double)o.y;
+                    } else if (g == 1) {
+                        L[q] = __fma_rn(L[q], f, l);
+                        O0[q] = __fma_rn(O0[q], f, (double)o.x);
+                        O1[q] = __fma_rn(O1[q], f, (double)o.y);
+                    } else {
+                        L[q] = __fma_rn(l, f, L[q]);
+                        O0[q] = __fma_rn((double)o.x, f, O0[q]);
+                        O1[q] = __fma_rn((double)o.y, f, O1[q]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (tid < REP) {
+            float M = Mrun[tid];
+            for (int b = 0; b < nb; b++) M = fmaxf(M, m_s[b * REP + tid]);
+            Mrun[tid] = M;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < NE; q++) {
+        const int e = tid + q * DA_THREADS;
+        if (e >= REP * NP) continue;
+        const int h = e / NP, fp = e % NP;
         const int hg = kh * REP + h;
-        uint16_t v0 = d2bf(O0 / L), v1 = d2bf(O1 / L);
+        uint16_t v0 = d2bf(O0[q] / L[q]), v1 = d2bf(O1[q] / L[q]);
         if (a.gate) {
             const uint16_t *gp = a.qkv + (size_t)hg * qstride + D + 2 * fp;
             v0 = f2bf(__fmul_rn(bf2f(v0), sigmoid_bf16(bf2f(gp[0]))));

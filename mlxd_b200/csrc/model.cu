@@ -938,6 +938,85 @@ int mlxd_cuda_kv_reset(mlxd_kv *kv) {
     return 0;
 }
 
+// rows [pos, pos + n) of every kv head of one layer, ring-aware, as 2-D
+// copies: dev [hkv][n][D] <-> cache slots (pos + i) % cap
+static int kv_rows(mlxd_kv *kv, int layer, bool value, int pos, int n, uint16_t *dev, bool to_cache,
+                   cudaStream_t st) {
+    if (!kv || layer < 0 || layer >= kv->layers || pos < 0 || n < 0 || n > kv->cap || !dev) {
+        set_error("kv rows: bad arguments");
+        return -1;
+    }
+    const size_t layer_elems = (size_t)kv->hkv * kv->cap * kv->d, row = (size_t)kv->d * 2;
+    uint16_t *base = (value ? kv->v : kv->k) + (size_t)layer * layer_elems;
+    for (int part = 0, done = 0; done < n; part++) {
+        const int slot = (pos + done) % kv->cap;
+        const int len = n - done < kv->cap - slot ? n - done : kv->cap - slot;
+        uint16_t *c = base + (size_t)slot * kv->d;
+        uint16_t *d = dev + (size_t)done * kv->d;
+        // one 2-D copy per contiguous run: hkv rows of len * D elements
+        MLXD_CHECK(cudaMemcpy2DAsync(to_cache ? (void *)c : (void *)d, to_cache ? (size_t)kv->cap * row : (size_t)n * row,
+                                     to_cache ? (const void *)d : (const void *)c,
+                                     to_cache ? (size_t)n * row : (size_t)kv->cap * row, (size_t)len * row,
+                                     (size_t)kv->hkv, cudaMemcpyDeviceToDevice, st));
+        done += len;
+    }
+    return 0;
+}
+
+int mlxd_cuda_kv_write(mlxd_kv *kv, int layer, int pos, int n, const void *k_dev, const void *v_dev,
+                       void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (kv_rows(kv, layer, false, pos, n, (uint16_t *)k_dev, true, st)) return -1;
+    return kv_rows(kv, layer, true, pos, n, (uint16_t *)v_dev, true, st);
+}
+
+int mlxd_cuda_kv_gather(mlxd_kv *kv, int layer, int is_value, int pos, int n, void *dst_dev, void *stream) {
+    return kv_rows(kv, layer, is_value != 0, pos, n, (uint16_t *)dst_dev, false, (cudaStream_t)stream);
+}
+
+int mlxd_cuda_kv_set_offset(mlxd_kv *kv, int offset, void *stream) {
+    if (!kv || offset < 0 || (kv->window <= 0 && offset > kv->cap)) {
+        set_error("kv_set_offset: bad arguments");
+        return -1;
+    }
+    kv->offset = offset;
+    set_pos_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(kv->d_pos, offset);
+    MLXD_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int mlxd_cuda_step_async(mlxd_model *m, mlxd_kv *kv, const int32_t *tok_in_dev, const mlxd_sampling *sp,
+                         const int32_t *ctx_dev, int n_ctx, uint64_t step, int32_t *tok_out_dev, float *logprob_dev,
+                         void *stream) {
+    if (!m || !kv || !tok_in_dev || !sp || !tok_out_dev) {
+        set_error("step_async: bad arguments");
+        return -1;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    if (ensure_prefill(m, 1) || forward_dev(m, kv, tok_in_dev, 1, true, m->logits, st)) return -1;
+    const uint16_t *row = m->logits;
+    if (m->tp) {
+        if (tp_gather_logits(m, m->logits, st, false)) return -1;
+        row = tp_full_logits(m);
+    }
+    return sample(m->samp, row, MLXD_BF16, m->c.vocab, *sp, ctx_dev, n_ctx, step, tok_out_dev, logprob_dev, nullptr,
+                  st);
+}
+
+int mlxd_cuda_read_token(const int32_t *tok_dev, int32_t *out, void *stream) {
+    if (!tok_dev || !out) {
+        set_error("read_token: bad arguments");
+        return -1;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    static thread_local int32_t *pin = nullptr;
+    if (!pin) MLXD_CHECK(cudaMallocHost(&pin, 4));
+    MLXD_CHECK(cudaMemcpyAsync(pin, tok_dev, 4, cudaMemcpyDeviceToHost, st));
+    MLXD_CHECK(cudaStreamSynchronize(st));
+    *out = *pin;
+    return 0;
+}
+
 int mlxd_cuda_kv_read(mlxd_kv *kv, int layer, int is_value, uint16_t *host_out, int *n_out) {
     if (!kv || layer < 0 || layer >= kv->layers || !host_out) return -1;
     MLXD_CHECK(cudaDeviceSynchronize());

@@ -25,7 +25,6 @@
 // quantities (max, argmax key, histogram counts) decide the candidate set, so
 // it does not depend on the split. The logsumexp (logprob only) combines
 // per-chunk partial sums.
-#include <cub/cub.cuh>
 #include "common.cuh"
 #include "kernels.h"
 
@@ -57,9 +56,9 @@ struct SampWork {
     int *cand_i = nullptr;
     float *sorted_v = nullptr;  // [V] (full-sort path)
     int *sorted_i = nullptr;
-    int *idx_in = nullptr;
-    void *cub_tmp = nullptr;
-    size_t cub_bytes = 0;
+    uint32_t *rs_k = nullptr;       // [V] radix sort: keys and indices between passes
+    int *rs_i = nullptr;
+    unsigned *rs_off = nullptr;     // [256 * ceil(V / 1024)] per (digit, tile) counts, then offsets
     SampMeta *meta = nullptr;
     // per-CTA partials of the parallel passes ([ceil(V / SAMP_CH)])
     float *p_max = nullptr, *p_sum = nullptr, *p_smax = nullptr;
@@ -444,33 +443,97 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_cand_kernel(
     float *lp, uint8_t *keep, const unsigned long long *d_step, int finish_here) {
     __shared__ float sv[SAMP_CAND];
     __shared__ int si[SAMP_CAND];
-    if (w.meta->mode == 2 && !full_scheduled) {
-        // more tied survivors than the candidate list holds and no full sort
-        // was scheduled: report an invalid token instead of a wrong one
-        if (threadIdx.x == 0) *tok = -1;
-        return;
-    }
-    if (w.meta->mode != 1) return;
-    int n = w.meta->n_surv;
-    int np2 = 1;
-    while (np2 < n) np2 <<= 1;
-    for (int i = threadIdx.x; i < np2; i += blockDim.x) {
-        sv[i] = i < n ? w.cand_v[i] : __int_as_float(0x7f800000);
-        si[i] = i < n ? w.cand_i[i] : 0x7fffffff;
-    }
-    __syncthreads();
-    bitonic_sort_asc(sv, si, np2);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        w.sorted_v[V - n + i] = sv[i];
-        w.sorted_i[V - n + i] = si[i];
+    __shared__ int s_gt, s_tie, s_tot, s_wsum[SAMP_THREADS / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int mode = w.meta->mode;
+    const int n = w.meta->n_surv;
+    if (mode == 0 || (mode == 2 && full_scheduled)) return;
+    if (mode == 2) {
+        // more survivors than the candidate list holds under a top-k bound:
+        // ties at the cutoff ck (the values above it are fewer than
+        // k <= 1024). Ascending (value, index) is the ties in index order,
+        // then the values above the cutoff: one ordered pass over the row
+        // places the ties, the others are sorted here.
+        const float ck = w.meta->ck;
+        if (tid == 0) s_gt = s_tie = 0;
+        __syncthreads();
+        for (int c0 = 0; c0 < V; c0 += SAMP_THREADS) {
+            const int i = c0 + tid;
+            const float v = i < V ? w.sw[i] : -INFINITY;
+            if (v > ck) {
+                const int slot = atomicAdd(&s_gt, 1);
+                if (slot < SAMP_NB) {
+                    sv[slot] = v;
+                    si[slot] = i;
+                }
+            }
+            const bool tie = i < V && v == ck;
+            const unsigned bal = __ballot_sync(0xffffffffu, tie);
+            if (lane == 0) s_wsum[warp] = __popc(bal);
+            __syncthreads();
+            if (warp == 0) {   // exclusive prefix of the warps' tie counts
+                const int x = s_wsum[lane];
+                int inc = x;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += y;
+                }
+                s_wsum[lane] = inc - x;
+                if (lane == 31) s_tot = inc;
+            }
+            __syncthreads();
+            if (tie) {
+                const int p = V - n + s_tie + s_wsum[warp] + __popc(bal & ((1u << lane) - 1u));
+                if (p >= V - n && p < V) {
+                    w.sorted_v[p] = v;
+                    w.sorted_i[p] = i;
+                }
+            }
+            __syncthreads();
+            if (tid == 0) s_tie += s_tot;
+            __syncthreads();
+        }
+        const int ngt = s_gt;
+        if (ngt > SAMP_NB || s_tie + ngt != n) {
+            // not a top-k cut with ties: report an invalid token, never a wrong one
+            if (tid == 0) *tok = -1;
+            return;
+        }
+        int np2 = 1;
+        while (np2 < ngt) np2 <<= 1;
+        for (int i = ngt + tid; i < np2; i += blockDim.x) {
+            sv[i] = __int_as_float(0x7f800000);
+            si[i] = 0x7fffffff;
+        }
+        __syncthreads();
+        bitonic_sort_asc(sv, si, np2);
+        for (int i = tid; i < ngt; i += blockDim.x) {
+            w.sorted_v[V - ngt + i] = sv[i];
+            w.sorted_i[V - ngt + i] = si[i];
+        }
+    } else {
+        int np2 = 1;
+        while (np2 < n) np2 <<= 1;
+        for (int i = threadIdx.x; i < np2; i += blockDim.x) {
+            sv[i] = i < n ? w.cand_v[i] : __int_as_float(0x7f800000);
+            si[i] = i < n ? w.cand_i[i] : 0x7fffffff;
+        }
+        __syncthreads();
+        bitonic_sort_asc(sv, si, np2);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            w.sorted_v[V - n + i] = sv[i];
+            w.sorted_i[V - n + i] = si[i];
+        }
     }
     if (!finish_here) return;
+    __syncthreads();   // the sorted survivors (global), seen by every thread
     // exp(v - m) in the final stage's block-transposed layout
     const float m = w.meta->m;
     const int bs = max(1, (V + SAMP_NB - 1) / SAMP_NB);
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
         const int i = V - n + j;
-        w.ev[(i % bs) * SAMP_NB + i / bs] = own_expf(__fsub_rn(sv[j], m));
+        w.ev[(i % bs) * SAMP_NB + i / bs] = own_expf(__fsub_rn(w.sorted_v[i], m));
     }
     __syncthreads();   // the CTA's global writes above, seen by every thread
     finish_stage(V, sp, log_mp, step, w, tok, lp, keep, d_step);
@@ -677,15 +740,131 @@ __global__ void __launch_bounds__(SAMP_THREADS) samp_finish_kernel(
     finish_stage(V, sp, log_mp, step, w, tok, lp, keep, d_step);
 }
 
-__global__ void iota_kernel(int *p, int n) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) p[i] = i;
+// ------------------------------------------------ full-row sort (no top-k)
+//
+// Stable LSD radix sort of the masked row by its order key (ord_key, the
+// float order with -inf first; equal values keep index order), 8 bits per
+// pass: per pass a histogram of each 1024-entry tile, one CTA's exclusive
+// scan over (digit, tile), and a stable scatter. Pass 0 reads the row
+// itself, pass 3 writes the values back as floats; the passes ping-pong
+// between the sorted arrays and a second key/index pair. Every kernel is a
+// no-op unless the row took the full path (mode 2).
+constexpr int RS_TILE = 1024, RS_T = 256;
+
+__global__ void __launch_bounds__(RS_T) rs_hist_kernel(int V, SampWork w, int pass, const uint32_t *keys) {
+    if (w.meta->mode != 2) return;
+    __shared__ unsigned h[256];
+    const int tid = threadIdx.x, c0 = blockIdx.x * RS_TILE, G = gridDim.x;
+    h[tid] = 0u;
+    __syncthreads();
+    for (int r = 0; r < RS_TILE / RS_T; r++) {
+        const int i = c0 + r * RS_T + tid;
+        if (i < V) {
+            const uint32_t k = pass == 0 ? ord_key(w.sw[i]) : keys[i];
+            atomicAdd(&h[(k >> (8 * pass)) & 255u], 1u);
+        }
+    }
+    __syncthreads();
+    w.rs_off[tid * G + blockIdx.x] = h[tid];
+}
+
+// exclusive prefix over the (digit, tile) counts in digit-major order
+__global__ void __launch_bounds__(1024) rs_scan_kernel(SampWork w, int G) {
+    if (w.meta->mode != 2) return;
+    __shared__ unsigned part[1024];
+    const int tid = threadIdx.x, n = 256 * G;
+    const int per = (n + 1023) / 1024, lo = tid * per, hi = min(n, lo + per);
+    unsigned s = 0;
+    for (int i = lo; i < hi; i++) s += w.rs_off[i];
+    part[tid] = s;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+        const unsigned v = tid >= o ? part[tid - o] : 0u;
+        __syncthreads();
+        part[tid] += v;
+        __syncthreads();
+    }
+    unsigned run = part[tid] - s;
+    for (int i = lo; i < hi; i++) {
+        const unsigned c = w.rs_off[i];
+        w.rs_off[i] = run;
+        run += c;
+    }
+}
+
+// stable scatter of one tile: rounds of 256 consecutive entries; in a round
+// an entry's place among equal digits is its lane rank in the warp plus the
+// counts of the earlier warps and of the earlier rounds
+__global__ void __launch_bounds__(RS_T) rs_scatter_kernel(int V, SampWork w, int pass, const uint32_t *kin,
+                                                          const int *iin, uint32_t *kout, int *iout) {
+    if (w.meta->mode != 2) return;
+    __shared__ unsigned base[256];
+    __shared__ unsigned wc[RS_T / 32][256];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, G = gridDim.x;
+    const int c0 = blockIdx.x * RS_TILE;
+    base[tid] = w.rs_off[tid * G + blockIdx.x];
+    for (int r = 0; r < RS_TILE / RS_T; r++) {
+        for (int x = 0; x < RS_T / 32; x++) wc[x][tid] = 0u;
+        __syncthreads();
+        const int i = c0 + r * RS_T + tid;
+        const bool valid = i < V;
+        uint32_t k = 0u;
+        int ix = 0;
+        if (valid) {
+            k = pass == 0 ? ord_key(w.sw[i]) : kin[i];
+            ix = pass == 0 ? i : iin[i];
+        }
+        const unsigned d = valid ? (k >> (8 * pass)) & 255u : 256u;
+        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        const unsigned rank = __popc(peers & ((1u << lane) - 1u));
+        if (valid && rank == 0) wc[warp][d] = __popc(peers);
+        __syncthreads();
+        // per digit (thread = digit): the earlier warps' counts, and the total
+        unsigned run = 0u;
+#pragma unroll
+        for (int x = 0; x < RS_T / 32; x++) {
+            const unsigned c = wc[x][tid];
+            wc[x][tid] = run;
+            run += c;
+        }
+        __syncthreads();
+        if (valid) {
+            const unsigned dst = base[d] + wc[warp][d] + rank;
+            if (pass == 3) {
+                w.sorted_v[dst] = key_val(k);
+                w.sorted_i[dst] = ix;
+            } else {
+                kout[dst] = k;
+                iout[dst] = ix;
+            }
+        }
+        __syncthreads();
+        base[tid] += run;
+    }
+}
+
+// the four passes: sw -> (rs_k, rs_i) -> (sorted as keys) -> (rs_k, rs_i) -> sorted
+static void rs_sort(int V, const SampWork &w, cudaStream_t st) {
+    const int G = (V + RS_TILE - 1) / RS_TILE;
+    uint32_t *ka = w.rs_k, *kb = reinterpret_cast<uint32_t *>(w.sorted_v);
+    int *ia = w.rs_i, *ib = w.sorted_i;
+    const uint32_t *kin = nullptr;
+    const int *iin = nullptr;
+    for (int pass = 0; pass < 4; pass++) {
+        uint32_t *ko = pass % 2 == 0 ? ka : kb;
+        int *io = pass % 2 == 0 ? ia : ib;
+        rs_hist_kernel<<<G, RS_T, 0, st>>>(V, w, pass, kin);
+        rs_scan_kernel<<<1, 1024, 0, st>>>(w, G);
+        rs_scatter_kernel<<<G, RS_T, 0, st>>>(V, w, pass, kin, iin, ko, io);
+        kin = ko;
+        iin = io;
+    }
 }
 
 void samp_work_destroy(SampWork *w) {
     if (!w) return;
     dev_free(w->xw); dev_free(w->sw); dev_free(w->cand_v); dev_free(w->cand_i);
-    dev_free(w->sorted_v); dev_free(w->sorted_i); dev_free(w->idx_in); dev_free(w->cub_tmp);
+    dev_free(w->sorted_v); dev_free(w->sorted_i); dev_free(w->rs_k); dev_free(w->rs_i); dev_free(w->rs_off);
     dev_free(w->meta);
     dev_free(w->p_max); dev_free(w->p_sum); dev_free(w->p_smax); dev_free(w->p_key);
     dev_free(w->hist); dev_free(w->ctr); dev_free(w->ev); dev_free(w->pv);
@@ -709,7 +888,9 @@ SampWork *samp_work_create(int V) {
     w.cand_i = (int *)dev_alloc(sizeof(int) * SAMP_CAND);
     w.sorted_v = (float *)dev_alloc(sizeof(float) * V);
     w.sorted_i = (int *)dev_alloc(sizeof(int) * V);
-    w.idx_in = (int *)dev_alloc(sizeof(int) * V);
+    w.rs_k = (uint32_t *)dev_alloc(sizeof(uint32_t) * V);
+    w.rs_i = (int *)dev_alloc(sizeof(int) * V);
+    w.rs_off = (unsigned *)dev_alloc(sizeof(unsigned) * 256 * (size_t)((V + RS_TILE - 1) / RS_TILE));
     w.meta = (SampMeta *)dev_alloc(sizeof(SampMeta));
     const int G = (V + SAMP_CH - 1) / SAMP_CH;
     w.p_max = (float *)dev_alloc(sizeof(float) * G);
@@ -720,13 +901,9 @@ SampWork *samp_work_create(int V) {
     w.ctr = (unsigned int *)dev_alloc(sizeof(unsigned int) * 2);
     w.ev = (float *)dev_alloc(sizeof(float) * ((V + SAMP_NB - 1) / SAMP_NB) * SAMP_NB);
     w.pv = (float *)dev_alloc(sizeof(float) * ((V + SAMP_NB - 1) / SAMP_NB) * SAMP_NB);
-    size_t tmp = 0;
-    cub::DeviceRadixSort::SortPairs(nullptr, tmp, (const float *)nullptr, (float *)nullptr,
-                                    (const int *)nullptr, (int *)nullptr, V);
-    w.cub_tmp = dev_alloc(tmp);
-    w.cub_bytes = tmp;
-    if (!w.xw || !w.sw || !w.cand_v || !w.cand_i || !w.sorted_v || !w.sorted_i || !w.idx_in || !w.meta ||
-        !w.cub_tmp || !w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev || !w.pv) {
+    if (!w.xw || !w.sw || !w.cand_v || !w.cand_i || !w.sorted_v || !w.sorted_i || !w.rs_k || !w.rs_i ||
+        !w.rs_off || !w.meta || !w.p_max || !w.p_sum || !w.p_smax || !w.p_key || !w.hist || !w.ctr || !w.ev ||
+        !w.pv) {
         samp_work_destroy(pw);
         return nullptr;
     }
@@ -781,14 +958,9 @@ int sample(SampWork *pw, const void *logits, int dtype, int V, const mlxd_sampli
                                                  !need_full);
     MLXD_CHECK(cudaGetLastError());
     if (!need_full) return 0;   // the candidate kernel finished the draw
-    {
-        // ascending (value, index) over the whole vocabulary: a stable radix
-        // sort of the masked values with the indices in order
-        iota_kernel<<<(V + 255) / 256, 256, 0, st>>>(w.idx_in, V);
-        size_t tmp = w.cub_bytes;
-        MLXD_CHECK(cub::DeviceRadixSort::SortPairs(w.cub_tmp, tmp, w.sw, w.sorted_v, w.idx_in,
-                                                   w.sorted_i, V, 0, 32, st));
-    }
+    // ascending (value, index) over the whole row: the stable radix sort
+    rs_sort(V, w, st);
+    MLXD_CHECK(cudaGetLastError());
     samp_exp_kernel<<<(V + 1023) / 1024, 256, 0, st>>>(V, w, need_full);
     samp_finish_kernel<<<1, SAMP_THREADS, 0, st>>>(V, sp, log_mp, step, w, tok, lp, keep, need_full, d_step);
     MLXD_CHECK(cudaGetLastError());

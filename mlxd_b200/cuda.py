@@ -123,6 +123,11 @@ _SIGS = {
                                      P, P, P]),
     "mlxd_cuda_generate_ctl": (C.c_int, [P, P, P, C.c_int, C.c_int, C.POINTER(Sampling), C.c_int,
                                          P, P, P, C.POINTER(GenControl)]),
+    "mlxd_cuda_step_async": (C.c_int, [P, P, P, C.POINTER(Sampling), P, C.c_int, C.c_uint64, P, P, P]),
+    "mlxd_cuda_read_token": (C.c_int, [P, P, P]),
+    "mlxd_cuda_kv_write": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, P]),
+    "mlxd_cuda_kv_gather": (C.c_int, [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P]),
+    "mlxd_cuda_kv_set_offset": (C.c_int, [P, C.c_int, P]),
     "mlxd_cuda_synth_quantized": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_uint64,
                                             C.c_float, P]),
     "mlxd_cuda_synth_bf16": (C.c_int, [P, C.c_size_t, C.c_uint64, C.c_float, C.c_float, P]),

@@ -29,6 +29,26 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert set(syms) == set(cuda._SIGS), set(syms) ^ set(cuda._SIGS)
 
 
+def test_engine_library_exports_every_declared_function():
+    """libmlxd_engine (the C11 engine surface) exports every function its
+    header mlxd_engine.h declares."""
+    import ctypes
+    lib = os.path.join(ROOT, "mlxd_b200", "libmlxd_engine.so")
+    if not os.path.exists(lib):
+        pytest.skip("libmlxd_engine.so not built")
+    L = ctypes.CDLL(lib)
+    src = open(os.path.join(ROOT, "mlxd_b200", "engine", "mlxd_engine.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"#define[^\n]*(\\\n[^\n]*)*", "", src)
+    names = sorted(set(re.findall(r"\b([a-z_][a-z0-9_]*)\s*\([^;{]*\)\s*;", src)))
+    for want in ("engine_model_load", "model_forward", "kvcache_update", "sampler_sample_lazy",
+                 "mlxbridge_async_eval_n", "mlxbridge_item_int32", "mlx_reshape", "mlxd_checkpoint_open"):
+        assert want in names
+    assert len(names) >= 35, names
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
 def test_last_error_is_empty_string_initially():
     assert cuda.lib().mlxd_cuda_last_error() == b""
 

@@ -166,6 +166,27 @@ def test_sampler_sets_and_draws_bit_exact(case, V):
         assert abs(glp - olp) < 1e-4
 
 
+@pytest.mark.parametrize("V,ties", [(151936, 5000), (32768, 4200)])
+def test_sampler_top_k_with_ties_past_the_candidate_list(V, ties):
+    """A top-k cut whose cutoff value is shared by more logits than the
+    candidate list holds (4096): every tie survives (mlx keeps values >= the
+    k-th largest) and the draw is still the oracle's."""
+    rng = np.random.default_rng(V)
+    lf = np.full(V, -3.0, np.float32)
+    idx = rng.permutation(V)
+    lf[idx[:10]] = rng.uniform(2.0, 5.0, 10).astype(np.float32)
+    lf[idx[10:10 + ties]] = 1.0
+    logits = f32_to_bf16(lf)
+    lf = bf16_to_f32(logits)
+    for kw in (dict(temperature=0.7, top_k=50, seed=3), dict(temperature=1.0, top_k=20, top_p=0.95, seed=8)):
+        sp, osp = cuda.sampling(**kw), po.sampling(**kw)
+        for step in range(3):
+            gt, glp, gk = cuda.sample(logits, sp, step=step)
+            ot, olp, ok = po.sample(lf, osp, step=step)
+            assert int(gk.sum()) >= ties and np.array_equal(gk, ok)
+            assert gt == ot and abs(glp - olp) < 1e-4
+
+
 # ---------------------------------------------------------- whole forwards
 
 def fixture_models(golden_dir, name):
