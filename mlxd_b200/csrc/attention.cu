@@ -20,14 +20,18 @@
 // keys once, and both give the same bits at the same position. Head dims
 // other than 64/128 take mlx's composed fallback (q scaled in bf16, bf16
 // scores, precise softmax rounded to bf16, bf16 output).
+#include <cooperative_groups.h>
 #include <mutex>
 #include <stdlib.h>
+#include <vector>
 
 #include "common.cuh"
 #include "gemv_i8.cuh"
 #include "kernels.h"
 
 namespace mlxd {
+
+MLXD_TRACE_BINDER(attention)
 
 constexpr int AB = 64;            // key block of the arithmetic (absolute positions)
 
@@ -60,9 +64,11 @@ constexpr int DA_THREADS = 256;
 constexpr int DR = DA_THREADS / AB;   // blocks per round (thread = position in phase A)
 
 struct DaLayout {
-    size_t kring, vring, qs, stage, newkv, sc, red, total;
+    size_t kring, vring, qs, stage, newkv, sc, red, inbox, total;
 };
-static __host__ __device__ inline DaLayout da_layout(int D, int REP) {
+// inbox_floats: the cluster path's inbox (block results of the CTA's output
+// slice), 0 on the global path
+static __host__ __device__ inline DaLayout da_layout(int D, int REP, size_t inbox_floats = 0) {
     DaLayout l;
     l.kring = 0;
     l.vring = l.kring + (size_t)DR * AB * D * 2;
@@ -71,9 +77,21 @@ static __host__ __device__ inline DaLayout da_layout(int D, int REP) {
     l.newkv = l.stage + (size_t)8 * D * 4;
     l.sc = l.newkv + (size_t)2 * D * 2;
     l.red = l.sc + (size_t)DR * AB * REP * 4;
-    l.total = l.red + (size_t)8 * REP * 4 + 16;
+    l.inbox = l.red + (size_t)8 * REP * 4 + 16;
+    l.total = l.inbox + inbox_floats * 4;
     return l;
 }
+
+// cluster path: blocks an inbox holds, and its floats (per block the CTA's
+// slice of o, then m and l of the slice's head)
+constexpr int DA_NBX = 128;
+template <int D, int REP, int CL>
+__host__ __device__ constexpr int da_es() { return CL > 0 ? REP * D / CL : 2; }
+template <int D, int REP, int CL>
+__host__ __device__ constexpr size_t da_inbox_floats(int nbx) { return (size_t)nbx * (da_es<D, REP, CL>() + 2); }
+
+MLXD_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+MLXD_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 static __device__ int g_attn_err;
 
@@ -123,15 +141,26 @@ MLXD_DEV void lds_rep(float (&o)[REP], const float *p) {
     }
 }
 
-template <int D, int REP>
+// CL = 0: the global path (block results in the cache's step partials, the
+// last CTA of the head group merges); CL > 0: one cluster of CL CTAs per kv
+// head, block results pushed into the inbox of the CTA owning each output
+// slice (distributed shared memory), one cluster barrier, every CTA merges
+// its slice
+template <int D, int REP, int CL>
 __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeArgs a) {
     constexpr int NCH = D / 8;               // 16-byte chunks per row
     constexpr int NP = D / 2;                // feature pairs
     constexpr int DS = D / 32;
+    constexpr int ES = CL > 0 ? da_es<D, REP, CL>() : 2;   // outputs per CTA slice (cluster path)
+    static_assert(CL == 0 || (ES % 2 == 0 && D % ES == 0), "a slice holds whole feature pairs of one head");
     const int NS = gridDim.x, rank = blockIdx.x, kh = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     extern __shared__ __align__(128) unsigned char sm[];
-    const DaLayout Ly = da_layout(D, REP);
+    const DaLayout Ly = da_layout(D, REP, CL > 0 ? da_inbox_floats<D, REP, CL>(a.nbmax) : 0);
+    float *inbox_o = reinterpret_cast<float *>(sm + Ly.inbox);            // [nbmax][ES]
+    float *inbox_ml = inbox_o + (size_t)a.nbmax * ES;                      // [nbmax][2]
+    namespace cg = cooperative_groups;
+    if constexpr (CL > 0) cluster_arrive_relaxed();   // every CTA of the cluster has started
     unsigned char *kring = sm + Ly.kring, *vring = sm + Ly.vring;
     float *qs = reinterpret_cast<float *>(sm + Ly.qs);          // [D][REP], scaled
     float *stage = reinterpret_cast<float *>(sm + Ly.stage) + (size_t)warp * D;
@@ -139,6 +168,7 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     float *sc = reinterpret_cast<float *>(sm + Ly.sc);          // [DR][AB][REP]: z, then p
     float *red = reinterpret_cast<float *>(sm + Ly.red);        // [8 warps][REP]
     int *s_last = reinterpret_cast<int *>(red + 8 * REP);
+    MLXD_TRACE_START
 
     const int pos = *a.d_pos;
     const int T = pos + 1;
@@ -193,6 +223,8 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     }
     pdl_trigger();
     pdl_wait();
+    MLXD_TRACE_WAITED
+    if constexpr (CL > 0) cluster_wait();
 
     // q heads (and the new k) of the group: warp h takes heads h, h + 8, ...
     const int qstride = D * (a.gate ? 2 : 1);
@@ -235,12 +267,20 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
         }
     }
 
+    MLXD_TRACE_T(tr_q_)
     const int pp = tid % AB, s1 = tid / AB;      // phase A: (position, slot)
     const int dp = tid % NP, s2 = tid / NP;      // phase B: (feature pair, slot)
     const size_t gbase = (size_t)kh * a.nbmax;   // the head group's block results
+#ifdef MLXD_TRACE
+    unsigned long long tr_r_[4] = {0, 0, 0, 0};
+#define DA_TR(i) if (r0 == 0) tr_r_[i] = gtime();
+#else
+#define DA_TR(i)
+#endif
     for (int r0 = 0; r0 < nbm; r0 += DR) {
         cp_async_wait<1>();   // this round's K (V may still be in flight)
         __syncthreads();      // (first round: also orders the q and new-k stores)
+        DA_TR(0)
         if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + DR) {
             unsigned char *blk = kring + (size_t)((blast - mb0) % DR) * AB * D * 2;
             const int r = pos - blast * AB;
@@ -294,8 +334,10 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
             const float mb = fmaxf(red[(2 * s1) * REP + h], red[(2 * s1 + 1) * REP + h]);
             sc[(s1 * AB + pp) * REP + h] = z[h] == -INFINITY ? 0.f : own_expf(__fsub_rn(z[h], mb));
         }
+        DA_TR(1)
         cp_async_wait<1>();   // this round's V
         __syncthreads();
+        DA_TR(2)
         if (has_new && blast - mb0 >= r0 && blast - mb0 < r0 + DR) {
             unsigned char *blk = vring + (size_t)((blast - mb0) % DR) * AB * D * 2;
             const int r = pos - blast * AB;
@@ -327,22 +369,43 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
                 }
                 l = __fadd_rn(l, ps[q * REP + lh]);
             }
-            const size_t gb = (gbase + (size_t)(mb0 + ib - bfirst)) * REP;
+            const int bi = mb0 + ib - bfirst;
+            if constexpr (CL == 0) {
+                const size_t gb = (gbase + (size_t)bi) * REP;
 #pragma unroll
-            for (int h = 0; h < REP; h++)
-                *reinterpret_cast<float2 *>(a.part_o + (gb + h) * D + 2 * dp) = make_float2(o0[h], o1[h]);
-            if (dp < REP) {
-                a.part_l[gb + dp] = l;
-                a.part_m[gb + dp] = fmaxf(red[(2 * s2) * REP + dp], red[(2 * s2 + 1) * REP + dp]);
+                for (int h = 0; h < REP; h++)
+                    *reinterpret_cast<float2 *>(a.part_o + (gb + h) * D + 2 * dp) = make_float2(o0[h], o1[h]);
+                if (dp < REP) {
+                    a.part_l[gb + dp] = l;
+                    a.part_m[gb + dp] = fmaxf(red[(2 * s2) * REP + dp], red[(2 * s2 + 1) * REP + dp]);
+                }
+            } else {
+                cg::cluster_group cluster = cg::this_cluster();
+#pragma unroll
+                for (int h = 0; h < REP; h++) {
+                    const int e = h * D + 2 * dp, dst = e / ES;
+                    *reinterpret_cast<float2 *>(cluster.map_shared_rank(inbox_o + (size_t)bi * ES + (e - dst * ES),
+                                                                        dst)) = make_float2(o0[h], o1[h]);
+                }
+                if (dp < REP) {
+                    const float2 ml = make_float2(fmaxf(red[(2 * s2) * REP + dp], red[(2 * s2 + 1) * REP + dp]), l);
+                    for (int r = dp * (D / ES); r < (dp + 1) * (D / ES); r++)
+                        *reinterpret_cast<float2 *>(cluster.map_shared_rank(inbox_ml + (size_t)bi * 2, r)) = ml;
+                }
             }
         }
         __syncthreads();
+        DA_TR(3)
         if (r0 + DR < nbm) {
             for (int s = 0; s < DR; s++) load_block(r0 + DR + s, true);
         }
         cp_async_commit();
     }
+#undef DA_TR
+    MLXD_TRACE_REC(tid == 0 && nbm > 0, 0x25, tr_r_[0], tr_r_[1], tr_r_[2])
+    MLXD_TRACE_REC(tid == 0 && nbm > 0, 0x26, tr_r_[3], tr_q_, (unsigned long long)nbm)
     cp_async_wait<0>();
+    MLXD_TRACE_T(tr_ab_)
     // the new position's k/v rows into the cache
     if (has_new) {
         uint16_t *kd = a.kc + ((size_t)kh * a.cap + pos % a.cap) * D;
@@ -352,12 +415,76 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
             vd[d] = newv[d];
         }
     }
+    if constexpr (CL > 0) {
+        // every block result is in its owner's inbox after the barrier; this
+        // CTA merges its slice (outputs rank*ES .. +ES of the group, one head)
+        cg::this_cluster().sync();
+        MLXD_TRACE_T(tr_cs_)
+        const int e0 = rank * ES, hh = e0 / D, d0 = e0 % D;
+        const int nmerge = nbt <= a.nbmax ? nbt : 0;
+        float *f_s = reinterpret_cast<float *>(sm + Ly.kring);   // the rings are free
+        int *g_s = reinterpret_cast<int *>(f_s + DA_NBX);
+        for (int b = tid; b < nmerge; b += DA_THREADS) {
+            float mp = -INFINITY;
+            for (int bb = 0; bb < b; bb++) mp = fmaxf(mp, inbox_ml[2 * bb]);
+            const float mb = inbox_ml[2 * b];
+            int g = 0;
+            float f = 1.f;
+            if (mp != -INFINITY) {
+                g = mb > mp ? 1 : 2;
+                f = own_expf(g == 1 ? __fsub_rn(mp, mb) : __fsub_rn(mb, mp));
+            }
+            f_s[b] = f;
+            g_s[b] = g;
+        }
+        __syncthreads();
+        for (int p = tid; p < ES / 2; p += DA_THREADS) {
+            double L = 0.0, O0 = 0.0, O1 = 0.0;
+#pragma unroll 4
+            for (int b = 0; b < nmerge; b++) {
+                const float2 o = *reinterpret_cast<const float2 *>(inbox_o + (size_t)b * ES + 2 * p);
+                const double l = (double)inbox_ml[2 * b + 1], f = (double)f_s[b];
+                const int g = g_s[b];
+                if (g == 0) {
+                    L = l;
+                    O0 = (double)o.x;
+                    O1 = (double)o.y;
+                } else if (g == 1) {
+                    L = __fma_rn(L, f, l);
+                    O0 = __fma_rn(O0, f, (double)o.x);
+                    O1 = __fma_rn(O1, f, (double)o.y);
+                } else {
+                    L = __fma_rn(l, f, L);
+                    O0 = __fma_rn((double)o.x, f, O0);
+                    O1 = __fma_rn((double)o.y, f, O1);
+                }
+            }
+            const int hg = kh * REP + hh, d = d0 + 2 * p;
+            uint16_t v0 = d2bf(O0 / L), v1 = d2bf(O1 / L);
+            if (a.gate) {
+                const uint16_t *gp = a.qkv + (size_t)hg * qstride + D + d;
+                v0 = f2bf(__fmul_rn(bf2f(v0), sigmoid_bf16(bf2f(gp[0]))));
+                v1 = f2bf(__fmul_rn(bf2f(v1), sigmoid_bf16(bf2f(gp[1]))));
+            }
+            *reinterpret_cast<uint32_t *>(a.out + (size_t)hg * D + d) = (uint32_t)v0 | ((uint32_t)v1 << 16);
+        }
+        MLXD_TRACE_T(tr_ce_)
+        MLXD_TRACE_REC(tid == 0, 0x27, tr_ab_, tr_cs_, tr_ce_)
+        MLXD_TRACE_END(0x24)
+        return;
+    }
     // the last CTA of the head group merges its blocks
     __threadfence();
     __syncthreads();
     if (tid == 0) *s_last = atomicAdd(a.cnt + kh, 1) == NS - 1;
     __syncthreads();
-    if (!*s_last) return;
+    MLXD_TRACE_T(tr_arr_)
+    MLXD_TRACE_REC(tid == 0, 0x22, tr_q_, tr_ab_, tr_arr_)
+    if (!*s_last) {
+        MLXD_TRACE_END(0x20)
+        return;
+    }
+    MLXD_TRACE_RESTART
     __threadfence();
     const int nmerge = nbt <= a.nbmax ? nbt : 0;
     // The merge runs in chunks of MCH blocks staged in shared memory (the
@@ -365,13 +492,13 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     // (block, head) gets its factor from the running maximum before it (a
     // prefix maximum, in parallel), then thread (head, feature pair) runs its
     // f64 chain over the chunk in key order.
-    constexpr int MCH = (2 * DR * AB * D * 2 - REP * 4) / (REP * (D + 4) * 4);
+    constexpr int MCH = (2 * DR * AB * D * 2 - 64 * 4) / (REP * (D + 4) * 4) / 4 * 4;
     constexpr int NE = (REP * NP + DA_THREADS - 1) / DA_THREADS;
     float *o_s = reinterpret_cast<float *>(sm);                 // [MCH][REP][D]
-    float *m_s = o_s + (size_t)MCH * REP * D;                    // [MCH][REP]
-    float *l_s = m_s + MCH * REP;
+    float *m_s = o_s + (size_t)MCH * REP * D;                    // [MCH][REP] (+ REP: the chunk's maximum)
+    float *l_s = m_s + MCH * REP + 16;
     float *f_s = l_s + MCH * REP;
-    int *g_s = reinterpret_cast<int *>(f_s + MCH * REP);         // 0 first, 1 new maximum, 2 other
+    int *g_s = reinterpret_cast<int *>(f_s + MCH * REP);         // 1 new maximum (or first), 2 other
     float *Mrun = reinterpret_cast<float *>(g_s + MCH * REP);    // [REP]
     double L[NE], O0[NE], O1[NE];
 #pragma unroll
@@ -380,62 +507,61 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
     for (int c0 = 0; c0 < nmerge; c0 += MCH) {
         const int nb = min(MCH, nmerge - c0);
         __syncthreads();   // the previous chunk is consumed (first: Mrun is set)
+        // the chunk's results into shared memory, every copy in flight at once
         const size_t r0 = (gbase + c0) * REP;
-        const float4 *src = reinterpret_cast<const float4 *>(a.part_o + r0 * D);
-        for (int i = tid; i < nb * REP * D / 4; i += DA_THREADS) reinterpret_cast<float4 *>(o_s)[i] = __ldcg(src + i);
+        const float *src = a.part_o + r0 * D;
+        for (int i = tid; i < nb * REP * D / 4; i += DA_THREADS) cp_async16(o_s + 4 * i, src + 4 * i);
+        cp_async_commit();
         for (int i = tid; i < nb * REP; i += DA_THREADS) {
             m_s[i] = __ldcg(a.part_m + r0 + i);
             l_s[i] = __ldcg(a.part_l + r0 + i);
         }
+        cp_async_wait<0>();
         __syncthreads();
+        MLXD_TRACE_T(tr_ld_)
+        // factor of (block b, head h): the running maximum before it is the
+        // maximum of the earlier blocks; the thread of the chunk's last block
+        // also leaves the maximum after the chunk
         for (int i = tid; i < nb * REP; i += DA_THREADS) {
             const int b = i / REP, h = i % REP;
             float mp = Mrun[h];
             for (int bb = 0; bb < b; bb++) mp = fmaxf(mp, m_s[bb * REP + h]);
             const float mb = m_s[i];
-            int g = 0;
+            // first block (sums still zero): fma(0, 1, x) = x
             float f = 1.f;
+            int g = 1;
             if (mp != -INFINITY) {
                 g = mb > mp ? 1 : 2;
                 f = own_expf(g == 1 ? __fsub_rn(mp, mb) : __fsub_rn(mb, mp));
             }
             g_s[i] = g;
             f_s[i] = f;
+            if (b == nb - 1) m_s[MCH * REP + h] = fmaxf(mp, mb);
         }
         __syncthreads();
+        MLXD_TRACE_T(tr_f_)
 #pragma unroll
         for (int q = 0; q < NE; q++) {
             const int e = tid + q * DA_THREADS;
             if (e < REP * NP) {
                 const int h = e / NP, fp = e % NP;
-#pragma unroll 4
+#pragma unroll 8
                 for (int b = 0; b < nb; b++) {
                     const int i = b * REP + h;
                     const float2 o = *reinterpret_cast<const float2 *>(o_s + (size_t)i * D + 2 * fp);
                     const double l = (double)l_s[i], f = (double)f_s[i];
-                    const int g = g_s[i];
-                    if (g == 0) {
-                        L[q] = l;
-                        O0[q] = (double)o.x;
-                        O1[q] = (double)o.y;
-                    } else if (g == 1) {
-                        L[q] = __fma_rn(L[q], f, l);
-                        O0[q] = __fma_rn(O0[q], f, (double)o.x);
-                        O1[q] = __fma_rn(O1[q], f, (double)o.y);
-                    } else {
-                        L[q] = __fma_rn(l, f, L[q]);
-                        O0[q] = __fma_rn((double)o.x, f, O0[q]);
-                        O1[q] = __fma_rn((double)o.y, f, O1[q]);
-                    }
+                    // new maximum: S = fma(S, s, x); otherwise S = fma(x, e, S)
+                    const bool nm = g_s[i] == 1;
+                    L[q] = __fma_rn(nm ? L[q] : l, f, nm ? l : L[q]);
+                    O0[q] = __fma_rn(nm ? O0[q] : (double)o.x, f, nm ? (double)o.x : O0[q]);
+                    O1[q] = __fma_rn(nm ? O1[q] : (double)o.y, f, nm ? (double)o.y : O1[q]);
                 }
             }
         }
         __syncthreads();
-        if (tid < REP) {
-            float M = Mrun[tid];
-            for (int b = 0; b < nb; b++) M = fmaxf(M, m_s[b * REP + tid]);
-            Mrun[tid] = M;
-        }
+        MLXD_TRACE_T(tr_c_)
+        MLXD_TRACE_REC(tid == 0 && c0 == 0, 0x23, tr_ld_, tr_f_, tr_c_)
+        if (tid < REP) Mrun[tid] = m_s[MCH * REP + tid];
     }
 #pragma unroll
     for (int q = 0; q < NE; q++) {
@@ -452,44 +578,137 @@ __global__ void __launch_bounds__(DA_THREADS, 1) attn_decode_kernel(AttnDecodeAr
         *reinterpret_cast<uint32_t *>(a.out + (size_t)hg * D + 2 * fp) = (uint32_t)v0 | ((uint32_t)v1 << 16);
     }
     if (tid == 0) a.cnt[kh] = 0;   // ready for the next launch
+    MLXD_TRACE_END(0x21)
 }
 
-// CTAs per kv head: about DR blocks each over the cache's attended span,
-// all kv heads' CTAs on distinct SMs
+// global path: CTAs per kv head, as many as the SMs allow (one block each
+// at most, if the span is short), all kv heads' CTAs on distinct SMs
 static int da_splits(const AttnDecodeArgs &a) {
     const int sms = num_sms();
-    int ns = (a.nbmax + DR - 1) / DR;
+    int ns = a.nbmax;
     const int cap_ns = sms / a.hkv > 0 ? sms / a.hkv : 1;
     if (ns > cap_ns) ns = cap_ns;
     return ns < 1 ? 1 : ns;
 }
 
-template <int D, int REP>
-static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
-    auto kern = attn_decode_kernel<D, REP>;
-    // one CTA per SM (dynamic shared memory above half of an SM's): with two
-    // attention CTAs on one SM the projections that follow ran slower on
-    // those SMs for the rest of the step
-    size_t smem = da_layout(D, REP).total;
-    if (smem < 116 * 1024) smem = 116 * 1024;
-    if (!smem_allowed((const void *)kern, smem)) return -1;
+// One CTA per SM (dynamic shared memory above half of an SM's): with two
+// attention CTAs on one SM the projections that follow ran slower on those
+// SMs for the rest of the step
+template <int D, int REP, int CL>
+static size_t da_smem(const AttnDecodeArgs &a) {
+    const size_t t = da_layout(D, REP, CL > 0 ? da_inbox_floats<D, REP, CL>(a.nbmax) : 0).total;
+    return t > 116 * 1024 ? t : 116 * 1024;
+}
+
+// cudaFuncSetAttribute is per device: clusters above 8 CTAs allowed once per
+// (kernel, device)
+static bool nonportable_allowed(const void *kern) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto &e : done)
+        if (e.first == kern && e.second == dev) return true;
+    if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1), "cluster attribute"))
+        return false;
+    done.push_back({kern, dev});
+    return true;
+}
+
+template <int D, int REP, int CL>
+static cudaLaunchConfig_t da_config(const AttnDecodeArgs &a, size_t smem, cudaLaunchAttribute *attr, bool pdl,
+                                    cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(da_splits(a), a.hkv);
+    cfg.gridDim = dim3(CL > 0 ? CL : da_splits(a), a.hkv);
     cfg.blockDim = dim3(DA_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int n = 0;
+    if (CL > 0) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = CL;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        n++;
+    }
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    MLXD_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
+    cfg.numAttrs = n;
+    return cfg;
+}
+
+template <int D, int REP, int CL>
+static bool da_prepare(const AttnDecodeArgs &a) {
+    auto kern = attn_decode_kernel<D, REP, CL>;
+    const size_t smem = da_smem<D, REP, CL>(a);
+    if (smem > 227 * 1024 || !smem_allowed((const void *)kern, smem)) return false;
+    return CL <= 8 || nonportable_allowed((const void *)kern);
+}
+
+// whether hkv clusters of CL CTAs are resident at once on this device
+template <int D, int REP, int CL>
+static bool da_fits(const AttnDecodeArgs &a) {
+    if (a.nbmax > DA_NBX || !da_prepare<D, REP, CL>(a)) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = da_config<D, REP, CL>(a, da_smem<D, REP, CL>(a), attr, false, nullptr);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<D, REP, CL>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return n >= a.hkv;
+}
+
+// the path per (device, kv heads, inbox size): clusters of 16 when hkv of
+// them are resident at once, else the global path (spans beyond the inbox
+// too)
+template <int D, int REP>
+static int da_choice(const AttnDecodeArgs &a) {
+    static std::mutex mu;
+    static std::vector<std::pair<std::pair<int, long long>, int>> memo;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const long long key = ((long long)a.hkv << 32) | (unsigned)a.nbmax;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (auto &m : memo)
+            if (m.first.first == dev && m.first.second == key) return m.second;
+    }
+    // clusters of 8 (hkv x 8 CTAs, 4+ blocks each at 2k positions) measured
+    // slower than the global path over all SMs
+    const int cl = da_fits<D, REP, 16>(a) ? 16 : 0;
+    std::lock_guard<std::mutex> lock(mu);
+    memo.push_back({{dev, key}, cl});
+    return cl;
+}
+
+template <int D, int REP, int CL>
+static int da_launch_cl(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+    if (!da_prepare<D, REP, CL>(a)) return -1;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = da_config<D, REP, CL>(a, da_smem<D, REP, CL>(a), attr, pdl, st);
+    MLXD_CHECK(cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, REP, CL>, a));
     return 0;
 }
 
 template <int D, int REP>
+static int da_launch(const AttnDecodeArgs &a, cudaStream_t st, bool pdl) {
+    if (da_choice<D, REP>(a) == 16) return da_launch_cl<D, REP, 16>(a, st, pdl);
+    return da_launch_cl<D, REP, 0>(a, st, pdl);
+}
+
+template <int D, int REP>
 static int da_sms(const AttnDecodeArgs &a) {
-    return da_splits(a) * a.hkv;
+    const int cl = da_choice<D, REP>(a);
+    return (cl > 0 ? cl : da_splits(a)) * a.hkv;
 }
 
 // result floats per kv head of a cache whose attended span holds at most

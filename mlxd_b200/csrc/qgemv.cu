@@ -25,6 +25,8 @@
 
 namespace mlxd {
 
+MLXD_TRACE_BINDER(qgemv)
+
 // ------------------------------------------------------------------ repack
 
 // Integer-MMA tile layout (group 64): lane L = 4g + t of tile (rb, grp) holds
@@ -224,6 +226,7 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(16) float s_red[NW];
     __shared__ unsigned long long s_key[NW];
+    MLXD_TRACE_START
     const int nbk = a.cols / 512;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = lane & 3, gq = lane >> 2;
     const int n_units = a.rows / 16 / UNIT_RB;
@@ -277,6 +280,7 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
     I8Pre<NT> pre;
     i8_stage_pre<NT>(pre, PRO == PRO_RMSNORM ? a.norm_w : nullptr, a.cols);
     pdl_wait();
+    MLXD_TRACE_WAITED
     if (res_mine) cp_async_wait<0>();
     uint32_t *xbw = reinterpret_cast<uint32_t *>(smem_raw + L.xb);
     GTab *gt = reinterpret_cast<GTab *>(smem_raw + L.gt);
@@ -370,6 +374,7 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
             if (m) atomicMax(a.amax, m);
         }
     }
+    MLXD_TRACE_END(0x10 + EPI + 8 * PRO)
 }
 
 int num_sms() {

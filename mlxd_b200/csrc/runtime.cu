@@ -62,6 +62,23 @@ void dev_free(void *p) {
 
 using namespace mlxd;
 
+#ifdef MLXD_TRACE
+// timeline trace (instrumented builds only): one device buffer for every
+// traced kernel, word 0 the record count, records of 4 words from word 4
+namespace mlxd {
+void trace_bind_sampler(unsigned long long *p);
+void trace_bind_qgemv(unsigned long long *p);
+void trace_bind_attention(unsigned long long *p);
+void trace_bind_tp(unsigned long long *p);
+}  // namespace mlxd
+extern "C" void mlxd_trace_bind(unsigned long long *p) {
+    mlxd::trace_bind_sampler(p);
+    mlxd::trace_bind_qgemv(p);
+    mlxd::trace_bind_attention(p);
+    mlxd::trace_bind_tp(p);
+}
+#endif
+
 extern "C" {
 
 const char *mlxd_cuda_last_error(void) { return g_err; }

@@ -38,6 +38,8 @@
 
 namespace mlxd {
 
+MLXD_TRACE_BINDER(tp)
+
 constexpr int TP_SLICE = 128;      // rows per CTA (and per flag)
 constexpr int TP_MAX = 8;          // ranks
 
@@ -94,7 +96,9 @@ __global__ void __launch_bounds__(TP_SLICE) tp_sum_kernel(TpPeers peers, unsigne
                                                           size_t off_vflag, int n, int rank, int H, int slices,
                                                           const double *part, const uint16_t *res, uint16_t *out,
                                                           const unsigned *seq, int L2, int idx, int *err) {
+    MLXD_TRACE_START
     pdl_wait();
+    MLXD_TRACE_WAITED
     const int c = blockIdx.x, tid = threadIdx.x, row = c * TP_SLICE + tid;
     const unsigned epoch = *seq * (unsigned)L2 + (unsigned)idx + 1u;
     const int buf = idx & 1;
@@ -123,6 +127,7 @@ __global__ void __launch_bounds__(TP_SLICE) tp_sum_kernel(TpPeers peers, unsigne
         for (int src = 0; src < n; src++) s += __ldcv(slots + (size_t)src * H + row);
         out[row] = f2bf(__fadd_rn(bf2f(res[row]), bf2f(d2bf(s))));
     }
+    MLXD_TRACE_END(0x30)
 }
 
 // greedy: the ranks' argmax keys; every rank takes the largest and ends the

@@ -297,16 +297,22 @@ def test_incremental_equals_full_on_gpu():
                                        (cuda.QWEN3, dict(n_kv_heads=4)),
                                        (cuda.QWEN3, dict(n_heads=16, n_kv_heads=2)),
                                        (cuda.QWEN3, dict(head_dim=64, n_heads=8, n_kv_heads=1)),
-                                       (cuda.QWEN3, dict(head_dim=64, n_heads=8, n_kv_heads=4))])
+                                       (cuda.QWEN3, dict(head_dim=64, n_heads=8, n_kv_heads=4)),
+                                       (cuda.QWEN3, dict(kvcap=9000, max_pos=9000)),
+                                       (cuda.QWEN3, dict(kvcap=9000, max_pos=9000, n_kv_heads=8)),
+                                       (cuda.MISTRAL, dict(window=8500, max_pos=9000))])
 def test_decode_attention_variants_bit_exact(family, kw):
-    """The cluster decode attention on a plain cache, wrapping sliding-window
-    rings (positions spread over several CTAs), and 1, 2, 4 and 8 query heads
-    per kv head at head dims 128 and 64."""
+    """The decode attention on a plain cache, wrapping sliding-window rings
+    (positions spread over several CTAs), and 1, 2, 4 and 8 query heads per kv
+    head at head dims 128 and 64; caches whose attended span exceeds the
+    cluster inbox (more than 128 blocks) take the global path."""
+    kw = dict(kw)
+    kvcap = kw.pop("kvcap", None)
     cfg = qwen3_small(family=family, layers=2, **kw)
     m, o = synth_pair(cfg, seed=6)
     rng = np.random.default_rng(6)
     ids = rng.integers(0, cfg.vocab, 330).tolist()
-    kv = m.new_kv(kw["window"] + 16 if kw.get("window") else 340)
+    kv = m.new_kv(kvcap or (kw["window"] + 16 if kw.get("window") else 340))
     okv = o.new_kv(340)
     for a0 in range(0, 320, 16):
         m.forward(kv, ids[a0:a0 + 16], want_logits=False)
