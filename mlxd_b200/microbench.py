@@ -9,6 +9,7 @@ weights + bf16 scale/bias per group + x in + y out) / mean launch time.
     python -m mlxd_b200.microbench [--shape gate_up] [--iters N] [--copies C]
     python -m mlxd_b200.microbench --prefill-gemm   # tcgen05 GEMM, 24576 x 4096, 512 tokens
     python -m mlxd_b200.microbench --attention      # decode attention, 32/8 heads, context 2048
+    python -m mlxd_b200.microbench --prefill-layer  # chunked 2048-token prefill of one Qwen3-8B layer
     python -m mlxd_b200.microbench --sampler        # sampler, V 151936, T 0.7 k 50 p 0.9 rep 1.1
 """
 import argparse
@@ -97,6 +98,25 @@ def decode_attention(context=2048, steps=6):
     return {"decode_attention": {"context": context, "steps": steps, "last_token": t}}
 
 
+def prefill_layer(prompt=2048, chunk=512):
+    """A chunked prefill of `prompt` tokens through one Qwen3-8B-shaped decoder
+    layer (vocab 1024, so the projections, attention and norms dominate), for
+    launch lists of the prefill's kernels."""
+    cfg = cuda.synth_config(hidden=4096, layers=1, n_heads=32, n_kv_heads=8, head_dim=128, inter=12288,
+                            vocab=1024, max_pos=prompt + 64)
+    dev = cuda.synth_device_tensors(cfg, seed=0)
+    m = cuda.Model(cfg, dev, on_device=True)
+    for v in dev.values():
+        v[0].free()
+    kv = m.new_kv(prompt + 64)
+    ids = cuda.synth_prompt(prompt, cfg.vocab, 0).tolist()
+    for a in range(0, prompt, chunk):
+        m.forward(kv, ids[a:a + chunk], want_logits=False)
+    cuda.synchronize()
+    m.close()
+    return {"prefill_layer": {"prompt": prompt, "chunk": chunk}}
+
+
 SAMPLER_DEFAULT = dict(temperature=0.7, top_k=50, top_p=0.9, seed=7, repetition_penalty=1.1,
                       repetition_context=256)
 
@@ -148,6 +168,8 @@ def main():
     ap.add_argument("--copies", type=int, default=None)
     ap.add_argument("--prefill-gemm", action="store_true", help="run the tcgen05 prefill GEMM workload")
     ap.add_argument("--attention", action="store_true", help="run the decode attention workload")
+    ap.add_argument("--prefill-layer", action="store_true",
+                    help="chunked 2048-token prefill through one Qwen3-8B-shaped layer")
     ap.add_argument("--sampler", action="store_true", help="run the sampler on a 151936-entry row")
     ap.add_argument("--sampler-settings", default=None,
                     help="JSON sampling settings for --sampler (default: the sampled-decode settings)")
@@ -158,6 +180,9 @@ def main():
         return
     if args.attention:
         print(json.dumps(decode_attention()))
+        return
+    if args.prefill_layer:
+        print(json.dumps(prefill_layer()))
         return
     if args.sampler:
         print(json.dumps(sampler(settings=json.loads(args.sampler_settings) if args.sampler_settings else None)))

@@ -73,13 +73,33 @@ def _rank_parity(rank, size, uid_q, out_q):
 
 
 def _spawn(target, size, extra=()):
+    """Start one process per rank. Returns the processes and the queues: the
+    caller keeps every queue referenced until the ranks are done (a queue
+    that is garbage-collected unlinks its semaphore, and a rank still
+    starting up then fails to open it)."""
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     ctx = mp.get_context("spawn")
     uid_q, out_q = ctx.Queue(), ctx.Queue()
     procs = [ctx.Process(target=target, args=(r, size, uid_q, out_q) + tuple(extra)) for r in range(size)]
     for p in procs:
         p.start()
-    return procs, out_q
+    return procs, out_q, uid_q
+
+
+def _get(q, procs, timeout):
+    """The next result, failing early when a rank has exited with an error."""
+    t_end = time.time() + timeout
+    while time.time() < t_end:
+        try:
+            return q.get(timeout=2)
+        except Exception:
+            bad = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if bad:
+                for p in procs:
+                    if p.exitcode is None:
+                        p.kill()
+                raise AssertionError("a rank exited with %s" % bad)
+    raise AssertionError("no result within %d s" % timeout)
 
 
 def _finish(procs):
@@ -96,10 +116,10 @@ def _finish(procs):
 def test_tp_matches_oracle_bit_exact(size):
     if _gpu_count() < size:
         pytest.skip(f"needs {size} GPUs")
-    procs, out_q = _spawn(_rank_parity, size)
+    procs, out_q, uid_q = _spawn(_rank_parity, size)
     res = {}
     for _ in range(size):
-        r, *rest = out_q.get(timeout=600)
+        r, *rest = _get(out_q, procs, 600)
         res[r] = rest
     _finish(procs)
     cfg = cuda.synth_config(**KW)
@@ -159,8 +179,8 @@ def test_tp_peer_that_never_arrives_fails_the_step():
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     go_q = ctx.Queue()
-    procs, out_q = _spawn(_rank_stall, 2, (go_q,))
-    msg, dt, ok = out_q.get(timeout=300)
+    procs, out_q, uid_q = _spawn(_rank_stall, 2, (go_q,))
+    msg, dt, ok = _get(out_q, procs, 300)
     _finish(procs)
     assert "gave up waiting for a peer GPU" in msg, msg
     # six exchanges (two per layer), each giving up after about a second
