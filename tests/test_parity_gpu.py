@@ -516,3 +516,36 @@ def test_config_c3_qwen3_8b_shortened():
     gt, ot, g, ol, (ok, mx, mr) = run_config(cfg, 128, 64)
     assert np.array_equal(gt, ot) and len(gt) == 64
     assert same_bits(g, ol) and ok
+
+
+def test_config_c4_mistral_window_shortened():
+    """C4 shortened to 2 layers: Mistral-7B width (hidden 4096, 32/8 heads,
+    head dim 128, MLP 14336, vocab 32768), sliding window 4096 over a ring of
+    4607 slots, an 8192-token prompt in 512-token chunks (the ring wraps
+    twice), then 48 sampled tokens at temperature 0.7, top-k 50, top-p 0.9,
+    repetition penalty 1.1 over the last 256 tokens. The oracle keeps a dense
+    cache and masks the window: identical tokens, logprobs within 1e-4."""
+    cfg = cuda.synth_config(hidden=4096, layers=2, n_heads=32, n_kv_heads=8, head_dim=128, inter=14336,
+                            vocab=32768, family=cuda.MISTRAL, window=4096, max_pos=8192 + 64)
+    m, o = baseline_pair(cfg, seed=2)
+    kw = dict(temperature=0.7, top_k=50, top_p=0.9, repetition_penalty=1.1, repetition_context=256, seed=3)
+    prompt = cuda.synth_prompt(8192, cfg.vocab, seed=2)
+    kv = m.new_kv(4096 + 512 - 1)
+    gt, glp, _ = m.generate(prompt, 48, sp=cuda.sampling(**kw), logprobs=True, kv=kv, chunk=512)
+    ot, olp, _ = o.generate(prompt, 48, sp=po.sampling(**kw), chunk=512)
+    assert len(gt) == 48
+    assert np.array_equal(gt, ot)
+    assert np.abs(glp - olp).max() < 1e-4
+
+
+def test_config_c5_llama3_70b_shortened():
+    """C5 shortened to 2 layers on one GPU: Llama-3-70B width (hidden 8192,
+    64/8 heads, head dim 128, MLP 28672, vocab 128256) with the llama3-scaled
+    RoPE (theta 500000, factor 8, low 1, high 4, original 8192), 512 prompt
+    ids then 32 greedy tokens: identical tokens and first-position logits."""
+    cfg = cuda.synth_config(hidden=8192, layers=2, n_heads=64, n_kv_heads=8, head_dim=128, inter=28672,
+                            vocab=128256, family=cuda.LLAMA, theta=500000.0, llama3=(8.0, 1.0, 4.0, 8192),
+                            max_pos=1024)
+    gt, ot, g, ol, (ok, mx, mr) = run_config(cfg, 512, 32)
+    assert np.array_equal(gt, ot) and len(gt) == 32
+    assert same_bits(g, ol) and ok
