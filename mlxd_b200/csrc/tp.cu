@@ -7,22 +7,25 @@
 // in the library's projection arithmetic. The step needs, on every rank,
 // bf16(h + bf16(sum of the partials)), which equals the one-GPU result. A
 // mailbox per rank (cudaMalloc'd, mapped into every peer with cudaIpc) holds,
-// per exchange parity, one slot of rows per source rank and one flag per
-// (source rank, slice of 128 rows):
+// per exchange parity, one slot of rows per source rank. A row travels as one
+// 16-byte line {low word, epoch, high word, epoch} written by a single vector
+// store (plain st.global over NVLink, no bulk or TMA copy): each 8-byte half
+// is written at once, so a reader that sees the epoch in both halves has the
+// whole value, and no fence or separate flag is needed (the LL protocol of
+// NCCL's low-latency kernels):
 //
-//   CTA c of every rank stores its slice of the partial into slot [rank] of
-//   every rank's mailbox (plain st.global over NVLink, no bulk or TMA copy),
-//   fences at system scope and writes the epoch into flag [rank][c] of every
-//   rank; then it waits (bounded) until flags [0..N)[c] of its own mailbox
-//   hold the epoch, adds the N slots in rank order and the residual.
+//   thread r of CTA c of every rank stores row c*128 + r of its partial into
+//   slot [rank] of every rank's mailbox; then it polls (bounded) slots
+//   [0..N) of its own mailbox until each holds the epoch, adds the N values in
+//   rank order and the residual.
 //
 // Every rank keeps a device step counter s, advanced once at the end of
 // every one-token step (all ranks run the same steps). The epoch of exchange
 // idx of step s is s * 2L + idx + 1, read on the device, so a captured graph
 // replays it, and no epoch repeats across generations or caches.
 // Exchanges alternate between two buffers: when a rank writes exchange e + 2
-// into a peer's buffer, it has seen every peer's flag of exchange e + 1, so
-// every peer has finished reading exchange e. A wait that exceeds its limit
+// into a peer's buffer, it has seen every peer's rows of exchange e + 1, which
+// each peer stored after finishing exchange e (its reads included). A wait that exceeds its limit
 // sets the error word and returns; the host reports it (no hang, no trap).
 // The greedy argmax keys and, for sampled decoding, the vocabulary shards of
 // the logits travel the same way in mailboxes of their own.
@@ -49,7 +52,7 @@ struct TpPeers {
 
 struct TpState {
     int n = 1, rank = 0, H = 0, slices = 0, L2 = 0, V = 0, vslices = 0;
-    size_t off_vec, off_vflag, off_key, off_kflag, off_log, off_lflag, bytes;
+    size_t off_vec, off_key, off_kflag, off_log, off_lflag, bytes;
     unsigned char *mine = nullptr;             // this rank's mailbox
     std::vector<void *> opened;                // peers' mappings (cudaIpcCloseMemHandle)
     TpPeers peers = {};
@@ -57,13 +60,12 @@ struct TpState {
     unsigned *seq = nullptr;                   // device step counter
 };
 
-// layout of a mailbox: vector slots, vector flags, key slots, key flags,
-// logits row, logits flags
+// layout of a mailbox: vector lines, key slots, key flags, logits row,
+// logits flags
 static void tp_layout(TpState &t) {
     const size_t N = (size_t)t.n;
     t.off_vec = 0;
-    t.off_vflag = t.off_vec + 2 * N * t.H * sizeof(double);
-    t.off_key = t.off_vflag + ((2 * N * t.slices * 4 + 255) / 256) * 256;
+    t.off_key = t.off_vec + 2 * N * t.H * 16;
     t.off_kflag = t.off_key + 2 * N * 8;
     t.off_log = t.off_kflag + 256;
     t.off_lflag = t.off_log + (((size_t)t.V * 2 + 255) / 256) * 256;
@@ -91,40 +93,64 @@ MLXD_DEV bool wait_flag(const unsigned *p, unsigned v, int *err) {
     }
 }
 
-// out = bf16(res + bf16(sum over ranks of part)), slice per CTA
-__global__ void __launch_bounds__(TP_SLICE) tp_sum_kernel(TpPeers peers, unsigned char *mine, size_t off_vec,
-                                                          size_t off_vflag, int n, int rank, int H, int slices,
-                                                          const double *part, const uint16_t *res, uint16_t *out,
-                                                          const unsigned *seq, int L2, int idx, int *err) {
+MLXD_DEV void st_line(uint32_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+MLXD_DEV uint4 ld_line(const uint32_t *p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+// the line at p once both halves hold the epoch; false (error word set)
+// after about one second
+MLXD_DEV bool wait_line(const uint32_t *p, unsigned epoch, uint4 &v, int *err) {
+    v = ld_line(p);
+    if (v.y == epoch && v.w == epoch) return true;
+    const unsigned long long t0 = global_ns();
+    for (unsigned i = 1;; i++) {
+        v = ld_line(p);
+        if (v.y == epoch && v.w == epoch) return true;
+        if ((i & 255u) == 0 && global_ns() - t0 > 1000000000ull) {
+            atomicExch(err, 1);
+            return false;
+        }
+    }
+}
+
+// out = bf16(res + bf16(sum over ranks of part)), one row per thread
+__global__ void __launch_bounds__(TP_SLICE) tp_sum_kernel(TpPeers peers, unsigned char *mine, size_t off_vec, int n,
+                                                          int rank, int H, const double *part, const uint16_t *res,
+                                                          uint16_t *out, const unsigned *seq, int L2, int idx,
+                                                          int *err) {
     MLXD_TRACE_START
     pdl_wait();
     MLXD_TRACE_WAITED
-    const int c = blockIdx.x, tid = threadIdx.x, row = c * TP_SLICE + tid;
+    const int row = blockIdx.x * TP_SLICE + threadIdx.x;
     const unsigned epoch = *seq * (unsigned)L2 + (unsigned)idx + 1u;
     const int buf = idx & 1;
-    const double v = row < H ? part[row] : 0.0;
-    for (int p = 0; p < n; p++) {
-        double *slot = reinterpret_cast<double *>(peers.mb[p] + off_vec) + ((size_t)buf * n + rank) * H;
-        if (row < H) slot[row] = v;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
+    if (row < H) {
+        const unsigned long long bits = (unsigned long long)__double_as_longlong(part[row]);
+        const uint32_t lo = (uint32_t)bits, hi = (uint32_t)(bits >> 32);
         for (int p = 0; p < n; p++) {
-            unsigned *fl = reinterpret_cast<unsigned *>(peers.mb[p] + off_vflag) + ((size_t)buf * n + rank) * slices + c;
-            st_release_sys(fl, epoch);
+            uint32_t *line = reinterpret_cast<uint32_t *>(peers.mb[p] + off_vec) + (((size_t)buf * n + rank) * H + row) * 4;
+            st_line(line, lo, epoch, hi, epoch);
         }
     }
-    if (tid < n) {
-        const unsigned *fl = reinterpret_cast<const unsigned *>(mine + off_vflag) + ((size_t)buf * n + tid) * slices + c;
-        wait_flag(fl, epoch, err);
-    }
-    __syncthreads();
+    // the next projection's CTAs may start loading weights during the wait
     pdl_trigger();
     if (row < H) {
-        const double *slots = reinterpret_cast<const double *>(mine + off_vec) + (size_t)buf * n * H;
         double s = 0.0;
-        for (int src = 0; src < n; src++) s += __ldcv(slots + (size_t)src * H + row);
+        bool ok = true;
+        for (int src = 0; src < n && ok; src++) {
+            const uint32_t *line = reinterpret_cast<const uint32_t *>(mine + off_vec) + (((size_t)buf * n + src) * H + row) * 4;
+            uint4 v;
+            ok = wait_line(line, epoch, v, err);
+            s += __longlong_as_double((long long)(((unsigned long long)v.z << 32) | v.x));
+        }
         out[row] = f2bf(__fadd_rn(bf2f(res[row]), bf2f(d2bf(s))));
     }
     MLXD_TRACE_END(0x30)
@@ -309,13 +335,12 @@ int tp_sum(mlxd_model *m, const double *part, const uint16_t *res, uint16_t *out
     }
     TpPeers peers = t->peers;
     unsigned char *mine = t->mine;
-    size_t ov = t->off_vec, of = t->off_vflag;
-    int n = t->n, rank = t->rank, H = t->H, slices = t->slices, L2 = t->L2;
+    size_t ov = t->off_vec;
+    int n = t->n, rank = t->rank, H = t->H, L2 = t->L2;
     int *err = t->err;
     const unsigned *seq = t->seq;
-    void *args[] = {&peers, &mine, &ov, &of, &n, &rank, &H, &slices, (void *)&part, (void *)&res, &out,
-                    (void *)&seq, &L2, &idx, &err};
-    return launch_pdl(st, pdl, dim3(slices), dim3(TP_SLICE), (const void *)tp_sum_kernel, args);
+    void *args[] = {&peers, &mine, &ov, &n, &rank, &H, (void *)&part, (void *)&res, &out, (void *)&seq, &L2, &idx, &err};
+    return launch_pdl(st, pdl, dim3(t->slices), dim3(TP_SLICE), (const void *)tp_sum_kernel, args);
 }
 
 int tp_argmax(mlxd_model *m, unsigned long long *amax, int32_t *d_pos, int32_t *token, cudaStream_t st, bool pdl) {
