@@ -410,7 +410,8 @@ def main():
         dom = g["gate_up"]
         tr = load_traffic().get("gate_up") if world == 1 and args.workload == "qwen3-8b-4bit" else None
         line["roofline"] = {
-            "kernel": "qgemv (decode 4-bit GEMV, fused SwiGLU epilogue), gate_up shard %dx%d" % (
+            "kernel": "qgemv_i8 (decode 4-bit GEMV, plain prologue and store epilogue, launched alone), "
+                      "gate_up shape %dx%d" % (
                 dom["rows"], dom["cols"]),
             "bound": "hbm", "achieved": dom["gbs"], "peak": hbm,
             "unit": "GB/s", "frac": round(dom["gbs"] / hbm, 4),

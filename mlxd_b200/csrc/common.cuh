@@ -129,6 +129,20 @@ MLXD_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// A 16-byte line {a, b, c, d} written by one vector store / read by one
+// vector load, bypassing L1 (the tensor-parallel exchange lines)
+MLXD_DEV void st_line(uint32_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+MLXD_DEV uint4 ld_line(const uint32_t *p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
 MLXD_DEV unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -31,6 +31,14 @@ struct GemvArgs {
     int grid_cap;               // decode layout: at most this many CTAs (0: one per SM)
     int res_early;              // EPI_RESIDUAL: the residual was complete before the producer of
                                 // x started, so a chained launch requests it before its wait
+    // EPI_PARTIAL inside a tensor-parallel decode step (decode layout only):
+    // each row value leaves as a 16-byte line {low word, epoch, high word,
+    // epoch} at tp_line[p] + 4 row for every rank p (tp.cu), epoch =
+    // *tp_seq * tp_mul + tp_add; yf is not written
+    uint32_t *tp_line[8];
+    int tp_n;
+    const unsigned *tp_seq;
+    unsigned tp_mul, tp_add;
 };
 // one token (decode); PDL-chained when pdl
 int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl);
@@ -78,6 +86,11 @@ int tp_sum(mlxd_model *m, const double *part, const uint16_t *res, uint16_t *out
            bool pdl);
 // greedy: the largest of the ranks' argmax keys -> token; position + 1,
 // step counter + 1
+// the row-parallel projection's send half of exchange idx, for its GEMV
+// epilogue (GemvArgs tp_*), and the receive half: out = bf16(res + bf16(sum
+// over ranks of the lines)); only for decode-layout projections
+int tp_send_args(mlxd_model *m, int idx, GemvArgs &a);
+int tp_recv(mlxd_model *m, const uint16_t *res, uint16_t *out, int idx, cudaStream_t st, bool pdl);
 int tp_argmax(mlxd_model *m, unsigned long long *amax, int32_t *d_pos, int32_t *token, cudaStream_t st, bool pdl);
 // every rank's logits shard into every rank's full row (tp_full_logits)
 int tp_gather_logits(mlxd_model *m, const uint16_t *logits, cudaStream_t st, bool pdl);

@@ -384,6 +384,10 @@ int linear_any(mlxd_model *m, const QMat &W, const uint16_t *x, int S, int epi, 
 namespace mlxd {
 
 // one token through every layer with the fused decode kernels
+// a row-parallel projection whose decode GEMV sends its rows' exchange lines
+// itself (decode layout); others go through tp_sum's f64 partials
+static bool tp_fused(const QMat &W) { return W.ti8 && W.sbi && W.fast(); }
+
 static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool want_logits,
                        uint16_t *logits_out, bool argmax, cudaStream_t st, bool pdl) {
     const mlxd_model_config &c = m->c;
@@ -441,7 +445,12 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         o.gws = m->gws;
         o.gws_bytes = m->gws_bytes;
         o.x = m->att;
-        if (tp) {
+        if (tp && tp_fused(L.o)) {
+            // the GEMV's epilogue sends its rows; the exchange kernel receives
+            if (tp_send_args(m, 2 * l, o) || qgemv(L.o, PRO_PLAIN, EPI_PARTIAL, o, st, pdl) ||
+                tp_recv(m, m->h, m->h1, 2 * l, st, pdl))
+                return -1;
+        } else if (tp) {
             o.yf = m->part_h;
             if (qgemv(L.o, PRO_PLAIN, EPI_PARTIAL, o, st, pdl)) return -1;
             if (tp_sum(m, m->part_h, m->h, m->h1, 2 * l, st, pdl)) return -1;
@@ -463,7 +472,11 @@ static int decode_step(mlxd_model *m, mlxd_kv *kv, const int32_t *ids_dev, bool 
         dn.gws = m->gws;
         dn.gws_bytes = m->gws_bytes;
         dn.x = m->act;
-        if (tp) {
+        if (tp && tp_fused(L.down)) {
+            if (tp_send_args(m, 2 * l + 1, dn) || qgemv(L.down, PRO_PLAIN, EPI_PARTIAL, dn, st, pdl) ||
+                tp_recv(m, m->h1, m->h, 2 * l + 1, st, pdl))
+                return -1;
+        } else if (tp) {
             dn.yf = m->part_h;
             if (qgemv(L.down, PRO_PLAIN, EPI_PARTIAL, dn, st, pdl)) return -1;
             if (tp_sum(m, m->part_h, m->h1, m->h, 2 * l + 1, st, pdl)) return -1;

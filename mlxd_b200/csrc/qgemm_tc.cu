@@ -48,12 +48,20 @@ constexpr size_t XG_SMEM = 1024 + (size_t)XG_NS * XG_STAGE + 256 + (size_t)XG_BM
 static __device__ int g_xgemm_err;
 
 // per (group, token) entry of the GEMM's input table: tf = T_g * 2^(E_g - 20)
-// (NaN for a non-finite group) and E_g
+// (NaN for a non-finite group), E_g, and the high word 0x43300000 +
+// (E_g - 20) << 20 that scales a group sum by 2^(E_g - 20) (int_times_pow2),
+// made once here instead of per output row
 struct XTab {
     double tf;
     int e;
-    int pad;
+    int hi;
 };
+
+// v * 2^(E_g - 20) for |v| < 2^31, exactly: int_times_pow2 with the table's
+// high word
+MLXD_DEV double int_times_pow2_hi(int v, int hi) {
+    return __hiloint2double(hi, v ^ (int)0x80000000) - __hiloint2double(hi, (int)0x80000000);
+}
 
 // K-major operand with 128-byte rows in the 128B swizzle: 8-row atoms of
 // 1024 B (stride byte offset), leading offset unused (1), descriptor version 1
@@ -139,7 +147,7 @@ __global__ void xq_kernel(const uint16_t *__restrict__ x, int S, int S_pad, int 
         XTab e;
         e.tf = bad ? __longlong_as_double(0x7ff8000000000000ll) : int_times_pow2(tsum, E - 20);
         e.e = E;
-        e.pad = 0;
+        e.hi = 0x43300000 + (E - 20) * (1 << 20);
         tab[(size_t)g * S_pad + s] = e;
     }
 }
@@ -344,7 +352,7 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                     const int t = tp * 8 + k;
                     const int P = (int)v[3 * k] + ((int)v[3 * k + 1] << 7) + ((int)v[3 * k + 2] << 14);
                     const XTab e = tb[t];
-                    acc[t] = fma(sc, int_times_pow2(P, e.e - 20), acc[t]);
+                    acc[t] = fma(sc, int_times_pow2_hi(P, e.hi), acc[t]);
                     acc[t] = fma(bi, e.tf, acc[t]);
                 }
             }

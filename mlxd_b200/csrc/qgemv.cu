@@ -86,14 +86,14 @@ __global__ void repack_sbi_kernel(const uint16_t *__restrict__ s, const uint16_t
 }
 
 // decode layout of a whole matrix from its MLX arrays (already in device
-// memory, rows in the matrix's own order: for gate|up the decode row block
-// 2p is gate rows 16p.., 2p+1 the up rows, i.e. the MLX arrays' 64-row
-// blocks regrouped by 16)
+// memory, rows in the matrix's own order: for gate|up the decode row block p
+// holds gate rows 8p..8p+7 then up rows 8p..8p+7, so that one row block is
+// a whole SwiGLU unit; the MLX arrays alternate 64 gate and 64 up rows)
 __global__ void gateup_rows_kernel(int inter, int *map) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;   // decode row
     if (r >= 2 * inter) return;
-    const int rb = r / 16, within = r % 16, p = rb >> 1, up = rb & 1;
-    const int logical = p * 16 + within;                    // gate/up row index
+    const int rb = r / 16, within = r % 16, up = within >> 3;
+    const int logical = rb * 8 + (within & 7);              // gate/up row index
     map[r] = (logical / 64) * 128 + up * 64 + logical % 64;
 }
 
@@ -171,7 +171,14 @@ MLXD_DEV void epi_out(const GemvArgs &a, int row, double v, double vu, const uin
         const float r = bf2f(res_s ? *res_s : a.residual[row]);
         a.y[row] = f2bf(__fadd_rn(r, bf2f(d2bf(v))));
     } else if constexpr (EPI == EPI_PARTIAL) {
-        a.yf[row] = v;
+        if (a.tp_n > 0) {
+            const unsigned epoch = *a.tp_seq * a.tp_mul + a.tp_add;
+            const unsigned long long bits = (unsigned long long)__double_as_longlong(v);
+            for (int p = 0; p < a.tp_n; p++)
+                st_line(a.tp_line[p] + (size_t)row * 4, (uint32_t)bits, epoch, (uint32_t)(bits >> 32), epoch);
+        } else {
+            a.yf[row] = v;
+        }
     } else {
         a.y[row] = d2bf(v);
     }
@@ -208,8 +215,8 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
     return L;
 }
 
-// CTA c owns units [c*U/G, (c+1)*U/G) (a unit is a row block, or a gate|up
-// pair of row blocks for SwiGLU); warp w of the NW warps takes items w, w+NW,
+// CTA c owns units [c*U/G, (c+1)*U/G) (a unit is a row block: for SwiGLU
+// 8 gate rows and their 8 up rows); warp w of the NW warps takes items w, w+NW,
 // ... of that range and keeps the next DEPTH items in registers while
 // computing the current one, the first DEPTH of them requested before the
 // PDL wait. Each item's 16 f64 partials go to their own place in shared
@@ -221,7 +228,7 @@ static __host__ __device__ inline I8Smem i8_layout(int cols, int pool_items, int
 template <int PRO, int EPI, int NW, int DEPTH, bool SM2>
 __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int pool_items) {
     constexpr int NT = NW * 32;
-    constexpr int UNIT_RB = EPI == EPI_SWIGLU ? 2 : 1;
+    constexpr int UNIT_RB = 1;
     static_assert(DEPTH == 1 || DEPTH == 2, "register item buffers");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(16) float s_red[NW];
@@ -309,15 +316,16 @@ __global__ void __launch_bounds__(NW * 32, 1) qgemv_i8_kernel(GemvArgs a, int po
         done = __shfl_sync(0xffffffffu, done, 0);
         if (done && lane < 16) {
             __threadfence_block();
-            double acc[UNIT_RB];
-#pragma unroll
-            for (int u = 0; u < UNIT_RB; u++) {
-                double sum = 0.0;
-                for (int i = u * nbk; i < (u + 1) * nbk; i++) sum += ps[i * 16 + lane];
-                acc[u] = sum;
+            double acc = 0.0;
+            for (int i = 0; i < nbk; i++) acc += ps[i * 16 + lane];
+            if constexpr (EPI == EPI_SWIGLU) {
+                // lane l < 8: gate row l of the block; its up row is lane l + 8
+                const double up = __shfl_sync(0x0000ffffu, acc, (lane & 7) + 8);
+                if (lane < 8) epi_out<EPI>(a, (u0 + unit) * 8 + lane, acc, up, nullptr, best);
+            } else {
+                const int row = (u0 + unit) * 16 + lane;
+                epi_out<EPI>(a, row, acc, acc, res_s ? s_res + unit * 16 + lane : nullptr, best);
             }
-            const int row = (u0 + unit) * 16 + lane;
-            epi_out<EPI>(a, row, acc[0], acc[UNIT_RB - 1], res_s ? s_res + unit * 16 + lane : nullptr, best);
         }
     };
     // item k from register buffer d, refilled with item kn as it is read
@@ -418,7 +426,7 @@ bool smem_allowed(const void *kern, size_t bytes) {
 template <int PRO, int EPI, int NW, int DEPTH, bool SM2>
 static int launch_gemv_i8_cfg(GemvArgs a, cudaStream_t st, bool pdl) {
     auto kern = qgemv_i8_kernel<PRO, EPI, NW, DEPTH, SM2>;
-    const int unit_rb = EPI == EPI_SWIGLU ? 2 : 1;
+    const int unit_rb = 1;
     const int n_units = a.rows / 16 / unit_rb;
     int grid = num_sms();
     if (a.grid_cap > 0 && grid > a.grid_cap) grid = a.grid_cap;
@@ -662,8 +670,12 @@ int qgemv(const QMat &W, int pro, int epi, GemvArgs a, cudaStream_t st, bool pdl
         set_error("qgemv: x and the norm weights must be 16-byte aligned");
         return -1;
     }
+    if (a.tp_n > 0 && !(W.ti8 && W.sbi && W.fast() && epi == EPI_PARTIAL)) {
+        set_error("qgemv: the tensor-parallel send needs a decode-layout partial projection");
+        return -1;
+    }
     if (W.ti8 && W.sbi && W.fast()) {
-        if (W.rows % (epi == EPI_SWIGLU ? 32 : 16)) {
+        if (W.rows % 16) {
             set_error("qgemv: rows %d not a multiple of the row block", W.rows);
             return -1;
         }

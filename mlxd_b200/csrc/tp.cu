@@ -93,18 +93,6 @@ MLXD_DEV bool wait_flag(const unsigned *p, unsigned v, int *err) {
     }
 }
 
-MLXD_DEV void st_line(uint32_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
-                 : "memory");
-}
-MLXD_DEV uint4 ld_line(const uint32_t *p) {
-    uint4 v;
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p)
-                 : "memory");
-    return v;
-}
 // the line at p once both halves hold the epoch; false (error word set)
 // after about one second
 MLXD_DEV bool wait_line(const uint32_t *p, unsigned epoch, uint4 &v, int *err) {
@@ -154,6 +142,32 @@ __global__ void __launch_bounds__(TP_SLICE) tp_sum_kernel(TpPeers peers, unsigne
         out[row] = f2bf(__fadd_rn(bf2f(res[row]), bf2f(d2bf(s))));
     }
     MLXD_TRACE_END(0x30)
+}
+
+// the receive half alone, for a projection whose GEMV epilogue stored its
+// rows' lines itself: out = bf16(res + bf16(sum over ranks)), one row per
+// thread
+__global__ void __launch_bounds__(TP_SLICE) tp_recv_kernel(const unsigned char *mine, size_t off_vec, int n, int H,
+                                                           const uint16_t *res, uint16_t *out, const unsigned *seq,
+                                                           int L2, int idx, int *err) {
+    MLXD_TRACE_START
+    pdl_wait();
+    MLXD_TRACE_WAITED
+    pdl_trigger();
+    const int row = blockIdx.x * TP_SLICE + threadIdx.x;
+    if (row >= H) return;
+    const unsigned epoch = *seq * (unsigned)L2 + (unsigned)idx + 1u;
+    const int buf = idx & 1;
+    double s = 0.0;
+    bool ok = true;
+    for (int src = 0; src < n && ok; src++) {
+        const uint32_t *line = reinterpret_cast<const uint32_t *>(mine + off_vec) + (((size_t)buf * n + src) * H + row) * 4;
+        uint4 v;
+        ok = wait_line(line, epoch, v, err);
+        s += __longlong_as_double((long long)(((unsigned long long)v.z << 32) | v.x));
+    }
+    out[row] = f2bf(__fadd_rn(bf2f(res[row]), bf2f(d2bf(s))));
+    MLXD_TRACE_END(0x31)
 }
 
 // greedy: the ranks' argmax keys; every rank takes the largest and ends the
@@ -341,6 +355,37 @@ int tp_sum(mlxd_model *m, const double *part, const uint16_t *res, uint16_t *out
     const unsigned *seq = t->seq;
     void *args[] = {&peers, &mine, &ov, &n, &rank, &H, (void *)&part, (void *)&res, &out, (void *)&seq, &L2, &idx, &err};
     return launch_pdl(st, pdl, dim3(t->slices), dim3(TP_SLICE), (const void *)tp_sum_kernel, args);
+}
+
+int tp_send_args(mlxd_model *m, int idx, GemvArgs &a) {
+    TpState *t = (TpState *)m->tp;
+    if (!t) {
+        set_error("tensor parallel exchange used before tp_init");
+        return -1;
+    }
+    const int buf = idx & 1;
+    for (int p = 0; p < t->n; p++)
+        a.tp_line[p] = reinterpret_cast<uint32_t *>(t->peers.mb[p] + t->off_vec) + ((size_t)buf * t->n + t->rank) * t->H * 4;
+    a.tp_n = t->n;
+    a.tp_seq = t->seq;
+    a.tp_mul = (unsigned)t->L2;
+    a.tp_add = (unsigned)idx + 1u;
+    return 0;
+}
+
+int tp_recv(mlxd_model *m, const uint16_t *res, uint16_t *out, int idx, cudaStream_t st, bool pdl) {
+    TpState *t = (TpState *)m->tp;
+    if (!t) {
+        set_error("tensor parallel exchange used before tp_init");
+        return -1;
+    }
+    const unsigned char *mine = t->mine;
+    size_t ov = t->off_vec;
+    int n = t->n, H = t->H, L2 = t->L2;
+    int *err = t->err;
+    const unsigned *seq = t->seq;
+    void *args[] = {(void *)&mine, &ov, &n, &H, (void *)&res, &out, (void *)&seq, &L2, &idx, &err};
+    return launch_pdl(st, pdl, dim3(t->slices), dim3(TP_SLICE), (const void *)tp_recv_kernel, args);
 }
 
 int tp_argmax(mlxd_model *m, unsigned long long *amax, int32_t *d_pos, int32_t *token, cudaStream_t st, bool pdl) {
