@@ -174,6 +174,12 @@ int  mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void
    x: device bf16 input of max(cols); y: device output of max(rows). */
 int  mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x,
                             void *y, float *ms_out);
+/* The same with every launch chained to the previous one by programmatic
+   dependent launch (a launch's CTAs start and load their first weights while
+   the previous one finishes), the launch mode of the decode step's graph
+   (no reference counterpart). */
+int  mlxd_cuda_linear_timed_chained(const mlxd_linear *const *ls, int n, int iters,
+                                    const void *x, void *y, float *ms_out);
 /* fwd_rmsnorm (forward.c:186-219) over rows of n; device pointers */
 int  mlxd_cuda_rmsnorm(const void *x, int rows, int n, const void *w, float eps,
                        void *y, void *stream);

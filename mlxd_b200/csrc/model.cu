@@ -1157,8 +1157,10 @@ int mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void 
     return qgemv_static_scratch(l->W, (const uint16_t *)x, (uint16_t *)y, (cudaStream_t)stream);
 }
 
-int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y,
-                           float *ms_out) {
+// pdl: each launch chained to the previous one by programmatic dependent
+// launch, as the decode step's graph chains its kernels
+static int linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y, bool pdl,
+                        float *ms_out) {
     if (!ls || n <= 0 || iters <= 0 || !x || !y || !ms_out) return -1;
     cudaStream_t st;
     MLXD_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
@@ -1172,7 +1174,7 @@ int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const
         g.y = (uint16_t *)y;
         g.gws = ls[i]->ws;
         g.gws_bytes = ls[i]->ws_bytes;
-        return qgemv(ls[i]->W, PRO_PLAIN, EPI_STORE, g, st, false);
+        return qgemv(ls[i]->W, PRO_PLAIN, EPI_STORE, g, st, pdl);
     };
     for (int i = 0; i < n && !rc; i++) rc = one(i);   // warm-up
     cudaEventRecord(a, st);
@@ -1190,6 +1192,16 @@ int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const
     cudaEventDestroy(b);
     cudaStreamDestroy(st);
     return rc;
+}
+
+int mlxd_cuda_linear_timed(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y,
+                           float *ms_out) {
+    return linear_timed(ls, n, iters, x, y, false, ms_out);
+}
+
+int mlxd_cuda_linear_timed_chained(const mlxd_linear *const *ls, int n, int iters, const void *x, void *y,
+                                   float *ms_out) {
+    return linear_timed(ls, n, iters, x, y, true, ms_out);
 }
 
 int mlxd_cuda_rmsnorm(const void *x, int rows, int n, const void *w, float eps, void *y, void *stream) {

@@ -116,6 +116,8 @@ _SIGS = {
     "mlxd_cuda_linear_noalloc": (C.c_int, [P, P, P, P]),
     "mlxd_cuda_linear_timed": (C.c_int, [C.POINTER(P), C.c_int, C.c_int, P, P,
                                          C.POINTER(C.c_float)]),
+    "mlxd_cuda_linear_timed_chained": (C.c_int, [C.POINTER(P), C.c_int, C.c_int, P, P,
+                                                 C.POINTER(C.c_float)]),
     "mlxd_cuda_rmsnorm": (C.c_int, [P, C.c_int, C.c_int, P, C.c_float, P, P]),
     "mlxd_cuda_sample": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(Sampling), P, C.c_int,
                                    C.c_uint64, P, P, P, P]),
@@ -488,12 +490,14 @@ class Linear:
             pass
 
 
-def linear_timed(linears, iters, x_dev, y_dev):
-    """Mean ms per decode-GEMV launch over round-robin launches."""
+def linear_timed(linears, iters, x_dev, y_dev, chained=False):
+    """Mean ms per decode-GEMV launch over round-robin launches; chained:
+    each launch chained to the previous one by programmatic dependent launch
+    (the decode graph's launch mode)."""
     arr = (C.c_void_p * len(linears))(*[l.h.value for l in linears])
     ms = C.c_float()
-    check(lib().mlxd_cuda_linear_timed(arr, len(linears), iters, x_dev.ptr, y_dev.ptr,
-                                       C.byref(ms)), "linear_timed")
+    fn = lib().mlxd_cuda_linear_timed_chained if chained else lib().mlxd_cuda_linear_timed
+    check(fn(arr, len(linears), iters, x_dev.ptr, y_dev.ptr, C.byref(ms)), "linear_timed")
     return ms.value
 
 

@@ -1,7 +1,9 @@
 """Decode-GEMV microbenchmark (the qmv measurement of the decoder step).
 
 Times the 4-bit decode GEMV of libmlxd_cuda at a model's projection shapes
-with CUDA events inside the library (mlxd_cuda_linear_timed). Weights are
+with CUDA events inside the library: launched alone (mlxd_cuda_linear_timed)
+and chained to the previous launch by programmatic dependent launch as in
+the decode step's graph (mlxd_cuda_linear_timed_chained). Weights are
 rotated over copies that together exceed the 126 MB L2, so every launch
 streams its weights from HBM. Achieved GB/s = algorithmic bytes (packed
 weights + bf16 scale/bias per group + x in + y out) / mean launch time.
@@ -54,11 +56,13 @@ def measure(rows, cols, iters=None, copies=None, group=64, min_bytes=400e6):
         lins.append(cuda.Linear(w, s, b, group, rows=rows, cols=cols))
         w.free(), s.free(), b.free()
     ms = cuda.linear_timed(lins, iters, x, y)
+    ms_c = cuda.linear_timed(lins, iters, x, y, chained=True)
     for l in lins:
         l.close()
     gbs = wbytes / (ms * 1e-3) / 1e9
     return {"rows": rows, "cols": cols, "us": round(ms * 1e3, 2), "bytes": wbytes,
-            "gbs": round(gbs, 1), "copies": copies, "iters": iters}
+            "gbs": round(gbs, 1), "copies": copies, "iters": iters,
+            "chained_us": round(ms_c * 1e3, 2), "chained_gbs": round(wbytes / (ms_c * 1e-3) / 1e9, 1)}
 
 
 def prefill_gemm(rows=24576, cols=4096, S=512, reps=3):
