@@ -45,6 +45,8 @@ MLXD_TRACE_BINDER(tp)
 
 constexpr int TP_SLICE = 128;      // rows per CTA (and per flag)
 constexpr int TP_MAX = 8;          // ranks
+static_assert(TP_MAX <= (int)(sizeof(GemvArgs::tp_line) / sizeof(GemvArgs::tp_line[0])),
+              "the GEMV's send half addresses every rank's mailbox");
 
 struct TpPeers {
     unsigned char *mb[TP_MAX];     // every rank's mailbox (own included), mapped here
