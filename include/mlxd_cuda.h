@@ -168,7 +168,7 @@ int  mlxd_cuda_linear(const mlxd_linear *l, const void *x, int S, void *y, void 
    capture. Calls whose kernels can overlap on the GPU (unordered streams)
    race on the array. Device pointers. */
 int  mlxd_cuda_linear_noalloc(const mlxd_linear *l, const void *x, void *y, void *stream);
-/* qGEMV measurement (no reference counterpart; the survey's qmv microbench):
+/* qGEMV measurement (no reference counterpart; the decode-GEMV microbenchmark):
    launches the decode GEMV of n projections round-robin, iters rounds, on an
    internal stream bracketed by CUDA events; *ms_out = mean ms per launch.
    x: device bf16 input of max(cols); y: device output of max(rows). */
