@@ -768,27 +768,49 @@ __global__ void __launch_bounds__(RS_T) rs_hist_kernel(int V, SampWork w, int pa
     w.rs_off[tid * G + blockIdx.x] = h[tid];
 }
 
-// exclusive prefix over the (digit, tile) counts in digit-major order
+// exclusive prefix over the (digit, tile) counts in digit-major order: the
+// counts go in chunks of 1024, one per thread (coalesced; the loads of 8
+// chunks issued together), each chunk scanned across the CTA (warp shuffles,
+// then the 32 warp totals) and offset by the total of the chunks before it
 __global__ void __launch_bounds__(1024) rs_scan_kernel(SampWork w, int G) {
     if (w.meta->mode != 2) return;
-    __shared__ unsigned part[1024];
-    const int tid = threadIdx.x, n = 256 * G;
-    const int per = (n + 1023) / 1024, lo = tid * per, hi = min(n, lo + per);
-    unsigned s = 0;
-    for (int i = lo; i < hi; i++) s += w.rs_off[i];
-    part[tid] = s;
-    __syncthreads();
-    for (int o = 1; o < 1024; o <<= 1) {
-        const unsigned v = tid >= o ? part[tid - o] : 0u;
-        __syncthreads();
-        part[tid] += v;
-        __syncthreads();
-    }
-    unsigned run = part[tid] - s;
-    for (int i = lo; i < hi; i++) {
-        const unsigned c = w.rs_off[i];
-        w.rs_off[i] = run;
-        run += c;
+    __shared__ unsigned wsum[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, n = 256 * G;
+    const int nch = (n + 1023) / 1024;
+    unsigned run = 0u;   // the counts of the chunks before this one
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+        unsigned v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = (c0 + j) * 1024 + tid;
+            v[j] = i < n ? w.rs_off[i] : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (c0 + j >= nch) break;
+            unsigned x = v[j];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            if (lane == 31) wsum[warp] = x;
+            __syncthreads();
+            if (warp == 0) {
+                unsigned t = wsum[lane];
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned y = __shfl_up_sync(0xffffffffu, t, o);
+                    if (lane >= o) t += y;
+                }
+                wsum[lane] = t;
+            }
+            __syncthreads();
+            const int i = (c0 + j) * 1024 + tid;
+            if (i < n) w.rs_off[i] = run + (warp ? wsum[warp - 1] : 0u) + (x - v[j]);
+            run += wsum[31];
+            __syncthreads();   // wsum is rewritten by the next chunk
+        }
     }
 }
 
