@@ -768,49 +768,46 @@ __global__ void __launch_bounds__(RS_T) rs_hist_kernel(int V, SampWork w, int pa
     w.rs_off[tid * G + blockIdx.x] = h[tid];
 }
 
-// exclusive prefix over the (digit, tile) counts in digit-major order: the
-// counts go in chunks of 1024, one per thread (coalesced; the loads of 8
-// chunks issued together), each chunk scanned across the CTA (warp shuffles,
-// then the 32 warp totals) and offset by the total of the chunks before it
+// exclusive prefix over the (digit, tile) counts in digit-major order: warp w
+// owns a contiguous segment (a multiple of 32 counts); it sums its segment,
+// the 32 segment totals are scanned once, then each warp walks its segment
+// 32 counts at a time (coalesced), a warp scan per step plus the carry
 __global__ void __launch_bounds__(1024) rs_scan_kernel(SampWork w, int G) {
     if (w.meta->mode != 2) return;
-    __shared__ unsigned wsum[32];
+    __shared__ unsigned wtot[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, n = 256 * G;
-    const int nch = (n + 1023) / 1024;
-    unsigned run = 0u;   // the counts of the chunks before this one
-    for (int c0 = 0; c0 < nch; c0 += 8) {
-        unsigned v[8];
+    const int seg = ((n + 32 * 32 - 1) / (32 * 32)) * 32;
+    const int s0 = warp * seg, s1 = min(n, s0 + seg);
+    unsigned t = 0u;
+#pragma unroll 8
+    for (int i = s0 + lane; i < s1; i += 32) t += w.rs_off[i];
+    t = __reduce_add_sync(0xffffffffu, t);
+    if (lane == 0) wtot[warp] = t;
+    __syncthreads();
+    if (warp == 0) {
+        const unsigned own = wtot[lane];
+        unsigned x = own;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int i = (c0 + j) * 1024 + tid;
-            v[j] = i < n ? w.rs_off[i] : 0u;
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
+        wtot[lane] = x - own;
+    }
+    __syncthreads();
+    unsigned carry = wtot[warp];
+#pragma unroll 4
+    for (int b0 = s0; b0 < s1; b0 += 32) {
+        const int i = b0 + lane;
+        const unsigned v = i < s1 ? w.rs_off[i] : 0u;
+        unsigned x = v;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            if (c0 + j >= nch) break;
-            unsigned x = v[j];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
-                if (lane >= o) x += y;
-            }
-            if (lane == 31) wsum[warp] = x;
-            __syncthreads();
-            if (warp == 0) {
-                unsigned t = wsum[lane];
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const unsigned y = __shfl_up_sync(0xffffffffu, t, o);
-                    if (lane >= o) t += y;
-                }
-                wsum[lane] = t;
-            }
-            __syncthreads();
-            const int i = (c0 + j) * 1024 + tid;
-            if (i < n) w.rs_off[i] = run + (warp ? wsum[warp - 1] : 0u) + (x - v[j]);
-            run += wsum[31];
-            __syncthreads();   // wsum is rewritten by the next chunk
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
+        if (i < s1) w.rs_off[i] = carry + x - v;
+        carry += __shfl_sync(0xffffffffu, x, 31);
     }
 }
 
